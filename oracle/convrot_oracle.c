@@ -1,0 +1,227 @@
+/*
+ * CPU oracle for the ConvRot quantized-linear path.  TEST INFRASTRUCTURE ONLY:
+ * nothing in the shipped library links or calls this file.  It is imported by
+ * tests/, by __graft_entry__.smoke() as the checker, and by bench.py's
+ * cpu_baseline leg / `--impl reference` arm.
+ *
+ * It restates, in plain C with IEEE single precision and no FMA contraction
+ * (built with -ffp-contract=off, no -ffast-math), the arithmetic of the
+ * reference kernels of comfyui-turing-utils (kernel package 0.31.0):
+ *
+ *   kernel/csrc/turing/convrot_quant.cu:104-116   radix-4 stage, fp32 order
+ *   kernel/csrc/turing/convrot_quant.cu:444-473   stage order S = 1, 4, 16, 64
+ *   kernel/csrc/turing/convrot_quant.cu:360-376   fp32 -> bf16 RNE, NaN -> 0x7fff
+ *   kernel/csrc/turing/convrot_quant.cu:378-397   bf16 store of y, fp32 absmax
+ *   kernel/csrc/turing/convrot_quant.cu:475-510   per-token scale and codes
+ *   kernel/csrc/turing/convrot_quant.cu:163-182   SwiGLU / tanh-GELU loaders
+ *   kernel/csrc/turing/w4a8.cu:474-525            epilogue ((acc*a_s)*w_s)+bias
+ *   kernel/csrc/turing/bf16_epilogue.cu:105-113   epilogue (acc*a_s)*w_s
+ *   kernel/csrc/turing/w4a8.cu:34-72              signed int4, low nibble first
+ *
+ * The int32 contraction itself is exact integer arithmetic and lives in the
+ * Python wrapper (torch._int_mm / numpy).
+ */
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#define KGROUP 256
+
+static inline uint32_t f2u(float v) { uint32_t u; memcpy(&u, &v, 4); return u; }
+static inline float u2f(uint32_t u) { float v; memcpy(&v, &u, 4); return v; }
+
+/* convrot_quant.cu:360-372: round to nearest even, any NaN -> 0x7fff. */
+uint16_t ctu_oracle_f32_to_bf16(float value) {
+    const uint32_t bits = f2u(value);
+    if ((bits & 0x7fffffffu) > 0x7f800000u) return 0x7fffu;
+    uint16_t upper = (uint16_t)(bits >> 16);
+    const uint32_t rem = bits << 16;
+    if (rem > 0x80000000u || (rem == 0x80000000u && (upper & 1u))) ++upper;
+    return upper;
+}
+
+static inline float bf16_to_f32(uint16_t v) { return u2f((uint32_t)v << 16); }
+static inline float round_bf16(float v) { return bf16_to_f32(ctu_oracle_f32_to_bf16(v)); }
+
+/* convrot_quant.cu:104-116 for one stride S over a 256-group, out of place.
+ * Lane l of the reference's 64-thread group owns base = l%S + (l/S)*4S. */
+static void fht_stage(const float *src, float *dst, int S) {
+    for (int lane = 0; lane < 64; ++lane) {
+        const int base = (lane % S) + (lane / S) * (4 * S);
+        const float x0 = src[base], x1 = src[base + S];
+        const float x2 = src[base + 2 * S], x3 = src[base + 3 * S];
+        dst[base] = 0.5f * (x0 + x1 + x2 - x3);
+        dst[base + S] = 0.5f * (x0 + x1 - x2 + x3);
+        dst[base + 2 * S] = 0.5f * (x0 - x1 + x2 + x3);
+        dst[base + 3 * S] = 0.5f * (-x0 + x1 + x2 + x3);
+    }
+}
+
+/* The 4-stage radix-4 rotation of one 256-group (strides 1, 4, 16, 64). */
+void ctu_oracle_rotate_group(const float *in, float *out) {
+    float a[KGROUP], b[KGROUP];
+    fht_stage(in, a, 1);
+    fht_stage(a, b, 4);
+    fht_stage(b, a, 16);
+    fht_stage(a, out, 64);
+}
+
+/* convrot_quant.cu:163-169: silu(gate) * up in fp32 with the accurate expf. */
+static inline float swiglu_value(float gate, float up) {
+    return (gate / (1.0f + expf(-gate))) * up;
+}
+
+/* convrot_quant.cu:171-182: tanh-GELU in fp32, rounded to the input dtype.
+ * The reference is compiled with nvcc's default FMA contraction; the two
+ * products feeding an addition are contracted exactly as written here with
+ * fmaf so the C restatement follows the device's evaluation. */
+static inline float gelu_tanh_value(float x, int contract) {
+    const float kAlpha = 0.7978845608028654f;
+    const float kBeta = 0.044715f;
+    float inner;
+    if (contract) {
+        inner = fmaf((kBeta * x) * x, x, x);
+    } else {
+        inner = x + ((kBeta * x) * x) * x;
+    }
+    const float t = tanhf(kAlpha * inner);
+    const float activated = (0.5f * x) * (1.0f + t);
+    return round_bf16(activated);
+}
+
+/*
+ * Rotate one activation row and return the fp32 absmax over the rotated
+ * (unrounded) values, writing bf16(y) into ybits.  `mode`: 0 = plain bf16 row of
+ * k values, 1 = SwiGLU row of 2k values [gate | up], 2 = tanh-GELU row, 3 = GELU
+ * evaluated without contraction.
+ */
+static float rotate_row(const uint16_t *row, int k, int mode, uint16_t *ybits, float *yf) {
+    float absmax = 0.0f;
+    float in[KGROUP], out[KGROUP];
+    for (int g = 0; g < k / KGROUP; ++g) {
+        for (int i = 0; i < KGROUP; ++i) {
+            const int col = g * KGROUP + i;
+            float v;
+            if (mode == 1) {
+                v = swiglu_value(bf16_to_f32(row[col]), bf16_to_f32(row[k + col]));
+            } else if (mode == 2 || mode == 3) {
+                v = gelu_tanh_value(bf16_to_f32(row[col]), mode == 2);
+            } else {
+                v = bf16_to_f32(row[col]);
+            }
+            in[i] = v;
+        }
+        ctu_oracle_rotate_group(in, out);
+        for (int i = 0; i < KGROUP; ++i) {
+            const float y = out[i];
+            ybits[g * KGROUP + i] = ctu_oracle_f32_to_bf16(y);
+            if (yf) yf[g * KGROUP + i] = y;
+            /* convrot_quant.cu:396: fmaxf(fmaxf(|y0|,|y1|), fmaxf(|y2|,|y3|)),
+             * fmaxf ignores NaN, so the reduction order is immaterial. */
+            absmax = fmaxf(absmax, fabsf(y));
+        }
+    }
+    return absmax;
+}
+
+/* Rotated values only (fp32), for the rotation parity checks. */
+void ctu_oracle_rotate(const uint16_t *x, float *y, long rows, int k, int mode) {
+    const int width = mode == 1 ? 2 * k : k;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            if (k <= 65536) rotate_row(x + r * width, k, mode, ybits, y + r * (long)k);
+        }
+    }
+}
+
+/* convrot_quant.cu:475-510, int8 branch. */
+static void quantize_row_int8(const uint16_t *ybits, int k, float absmax, int8_t *codes, float *scale_out) {
+    const float scale = fmaxf(fminf(absmax, 3.38953139e38f) / 127.0f, 1.0e-30f);
+    *scale_out = scale;
+    const float rounded_scale = round_bf16(scale);
+    for (int c = 0; c < k; ++c) {
+        const float value = bf16_to_f32(ybits[c]);
+        const float divided = round_bf16(value / rounded_scale);
+        float q = nearbyintf(divided);
+        q = fminf(127.0f, fmaxf(-128.0f, q));
+        codes[c] = (int8_t)q;
+    }
+}
+
+/* convrot_quant.cu:475-500, int4 branch: multiply by the fp32 reciprocal of the
+ * unrounded scale, clamp to [-7, 7], pack the even column in the low nibble. */
+static void quantize_row_int4(const uint16_t *ybits, int k, float absmax, int8_t *packed, float *scale_out) {
+    const float scale = fmaxf(fminf(absmax, 3.38953139e38f) / 7.0f, 1.0e-10f);
+    *scale_out = scale;
+    const float inv_scale = 1.0f / scale;
+    for (int p = 0; p < k / 2; ++p) {
+        float lo = nearbyintf(bf16_to_f32(ybits[2 * p]) * inv_scale);
+        float hi = nearbyintf(bf16_to_f32(ybits[2 * p + 1]) * inv_scale);
+        lo = fminf(7.0f, fmaxf(-7.0f, lo));
+        hi = fminf(7.0f, fmaxf(-7.0f, hi));
+        const uint8_t lb = (uint8_t)(int8_t)lo & 0x0f;
+        const uint8_t hb = (uint8_t)(int8_t)hi & 0x0f;
+        packed[p] = (int8_t)(lb | (hb << 4));
+    }
+}
+
+/*
+ * Whole-row ConvRot quantize (the reference's bf16 row-buffer kernel,
+ * convrot_quant.cu:417-511).  x: rows x (mode==1 ? 2k : k) bf16 bit patterns.
+ * bits = 8: codes rows x k int8; bits = 4: rows x k/2 packed int4.  Returns 0, or
+ * -1 on an unsupported k.
+ */
+int ctu_oracle_convrot_quantize(const uint16_t *x, int8_t *codes, float *scales,
+                                long rows, int k, int bits, int mode) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
+    const int width = mode == 1 ? 2 * k : k;
+    const int out_width = bits == 4 ? k / 2 : k;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            const float absmax = rotate_row(x + r * width, k, mode, ybits, 0);
+            if (bits == 4) {
+                quantize_row_int4(ybits, k, absmax, codes + r * out_width, scales + r);
+            } else {
+                quantize_row_int8(ybits, k, absmax, codes + r * out_width, scales + r);
+            }
+        }
+    }
+    return 0;
+}
+
+/*
+ * Epilogue over an int32 accumulator (row stride acc_stride), w4a8.cu:474-525:
+ * out = bf16(((float(acc) * a_s[m]) * w_s[n]) + bias[n]).  `fused` selects a
+ * single-rounding fma for the last multiply-add (what nvcc's default FMA
+ * contraction produces when the bias node is inlined after the scale node);
+ * `has_bias` = 0 reproduces bf16_epilogue.cu:105-113 (no addition at all).
+ * w_scale_count = 1 broadcasts a scalar weight scale.
+ */
+void ctu_oracle_epilogue(const int32_t *acc, long acc_stride, const float *a_scale,
+                         const float *w_scale, long w_scale_count, const float *bias,
+                         uint16_t *out, long m, long n, int has_bias, int fused) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < m; ++i) {
+        const float as = a_scale[i];
+        for (long j = 0; j < n; ++j) {
+            const float ws = w_scale[w_scale_count == 1 ? 0 : j];
+            const float scaled = (float)acc[i * acc_stride + j] * as;
+            float v;
+            if (!has_bias) {
+                v = scaled * ws;
+            } else if (fused) {
+                v = fmaf(scaled, ws, bias[j]);
+            } else {
+                const float t = scaled * ws;
+                v = t + bias[j];
+            }
+            out[i * n + j] = ctu_oracle_f32_to_bf16(v);
+        }
+    }
+}

@@ -1,0 +1,194 @@
+"""CPU oracle for the ConvRot quantized-linear path (TEST INFRASTRUCTURE ONLY).
+
+Only ``tests/``, ``__graft_entry__.smoke()`` (as the checker) and ``bench.py``'s
+CPU-baseline leg may import this module.  The shipped library never calls it and
+has no CPU fallback.
+
+The arithmetic lives in ``convrot_oracle.c`` (a plain-C restatement of the
+reference kernels, see its header for the file:line it follows); this wrapper
+compiles/loads it and adds the exact int32 contraction and int4 packing helpers.
+
+Reference anchors (comfyui-turing-utils, kernel package 0.31.0):
+  * rotate + quantize: ``kernel/csrc/turing/convrot_quant.cu:104-135,378-510``
+  * int32 contraction: exact, pinned by ``kernel/scripts/validate_compatible.py:124-136``
+  * epilogue: ``kernel/csrc/turing/w4a8.cu:474-525``, ``bf16_epilogue.cu:105-113``
+  * signed int4 packing: ``kernel/csrc/turing/w4a8.cu:34-72``,
+    ``kernel/scripts/validate_compatible.py:28-40``
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+_HERE = Path(__file__).resolve().parent
+_SRC = _HERE / "convrot_oracle.c"
+_LIB_PATH = _HERE / "libconvrot_oracle.so"
+_lib = None
+
+MODE_PLAIN = 0
+MODE_SWIGLU = 1
+MODE_GELU = 2
+MODE_GELU_UNCONTRACTED = 3
+
+
+def build(force: bool = False) -> Path:
+    """Compile the C restatement (gcc, IEEE float, no contraction)."""
+    if force or not _LIB_PATH.exists() or _LIB_PATH.stat().st_mtime < _SRC.stat().st_mtime:
+        tmp = _LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
+        subprocess.run(
+            [
+                "gcc", "-O2", "-fopenmp", "-ffp-contract=off", "-fno-fast-math",
+                "-fPIC", "-shared", "-o", str(tmp), str(_SRC), "-lm",
+            ],
+            check=True,
+        )
+        os.replace(tmp, _LIB_PATH)
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is None:
+        lib = ctypes.CDLL(str(build()))
+        vp, i64, i32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int
+        lib.ctu_oracle_convrot_quantize.argtypes = [vp, vp, vp, i64, i32, i32, i32]
+        lib.ctu_oracle_convrot_quantize.restype = i32
+        lib.ctu_oracle_rotate.argtypes = [vp, vp, i64, i32, i32]
+        lib.ctu_oracle_rotate.restype = None
+        lib.ctu_oracle_epilogue.argtypes = [vp, i64, vp, vp, i64, vp, vp, i64, i64, i32, i32]
+        lib.ctu_oracle_epilogue.restype = None
+        lib.ctu_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
+        lib.ctu_oracle_f32_to_bf16.restype = ctypes.c_uint16
+        _lib = lib
+    return _lib
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round fp32 to bf16 (RNE, NaN -> 0x7fff) and return the uint16 bit patterns."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    bits = x.view(np.uint32)
+    upper = (bits >> 16).astype(np.uint32)
+    rem = bits & 0xFFFF
+    round_up = (rem > 0x8000) | ((rem == 0x8000) & ((upper & 1) == 1))
+    out = (upper + round_up).astype(np.uint16)
+    nan = (bits & 0x7FFFFFFF) > 0x7F800000
+    out[nan] = 0x7FFF
+    return out
+
+
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (np.asarray(bits, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def rotate(x_bits: np.ndarray, mode: int = MODE_PLAIN) -> np.ndarray:
+    """fp32 rotated activations (before bf16 rounding) for a [M, K] (or [M, 2K]) bf16 row block."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, width = x_bits.shape
+    k = width // 2 if mode == MODE_SWIGLU else width
+    y = np.empty((rows, k), dtype=np.float32)
+    _load().ctu_oracle_rotate(_ptr(x_bits), _ptr(y), rows, k, mode)
+    return y
+
+
+def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN):
+    """Reference ConvRot row quantizer on bf16 bit patterns.
+
+    Returns ``(codes, scales)``: int8 ``[M, K]`` (bits=8) or packed int4 ``[M, K/2]``
+    (bits=4), and fp32 ``[M]`` per-token scales.
+    """
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, width = x_bits.shape
+    k = width // 2 if mode == MODE_SWIGLU else width
+    if k % 256 != 0:
+        raise ValueError("ConvRot requires K divisible by 256")
+    codes = np.empty((rows, k // 2 if bits == 4 else k), dtype=np.int8)
+    scales = np.empty((rows,), dtype=np.float32)
+    rc = _load().ctu_oracle_convrot_quantize(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k, bits, mode)
+    if rc != 0:
+        raise ValueError(f"unsupported ConvRot width {k}")
+    return codes, scales
+
+
+def int8_gemm_s32(a: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Exact int32 contraction ``a[M,K] @ w[N,K]^T`` (no overflow for K < 131072)."""
+    import torch
+
+    a_t = torch.from_numpy(np.ascontiguousarray(a, dtype=np.int8))
+    w_t = torch.from_numpy(np.ascontiguousarray(w, dtype=np.int8))
+    m, k = a_t.shape
+    n = w_t.shape[0]
+    if m >= 17 and n % 8 == 0 and k % 8 == 0:
+        return torch._int_mm(a_t, w_t.t().contiguous()).numpy()
+    return (a_t.to(torch.int64) @ w_t.to(torch.int64).t()).to(torch.int32).numpy()
+
+
+def epilogue(acc: np.ndarray, a_scale: np.ndarray, w_scale: np.ndarray, bias=None,
+             fused: bool = False, add_zero_bias: bool = True) -> np.ndarray:
+    """bf16 bits of ``((acc * a_s) * w_s) + bias`` (w4a8.cu:474-525).
+
+    ``bias=None`` with ``add_zero_bias`` mirrors the GEMM's null bias broadcast (a
+    +0.0 addition); ``add_zero_bias=False`` mirrors ``turing_dequantize_int8_bf16``
+    (bf16_epilogue.cu:105-113), which has no addition.
+    """
+    acc = np.ascontiguousarray(acc, dtype=np.int32)
+    m, n = acc.shape
+    a_scale = np.ascontiguousarray(a_scale, dtype=np.float32).reshape(-1)
+    w_scale = np.ascontiguousarray(w_scale, dtype=np.float32).reshape(-1)
+    has_bias = 1
+    if bias is None:
+        if add_zero_bias:
+            bias = np.zeros((n,), dtype=np.float32)
+        else:
+            has_bias = 0
+            bias = np.zeros((1,), dtype=np.float32)
+    bias = np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+    out = np.empty((m, n), dtype=np.uint16)
+    _load().ctu_oracle_epilogue(
+        _ptr(acc), n, _ptr(a_scale), _ptr(w_scale), w_scale.size, _ptr(bias), _ptr(out),
+        m, n, has_bias, 1 if fused else 0,
+    )
+    return out
+
+
+def pack_int4(values: np.ndarray) -> np.ndarray:
+    """Signed int4 values in [-8, 7] -> packed bytes, even column in the low nibble."""
+    v = np.asarray(values, dtype=np.int32)
+    lo = v[:, 0::2] & 0x0F
+    hi = v[:, 1::2] & 0x0F
+    return (lo | (hi << 4)).astype(np.uint8).view(np.int8)
+
+
+def unpack_int4(packed: np.ndarray) -> np.ndarray:
+    """Packed bytes -> signed int4 values as int8, low nibble first (w4a8.cu:49-66)."""
+    p = np.asarray(packed).view(np.uint8).astype(np.int32)
+    lo = p & 0x0F
+    hi = (p >> 4) & 0x0F
+    lo = np.where(lo >= 8, lo - 16, lo)
+    hi = np.where(hi >= 8, hi - 16, hi)
+    out = np.stack((lo, hi), axis=-1).reshape(p.shape[0], -1)
+    return out.astype(np.int8)
+
+
+def int8_linear(a, w, a_scale, w_scale, bias=None, fused=False):
+    """``turing_utils::int8_linear`` oracle: bf16 bits [M, N]."""
+    return epilogue(int8_gemm_s32(a, w), a_scale, w_scale, bias, fused=fused)
+
+
+def w4a8_linear(a, w_packed, a_scale, w_scale, bias=None, fused=False):
+    """``turing_utils::w4a8_linear`` oracle (signed int4 weights, per-channel scale)."""
+    return epilogue(int8_gemm_s32(a, unpack_int4(w_packed)), a_scale, w_scale, bias, fused=fused)
+
+
+def convrot_w8a8_linear(x_bits, w, w_scale, bias=None, fused=False):
+    """Whole path: ConvRot quantize, int32 GEMM, dequant+bias epilogue (bf16 bits)."""
+    codes, scales = convrot_quantize(x_bits, 8)
+    return int8_linear(codes, w, scales, w_scale, bias, fused=fused)

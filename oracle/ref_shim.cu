@@ -1,0 +1,135 @@
+// C-ABI shim over the REFERENCE kernels of comfyui-turing-utils (TEST
+// INFRASTRUCTURE ONLY).  oracle/Makefile compiles this file together with the
+// reference's own sources, read in place from the reference tree
+// (kernel/csrc/turing/{convrot_quant,bf16_epilogue,w4a8}.cu), into
+// oracle/_ref/libctu_ref.so.  Only tests/golden/make_golden.py and the tests
+// load it, to pin the CPU oracle against the reference's device results.
+//
+// Each entry builds the reference's ATen-free `Tensor` views
+// (kernel/csrc/tensor_bridge.h:137-236) over caller pointers, pushes the caller's
+// stream on the reference's thread-local stream stack (tensor_bridge.h:57-61,
+// as bindings.cpp:17-31 does) and calls the reference host entry.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <exception>
+#include <string>
+
+#include "kernel_api.h"
+
+namespace ref = comfyui_turing_utils::kernels;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+Tensor view(void *ptr, std::initializer_list<int> shape, Tensor::ScalarType type) {
+    Tensor t;
+    t.ptr = ptr;
+    t.scalarType = type;
+    for (int d : shape) t.shape.dataExtent.push_back(d);
+    int device = 0;
+    cudaGetDevice(&device);
+    t.dev = Device{Device::CUDA, device};
+    return t;
+}
+
+struct StreamScope {
+    explicit StreamScope(void *stream) { stackCUDAStreams.push_back(static_cast<cudaStream_t>(stream)); }
+    ~StreamScope() { stackCUDAStreams.pop_back(); }
+};
+
+template <typename F>
+int guarded(F &&fn) {
+    try {
+        fn();
+        return 0;
+    } catch (const std::exception &e) {
+        g_last_error = e.what();
+        return 1;
+    }
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *ref_last_error() { return g_last_error.c_str(); }
+
+// kernel/csrc/turing/convrot_quant.cu:665-713 (row-buffer int8 / int4, optional SwiGLU).
+int ref_bf16_convrot_quantize(const void *x, void *codes, void *scales, int rows, int k,
+                              int bits, int swiglu, int block_threads, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        const int width = swiglu ? 2 * k : k;
+        Tensor in = view(const_cast<void *>(x), {rows, width}, Tensor::BF16);
+        Tensor out = view(codes, {rows, bits == 4 ? k / 2 : k}, Tensor::INT8);
+        Tensor sc = view(scales, {rows, 1}, Tensor::FP32);
+        if (bits == 4) {
+            ref::turing_bf16_int4_convrot_quantize(in, out, sc, swiglu != 0, block_threads);
+        } else {
+            ref::turing_bf16_int8_convrot_quantize(in, out, sc, swiglu != 0, block_threads);
+        }
+    });
+}
+
+// kernel/csrc/turing/convrot_quant.cu:715-745 (row-buffer tanh-GELU int8 / int4).
+int ref_bf16_gelu_convrot_quantize(const void *x, void *codes, void *scales, int rows, int k,
+                                   int bits, int block_threads, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        Tensor in = view(const_cast<void *>(x), {rows, k}, Tensor::BF16);
+        Tensor out = view(codes, {rows, bits == 4 ? k / 2 : k}, Tensor::INT8);
+        Tensor sc = view(scales, {rows, 1}, Tensor::FP32);
+        if (bits == 4) {
+            ref::turing_bf16_gelu_int4_convrot_quantize(in, out, sc, block_threads);
+        } else {
+            ref::turing_bf16_gelu_int8_convrot_quantize(in, out, sc, block_threads);
+        }
+    });
+}
+
+// kernel/csrc/turing/w4a8.cu:1185-1219 (W8A8 GEMM + dequant/bias epilogue).
+int ref_int8_linear(const void *a, const void *w, const void *a_scale, const void *w_scale,
+                    const void *bias, void *out, int m, int n, int k, int tile_policy, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        ref::turing_int8_linear(view(const_cast<void *>(a), {m, k}, Tensor::INT8),
+                                view(const_cast<void *>(w), {n, k}, Tensor::INT8),
+                                view(const_cast<void *>(a_scale), {m}, Tensor::FP32),
+                                view(const_cast<void *>(w_scale), {n}, Tensor::FP32),
+                                bias ? view(const_cast<void *>(bias), {n}, Tensor::FP32) : Tensor{},
+                                view(out, {m, n}, Tensor::BF16), tile_policy);
+    });
+}
+
+// kernel/csrc/turing/w4a8.cu:1000-1086 (signed packed-int4 W4A8, N % 8 == 0).
+int ref_w4a8_linear(const void *a, const void *w_packed, const void *a_scale, const void *w_scale,
+                    const void *bias, void *out, int m, int n, int k, int tile_policy, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        ref::turing_w4a8_linear(view(const_cast<void *>(a), {m, k}, Tensor::INT8),
+                                view(const_cast<void *>(w_packed), {n, k / 2}, Tensor::INT8),
+                                view(const_cast<void *>(a_scale), {m}, Tensor::FP32),
+                                view(const_cast<void *>(w_scale), {n}, Tensor::FP32),
+                                bias ? view(const_cast<void *>(bias), {n}, Tensor::FP32) : Tensor{},
+                                view(out, {m, n}, Tensor::BF16), tile_policy);
+    });
+}
+
+// kernel/csrc/turing/bf16_epilogue.cu:146-217 (int32 accumulator -> bf16).
+int ref_dequantize_int8_bf16(const void *acc, const void *a_scale, const void *w_scale,
+                             int w_scale_count, void *out, int m, int acc_cols, int out_cols,
+                             void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        Tensor accumulator = view(const_cast<void *>(acc), {m, acc_cols}, Tensor::INT32);
+        ref::turing_dequantize_int8_bf16(accumulator,
+                                         view(const_cast<void *>(a_scale), {m}, Tensor::FP32),
+                                         view(const_cast<void *>(w_scale), {w_scale_count}, Tensor::FP32),
+                                         view(out, {m, out_cols}, Tensor::BF16));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,94 @@
+"""The CPU oracle reproduces the reference kernels' device outputs (golden vectors).
+
+The fixtures in tests/golden/ were produced by tests/golden/make_golden.py, which runs
+the reference's own kernels (kernel/csrc/turing/{convrot_quant,w4a8,bf16_epilogue}.cu,
+compiled for sm_100a by oracle/Makefile) on a B200.
+"""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import convrot_oracle as oracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _quant_cases():
+    data = np.load(GOLDEN / "convrot_quant.npz")
+    names = sorted({k.split("__")[0] for k in data.files})
+    return data, names
+
+
+QUANT, QUANT_NAMES = _quant_cases()
+
+
+def _mode(name):
+    if "swiglu" in name:
+        return oracle.MODE_SWIGLU
+    if name.startswith("gelu"):
+        return oracle.MODE_GELU
+    return oracle.MODE_PLAIN
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("name", QUANT_NAMES)
+def test_convrot_quantize_matches_reference(name, bits):
+    x = QUANT[f"{name}__x"]
+    codes, scales = oracle.convrot_quantize(x, bits, _mode(name))
+    ref_codes = QUANT[f"{name}__int{bits}_codes"]
+    ref_scales = QUANT[f"{name}__int{bits}_scales"]
+    assert np.array_equal(codes, ref_codes)
+    if _mode(name) == oracle.MODE_SWIGLU:
+        # SwiGLU uses expf; glibc's and CUDA's expf may differ by one ulp, which can
+        # move the fp32 scale by one ulp while leaving the codes unchanged.
+        diff = np.abs(scales.view(np.int32).astype(np.int64) - ref_scales.view(np.int32).astype(np.int64))
+        assert diff.max() <= 1
+    else:
+        assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
+
+
+GEMM = np.load(GOLDEN / "gemm.npz")
+GEMM_KEYS = sorted({k.split("__")[0] for k in GEMM.files if k.startswith("m")})
+
+
+@pytest.mark.parametrize("key", GEMM_KEYS)
+def test_int8_and_w4a8_linear_match_reference(key):
+    a, w, w4 = GEMM[f"{key}__a"], GEMM[f"{key}__w"], GEMM[f"{key}__w4_packed"]
+    a_s, w_s = GEMM[f"{key}__a_scale"], GEMM[f"{key}__w_scale"]
+    bias = GEMM[f"{key}__bias"] if f"{key}__bias" in GEMM.files else None
+    assert np.array_equal(oracle.int8_linear(a, w, a_s, w_s, bias), GEMM[f"{key}__int8_linear"])
+    assert np.array_equal(oracle.w4a8_linear(a, w4, a_s, w_s, bias), GEMM[f"{key}__w4a8_linear"])
+
+
+@pytest.mark.parametrize("tag", ["vec", "scalar"])
+def test_dequantize_matches_reference(tag):
+    out = oracle.epilogue(GEMM["dequant__acc"], GEMM["dequant__a_scale"], GEMM[f"dequant_{tag}__w_scale"],
+                          None, add_zero_bias=False)
+    assert np.array_equal(out, GEMM[f"dequant_{tag}__out"])
+
+
+def test_rotation_is_the_kronecker_radix4_transform():
+    m = 0.5 * np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=np.float64)
+    r = np.kron(np.kron(np.kron(m, m), m), m)
+    assert np.abs(r @ r.T - np.eye(256)).max() == 0.0
+    rng = np.random.default_rng(3)
+    x = oracle.f32_to_bf16_bits(rng.standard_normal((4, 512)).astype(np.float32))
+    y = oracle.rotate(x).astype(np.float64)
+    xf = oracle.bf16_bits_to_f32(x).astype(np.float64)
+    ref = np.concatenate([xf[:, g * 256:(g + 1) * 256] @ r.T for g in range(2)], axis=1)
+    assert np.abs(y - ref).max() <= 1e-5 * np.abs(ref).max()
+
+
+def test_int4_zero_rows_have_the_reference_scale_floor():
+    # kernel/scripts/validate_compatible.py:146-155
+    codes, scales = oracle.convrot_quantize(np.zeros((2, 512), np.uint16), 4)
+    assert not codes.any()
+    assert np.all(scales == np.float32(1.0e-10))
+
+
+def test_int4_pack_roundtrip():
+    rng = np.random.default_rng(0)
+    v = rng.integers(-8, 8, size=(5, 64)).astype(np.int8)
+    assert np.array_equal(oracle.unpack_int4(oracle.pack_int4(v)), v)
