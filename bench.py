@@ -1,0 +1,344 @@
+"""Benchmark of the ConvRot W8A8 linear at Wan-2.1-14B shapes.
+
+One step = the configs[1] sweep: six ConvRot W8A8 linears on M = 32760 tokens,
+(K, N) in {(5120, 5120) x 4 (Q, K, V, O), (5120, 13824) (FFN up), (13824, 5120)
+(FFN down)}; each linear is the fused rotate+quantize kernel followed by the
+tcgen05 GEMM with the dequant+bias epilogue.  Metric: int8 tera-ops per second
+(2*M*N*K per linear) summed over all GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N > 1 is launched by torchrun, one process per GPU; every rank runs its own full
+configs[1] workload (weak scaling: token rows of independent sequences never cross
+GPUs, so there is no collective on the data path).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "comfyui-turing-utils_b200"))
+
+M_TOKENS = 32760
+SHAPES = [(5120, 5120)] * 4 + [(5120, 13824), (13824, 5120)]  # (K, N)
+METRIC = "ConvRot W8A8 linear TOPS at Wan-14B shapes (configs[1] sweep)"
+UNIT = "TOPS"
+
+
+def ops_per_step(m: int) -> float:
+    return float(sum(2 * m * n * k for k, n in SHAPES))
+
+
+def synth_inputs(m, device, seed=0):
+    """Seeded synthetic inputs with the BASELINE distributions (random weights)."""
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    xs = {}
+    for k in sorted({k for k, _ in SHAPES}):
+        x = torch.randn((m, k), generator=g, dtype=torch.float32)
+        idx = torch.randperm(k, generator=g)[: k // 100]
+        x[:, idx] *= 30.0
+        xs[k] = x.to(torch.bfloat16).to(device)
+    layers = []
+    for i, (k, n) in enumerate(SHAPES):
+        gw = torch.Generator(device="cpu").manual_seed(1000 + i)
+        w = torch.randint(-127, 128, (n, k), generator=gw, dtype=torch.int8)
+        w_s = torch.rand((n,), generator=gw) * 0.009 + 1e-3
+        b = torch.randn((n,), generator=gw) * 0.02
+        layers.append((k, n, w.to(device), w_s.to(device), b.to(device)))
+    return xs, layers
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower().startswith("active"):
+                        reasons.add(name)
+        finally:
+            os.unlink(self.path)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_sample_time(rows: int, threads: int):
+    """Time the CPU oracle port (rotate+quantize in C/OpenMP, torch int32 GEMM on CPU,
+    C epilogue) on `rows` tokens of every configs[1] linear.  Returns seconds."""
+    import numpy as np
+    import torch
+
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import convrot_oracle as oracle
+
+    torch.set_num_threads(threads)
+    os.environ["OMP_NUM_THREADS"] = str(threads)
+    xs, layers = synth_inputs(rows, "cpu", seed=0)
+    xbits = {k: x.view(torch.int16).numpy().view(np.uint16) for k, x in xs.items()}
+    t0 = time.perf_counter()
+    for k, n, w, w_s, b in layers:
+        codes, scales = oracle.convrot_quantize(xbits[k], 8)
+        oracle.int8_linear(codes, w.numpy(), scales, w_s.numpy(), b.numpy())
+    return time.perf_counter() - t0
+
+
+def run_reference_arm(args, rank: int) -> None:
+    """`--impl reference`: the reference has no CPU path of its own for this op, so the
+    arm times the oracle's CPU restatement of its arithmetic (kind "port")."""
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    rows = 64
+    for _ in range(max(args.warmup, 1)):
+        cpu_sample_time(rows, threads)
+    times = [cpu_sample_time(rows, threads) for _ in range(args.steps)]
+    t = statistics.median(times)
+    value = ops_per_step(rows) / t / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * (M_TOKENS / rows),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "configs[1] Wan-14B W8A8 sweep, M=32760, rows sampled on CPU", "m": M_TOKENS,
+                   "shapes_kn": SHAPES},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} token rows of each of the 6 configs[1] linears per step, "
+                                   f"extrapolated linearly in M (rows are independent)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def run_b200(args, rank: int, world: int, local_rank: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    import comfyui_turing_utils_kernel as kops
+    from comfyui_turing_utils_kernel import _lib
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    m = args.m
+    xs, layers = synth_inputs(m, dev, seed=rank)
+    stream = torch.cuda.current_stream(dev)
+
+    quant_ev, gemm_ev = [], []
+
+    def step(record=False):
+        outs = []
+        for k, n, w, w_s, b in layers:
+            if record:
+                e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                e0.record(stream)
+            q, s = kops.turing_bf16_int8_convrot_quantize(xs[k], 256)
+            if record:
+                e1.record(stream)
+            outs.append(kops.turing_int8_linear(q, w, s, w_s, b))
+            if record:
+                e2.record(stream)
+                quant_ev.append((e0, e1, 2 * m * k + 4 * m + m * k))
+                gemm_ev.append((e1, e2, 2 * m * n * k))
+        return outs
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    _lib.device_error(local_rank, clear=True)
+
+    # ---------------------------------------------------------------- device-resident timing
+    barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step(record=True)
+        stop.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier()
+    elapsed_ms = start.elapsed_time(stop)
+    flags = _lib.device_error(local_rank, clear=True)
+    if flags:
+        raise RuntimeError(f"kernel bounded-wait flags {flags:#x} during the timed region")
+
+    gemm_ms = [a.elapsed_time(b) for a, b, _ in gemm_ev]
+    quant_ms = [a.elapsed_time(b) for a, b, _ in quant_ev]
+    gemm_tops = sum(o for _, _, o in gemm_ev) / (sum(gemm_ms) * 1e-3) / 1e12
+    quant_gbs = sum(o for _, _, o in quant_ev) / (sum(quant_ms) * 1e-3) / 1e9
+
+    # ---------------------------------------------------------------- end-to-end (host buffers)
+    host_x = {k: x.cpu().pin_memory() for k, x in xs.items()}
+    host_out = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _, n, _, _, _ in layers]
+    h2d = sum(x.numel() * x.element_size() for x in host_x.values())
+    d2h = sum(o.numel() * o.element_size() for o in host_out)
+
+    def e2e_step():
+        dev_x = {k: hx.to(dev, non_blocking=True) for k, hx in host_x.items()}
+        for i, (k, n, w, w_s, b) in enumerate(layers):
+            q, s = kops.turing_bf16_int8_convrot_quantize(dev_x[k], 256)
+            host_out[i].copy_(kops.turing_int8_linear(q, w, s, w_s, b), non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
+
+    # ---------------------------------------------------------------- reduce over ranks (max time)
+    t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+    value = world * ops_per_step(m) / (ms_per_step * 1e-3) / 1e12
+    e2e_value = world * ops_per_step(m) / (e2e_ms * 1e-3) / 1e12
+
+    if rank != 0:
+        return
+    peaks = {}
+    peaks_path = ROOT / "MEASURED_PEAKS.json"
+    if peaks_path.exists():
+        peaks = json.loads(peaks_path.read_text())
+    bf16_sus = peaks.get("bf16_tflops_sustained")
+    if bf16_sus:
+        peak, peak_src = 2.0 * bf16_sus, "2x measured sustained cuBLAS bf16 (MEASURED_PEAKS.json); int8 dense = 2x bf16 on B200"
+    else:
+        peak, peak_src = 2.0 * 1400.0, "2x fallback sustained bf16 1.4 PFLOP/s"
+    hbm = peaks.get("hbm_gbs", 6650.0)
+
+    cpu = None
+    if world == 1 and not args.skip_cpu:
+        threads = os.cpu_count() or 1
+        rows = 64
+        cpu_sample_time(rows, threads)
+        tcpu = statistics.median(cpu_sample_time(rows, threads) for _ in range(3))
+        cpu = {"value": ops_per_step(rows) / tcpu / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{rows} token rows of each configs[1] linear, oracle C/OpenMP rotate+quantize + "
+                         f"torch CPU int32 GEMM + C epilogue, extrapolated linearly in M"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "configs[1]: ConvRot W8A8 linear sweep at Wan-2.1-14B shapes", "m_per_gpu": m,
+                   "shapes_kn": SHAPES, "rotation_block": 256, "l2": "inputs (335-906 MB) larger than L2",
+                   "parallelism": f"token rows, {world} independent rank(s)"},
+        "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": UNIT,
+                     "frac": gemm_tops / peak, "traffic": args.gemm_traffic, "kernel": "ctu::gemm::w8a8_gemm_kernel",
+                     "peak_source": peak_src},
+        "quantizer_roofline": {"bound": "hbm", "achieved": quant_gbs, "peak": hbm, "unit": "GB/s",
+                               "frac": quant_gbs / hbm, "kernel": "ctu::rot::convrot_quant_kernel<0,8>"},
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "pinned host activations -> turing_utils ops -> pinned host outputs, one stream"},
+        "gpu_launches": 2 * len(SHAPES) * args.steps,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per GPU")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--gemm-traffic", type=float, default=None,
+                    help="ncu dram bytes per GEMM launch (profiles/), reported as roofline.traffic")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference_arm(args, rank)
+        return
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+"""Drop-in for the reference's native module ``comfyui_turing_utils_kernel._C``.
+
+Same attribute names, argument names, defaults, output allocation and error
+contract as the reference's pybind11 bindings (kernel/csrc/bindings.cpp:884-973),
+implemented over the C ABI of libctu_b200.so.  Torch is used only for device
+memory, the current stream and the device guard.
+
+Attributes that the reference exposes but this build does not implement are
+absent, so ``hasattr(_C, name)`` probes (kernel_api.py:26-37, dispatch.py:59-69)
+stay truthful.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_lib.load()  # fail at import time when the CUDA library is missing (no fallback)
+
+
+def _ptr(t: torch.Tensor | None):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _stream(device: torch.device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _check_cuda_2d(t: torch.Tensor, name: str) -> None:
+    # bindings.cpp:89-93
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if t.dim() != 2:
+        raise RuntimeError(f"{name} must be 2D")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def _aligned(t: torch.Tensor) -> torch.Tensor:
+    """The C ABI wants 16-byte aligned rows; copy the rare misaligned view."""
+    if t.data_ptr() % 16 == 0:
+        return t
+    out = torch.empty_like(t, memory_format=torch.contiguous_format)
+    out.copy_(t)
+    return out
+
+
+# ----------------------------------------------------------------------------- quantizers
+def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, what: str):
+    x = x.contiguous()
+    _check_cuda_2d(x, "input")
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError(f"{what} input must be bfloat16")
+    if group_size != 256:
+        raise RuntimeError(f"{what} only supports group_size=256")
+    rows, width = x.shape
+    if act == _lib.ACT_SWIGLU and width % 2 != 0:
+        raise RuntimeError(f"SwiGLU {what} input width must be even")
+    hidden = width // 2 if act == _lib.ACT_SWIGLU else width
+    if rows <= 0 or hidden <= 0 or hidden % group_size != 0:
+        raise RuntimeError(f"{what} width must be positive and divisible by 256")
+    x = _aligned(x)
+    codes = torch.empty((rows, hidden // 2 if bits == 4 else hidden), dtype=torch.int8, device=x.device)
+    scales = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().ctu_convrot_quantize(
+            _ptr(x), rows, hidden, act, bits, _ptr(codes), _ptr(scales), _stream(x.device)))
+    return codes, scales
+
+
+def turing_bf16_int8_convrot_quantize(input, group_size=256, swiglu=False, forced_threads=0):
+    """bindings.cpp:636-679.  ``forced_threads`` selected the SM75 block geometry; the
+    B200 kernel's geometry is fixed, so only the reference's value check remains."""
+    if forced_threads not in (0, 512, 768, 1024):
+        raise RuntimeError("forced_threads must be 0, 512, 768, or 1024")
+    act = _lib.ACT_SWIGLU if swiglu else _lib.ACT_NONE
+    return _convrot_quantize(input, group_size, act, 8, "BF16 row-buffer ConvRot")
+
+
+def turing_bf16_int4_convrot_quantize(input, group_size=256, swiglu=False):
+    """bindings.cpp:681-717."""
+    act = _lib.ACT_SWIGLU if swiglu else _lib.ACT_NONE
+    return _convrot_quantize(input, group_size, act, 4, "BF16 row-buffer INT4 ConvRot")
+
+
+def turing_bf16_gelu_int8_convrot_quantize(input, group_size=256):
+    """bindings.cpp:719-770 (int8)."""
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 8, "BF16 GELU row-buffer ConvRot")
+
+
+def turing_bf16_gelu_int4_convrot_quantize(input, group_size=256):
+    """bindings.cpp:719-770 (int4)."""
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "BF16 GELU row-buffer ConvRot")
+
+
+# The reference's staged two-kernel quantizers (convrot_quant.cu:184-358) produce the
+# same codes and scales as the row-buffer kernel (validate_compatible.py:43-64); on
+# B200 both names run the single fused kernel.  The staged entries accept bf16 only.
+def turing_swiglu_int8_convrot_quantize(input, group_size=256):
+    """bindings.cpp:474-510."""
+    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 8, "SwiGLU staged ConvRot")
+
+
+def turing_swiglu_int4_convrot_quantize(input, group_size=256):
+    """bindings.cpp:547-584."""
+    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 4, "SwiGLU staged INT4 ConvRot")
+
+
+def turing_gelu_int8_convrot_quantize(input, group_size=256):
+    """bindings.cpp:586-633 (int8)."""
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 8, "GELU staged ConvRot")
+
+
+def turing_gelu_int4_convrot_quantize(input, group_size=256):
+    """bindings.cpp:586-633 (int4)."""
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "GELU staged ConvRot")
+
+
+# ----------------------------------------------------------------------------- GEMMs
+def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=None, tile_policy=0):
+    """bindings.cpp:371-421: W8A8 GEMM with the fused dequant + bias epilogue.
+    ``tile_policy`` chose among SM75 CUTLASS tiles; the tcgen05 kernel has one
+    persistent tile schedule, so the argument is accepted and ignored."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
+    weight_scale = weight_scale.reshape(-1).to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.float32).contiguous()
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    if activation.dtype != torch.int8 or weight.dtype != torch.int8:
+        raise RuntimeError("Turing INT8 linear activation and weight must be int8")
+    dev = activation.device
+    if weight.device != dev or activation_scale.device != dev or weight_scale.device != dev:
+        raise RuntimeError("Turing INT8 linear tensors must use the same CUDA device")
+    m, k = activation.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k:
+        raise RuntimeError("INT8 linear K dimensions must match")
+    if k % 16 != 0 or n % 8 != 0:
+        raise RuntimeError("Turing INT8 linear requires K%16=0 and N%8=0")
+    if activation_scale.numel() != m:
+        raise RuntimeError("activation_scale must contain one value per row")
+    if weight_scale.numel() != n:
+        raise RuntimeError("weight_scale must contain one value per output channel")
+    if bias is not None and (not bias.is_cuda or bias.device != dev or bias.numel() != n):
+        raise RuntimeError("bias must contain one value per output channel on the same CUDA device")
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if m == 0 or n == 0 or k == 0:
+        return out  # the reference leaves the output unwritten for empty problems (w4a8.cu:1194-1196)
+    activation, weight = _aligned(activation), _aligned(weight)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ctu_int8_linear(
+            _ptr(activation), _ptr(weight), _ptr(activation_scale), _ptr(weight_scale), n,
+            _ptr(bias), _ptr(out), m, n, k, _stream(dev)))
+    return out
+
+
+def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, output_columns=-1):
+    """bindings.cpp:423-472."""
+    accumulator = accumulator.contiguous()
+    activation_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
+    weight_scale = weight_scale.reshape(-1).to(torch.float32).contiguous()
+    _check_cuda_2d(accumulator, "accumulator")
+    if accumulator.dtype != torch.int32:
+        raise RuntimeError("accumulator must be int32")
+    if not (activation_scale.is_cuda and weight_scale.is_cuda):
+        raise RuntimeError("scales must be CUDA tensors")
+    if activation_scale.device != accumulator.device or weight_scale.device != accumulator.device:
+        raise RuntimeError("accumulator and scales must use the same CUDA device")
+    rows, acc_cols = accumulator.shape
+    if output_columns < 0:
+        output_columns = acc_cols
+    if rows <= 0 or acc_cols <= 0:
+        raise RuntimeError("INT8 BF16 epilogue dimensions must be positive")
+    if output_columns <= 0 or output_columns > acc_cols:
+        raise RuntimeError("output_columns must be positive and no larger than the accumulator width")
+    if activation_scale.numel() != rows:
+        raise RuntimeError("activation_scale must contain one value per accumulator row")
+    if weight_scale.numel() not in (1, output_columns):
+        raise RuntimeError("weight_scale must be scalar or contain one value per output column")
+    out = torch.empty((rows, output_columns), dtype=torch.bfloat16, device=accumulator.device)
+    with torch.cuda.device(accumulator.device):
+        _lib.check(_lib.load().ctu_dequantize_int8_bf16(
+            _ptr(accumulator), acc_cols, _ptr(activation_scale), _ptr(weight_scale), weight_scale.numel(),
+            _ptr(out), rows, output_columns, _stream(accumulator.device)))
+    return out
+
+
+# ----------------------------------------------------------------------------- B200 extras
+def int8_gemm_s32(activation, weight, out=None):
+    """Exact int32 accumulators ``activation @ weight.T`` (no epilogue)."""
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    m, k = activation.shape
+    n = weight.shape[0]
+    if out is None:
+        out = torch.empty((m, n), dtype=torch.int32, device=activation.device)
+    with torch.cuda.device(activation.device):
+        _lib.check(_lib.load().ctu_int8_gemm_s32(
+            _ptr(_aligned(activation)), _ptr(_aligned(weight)), _ptr(out), out.stride(0), m, n, k,
+            _stream(activation.device)))
+    return out

@@ -1,0 +1,37 @@
+"""B200 (sm_100a) drop-in for the ``comfyui_turing_utils_kernel`` package.
+
+Exports the ConvRot quantized-linear operations of the reference kernel package
+(kernel/comfyui_turing_utils_kernel/__init__.py:1-39) implemented by hand-written
+tcgen05/TMA CUDA kernels in libctu_b200.so.  Attention (``turing_sage``) and the
+norm kernels of the reference are outside this build's scope.
+"""
+
+from .ops import (
+    turing_bf16_gelu_int4_convrot_quantize,
+    turing_bf16_gelu_int8_convrot_quantize,
+    turing_bf16_int4_convrot_quantize,
+    turing_bf16_int8_convrot_quantize,
+    turing_dequantize_int8_bf16,
+    turing_gelu_int4_convrot_quantize,
+    turing_gelu_int8_convrot_quantize,
+    turing_int8_linear,
+    turing_swiglu_int4_convrot_quantize,
+    turing_swiglu_int8_convrot_quantize,
+)
+
+# Version contract checked by the plugin (precision.py:31-32,91-104 of the reference).
+__version__ = "0.31.0"
+__b200_build__ = "0.1.0"
+
+__all__ = [
+    "turing_bf16_gelu_int4_convrot_quantize",
+    "turing_bf16_gelu_int8_convrot_quantize",
+    "turing_bf16_int4_convrot_quantize",
+    "turing_bf16_int8_convrot_quantize",
+    "turing_dequantize_int8_bf16",
+    "turing_gelu_int4_convrot_quantize",
+    "turing_gelu_int8_convrot_quantize",
+    "turing_int8_linear",
+    "turing_swiglu_int4_convrot_quantize",
+    "turing_swiglu_int8_convrot_quantize",
+]

@@ -1,0 +1,236 @@
+"""``turing_utils::*`` torch custom ops over the B200 kernels.
+
+Op names, signatures, defaults, device/capability errors and fake (meta) kernels
+follow the reference's kernel/comfyui_turing_utils_kernel/ops.py, so graph capture,
+torch.compile tracing and shape propagation see the same contract.  Each op calls
+the matching function of ``_C`` (the C-ABI shim); there is no CPU path.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _C
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if t.device.type != "cuda":
+        raise RuntimeError(f"{what} requires CUDA tensors")
+    if torch.cuda.get_device_capability(t.device) < (7, 5):
+        raise RuntimeError(f"{what} requires sm75 or newer")
+
+
+# ops.py:96-126
+@torch.library.custom_op("turing_utils::int8_linear", mutates_args=())
+def turing_int8_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """W8A8 contraction with the fused dequant + bias epilogue (tcgen05 kind::i8)."""
+    _require_cuda(activation, "Turing INT8 linear")
+    return _C.turing_int8_linear(
+        activation.contiguous(),
+        weight.contiguous(),
+        activation_scale.contiguous(),
+        weight_scale.contiguous(),
+        None if bias is None else bias.contiguous(),
+    )
+
+
+@turing_int8_linear.register_fake
+def _turing_int8_linear_fake(activation, weight, activation_scale, weight_scale, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
+
+
+# ops.py:129-160
+@torch.library.custom_op("turing_utils::dequantize_int8_bf16", mutates_args=())
+def turing_dequantize_int8_bf16(
+    accumulator: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    output_columns: int = -1,
+) -> torch.Tensor:
+    """Dequantize an INT32 GEMM workspace directly into bf16."""
+    _require_cuda(accumulator, "Turing BF16 epilogue")
+    if accumulator.dtype != torch.int32 or accumulator.ndim != 2:
+        raise TypeError("accumulator must be a 2D int32 tensor")
+    return _C.turing_dequantize_int8_bf16(
+        accumulator.contiguous(), activation_scale.contiguous(), weight_scale.contiguous(), output_columns
+    )
+
+
+@turing_dequantize_int8_bf16.register_fake
+def _turing_dequantize_int8_bf16_fake(accumulator, activation_scale, weight_scale, output_columns=-1):
+    columns = accumulator.size(1) if output_columns < 0 else output_columns
+    return torch.empty((accumulator.size(0), columns), dtype=torch.bfloat16, device=accumulator.device)
+
+
+def _check_bf16_2d(x: torch.Tensor, what: str) -> None:
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"{what} input must be bfloat16")
+    if x.ndim != 2:
+        raise ValueError(f"{what} input must be 2D")
+
+
+# ops.py:290-315
+@torch.library.custom_op("turing_utils::bf16_int8_convrot_quantize", mutates_args=())
+def turing_bf16_int8_convrot_quantize(
+    x: torch.Tensor,
+    group_size: int = 256,
+    *,
+    swiglu: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused ConvRot rotation + per-token int8 quantization of a bf16 row block."""
+    _require_cuda(x, "BF16 row-buffer ConvRot")
+    _check_bf16_2d(x, "BF16 row-buffer ConvRot")
+    return _C.turing_bf16_int8_convrot_quantize(x.contiguous(), group_size, swiglu)
+
+
+@turing_bf16_int8_convrot_quantize.register_fake
+def _turing_bf16_int8_convrot_quantize_fake(x, group_size=256, *, swiglu=False):
+    hidden = x.size(1) // 2 if swiglu else x.size(1)
+    return (
+        torch.empty((x.size(0), hidden), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+# ops.py:318-343
+@torch.library.custom_op("turing_utils::bf16_int4_convrot_quantize", mutates_args=())
+def turing_bf16_int4_convrot_quantize(
+    x: torch.Tensor,
+    group_size: int = 256,
+    *,
+    swiglu: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused ConvRot rotation + per-token packed-int4 quantization."""
+    _require_cuda(x, "BF16 row-buffer INT4 ConvRot")
+    _check_bf16_2d(x, "BF16 row-buffer INT4 ConvRot")
+    return _C.turing_bf16_int4_convrot_quantize(x.contiguous(), group_size, swiglu)
+
+
+@turing_bf16_int4_convrot_quantize.register_fake
+def _turing_bf16_int4_convrot_quantize_fake(x, group_size=256, *, swiglu=False):
+    hidden = x.size(1) // 2 if swiglu else x.size(1)
+    return (
+        torch.empty((x.size(0), hidden // 2), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+# ops.py:346-365
+@torch.library.custom_op("turing_utils::bf16_gelu_int8_convrot_quantize", mutates_args=())
+def turing_bf16_gelu_int8_convrot_quantize(
+    x: torch.Tensor,
+    group_size: int = 256,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused tanh-GELU + ConvRot + per-token int8 quantization."""
+    _require_cuda(x, "BF16 GELU ConvRot")
+    _check_bf16_2d(x, "BF16 GELU ConvRot")
+    return _C.turing_bf16_gelu_int8_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_bf16_gelu_int8_convrot_quantize.register_fake
+def _turing_bf16_gelu_int8_convrot_quantize_fake(x, group_size=256):
+    return (
+        torch.empty(x.shape, dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+# ops.py:368-385
+@torch.library.custom_op("turing_utils::bf16_gelu_int4_convrot_quantize", mutates_args=())
+def turing_bf16_gelu_int4_convrot_quantize(
+    x: torch.Tensor,
+    group_size: int = 256,
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Fused tanh-GELU + ConvRot + per-token packed-int4 quantization."""
+    _require_cuda(x, "BF16 GELU INT4 ConvRot")
+    _check_bf16_2d(x, "BF16 GELU INT4 ConvRot")
+    return _C.turing_bf16_gelu_int4_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_bf16_gelu_int4_convrot_quantize.register_fake
+def _turing_bf16_gelu_int4_convrot_quantize_fake(x, group_size=256):
+    return (
+        torch.empty((x.size(0), x.size(1) // 2), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+# ops.py:163-186, 222-287: the staged entries share the fused kernel (bf16 input).
+@torch.library.custom_op("turing_utils::swiglu_int8_convrot_quantize", mutates_args=())
+def turing_swiglu_int8_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """SwiGLU + ConvRot int8 quantization of a [M, 2K] (gate | up) block."""
+    _require_cuda(x, "Turing SwiGLU ConvRot")
+    if x.ndim != 2:
+        raise ValueError("SwiGLU ConvRot input must be 2D [M, 2K]")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("SwiGLU ConvRot input must be bfloat16 on the B200 build")
+    return _C.turing_swiglu_int8_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_swiglu_int8_convrot_quantize.register_fake
+def _turing_swiglu_int8_convrot_quantize_fake(x, group_size=256):
+    hidden = x.size(1) // 2
+    return (
+        torch.empty((x.size(0), hidden), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+@torch.library.custom_op("turing_utils::swiglu_int4_convrot_quantize", mutates_args=())
+def turing_swiglu_int4_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """SwiGLU + ConvRot packed-int4 quantization of a [M, 2K] block."""
+    _require_cuda(x, "Turing SwiGLU INT4 ConvRot")
+    if x.ndim != 2:
+        raise ValueError("SwiGLU INT4 ConvRot input must be 2D [M, 2K]")
+    if x.dtype != torch.bfloat16:
+        raise TypeError("SwiGLU INT4 ConvRot input must be bfloat16 on the B200 build")
+    return _C.turing_swiglu_int4_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_swiglu_int4_convrot_quantize.register_fake
+def _turing_swiglu_int4_convrot_quantize_fake(x, group_size=256):
+    hidden = x.size(1) // 2
+    return (
+        torch.empty((x.size(0), hidden // 2), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+@torch.library.custom_op("turing_utils::gelu_int8_convrot_quantize", mutates_args=())
+def turing_gelu_int8_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """tanh-GELU + ConvRot int8 quantization."""
+    _require_cuda(x, "Turing GELU ConvRot")
+    if x.dtype != torch.bfloat16 or x.ndim != 2:
+        raise TypeError("GELU ConvRot input must be a 2D bfloat16 tensor on the B200 build")
+    return _C.turing_gelu_int8_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_gelu_int8_convrot_quantize.register_fake
+def _turing_gelu_int8_convrot_quantize_fake(x, group_size=256):
+    return (
+        torch.empty(x.shape, dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )
+
+
+@torch.library.custom_op("turing_utils::gelu_int4_convrot_quantize", mutates_args=())
+def turing_gelu_int4_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """tanh-GELU + ConvRot packed-int4 quantization."""
+    _require_cuda(x, "Turing GELU INT4 ConvRot")
+    if x.dtype != torch.bfloat16 or x.ndim != 2:
+        raise TypeError("GELU INT4 ConvRot input must be a 2D bfloat16 tensor on the B200 build")
+    return _C.turing_gelu_int4_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_gelu_int4_convrot_quantize.register_fake
+def _turing_gelu_int4_convrot_quantize_fake(x, group_size=256):
+    return (
+        torch.empty((x.size(0), x.size(1) // 2), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
+    )

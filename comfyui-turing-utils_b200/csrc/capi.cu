@@ -1,0 +1,394 @@
+// C ABI of libctu_b200.so (declared in include/ctu_b200.h): argument checks,
+// TMA tensor-map encoding, launch geometry and the per-device error word.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/ctu_b200.h"
+#include "convrot_quant.cuh"
+#include "dequant.cuh"
+#include "gemm_i8.cuh"
+#include "ptx.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(CTU_ERR_CUDA, "CUDA error in %s: %s", what, cudaGetErrorString(e));
+}
+
+#define CTU_CUDA(call)                                  \
+    do {                                                \
+        cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return cuda_fail(e_, #call); \
+    } while (0)
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---------------------------------------------------------------------------- device state
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+uint32_t *g_err_word[kMaxDevices] = {};
+int g_num_sms[kMaxDevices] = {};
+int g_smem_optin[kMaxDevices] = {};
+
+struct DeviceInfo {
+    int device;
+    uint32_t *err;
+    int num_sms;
+    int smem_optin;
+};
+
+int device_info(DeviceInfo *info) {
+    int dev = 0;
+    CTU_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return fail(CTU_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (g_err_word[dev] == nullptr) {
+        cudaDeviceProp prop;
+        CTU_CUDA(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major != 10 || prop.minor != 0) {
+            return fail(CTU_ERR_UNSUPPORTED, "libctu_b200 targets sm_100a (B200); device %d is sm_%d%d", dev,
+                        prop.major, prop.minor);
+        }
+        uint32_t *w = nullptr;
+        CTU_CUDA(cudaMalloc(&w, sizeof(uint32_t)));
+        CTU_CUDA(cudaMemset(w, 0, sizeof(uint32_t)));
+        g_err_word[dev] = w;
+        g_num_sms[dev] = prop.multiProcessorCount;
+        g_smem_optin[dev] = static_cast<int>(prop.sharedMemPerBlockOptin);
+    }
+    info->device = dev;
+    info->err = g_err_word[dev];
+    info->num_sms = g_num_sms[dev];
+    info->smem_optin = g_smem_optin[dev];
+    return CTU_OK;
+}
+
+// ---------------------------------------------------------------------------- tensor maps
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int get_encoder(EncodeTiledFn *out) {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    static cudaError_t status = cudaSuccess;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        status = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+        if (status == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (fn == nullptr) return fail(CTU_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    *out = fn;
+    return CTU_OK;
+}
+
+// 2D row-major tensor [outer, inner] of `elem_bytes`-byte elements, 128-byte swizzle.
+int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const void *base, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+    EncodeTiledFn enc;
+    if (int rc = get_encoder(&enc)) return rc;
+    const cuuint64_t dims[2] = {inner, outer};
+    const cuuint64_t strides[1] = {inner * static_cast<uint64_t>(elem_bytes)};
+    const cuuint32_t box[2] = {box_inner, box_outer};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, type, 2, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(CTU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return CTU_OK;
+}
+
+// ---------------------------------------------------------------------------- quantizer geometry
+struct QuantPlan {
+    int rows_per_batch;
+    int warps;
+    int box_rows;
+    int copies;
+    size_t smem;
+};
+
+int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
+    const int groups = static_cast<int>(k / 256);
+    const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
+    // Rows per batch: keep every lane pair busy (a warp owns 16 groups), at most 4
+    // warps per CTA so two CTAs share an SM, and the double-buffered batch in budget.
+    const size_t budget = std::min<size_t>(static_cast<size_t>(smem_optin), 110 * 1024);
+    double best_util = -1.0;
+    int best_b = 0;
+    for (int b = 1; b <= 16; ++b) {
+        const int tasks = b * groups;
+        const int warps = (tasks + 15) / 16;
+        if (warps > 4 && b > 1) break;
+        if (ctu::rot::quant_smem_bytes(b, static_cast<int>(k), act, bits) > budget && b > 1) break;
+        const double util = static_cast<double>(tasks) / (16.0 * warps);
+        if (util > best_util + 1e-9) {
+            best_util = util;
+            best_b = b;
+        }
+    }
+    if (best_b == 0) best_b = 1;
+    plan->rows_per_batch = best_b;
+    plan->warps = std::min(8, (best_b * groups + 15) / 16);
+    plan->smem = ctu::rot::quant_smem_bytes(best_b, static_cast<int>(k), act, bits);
+    if (plan->smem > static_cast<size_t>(smem_optin)) {
+        return fail(CTU_ERR_UNSUPPORTED, "ConvRot width %lld needs %zu bytes of shared memory (limit %d)",
+                    static_cast<long long>(k), plan->smem, smem_optin);
+    }
+    ctu::rot::quant_copy_plan(best_b, static_cast<int>(k), act, &plan->box_rows, &plan->copies);
+    (void)k_in;
+    return CTU_OK;
+}
+
+template <int Act, int Bits>
+int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan, int num_sms,
+                 cudaStream_t stream) {
+    auto kernel = ctu::rot::convrot_quant_kernel<Act, Bits>;
+    CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem)));
+    int per_sm = 0;
+    CTU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, plan.warps * 32, plan.smem));
+    if (per_sm < 1) return fail(CTU_ERR_UNSUPPORTED, "ConvRot quantizer does not fit on an SM");
+    const int64_t batches = (args.m + plan.rows_per_batch - 1) / plan.rows_per_batch;
+    const int grid = static_cast<int>(std::min<int64_t>(batches, static_cast<int64_t>(num_sms) * per_sm));
+    kernel<<<grid, plan.warps * 32, plan.smem, stream>>>(map, args);
+    CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
+// ---------------------------------------------------------------------------- GEMM launch
+int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms, cudaStream_t stream) {
+    CUtensorMap map_a, map_b;
+    if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, args.k, args.m, ctu::gemm::kBK,
+                           ctu::gemm::kBM))
+        return rc;
+    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, ctu::gemm::kBK,
+                           ctu::gemm::kBN))
+        return rc;
+    static std::once_flag once;
+    static cudaError_t attr_status = cudaSuccess;
+    std::call_once(once, [] {
+        attr_status = cudaFuncSetAttribute(ctu::gemm::w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           ctu::gemm::kSmemBytes);
+    });
+    CTU_CUDA(attr_status);
+    const int64_t tiles = ((args.m + ctu::gemm::kBM - 1) / ctu::gemm::kBM) *
+                          static_cast<int64_t>((args.n + ctu::gemm::kBN - 1) / ctu::gemm::kBN);
+    const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
+    ctu::gemm::w8a8_gemm_kernel<<<grid, ctu::gemm::kThreads, ctu::gemm::kSmemBytes, stream>>>(map_a, map_b, args);
+    CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
+int check_gemm_shapes(const int8_t *a, const int8_t *w, const void *out, int64_t m, int64_t n, int64_t k) {
+    if (m < 0 || n < 0 || k < 0) return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions must be non-negative");
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions exceed the kernel range");
+    if (k % 16 != 0 || n % 8 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "INT8 linear requires K%%16=0 and N%%8=0 (got K=%lld, N=%lld)",
+                    static_cast<long long>(k), static_cast<long long>(n));
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!a || !w || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(a) || !aligned16(w) || !aligned16(out))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "activation, weight and output must be 16-byte aligned");
+    return CTU_OK;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI
+extern "C" {
+
+int ctu_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+const char *ctu_last_error(void) { return g_last_error.c_str(); }
+
+int ctu_get_device_error(int device, uint32_t *flags, int clear) {
+    if (device < 0 || device >= kMaxDevices || flags == nullptr)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "invalid device or flags pointer");
+    uint32_t *w = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        w = g_err_word[device];
+    }
+    *flags = 0;
+    if (w == nullptr) return CTU_OK;  // nothing launched on this device yet
+    int prev = 0;
+    CTU_CUDA(cudaGetDevice(&prev));
+    CTU_CUDA(cudaSetDevice(device));
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpy(flags, w, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && clear) e = cudaMemset(w, 0, sizeof(uint32_t));
+    cudaSetDevice(prev);
+    if (e != cudaSuccess) return cuda_fail(e, "ctu_get_device_error");
+    return CTU_OK;
+}
+
+int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
+                         void *stream) {
+    if (rows < 0 || k <= 0 || k % 256 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot width must be positive and divisible by 256 (got %lld)",
+                    static_cast<long long>(k));
+    if (bits != 8 && bits != 4) return fail(CTU_ERR_INVALID_ARGUMENT, "bits must be 8 or 4");
+    if (act != CTU_ACT_NONE && act != CTU_ACT_SWIGLU && act != CTU_ACT_GELU_TANH)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+    if (rows > INT32_MAX || k > (1 << 20)) return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot dimensions exceed range");
+    if (rows == 0) return CTU_OK;
+    if (!x || !codes || !scales) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(x) || !aligned16(codes)) return fail(CTU_ERR_INVALID_ARGUMENT, "x and codes must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    QuantPlan plan;
+    if (int rc = plan_quant(k, act, bits, dev.smem_optin, &plan)) return rc;
+    const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
+    CUtensorMap map;
+    if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k_in / 64, 64,
+                           static_cast<uint32_t>(plan.box_rows)))
+        return rc;
+    ctu::rot::QuantArgs args;
+    args.codes = codes;
+    args.scales = scales;
+    args.err = dev.err;
+    args.m = static_cast<int>(rows);
+    args.k = static_cast<int>(k);
+    args.rows_per_batch = plan.rows_per_batch;
+    args.box_rows = plan.box_rows;
+    args.copies = plan.copies;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    using ctu::rot::kActGelu;
+    using ctu::rot::kActNone;
+    using ctu::rot::kActSwiGLU;
+    if (act == CTU_ACT_NONE) {
+        return bits == 8 ? launch_quant<kActNone, 8>(map, args, plan, dev.num_sms, s)
+                         : launch_quant<kActNone, 4>(map, args, plan, dev.num_sms, s);
+    }
+    if (act == CTU_ACT_SWIGLU) {
+        return bits == 8 ? launch_quant<kActSwiGLU, 8>(map, args, plan, dev.num_sms, s)
+                         : launch_quant<kActSwiGLU, 4>(map, args, plan, dev.num_sms, s);
+    }
+    return bits == 8 ? launch_quant<kActGelu, 8>(map, args, plan, dev.num_sms, s)
+                     : launch_quant<kActGelu, 4>(map, args, plan, dev.num_sms, s);
+}
+
+int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    void *stream) {
+    if (int rc = check_gemm_shapes(a, w, out, m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!a_scale || !w_scale) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (w_scale_count != 1 && w_scale_count != n)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output channel");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    if (k == 0) {
+        // Empty contraction: acc = 0; route through the dequant epilogue semantics.
+        return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
+    }
+    ctu::gemm::GemmArgs args{};
+    args.a_scale = a_scale;
+    args.w_scale = w_scale;
+    args.bias = bias;
+    args.out = out;
+    args.err = dev.err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.w_scale_count = static_cast<int>(w_scale_count);
+    args.out_mode = ctu::gemm::kOutBf16;
+    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                      void *stream) {
+    if (int rc = check_gemm_shapes(a, w, acc, m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (ldc < n || ldc % 4 != 0) return fail(CTU_ERR_INVALID_ARGUMENT, "ldc must be >= N and a multiple of 4");
+    if (k == 0) return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    ctu::gemm::GemmArgs args{};
+    args.out = acc;
+    args.err = dev.err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(ldc);
+    args.w_scale_count = 1;
+    args.out_mode = ctu::gemm::kOutS32;
+    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *acc, int64_t m, int64_t n, int64_t k,
+                                    uint64_t timeout_ns, void *stream) {
+    if (int rc = check_gemm_shapes(a, w, acc, m, n, k)) return rc;
+    if (m == 0 || n == 0 || k == 0) return fail(CTU_ERR_INVALID_ARGUMENT, "empty problem");
+    if (timeout_ns == 0 || timeout_ns > 5000000000ull)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "timeout must be in (0, 5 s]");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    ctu::gemm::GemmArgs args{};
+    args.out = acc;
+    args.err = dev.err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.w_scale_count = 1;
+    args.out_mode = ctu::gemm::kOutS32;
+    args.inject_timeout = 1;
+    args.inject_timeout_ns = timeout_ns;
+    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_dequantize_int8_bf16(const int32_t *acc, int64_t acc_stride, const float *a_scale, const float *w_scale,
+                             int64_t w_scale_count, void *out, int64_t rows, int64_t cols, void *stream) {
+    if (rows < 0 || cols < 0 || acc_stride < cols)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "invalid accumulator shape or stride");
+    if (rows == 0 || cols == 0) return CTU_OK;
+    if (!acc || !a_scale || !w_scale || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (w_scale_count != 1 && w_scale_count != cols)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output column");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const bool vec = cols % 8 == 0 && acc_stride % 4 == 0 && aligned16(acc) && aligned16(out) &&
+                     (w_scale_count == 1 || aligned16(w_scale));
+    const int threads = 256;
+    if (vec) {
+        const int64_t work = rows * (cols / 8);
+        const int grid = static_cast<int>(std::min<int64_t>((work + threads - 1) / threads, dev.num_sms * 16));
+        ctu::deq::dequant_vec8_kernel<<<grid, threads, 0, s>>>(acc, acc_stride, a_scale, w_scale,
+                                                                static_cast<int>(w_scale_count),
+                                                                static_cast<__nv_bfloat16 *>(out), rows, cols);
+    } else {
+        const int64_t work = rows * cols;
+        const int grid = static_cast<int>(std::min<int64_t>((work + threads - 1) / threads, dev.num_sms * 16));
+        ctu::deq::dequant_scalar_kernel<<<grid, threads, 0, s>>>(acc, acc_stride, a_scale, w_scale,
+                                                                  static_cast<int>(w_scale_count),
+                                                                  static_cast<__nv_bfloat16 *>(out), rows, cols);
+    }
+    CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,52 @@
+// Launch arguments and shared-memory budget of the fused ConvRot quantizer.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace ctu {
+namespace rot {
+
+enum Act : int { kActNone = 0, kActSwiGLU = 1, kActGelu = 2 };
+
+constexpr int kMaxThreads = 256;   // 8 warps = 128 lane pairs = 128 groups in flight
+constexpr int kMaxBoxRows = 64;    // 128-byte slices per TMA copy (8 KiB)
+
+struct QuantArgs {
+    int8_t *codes;       // [m, k] int8 or [m, k/2] packed int4
+    float *scales;       // [m]
+    uint32_t *err;       // device error word
+    int m;               // rows
+    int k;               // rotated width (the SwiGLU input is 2k wide)
+    int rows_per_batch;  // rows per shared-memory batch
+    int box_rows;        // 128-byte slices per TMA copy (a multiple of 8: 1024-byte aligned copies)
+    int copies;          // TMA copies per batch; copies * box_rows >= rows_per_batch * k_in / 64
+};
+
+// Slices (128 bytes = 64 bf16) per TMA copy and copies per batch.  Every copy
+// starts on a 1024-byte boundary, as the 128-byte swizzle pattern requires.
+inline void quant_copy_plan(int rows, int k, int act, int *box_rows, int *copies) {
+    const long long k_in = act == kActSwiGLU ? 2LL * k : k;
+    const long long slices = rows * k_in / 64;
+    const long long box = slices >= kMaxBoxRows ? kMaxBoxRows : ((slices + 7) / 8) * 8;
+    *box_rows = static_cast<int>(box);
+    *copies = static_cast<int>((slices + box - 1) / box);
+}
+
+// Dynamic shared memory for a batch of `rows` rows.
+inline size_t quant_smem_bytes(int rows, int k, int act, int bits) {
+    int box = 0, copies = 0;
+    quant_copy_plan(rows, k, act, &box, &copies);
+    const size_t k_out = bits == 4 ? k / 2 : k;
+    const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
+    const size_t code_bytes = (static_cast<size_t>(rows) * k_out + 15) & ~size_t(15);
+    return 1024 + 2 * in_bytes + code_bytes + 16 * static_cast<size_t>(rows) + 64;
+}
+
+template <int Act, int Bits>
+__global__ void convrot_quant_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
+
+}  // namespace rot
+}  // namespace ctu

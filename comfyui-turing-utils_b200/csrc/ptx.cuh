@@ -73,7 +73,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // memory) lets one timed-out role stop the others quickly; `err` is the global
 // error word.  Returns false on timeout or abort.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          uint32_t *err, uint32_t code) {
+                                          uint32_t *err, uint32_t code, uint64_t limit_ns = kWaitLimitNs) {
     const uint32_t addr = smem_u32(bar);
     if (mbar_try_wait(addr, parity)) return true;
     const uint64_t start = globaltimer();
@@ -81,7 +81,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
         if (mbar_try_wait(addr, parity)) return true;
         if ((i & 31u) == 0u) {
             if (abort_flag != nullptr && *abort_flag) return false;
-            if (globaltimer() - start > kWaitLimitNs) {
+            if (globaltimer() - start > limit_ns) {
                 if (abort_flag != nullptr) *abort_flag = 1;
                 atomicOr(err, code);
                 return false;

@@ -1,0 +1,110 @@
+/*
+ * ctu_b200.h -- C ABI of the B200 (sm_100a) ConvRot quantized-linear library
+ * (libctu_b200.so).  Plain pointers, sizes and a CUDA stream; no framework types.
+ *
+ * Every device pointer must be a CUDA device (or managed) address on the current
+ * device.  Entry points enqueue work on `stream` (a cudaStream_t; NULL = legacy
+ * default stream) and return without synchronizing.  Return value: CTU_OK, or an
+ * error code with a message available from ctu_last_error() (thread-local).
+ *
+ * Each entry point names the reference interface it replaces (comfyui-turing-utils,
+ * kernel package 0.31.0; paths relative to the reference repository).
+ */
+#ifndef CTU_B200_H_
+#define CTU_B200_H_
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CTU_API __attribute__((visibility("default")))
+#else
+#define CTU_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CTU_OK 0
+#define CTU_ERR_INVALID_ARGUMENT 1 /* shape, alignment or dtype contract violated */
+#define CTU_ERR_UNSUPPORTED 2      /* valid request this build does not implement */
+#define CTU_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
+
+/* Activation fused in front of the rotation. */
+#define CTU_ACT_NONE 0
+#define CTU_ACT_SWIGLU 1    /* x is [rows, 2k] = [gate | up]; silu(gate) * up */
+#define CTU_ACT_GELU_TANH 2 /* tanh-approximate GELU, rounded to bf16 */
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+CTU_API int ctu_version(void);
+
+/* Message for the most recent failing call on this thread ("" if none). */
+CTU_API const char *ctu_last_error(void);
+
+/*
+ * Device error word: kernels record bounded-wait timeouts here instead of hanging.
+ * Reads (and, with clear != 0, resets) the flags for `device`.  Synchronizes the
+ * device.  Flag bits: 1 tile wait, 2 stage wait, 4 accumulator wait, 8 accumulator
+ * release wait, 16 teardown drain, 32 TMEM allocation, 64 injected test timeout.
+ */
+CTU_API int ctu_get_device_error(int device, uint32_t *flags, int clear);
+
+/*
+ * ConvRot rotate + per-token quantize of a bf16 activation.
+ *   x      bf16 [rows, k] (act NONE / GELU_TANH) or [rows, 2k] (act SWIGLU), row-major,
+ *          16-byte aligned
+ *   codes  bits = 8: int8 [rows, k]; bits = 4: packed int4 [rows, k/2], even column in
+ *          the low nibble; 16-byte aligned
+ *   scales fp32 [rows]
+ * k must be a positive multiple of 256 (the rotation group).
+ * Replaces turing_utils::bf16_int8_convrot_quantize / bf16_int4_convrot_quantize
+ * (kernel/comfyui_turing_utils_kernel/ops.py:290-343; kernel/csrc/bindings.cpp:636-717;
+ * kernel/csrc/turing/convrot_quant.cu:417-511,665-713) and, with act = GELU_TANH, the
+ * bf16_gelu_* variants (ops.py:346-385; convrot_quant.cu:715-745).
+ */
+CTU_API int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
+                         void *stream);
+
+/*
+ * W8A8 linear with the fused dequant + bias epilogue:
+ *   out[m, n] = bf16(((float(sum_k a[m,k] * w[n,k]) * a_scale[m]) * w_scale[n]) + bias[n])
+ *   a int8 [m, k], w int8 [n, k] (K-contiguous rows), a_scale fp32 [m],
+ *   w_scale fp32 [n] (w_scale_count = n) or a scalar (w_scale_count = 1),
+ *   bias fp32 [n] or NULL, out bf16 [m, n].
+ * Requires k % 16 == 0, n % 8 == 0, a/w/out 16-byte aligned.
+ * Replaces turing_utils::int8_linear (ops.py:96-126; bindings.cpp:371-421;
+ * kernel/csrc/turing/w4a8.cu:1185-1219, CUTLASS SM75 GEMM w4a8.cu:376-618).
+ */
+CTU_API int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    void *stream);
+
+/*
+ * Raw W8A8 contraction to int32: acc[m, n] (row stride ldc elements) = sum_k a[m,k] * w[n,k].
+ * Same alignment rules as ctu_int8_linear; ldc % 4 == 0.
+ * Replaces the int32 GEMM the reference takes from comfy-kitchen's cuBLAS binding
+ * (comfyui_turing_utils/quantization/dispatch.py:559-613, cublas_gemm_int8).
+ */
+CTU_API int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,
+                      void *stream);
+
+/*
+ * int32 accumulator -> bf16: out[r, c] = bf16((float(acc[r, c]) * a_scale[r]) * w_scale[c]),
+ * acc row stride acc_stride (>= cols), w_scale [cols] or scalar (w_scale_count = 1),
+ * out bf16 [rows, cols] contiguous.
+ * Replaces turing_utils::dequantize_int8_bf16 (ops.py:129-160; bindings.cpp:423-472;
+ * kernel/csrc/turing/bf16_epilogue.cu:146-217).
+ */
+CTU_API int ctu_dequantize_int8_bf16(const int32_t *acc, int64_t acc_stride, const float *a_scale, const float *w_scale,
+                             int64_t w_scale_count, void *out, int64_t rows, int64_t cols, void *stream);
+
+/* Test hook: launch the GEMM with its MMA issuer waiting on a barrier nothing arrives
+ * on, bounded by timeout_ns; the kernel must stop cleanly and raise flag 64. */
+CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *acc, int64_t m, int64_t n, int64_t k,
+                                    uint64_t timeout_ns, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CTU_B200_H_ */
