@@ -59,6 +59,18 @@ def synth_inputs(m, device, seed=0):
     return xs, layers
 
 
+def max_over_ranks(values, world: int, device=None):
+    """Element-wise maximum of per-rank timings (every rank calls it, same order)."""
+    import torch
+
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
 # ----------------------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
@@ -250,10 +262,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
 
     # ---------------------------------------------------------------- reduce over ranks (max time)
-    t = torch.tensor([elapsed_ms, e2e_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms = float(t[0]), float(t[1])
+    elapsed_ms, e2e_ms = max_over_ranks([elapsed_ms, e2e_ms], world, dev)
     ms_per_step = elapsed_ms / args.steps
     value = world * ops_per_step(m) / (ms_per_step * 1e-3) / 1e12
     e2e_value = world * ops_per_step(m) / (e2e_ms * 1e-3) / 1e12
