@@ -15,9 +15,11 @@
 #include "convrot_quant.cuh"
 #include "dequant.cuh"
 #include "gemm_i8.cuh"
+#include "host.cuh"
 #include "ptx.cuh"
 
-namespace {
+namespace ctu {
+namespace host {
 
 thread_local std::string g_last_error;
 
@@ -42,6 +44,20 @@ int cuda_fail(cudaError_t e, const char *what) {
     } while (0)
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int device_query(DeviceQuery *q) {
+    CTU_CUDA(cudaGetDevice(&q->device));
+    int major = 0, minor = 0;
+    CTU_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, q->device));
+    CTU_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, q->device));
+    if (major != 10 || minor != 0) {
+        return fail(CTU_ERR_UNSUPPORTED, "libctu_b200 targets sm_100a (B200); device %d is sm_%d%d", q->device, major,
+                    minor);
+    }
+    CTU_CUDA(cudaDeviceGetAttribute(&q->num_sms, cudaDevAttrMultiProcessorCount, q->device));
+    CTU_CUDA(cudaDeviceGetAttribute(&q->smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, q->device));
+    return CTU_OK;
+}
 
 // ---------------------------------------------------------------------------- device state
 constexpr int kMaxDevices = 64;
@@ -213,7 +229,84 @@ int check_gemm_shapes(const int8_t *a, const int8_t *w, const void *out, int64_t
     return CTU_OK;
 }
 
-}  // namespace
+int check_quantize_args(const void *x, int64_t rows, int64_t k, int act, int bits, const int8_t *codes,
+                        const float *scales) {
+    if (rows < 0 || k <= 0 || k % 256 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot width must be positive and divisible by 256 (got %lld)",
+                    static_cast<long long>(k));
+    if (bits != 8 && bits != 4) return fail(CTU_ERR_INVALID_ARGUMENT, "bits must be 8 or 4");
+    if (act != CTU_ACT_NONE && act != CTU_ACT_SWIGLU && act != CTU_ACT_GELU_TANH)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
+    if (rows > INT32_MAX || k > (1 << 20)) return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot dimensions exceed range");
+    if (rows == 0) return CTU_OK;
+    if (!x || !codes || !scales) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(x) || !aligned16(codes)) return fail(CTU_ERR_INVALID_ARGUMENT, "x and codes must be 16-byte aligned");
+    return CTU_OK;
+}
+
+int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
+                 uint32_t *err, const DeviceQuery &q, cudaStream_t stream) {
+    if (int rc = check_quantize_args(x, rows, k, act, bits, codes, scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    QuantPlan plan;
+    if (int rc = plan_quant(k, act, bits, q.smem_optin, &plan)) return rc;
+    const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
+    CUtensorMap map;
+    if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k_in / 64, 64,
+                           static_cast<uint32_t>(plan.box_rows)))
+        return rc;
+    ctu::rot::QuantArgs args;
+    args.codes = codes;
+    args.scales = scales;
+    args.err = err;
+    args.m = static_cast<int>(rows);
+    args.k = static_cast<int>(k);
+    args.rows_per_batch = plan.rows_per_batch;
+    args.box_rows = plan.box_rows;
+    args.copies = plan.copies;
+    using ctu::rot::kActGelu;
+    using ctu::rot::kActNone;
+    using ctu::rot::kActSwiGLU;
+    if (act == CTU_ACT_NONE) {
+        return bits == 8 ? launch_quant<kActNone, 8>(map, args, plan, q.num_sms, stream)
+                         : launch_quant<kActNone, 4>(map, args, plan, q.num_sms, stream);
+    }
+    if (act == CTU_ACT_SWIGLU) {
+        return bits == 8 ? launch_quant<kActSwiGLU, 8>(map, args, plan, q.num_sms, stream)
+                         : launch_quant<kActSwiGLU, 4>(map, args, plan, q.num_sms, stream);
+    }
+    return bits == 8 ? launch_quant<kActGelu, 8>(map, args, plan, q.num_sms, stream)
+                     : launch_quant<kActGelu, 4>(map, args, plan, q.num_sms, stream);
+}
+
+int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    uint32_t *err, const DeviceQuery &q, cudaStream_t stream) {
+    if (int rc = check_gemm_shapes(a, w, out, m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!a_scale || !w_scale) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (w_scale_count != 1 && w_scale_count != n)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output channel");
+    if (k == 0) return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
+    ctu::gemm::GemmArgs args{};
+    args.a_scale = a_scale;
+    args.w_scale = w_scale;
+    args.bias = bias;
+    args.out = out;
+    args.err = err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.w_scale_count = static_cast<int>(w_scale_count);
+    args.out_mode = ctu::gemm::kOutBf16;
+    return launch_gemm(a, w, args, q.num_sms, stream);
+}
+
+}  // namespace host
+}  // namespace ctu
+
+using namespace ctu::host;
 
 // ============================================================================ C ABI
 extern "C" {
@@ -230,63 +323,32 @@ int ctu_get_device_error(int device, uint32_t *flags, int clear) {
         std::lock_guard<std::mutex> lock(g_mutex);
         w = g_err_word[device];
     }
+    uint32_t regular = 0;
     *flags = 0;
-    if (w == nullptr) return CTU_OK;  // nothing launched on this device yet
+    uint32_t static_flags = 0;
+    if (int rc = static_scratch_error(device, &static_flags, clear != 0)) return rc;
+    *flags = static_flags;
+    if (w == nullptr) return CTU_OK;  // no other launch on this device yet
     int prev = 0;
     CTU_CUDA(cudaGetDevice(&prev));
     CTU_CUDA(cudaSetDevice(device));
     cudaError_t e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemcpy(flags, w, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&regular, w, sizeof(uint32_t), cudaMemcpyDeviceToHost);
     if (e == cudaSuccess && clear) e = cudaMemset(w, 0, sizeof(uint32_t));
     cudaSetDevice(prev);
     if (e != cudaSuccess) return cuda_fail(e, "ctu_get_device_error");
+    *flags |= regular;
     return CTU_OK;
 }
 
 int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
                          void *stream) {
-    if (rows < 0 || k <= 0 || k % 256 != 0)
-        return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot width must be positive and divisible by 256 (got %lld)",
-                    static_cast<long long>(k));
-    if (bits != 8 && bits != 4) return fail(CTU_ERR_INVALID_ARGUMENT, "bits must be 8 or 4");
-    if (act != CTU_ACT_NONE && act != CTU_ACT_SWIGLU && act != CTU_ACT_GELU_TANH)
-        return fail(CTU_ERR_INVALID_ARGUMENT, "unknown activation %d", act);
-    if (rows > INT32_MAX || k > (1 << 20)) return fail(CTU_ERR_INVALID_ARGUMENT, "ConvRot dimensions exceed range");
+    if (int rc = check_quantize_args(x, rows, k, act, bits, codes, scales)) return rc;
     if (rows == 0) return CTU_OK;
-    if (!x || !codes || !scales) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
-    if (!aligned16(x) || !aligned16(codes)) return fail(CTU_ERR_INVALID_ARGUMENT, "x and codes must be 16-byte aligned");
     DeviceInfo dev;
     if (int rc = device_info(&dev)) return rc;
-    QuantPlan plan;
-    if (int rc = plan_quant(k, act, bits, dev.smem_optin, &plan)) return rc;
-    const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
-    CUtensorMap map;
-    if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k_in / 64, 64,
-                           static_cast<uint32_t>(plan.box_rows)))
-        return rc;
-    ctu::rot::QuantArgs args;
-    args.codes = codes;
-    args.scales = scales;
-    args.err = dev.err;
-    args.m = static_cast<int>(rows);
-    args.k = static_cast<int>(k);
-    args.rows_per_batch = plan.rows_per_batch;
-    args.box_rows = plan.box_rows;
-    args.copies = plan.copies;
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    using ctu::rot::kActGelu;
-    using ctu::rot::kActNone;
-    using ctu::rot::kActSwiGLU;
-    if (act == CTU_ACT_NONE) {
-        return bits == 8 ? launch_quant<kActNone, 8>(map, args, plan, dev.num_sms, s)
-                         : launch_quant<kActNone, 4>(map, args, plan, dev.num_sms, s);
-    }
-    if (act == CTU_ACT_SWIGLU) {
-        return bits == 8 ? launch_quant<kActSwiGLU, 8>(map, args, plan, dev.num_sms, s)
-                         : launch_quant<kActSwiGLU, 4>(map, args, plan, dev.num_sms, s);
-    }
-    return bits == 8 ? launch_quant<kActGelu, 8>(map, args, plan, dev.num_sms, s)
-                     : launch_quant<kActGelu, 4>(map, args, plan, dev.num_sms, s);
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
 }
 
 int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
@@ -294,28 +356,11 @@ int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
                     void *stream) {
     if (int rc = check_gemm_shapes(a, w, out, m, n, k)) return rc;
     if (m == 0 || n == 0) return CTU_OK;
-    if (!a_scale || !w_scale) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
-    if (w_scale_count != 1 && w_scale_count != n)
-        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output channel");
     DeviceInfo dev;
     if (int rc = device_info(&dev)) return rc;
-    if (k == 0) {
-        // Empty contraction: acc = 0; route through the dequant epilogue semantics.
-        return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
-    }
-    ctu::gemm::GemmArgs args{};
-    args.a_scale = a_scale;
-    args.w_scale = w_scale;
-    args.bias = bias;
-    args.out = out;
-    args.err = dev.err;
-    args.m = static_cast<int>(m);
-    args.n = static_cast<int>(n);
-    args.k = static_cast<int>(k);
-    args.ldc = static_cast<int>(n);
-    args.w_scale_count = static_cast<int>(w_scale_count);
-    args.out_mode = ctu::gemm::kOutBf16;
-    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    return run_int8_linear(a, w, a_scale, w_scale, w_scale_count, bias, out, m, n, k, dev.err, q,
+                           static_cast<cudaStream_t>(stream));
 }
 
 int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,

@@ -98,6 +98,26 @@ CTU_API int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, in
 CTU_API int ctu_dequantize_int8_bf16(const int32_t *acc, int64_t acc_stride, const float *a_scale, const float *w_scale,
                              int64_t w_scale_count, void *out, int64_t rows, int64_t cols, void *stream);
 
+/*
+ * ConvRot W8A8 linear in one call that allocates no device memory (no counterpart in
+ * the reference).  For callers that cannot call cudaMalloc -- code inside a region
+ * where allocation is forbidden or would break a pre-reserved memory pool, or hosts
+ * without an allocator: the quantized activation (int8 codes and fp32 per-token
+ * scales) and the kernels' error word live in a file-scope device array of the
+ * library (16 MiB of codes + 65536 scales, held by every GPU that loads the library
+ * until exit) instead of caller- or library-allocated buffers.
+ *   x bf16 [m, k] (k % 256 == 0), w int8 [n, k] (n % 8 == 0), w_scale [n] or scalar,
+ *   bias fp32 [n] or NULL, out bf16 [m, n]; same numerics as ctu_convrot_quantize
+ *   followed by ctu_int8_linear.
+ * Rejects m * k > 16 MiB or m > 65536.  All calls on a device share the array: calls
+ * that can overlap on the GPU race and must be ordered.  The first call on each
+ * device resolves the array's address (cudaGetSymbolAddress) and clears the error
+ * word; make it before any stream capture.
+ */
+CTU_API int ctu_convrot_w8a8_linear_static_scratch(const void *x, const int8_t *w, const float *w_scale,
+                                                   int64_t w_scale_count, const float *bias, void *out, int64_t m,
+                                                   int64_t n, int64_t k, void *stream);
+
 /* Test hook: launch the GEMM with its MMA issuer waiting on a barrier nothing arrives
  * on, bounded by timeout_ns; the kernel must stop cleanly and raise flag 64. */
 CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *acc, int64_t m, int64_t n, int64_t k,
