@@ -90,7 +90,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
         return self
@@ -236,36 +236,38 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     quant_gbs = sum(o for _, _, o in quant_ev) / (sum(quant_ms) * 1e-3) / 1e9
 
     # ---------------------------------------------------------------- end-to-end (host buffers)
-    host_x = {k: x.cpu().pin_memory() for k, x in xs.items()}
-    host_out = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _, n, _, _, _ in layers]
-    h2d = sum(x.numel() * x.element_size() for x in host_x.values())
-    d2h = sum(o.numel() * o.element_size() for o in host_out)
+    e2e_ms, h2d, d2h = float("nan"), 0, 0
+    if not args.skip_e2e:
+        host_x = {k: x.cpu().pin_memory() for k, x in xs.items()}
+        host_out = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _, n, _, _, _ in layers]
+        h2d = sum(x.numel() * x.element_size() for x in host_x.values())
+        d2h = sum(o.numel() * o.element_size() for o in host_out)
 
-    def e2e_step():
-        dev_x = {k: hx.to(dev, non_blocking=True) for k, hx in host_x.items()}
-        for i, (k, n, w, w_s, b) in enumerate(layers):
-            q, s = kops.turing_bf16_int8_convrot_quantize(dev_x[k], 256)
-            host_out[i].copy_(kops.turing_int8_linear(q, w, s, w_s, b), non_blocking=True)
+        def e2e_step():
+            dev_x = {k: hx.to(dev, non_blocking=True) for k, hx in host_x.items()}
+            for i, (k, n, w, w_s, b) in enumerate(layers):
+                q, s = kops.turing_bf16_int8_convrot_quantize(dev_x[k], 256)
+                host_out[i].copy_(kops.turing_int8_linear(q, w, s, w_s, b), non_blocking=True)
 
-    e2e_steps = max(1, min(args.steps, 5))
-    for _ in range(2):
-        e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    e_stop.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier()
-    e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
+        e2e_steps = max(1, min(args.steps, 5))
+        for _ in range(2):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e_stop.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
 
     # ---------------------------------------------------------------- reduce over ranks (max time)
     elapsed_ms, e2e_ms = max_over_ranks([elapsed_ms, e2e_ms], world, dev)
     ms_per_step = elapsed_ms / args.steps
     value = world * ops_per_step(m) / (ms_per_step * 1e-3) / 1e12
-    e2e_value = world * ops_per_step(m) / (e2e_ms * 1e-3) / 1e12
+    e2e_value = None if args.skip_e2e else world * ops_per_step(m) / (e2e_ms * 1e-3) / 1e12
 
     if rank != 0:
         return
@@ -299,12 +301,15 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "parallelism": f"token rows, {world} independent rank(s)"},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": UNIT,
                      "frac": gemm_tops / peak, "traffic": args.gemm_traffic, "kernel": "ctu::gemm::w8a8_gemm_kernel",
+                     "traffic_note": "dram bytes of one 5120x5120 launch (ncu at M=16384, scaled to M=32760); "
+                                     "algorithmic 529 MB",
                      "peak_source": peak_src},
         "quantizer_roofline": {"bound": "hbm", "achieved": quant_gbs, "peak": hbm, "unit": "GB/s",
                                "frac": quant_gbs / hbm, "kernel": "ctu::rot::convrot_quant_kernel<0,8>"},
         "clocks": clocks.summary(),
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "path": "pinned host activations -> turing_utils ops -> pinned host outputs, one stream"},
+        "e2e": None if args.skip_e2e else {
+            "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "pinned host activations -> turing_utils ops -> pinned host outputs, one stream"},
         "gpu_launches": 2 * len(SHAPES) * args.steps,
         "cpu_baseline": cpu,
     }
@@ -314,12 +319,15 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per GPU")
     ap.add_argument("--skip-cpu", action="store_true")
-    ap.add_argument("--gemm-traffic", type=float, default=None,
+    ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host round trip")
+    # profiles/w8a8_gemm_k5120_n5120_m16384.md: dram read+write of one 5120x5120 launch at
+    # M=16384 (240.2 MB), scaled to M=32760 by rows processed.
+    ap.add_argument("--gemm-traffic", type=float, default=240.16e6 * 32760 / 16384,
                     help="ncu dram bytes per GEMM launch (profiles/), reported as roofline.traffic")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -47,14 +47,13 @@ constexpr float kBf16Max = 3.38953139e38f;
 // Radix-4 butterfly on two independent 4-tuples at once (packed f32x2), with the
 // reference's association: y0 = ((x0+x1)+x2)-x3, y1 = ((x0+x1)-x2)+x3,
 // y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, each times 0.5.
-__device__ __forceinline__ void butterfly2(float2 &x0, float2 &x1, float2 &x2, float2 &x3) {
-    const float2 half = make_float2(0.5f, 0.5f);
-    const float2 t = add2(x0, x1);
-    const float2 b = sub2(x0, x1);   // x0 - x1;  (-x0 + x1) == -(x0 - x1) exactly
-    const float2 y0 = mul2(half, sub2(add2(t, x2), x3));
-    const float2 y1 = mul2(half, add2(sub2(t, x2), x3));
-    const float2 y2 = mul2(half, add2(add2(b, x2), x3));
-    const float2 y3 = mul2(half, add2(sub2(x2, b), x3));  // (-b) + x2 == x2 - b exactly
+__device__ __forceinline__ void butterfly2(f32x2 &x0, f32x2 &x1, f32x2 &x2, f32x2 &x3, f32x2 half) {
+    const f32x2 t = fadd2(x0, x1);
+    const f32x2 b = fsub2(x0, x1);  // x0 - x1;  (-x0 + x1) == -(x0 - x1) exactly
+    const f32x2 y0 = fmul2(half, fsub2(fadd2(t, x2), x3));
+    const f32x2 y1 = fmul2(half, fadd2(fsub2(t, x2), x3));
+    const f32x2 y2 = fmul2(half, fadd2(fadd2(b, x2), x3));
+    const f32x2 y3 = fmul2(half, fadd2(fsub2(x2, b), x3));  // (-b) + x2 == x2 - b exactly
     x0 = y0;
     x1 = y1;
     x2 = y2;
@@ -94,9 +93,9 @@ __device__ __forceinline__ float activate<kActGelu>(uint32_t x_bits, uint32_t) {
 // Load one lane's 128 inputs of a group: chunk0 = elements h*64+[0,64) (bit 7 = 0),
 // chunk1 = 128+h*64+[0,64).  `row64` is the 128-byte slice index of chunk0 inside the
 // batch buffer; chunk1 sits two slices later.  For SwiGLU the `up` half of the row
-// starts `up_off` slices after the gate.
+// starts `up_off` slices after the gate.  v[j] = (chunk0[j], chunk1[j]).
 template <int Act>
-__device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, uint32_t up_off, float2 (&v)[64]) {
+__device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&v)[64]) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         const uint4 a = *reinterpret_cast<const uint4 *>(buf + sw128(row64, c));
@@ -110,17 +109,15 @@ __device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, u
             const uint32_t ubw[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = make_float2(activate<Act>(aw[q] << 16, uaw[q] << 16),
-                                               activate<Act>(bw[q] << 16, ubw[q] << 16));
-                v[8 * c + 2 * q + 1] = make_float2(activate<Act>(aw[q] & 0xFFFF0000u, uaw[q] & 0xFFFF0000u),
-                                                   activate<Act>(bw[q] & 0xFFFF0000u, ubw[q] & 0xFFFF0000u));
+                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, uaw[q] << 16), activate<Act>(bw[q] << 16, ubw[q] << 16));
+                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, uaw[q] & 0xFFFF0000u),
+                                           activate<Act>(bw[q] & 0xFFFF0000u, ubw[q] & 0xFFFF0000u));
             }
         } else {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = make_float2(activate<Act>(aw[q] << 16, 0), activate<Act>(bw[q] << 16, 0));
-                v[8 * c + 2 * q + 1] =
-                    make_float2(activate<Act>(aw[q] & 0xFFFF0000u, 0), activate<Act>(bw[q] & 0xFFFF0000u, 0));
+                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, 0), activate<Act>(bw[q] << 16, 0));
+                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, 0), activate<Act>(bw[q] & 0xFFFF0000u, 0));
             }
         }
     }
@@ -133,85 +130,93 @@ __device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, u
 template <int Act>
 __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint32_t up_off, int h, bool active,
                                              float &absmax, float &nan_probe) {
-    float2 v[64];
+    f32x2 v[64];
     load_group<Act>(buf, row64, up_off, v);
+    const f32x2 half = pk2(0.5f, 0.5f);
 
     // Stage 1 (stride 1): bits 0-1 of the element index.
 #pragma unroll
-    for (int q = 0; q < 16; ++q) butterfly2(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    for (int q = 0; q < 16; ++q) butterfly2(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3], half);
     // Stage 2 (stride 4): bits 2-3.
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
 #pragma unroll
-        for (int p = 0; p < 4; ++p) butterfly2(v[16 * c + p], v[16 * c + p + 4], v[16 * c + p + 8], v[16 * c + p + 12]);
+        for (int p = 0; p < 4; ++p)
+            butterfly2(v[16 * c + p], v[16 * c + p + 4], v[16 * c + p + 8], v[16 * c + p + 12], half);
     }
     // Stage 3 (stride 16): bits 4-5.
 #pragma unroll
-    for (int p = 0; p < 16; ++p) butterfly2(v[p], v[p + 16], v[p + 32], v[p + 48]);
+    for (int p = 0; p < 16; ++p) butterfly2(v[p], v[p + 16], v[p + 32], v[p + 48], half);
 
-    // Stage 4 (stride 64): bit 6 is the lane parity h, bit 7 is the pair index
-    // inside v[j] (.x: bit 7 = 0, .y: bit 7 = 1).  The four inputs of position j
-    // are x0 = lane0.x, x1 = lane1.x, x2 = lane0.y, x3 = lane1.y.  Lane h produces
-    // y_h into .x and y_{2+h} into .y:
+    // Stage 4 (stride 64): bit 6 is the lane parity h, bit 7 the half of v[j]
+    // (low: bit 7 = 0, high: bit 7 = 1).  The four inputs at position j are
+    // x0 = lane0.lo, x1 = lane1.lo, x2 = lane0.hi, x3 = lane1.hi.  Lane h produces
+    // y_h (bit 7 = 0) and y_{2+h} (bit 7 = 1):
     //   lane 0: y0 = ((x0+x1)+x2)-x3          y2 = ((x0-x1)+x2)+x3
     //   lane 1: y1 = -((-(x0+x1)+x2)-x3)      y3 = ((x1-x0)+x2)+x3
-    // which is the reference's y1 = ((x0+x1)-x2)+x3 with every rounding mirrored.
+    // which is the reference's y1 = ((x0+x1)-x2)+x3 with every rounding mirrored
+    // (IEEE rounding is symmetric in sign).  Two positions j, j+1 share each packed
+    // operation, and their outputs form the bf16x2 words stored back.
     const unsigned full = 0xffffffffu;
     const int lane = threadIdx.x & 31;
     const int lane0 = lane & ~1;
-    const float sgn = h ? -1.0f : 1.0f;
-    const float hsgn = h ? -0.5f : 0.5f;
+    const f32x2 sgn = h ? pk2(-1.0f, -1.0f) : pk2(1.0f, 1.0f);
+    const f32x2 hsgn = h ? pk2(-0.5f, -0.5f) : pk2(0.5f, 0.5f);
     float m = 0.0f;
-    float probe = 0.0f;
+    f32x2 probe = pk2(0.0f, 0.0f);
+    uint32_t wa[4], wb[4];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) {
-        const float own = v[j].x;
-        const float other = __shfl_xor_sync(full, own, 1);
-        const float x2 = __shfl_sync(full, v[j].y, lane0);
-        const float x3 = __shfl_sync(full, v[j].y, lane0 + 1);
-        const float p = __fadd_rn(own, other);   // x0 + x1 in both lanes
-        const float d = __fsub_rn(own, other);   // x0 - x1 (lane 0) or x1 - x0 (lane 1)
-        const float ya = __fmul_rn(hsgn, __fsub_rn(__fmaf_rn(sgn, p, x2), x3));
-        const float yb = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(d, x2), x3));
-        v[j] = make_float2(ya, yb);
-        m = fmaxf(m, fmaxf(fabsf(ya), fabsf(yb)));
-        probe = __fadd_rn(probe, __fadd_rn(ya, yb));
+    for (int j = 0; j < 64; j += 2) {
+        float o0, o0y, o1, o1y;
+        unpk2(v[j], o0, o0y);
+        unpk2(v[j + 1], o1, o1y);
+        const float t0 = __shfl_xor_sync(full, o0, 1);
+        const float t1 = __shfl_xor_sync(full, o1, 1);
+        const float a0 = __shfl_sync(full, o0y, lane0);
+        const float a1 = __shfl_sync(full, o1y, lane0);
+        const float b0 = __shfl_sync(full, o0y, lane0 + 1);
+        const float b1 = __shfl_sync(full, o1y, lane0 + 1);
+        const f32x2 own = pk2(o0, o1);
+        const f32x2 other = pk2(t0, t1);
+        const f32x2 x2 = pk2(a0, a1);
+        const f32x2 x3 = pk2(b0, b1);
+        const f32x2 p = fadd2(own, other);  // x0 + x1 in both lanes
+        const f32x2 d = fsub2(own, other);  // x0 - x1 (lane 0) or x1 - x0 (lane 1)
+        const f32x2 ya = fmul2(hsgn, fsub2(ffma2(sgn, p, x2), x3));
+        const f32x2 yb = fmul2(half, fadd2(fadd2(d, x2), x3));
+        probe = fadd2(probe, fadd2(ya, yb));
+        float ya0, ya1, yb0, yb1;
+        unpk2(ya, ya0, ya1);
+        unpk2(yb, yb0, yb1);
+        m = max_abs3(m, ya0, ya1);
+        m = max_abs3(m, yb0, yb1);
+        wa[(j >> 1) & 3] = pack_bf16x2(ya0, ya1);
+        wb[(j >> 1) & 3] = pack_bf16x2(yb0, yb1);
+        if ((j & 7) == 6 && active) {
+            // bf16(y) of 8 positions back in place over this lane's own (already
+            // consumed) input elements.
+            const int c = j >> 3;
+            *reinterpret_cast<uint4 *>(buf + sw128(row64, c)) = make_uint4(wa[0], wa[1], wa[2], wa[3]);
+            *reinterpret_cast<uint4 *>(buf + sw128(row64 + 2, c)) = make_uint4(wb[0], wb[1], wb[2], wb[3]);
+        }
     }
+    float p0, p1;
+    unpk2(probe, p0, p1);
     absmax = active ? m : 0.0f;
-    nan_probe = active ? probe : 0.0f;
-    if (!active) return;
-
-    // bf16(y) back in place (this lane's own element positions).
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        uint4 a, b;
-        a.x = pack_bf16x2(v[8 * c + 0].x, v[8 * c + 1].x);
-        a.y = pack_bf16x2(v[8 * c + 2].x, v[8 * c + 3].x);
-        a.z = pack_bf16x2(v[8 * c + 4].x, v[8 * c + 5].x);
-        a.w = pack_bf16x2(v[8 * c + 6].x, v[8 * c + 7].x);
-        b.x = pack_bf16x2(v[8 * c + 0].y, v[8 * c + 1].y);
-        b.y = pack_bf16x2(v[8 * c + 2].y, v[8 * c + 3].y);
-        b.z = pack_bf16x2(v[8 * c + 4].y, v[8 * c + 5].y);
-        b.w = pack_bf16x2(v[8 * c + 6].y, v[8 * c + 7].y);
-        *reinterpret_cast<uint4 *>(buf + sw128(row64, c)) = a;
-        *reinterpret_cast<uint4 *>(buf + sw128(row64 + 2, c)) = b;
-    }
+    nan_probe = active ? __fadd_rn(p0, p1) : 0.0f;
 }
 
 // Quantize 8 consecutive bf16(y) values of one row to int8 with the fast chain.
-__device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, float rcp) {
+__device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    uint32_t q[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float2 pr = mul2(make_float2(bf16lo(ww[i]), bf16hi(ww[i])), make_float2(rcp, rcp));
-        q[i] = pack_bf16x2(pr.x, pr.y);  // bf16(y / bf16(scale))
-    }
     int c[8];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        c[2 * i] = __float2int_rn(bf16lo(q[i]));
-        c[2 * i + 1] = __float2int_rn(bf16hi(q[i]));
+        float lo, hi;
+        unpk2(fmul2(pk2(bf16lo(ww[i]), bf16hi(ww[i])), rcp2), lo, hi);
+        const uint32_t qb = pack_bf16x2(lo, hi);
+        c[2 * i] = __float2int_rn(bf16lo(qb));
+        c[2 * i + 1] = __float2int_rn(bf16hi(qb));
     }
     // cvt.pack.sat.s8.s32.b32 d, a, b, c: d = {sat8(b), sat8(a), c[0:16)} from the low byte up.
     uint32_t t0, t1, lo, hi;
@@ -224,7 +229,7 @@ __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, float rcp) {
 
 // Exact reference chain including NaN (fmaxf(-128, NaN) == -128) for rows that
 // contain NaN or infinities.
-__device__ __forceinline__ uint2 quant8_int8_exact(uint4 w, float rounded_scale) {
+__device__ __noinline__ uint2 quant8_int8_exact(uint4 w, float rounded_scale) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     uint32_t out[2] = {0, 0};
 #pragma unroll
@@ -240,14 +245,15 @@ __device__ __forceinline__ uint2 quant8_int8_exact(uint4 w, float rounded_scale)
 }
 
 // Quantize 8 consecutive bf16(y) values to packed int4 (exact for every input).
-__device__ __forceinline__ uint32_t quant8_int4(uint4 w, float inv_scale) {
+__device__ __forceinline__ uint32_t quant8_int4(uint4 w, f32x2 inv2) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
     uint32_t out = 0;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float2 pr = mul2(make_float2(bf16lo(ww[i]), bf16hi(ww[i])), make_float2(inv_scale, inv_scale));
-        const float lo = fminf(7.0f, fmaxf(-7.0f, pr.x));
-        const float hi = fminf(7.0f, fmaxf(-7.0f, pr.y));
+        float plo, phi;
+        unpk2(fmul2(pk2(bf16lo(ww[i]), bf16hi(ww[i])), inv2), plo, phi);
+        const float lo = fminf(7.0f, fmaxf(-7.0f, plo));
+        const float hi = fminf(7.0f, fmaxf(-7.0f, phi));
         const uint32_t lb = static_cast<uint32_t>(__float2int_rn(lo)) & 0xFu;
         const uint32_t hb = static_cast<uint32_t>(__float2int_rn(hi)) & 0xFu;
         out |= (lb | (hb << 4)) << (8 * i);
@@ -357,13 +363,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 
         // -------------------------------------------------------------- quantize
         const int chunks_per_row = K / 8;
-        const int total_chunks = rows * chunks_per_row;
+        int r = tid / chunks_per_row;
+        int col8 = tid - r * chunks_per_row;
         int cur_row = -1;
         float qparam = 0.0f;
         bool exact = false;
-        for (int ch = tid; ch < total_chunks; ch += nthreads) {
-            const int r = ch / chunks_per_row;
-            const int col8 = ch - r * chunks_per_row;
+        while (r < rows) {
             if (r != cur_row) {
                 cur_row = r;
                 const float amax = __uint_as_float(absmax_rows[r]);
@@ -378,14 +383,17 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                     qparam = exact ? rs : __frcp_rn(rs);
                 }
             }
-            // bf16(y) chunk: slice = r*slices_per_row + col8/8, 16-byte chunk col8 % 8.
-            const uint4 w = *reinterpret_cast<const uint4 *>(
-                inbuf[buf] + sw128(r * slices_per_row + (col8 >> 3), col8 & 7));
+            const uint4 w = *reinterpret_cast<const uint4 *>(inbuf[buf] + sw128(r * slices_per_row + (col8 >> 3), col8 & 7));
             if (Bits == 4) {
-                *reinterpret_cast<uint32_t *>(codebuf + r * Kout + col8 * 4) = quant8_int4(w, qparam);
+                *reinterpret_cast<uint32_t *>(codebuf + r * Kout + col8 * 4) = quant8_int4(w, pk2(qparam, qparam));
             } else {
-                const uint2 q = exact ? quant8_int8_exact(w, qparam) : quant8_int8_fast(w, qparam);
+                const uint2 q = exact ? quant8_int8_exact(w, qparam) : quant8_int8_fast(w, pk2(qparam, qparam));
                 *reinterpret_cast<uint2 *>(codebuf + r * Kout + col8 * 8) = q;
+            }
+            col8 += nthreads;
+            while (col8 >= chunks_per_row) {
+                col8 -= chunks_per_row;
+                ++r;
             }
         }
         fence_proxy_async_smem();
