@@ -160,6 +160,68 @@ def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=
     return out
 
 
+def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=None, tile_policy=0):
+    """bindings.cpp:167-260: signed packed-int4 weights [N, K/2] (even k in the low
+    nibble), per-channel weight scale, per-token activation scale, fused epilogue.
+    The tcgen05 kernel takes K % 32 == 0 and N % 8 == 0; other shapes allowed by the
+    reference (K % 4 == 0, any N) are zero-padded here, as the reference pads its
+    N tail (bindings.cpp:229-255)."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = activation_scale.to(torch.float32).contiguous()
+    weight_scale = weight_scale.to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.to(torch.float32).contiguous()
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    if activation.dtype != torch.int8:
+        raise RuntimeError("activation must be int8")
+    if weight.dtype != torch.int8:
+        raise RuntimeError("weight must be packed int8 storage")
+    dev = activation.device
+    if weight.device != dev:
+        raise RuntimeError("activation and weight must be on the same CUDA device")
+    if not (activation_scale.is_cuda and weight_scale.is_cuda):
+        raise RuntimeError("scales must be CUDA tensors")
+    if activation_scale.device != dev or weight_scale.device != dev:
+        raise RuntimeError("scales must be on the activation device")
+    m, k = activation.shape
+    n = weight.shape[0]
+    if k % 4 != 0:
+        raise RuntimeError("activation K must be divisible by 4")
+    if weight.shape[1] * 2 != k:
+        raise RuntimeError("packed weight K must match activation K")
+    if activation_scale.numel() != m:
+        raise RuntimeError("activation_scale must contain one value per row")
+    if weight_scale.numel() != n:
+        raise RuntimeError("weight_scale must contain one value per output channel")
+    if bias is not None and (not bias.is_cuda or bias.device != dev):
+        raise RuntimeError("bias must be on the activation device")
+    if bias is not None and bias.numel() != n:
+        raise RuntimeError("bias must contain one value per output channel")
+    weight_scale = weight_scale.reshape(-1)
+    bias = None if bias is None else bias.reshape(-1)
+    k_pad = -(-k // 32) * 32
+    n_pad = -(-n // 8) * 8
+    if k_pad != k:
+        activation = torch.nn.functional.pad(activation, (0, k_pad - k))
+        weight = torch.nn.functional.pad(weight, (0, (k_pad - k) // 2))
+    if n_pad != n:
+        weight = torch.nn.functional.pad(weight, (0, 0, 0, n_pad - n))
+        weight_scale = torch.nn.functional.pad(weight_scale, (0, n_pad - n))
+        if bias is not None:
+            bias = torch.nn.functional.pad(bias, (0, n_pad - n))
+    out = torch.empty((m, n_pad), dtype=torch.bfloat16, device=dev)
+    if m == 0 or n == 0:
+        return out[:, :n]
+    activation, weight = _aligned(activation), _aligned(weight)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ctu_w4a8_linear(
+            _ptr(activation), _ptr(weight), _ptr(activation_scale), _ptr(weight_scale), n_pad,
+            _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+    return out if n_pad == n else out[:, :n].contiguous()
+
+
 def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, output_columns=-1):
     """bindings.cpp:423-472."""
     accumulator = accumulator.contiguous()

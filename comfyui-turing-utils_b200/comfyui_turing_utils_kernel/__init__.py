@@ -17,6 +17,7 @@ from .ops import (
     turing_int8_linear,
     turing_swiglu_int4_convrot_quantize,
     turing_swiglu_int8_convrot_quantize,
+    turing_w4a8_linear,
 )
 
 # Version contract checked by the plugin (precision.py:31-32,91-104 of the reference).
@@ -34,4 +35,5 @@ __all__ = [
     "turing_int8_linear",
     "turing_swiglu_int4_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize",
+    "turing_w4a8_linear",
 ]

@@ -20,6 +20,31 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
         raise RuntimeError(f"{what} requires sm75 or newer")
 
 
+# ops.py:8-35
+@torch.library.custom_op("turing_utils::w4a8_linear", mutates_args=())
+def turing_w4a8_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Signed packed-int4 W4A8 linear (int4 sign-extended in shared memory, tcgen05 MMA)."""
+    _require_cuda(activation, "Turing W4A8")
+    return _C.turing_w4a8_linear(
+        activation.contiguous(),
+        weight.contiguous(),
+        activation_scale.contiguous(),
+        weight_scale.contiguous(),
+        None if bias is None else bias.contiguous(),
+    )
+
+
+@turing_w4a8_linear.register_fake
+def _turing_w4a8_linear_fake(activation, weight, activation_scale, weight_scale, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
+
+
 # ops.py:96-126
 @torch.library.custom_op("turing_utils::int8_linear", mutates_args=())
 def turing_int8_linear(

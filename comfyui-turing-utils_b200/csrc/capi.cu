@@ -121,7 +121,8 @@ int get_encoder(EncodeTiledFn *out) {
 
 // 2D row-major tensor [outer, inner] of `elem_bytes`-byte elements, 128-byte swizzle.
 int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const void *base, uint64_t inner,
-              uint64_t outer, uint32_t box_inner, uint32_t box_outer) {
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
     EncodeTiledFn enc;
     if (int rc = get_encoder(&enc)) return rc;
     const cuuint64_t dims[2] = {inner, outer};
@@ -129,7 +130,7 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const 
     const cuuint32_t box[2] = {box_inner, box_outer};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = enc(map, type, 2, const_cast<void *>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(CTU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return CTU_OK;
@@ -192,27 +193,43 @@ int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const 
 }
 
 // ---------------------------------------------------------------------------- GEMM launch
-int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms, cudaStream_t stream) {
+template <bool kW4>
+int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms,
+                  cudaStream_t stream) {
     CUtensorMap map_a, map_b;
     if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, args.k, args.m, ctu::gemm::kBK,
-                           ctu::gemm::kBM))
+                           ctu::gemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
-    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, ctu::gemm::kBK,
-                           ctu::gemm::kBN))
-        return rc;
+    if (kW4) {
+        // Packed weights [n, k/2]: the converters read them with plain loads, no swizzle.
+        if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k / 2, args.n, ctu::gemm::kBK / 2,
+                               ctu::gemm::kBN, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return rc;
+    } else {
+        if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, ctu::gemm::kBK,
+                               ctu::gemm::kBN, CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    }
+    constexpr int smem = kW4 ? ctu::gemm::kSmemBytesW4 : ctu::gemm::kSmemBytes;
+    constexpr int threads = kW4 ? ctu::gemm::kThreadsW4 : ctu::gemm::kThreads;
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
     std::call_once(once, [] {
-        attr_status = cudaFuncSetAttribute(ctu::gemm::w8a8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           ctu::gemm::kSmemBytes);
+        attr_status = cudaFuncSetAttribute(ctu::gemm::int8_gemm_kernel<kW4>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     CTU_CUDA(attr_status);
     const int64_t tiles = ((args.m + ctu::gemm::kBM - 1) / ctu::gemm::kBM) *
                           static_cast<int64_t>((args.n + ctu::gemm::kBN - 1) / ctu::gemm::kBN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
-    ctu::gemm::w8a8_gemm_kernel<<<grid, ctu::gemm::kThreads, ctu::gemm::kSmemBytes, stream>>>(map_a, map_b, args);
+    ctu::gemm::int8_gemm_kernel<kW4><<<grid, threads, smem, stream>>>(map_a, map_b, args);
     CTU_CUDA(cudaGetLastError());
     return CTU_OK;
+}
+
+int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms, cudaStream_t stream,
+                bool w4 = false) {
+    return w4 ? launch_gemm_t<true>(a, w, args, num_sms, stream) : launch_gemm_t<false>(a, w, args, num_sms, stream);
 }
 
 int check_gemm_shapes(const int8_t *a, const int8_t *w, const void *out, int64_t m, int64_t n, int64_t k) {
@@ -361,6 +378,39 @@ int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_int8_linear(a, w, a_scale, w_scale, w_scale_count, bias, out, m, n, k, dev.err, q,
                            static_cast<cudaStream_t>(stream));
+}
+
+int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    void *stream) {
+    if (m < 0 || n < 0 || k < 0) return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions must be non-negative");
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions exceed the kernel range");
+    if (k % 32 != 0 || n % 8 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "W4A8 linear requires K%%32=0 and N%%8=0 (got K=%lld, N=%lld)",
+                    static_cast<long long>(k), static_cast<long long>(n));
+    if (m == 0 || n == 0) return CTU_OK;
+    if (k == 0) return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
+    if (!a || !w_packed || !out || !a_scale || !w_scale) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(a) || !aligned16(w_packed) || !aligned16(out))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "activation, weight and output must be 16-byte aligned");
+    if (w_scale_count != 1 && w_scale_count != n)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output channel");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    ctu::gemm::GemmArgs args{};
+    args.a_scale = a_scale;
+    args.w_scale = w_scale;
+    args.bias = bias;
+    args.out = out;
+    args.err = dev.err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.w_scale_count = static_cast<int>(w_scale_count);
+    args.out_mode = ctu::gemm::kOutBf16;
+    return launch_gemm(a, w_packed, args, dev.num_sms, static_cast<cudaStream_t>(stream), true);
 }
 
 int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,

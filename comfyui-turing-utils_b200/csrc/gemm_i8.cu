@@ -1,23 +1,29 @@
-// W8A8 integer GEMM on the 5th-generation tensor cores (tcgen05, kind::i8) with
-// the ConvRot dequant + bias epilogue fused:
+// Integer GEMMs on the 5th-generation tensor cores (tcgen05, kind::i8) with the
+// ConvRot dequant + bias epilogue fused:
 //
 //   out[m, n] = bf16( ((float(acc[m, n]) * a_scale[m]) * w_scale[n]) + bias[n] )
 //   acc[m, n] = sum_k a[m, k] * w[n, k]          (exact int32)
 //
-// This replaces the reference's CUTLASS SM75 mma.sync GEMM
-// (kernel/csrc/turing/w4a8.cu:376-618, entry w4a8.cu:1185-1219) and keeps its
-// epilogue order (w4a8.cu:474-525: scale by the activation scale, then the
-// weight scale, then add the bias, round to bf16).
+// W8A8 (kW4 = false) replaces the reference's CUTLASS SM75 mma.sync GEMM
+// (kernel/csrc/turing/w4a8.cu:376-618, entry w4a8.cu:1185-1219); W4A8 (kW4 = true)
+// replaces its signed packed-int4 variant (w4a8.cu:34-72, 1000-1086): weights hold
+// two signed 4-bit values per byte, the even k in the low nibble.  Both keep the
+// reference's epilogue order (w4a8.cu:474-525: activation scale, weight scale, bias,
+// round to bf16).
 //
-// Design (one CTA per SM, persistent over output tiles):
-//   warp 0      TMA producer: A [128 x 128 B] and B [256 x 128 B] tiles, 128-byte
-//               swizzle, into a kStages-deep shared-memory ring (mbarrier per stage)
-//   warp 1      MMA issuer: owns the TMEM allocation (512 columns = two 128x256
-//               int32 accumulators), issues tcgen05.mma M=128 N=256 K=32, frees
-//               smem stages with tcgen05.commit
+// Design (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0      TMA producer: A [128 x 128 B] (128-byte swizzle) and the weight tile
+//               (W8: [256 x 128 B] swizzled; W4: packed [256 x 64 B]) into a
+//               kStages-deep shared-memory ring (mbarrier per stage)
+//   warp 1      MMA issuer: owns the TMEM allocation (512 columns = two 128x256 int32
+//               accumulators), issues tcgen05.mma M=128 N=256 K=32, frees ring stages
+//               with tcgen05.commit
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused scale/bias/bf16,
 //               16-byte global stores; releases the accumulator buffer so the next
 //               tile's MMAs overlap this tile's epilogue
+//   warps 6..9  (W4 only) converters: sign-extend each packed weight tile into a
+//               double-buffered int8 tile in the same 128-byte-swizzled layout the
+//               MMA reads, then fence the generic writes for the async proxy
 // Tiles are visited n-fastest so the CTAs resident at one time share the same A
 // rows and the whole weight matrix stays L2-resident.
 #include <cuda.h>
@@ -37,15 +43,26 @@ struct Smem {
     uint64_t empty[kStages];
     uint64_t acc_full[2];
     uint64_t acc_empty[2];
+    uint64_t bu_full[2];   // W4: converted weight tile ready
+    uint64_t bu_empty[2];  // W4: converted weight tile consumed by the MMA
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
+    int conv_ok;
     float col_scale[kBN];
     float col_bias[kBN];
 };
 
-__device__ __forceinline__ void named_barrier_epilogue() {
-    asm volatile("bar.sync 1, %0;" ::"n"(kEpilogueThreads) : "memory");
+template <bool kW4>
+struct Layout {
+    static constexpr int kBStageBytes = kW4 ? kBPackedBytes : kBBytes;  // weight bytes per ring stage
+    static constexpr int kRingBytes = kStages * (kABytes + kBStageBytes);
+    static constexpr int kConvBytes = kW4 ? 2 * kBBytes : 0;             // W4: two unpacked tiles
+    static constexpr int kSmemStructOffset = kRingBytes + kConvBytes;
+};
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 __device__ __forceinline__ void store_chunk_bf16(__nv_bfloat16 *dst, const uint32_t (&acc)[32], float a_s,
@@ -79,14 +96,36 @@ __device__ __forceinline__ void store_chunk_s32(int32_t *dst, const uint32_t (&a
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+// Eight signed 4-bit values (one packed word, even k in each byte's low nibble) to
+// eight int8 values in k order.  A nibble's sign is bit 3 of its byte position;
+// prmt's sign-replicate selectors (8..b) turn each byte's top bit into 0x00/0xff.
+__device__ __forceinline__ uint2 unpack_s4x8(uint32_t w) {
+    const uint32_t zero = 0;
+    uint32_t se, so, lo, hi;
+    // Sign masks: odd nibbles' signs are the bytes' top bits; even nibbles' signs are
+    // bit 3 of each byte, moved to the top by a 4-bit shift.
+    asm("prmt.b32 %0, %1, %2, 0xBA98;" : "=r"(so) : "r"(w), "r"(zero));
+    asm("prmt.b32 %0, %1, %2, 0xBA98;" : "=r"(se) : "r"(w << 4), "r"(zero));
+    // (nibble & 0x0f) | (sign & 0xf0) per byte.
+    const uint32_t even = (w & 0x0F0F0F0Fu) | (se & 0xF0F0F0F0u);
+    const uint32_t odd = ((w >> 4) & 0x0F0F0F0Fu) | (so & 0xF0F0F0F0u);
+    // Interleave to k order: (e0, o0, e1, o1) and (e2, o2, e3, o3).
+    asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(lo) : "r"(even), "r"(odd));
+    asm("prmt.b32 %0, %1, %2, 0x7362;" : "=r"(hi) : "r"(even), "r"(odd));
+    return make_uint2(lo, hi);
+}
+
+template <bool kW4>
+__global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
+    int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const GemmArgs args) {
+    using L = Layout<kW4>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
-    uint8_t *sB = smem + kStages * kABytes;
-    Smem &S = *reinterpret_cast<Smem *>(sB + kStages * kBBytes);
+    uint8_t *sB = smem + kStages * kABytes;                 // ring weight tiles (packed for W4)
+    uint8_t *sBu = smem + L::kRingBytes;                    // W4: unpacked weight tiles
+    Smem &S = *reinterpret_cast<Smem *>(smem + L::kSmemStructOffset);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -98,14 +137,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&S.full[s], 1);
-            mbar_init(&S.empty[s], 1);
+            // W4: a stage is free once the MMA consumed A and the converters the packed B.
+            mbar_init(&S.empty[s], kW4 ? 2 : 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
             mbar_init(&S.acc_empty[b], kEpilogueWarps);
+            mbar_init(&S.bu_full[b], 1);
+            mbar_init(&S.bu_empty[b], 1);
         }
         mbar_init(&S.drain, 1);
         S.abort_flag = 0;
+        S.conv_ok = 1;
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -137,9 +180,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&S.full[s], kABytes + kBBytes);
+                    mbar_arrive_expect_tx(&S.full[s], kABytes + L::kBStageBytes);
                     tma_load_2d(sA + s * kABytes, &tmap_a, kb * kBK, m0, &S.full[s]);
-                    tma_load_2d(sB + s * kBBytes, &tmap_b, kb * kBK, n0, &S.full[s]);
+                    tma_load_2d(sB + s * L::kBStageBytes, &tmap_b, kb * (kW4 ? kBK / 2 : kBK), n0, &S.full[s]);
                     ++fills;
                     if (++s == kStages) {
                         s = 0;
@@ -162,6 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             constexpr uint32_t idesc = idesc_i8(kBM, kBN);
             int s = 0;
             uint32_t ph = 0;
+            uint32_t conv = 0;  // W4: converted tiles consumed so far
             int local = 0;
             bool ok = true;
             if (args.inject_timeout) {
@@ -184,15 +228,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
+                    const int bb = conv & 1;
+                    if (kW4 && !mbar_wait(&S.bu_full[bb], (conv >> 1) & 1u, abort_flag, args.err, kErrTimeoutFull)) {
+                        ok = false;
+                        break;
+                    }
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(sA + s * kABytes);
-                    const uint32_t b_addr = smem_u32(sB + s * kBBytes);
+                    const uint32_t b_addr = kW4 ? smem_u32(sBu + bb * kBBytes) : smem_u32(sB + s * kBBytes);
 #pragma unroll
                     for (int k = 0; k < kBK / kUmmaK; ++k) {
                         mma_i8(d_tmem, smem_desc_sw128(a_addr + k * kUmmaK), smem_desc_sw128(b_addr + k * kUmmaK),
                                idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     mma_commit(&S.empty[s]);
+                    if (kW4) {
+                        mma_commit(&S.bu_empty[bb]);
+                        ++conv;
+                    }
                     if (++s == kStages) {
                         s = 0;
                         ph ^= 1u;
@@ -205,7 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mma_commit(&S.drain);
             mbar_wait(&S.drain, 0u, nullptr, args.err, kErrTimeoutDrain);
         }
-    } else {
+    } else if (warp < 2 + kEpilogueWarps) {
         // ------------------------------------------------------------------ epilogue
         // Every epilogue warp runs the same number of named barriers per tile even
         // after an abort, so a failed wait can never strand a warp at bar.sync.
@@ -219,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int m0 = (t / num_n) * kBM;
             const int n0 = (t % num_n) * kBN;
             // Stage this tile's column scales and bias (previous tile's readers are done).
-            named_barrier_epilogue();
+            named_barrier(1, kEpilogueThreads);
             if (args.out_mode == kOutBf16) {
                 for (int c = ethread; c < kBN; c += kEpilogueThreads) {
                     const int n = n0 + c;
@@ -228,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     S.col_bias[c] = (in && args.bias != nullptr) ? args.bias[n] : 0.0f;
                 }
             }
-            named_barrier_epilogue();
+            named_barrier(1, kEpilogueThreads);
             if (alive) {
                 int ok = 1;
                 if (lane == 0) ok = mbar_wait(&S.acc_full[ab], aph, abort_flag, args.err, kErrTimeoutAccum) ? 1 : 0;
@@ -263,6 +316,62 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.acc_empty[ab]);
         }
+    } else if (kW4) {
+        // ------------------------------------------------------------------ W4 converters
+        // 128 threads turn the packed tile of ring stage s ([256 rows x 64 B], k-pairs
+        // per byte) into int8 tile bb ([256 rows x 128 B], 128-byte swizzle).  Thread q
+        // handles 16-byte packed chunks q, q+128, ...: row = chunk / 4, chunk % 4 -> k
+        // bytes [32 c, 32 c + 32) = swizzled 16-byte chunks 2c and 2c+1 of the row.
+        // Consecutive threads read consecutive 16-byte chunks and write distinct bank
+        // groups.  One leader waits on the barriers; the decision is shared through the
+        // converters' named barrier so all 128 threads always take the same path.
+        const int cthread = threadIdx.x - (2 + kEpilogueWarps) * 32;
+        int s = 0;
+        uint32_t ph = 0;
+        uint32_t conv = 0;
+        bool alive = true;
+        for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+            for (int kb = 0; kb < nk; ++kb) {
+                const int bb = conv & 1;
+                if (cthread == 0) {
+                    bool ok = alive && mbar_wait(&S.full[s], ph, abort_flag, args.err, kErrTimeoutFull);
+                    ok = ok && mbar_wait(&S.bu_empty[bb], ((conv >> 1) & 1u) ^ 1u, abort_flag, args.err,
+                                         kErrTimeoutEmpty);
+                    S.conv_ok = ok ? 1 : 0;
+                }
+                named_barrier(2, kConverterThreads);
+                alive = S.conv_ok != 0;
+                if (alive) {
+                    const uint8_t *src = sB + s * kBPackedBytes;
+                    uint8_t *dst = sBu + bb * kBBytes;
+#pragma unroll
+                    for (int i = 0; i < kBN * 4 / kConverterThreads; ++i) {
+                        const int q = i * kConverterThreads + cthread;
+                        const int row = q >> 2;
+                        const int c = q & 3;
+                        const uint4 p = *reinterpret_cast<const uint4 *>(src + row * 64 + c * 16);
+                        const uint2 w0 = unpack_s4x8(p.x), w1 = unpack_s4x8(p.y);
+                        const uint2 w2 = unpack_s4x8(p.z), w3 = unpack_s4x8(p.w);
+                        const uint32_t r7 = static_cast<uint32_t>(row & 7);
+                        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c) ^ r7) << 4)) =
+                            make_uint4(w0.x, w0.y, w1.x, w1.y);
+                        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c + 1) ^ r7) << 4)) =
+                            make_uint4(w2.x, w2.y, w3.x, w3.y);
+                    }
+                    fence_proxy_async_smem();  // generic writes -> visible to the MMA (async proxy)
+                }
+                named_barrier(2, kConverterThreads);
+                if (cthread == 0 && alive) {
+                    mbar_arrive(&S.bu_full[bb]);
+                    mbar_arrive(&S.empty[s]);  // packed stage consumed
+                }
+                ++conv;
+                if (++s == kStages) {
+                    s = 0;
+                    ph ^= 1u;
+                }
+            }
+        }
     }
 
     tc_fence_before();
@@ -272,6 +381,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_dealloc(tmem_base, kTmemCols);
     }
 }
+
+template __global__ void int8_gemm_kernel<false>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                                 const GemmArgs);
+template __global__ void int8_gemm_kernel<true>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
+                                                const GemmArgs);
 
 }  // namespace gemm
 }  // namespace ctu

@@ -16,11 +16,15 @@ constexpr int kUmmaK = 32;     // K per tcgen05.mma kind::i8
 constexpr int kStages = 4;     // shared-memory ring depth
 constexpr int kABytes = kBM * kBK;
 constexpr int kBBytes = kBN * kBK;
+constexpr int kBPackedBytes = kBN * kBK / 2;  // W4: two signed 4-bit weights per byte
 constexpr int kTmemCols = 512; // two 256-column int32 accumulators
 constexpr int kEpilogueWarps = 4;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
+constexpr int kConverterThreads = 128;  // W4: warps that sign-extend packed weight tiles
 constexpr int kThreads = 64 + kEpilogueThreads;
+constexpr int kThreadsW4 = kThreads + kConverterThreads;
 constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes) + 4096;
+constexpr int kSmemBytesW4 = 1024 + kStages * (kABytes + kBPackedBytes) + 2 * kBBytes + 4096;
 
 enum OutMode : int { kOutBf16 = 0, kOutS32 = 1 };
 
@@ -38,7 +42,9 @@ struct GemmArgs {
     unsigned long long inject_timeout_ns;
 };
 
-__global__ void w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+// kW4 = false: w int8 [n, k]; kW4 = true: w packed signed int4 [n, k/2].
+template <bool kW4>
+__global__ void int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                                  const GemmArgs args);
 
 }  // namespace gemm

@@ -80,6 +80,19 @@ CTU_API int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_sca
                     void *stream);
 
 /*
+ * W4A8 linear: as ctu_int8_linear, with signed 4-bit weights packed two per byte,
+ *   w_packed int8 [n, k/2], byte j of a row = k 2j (low nibble) and 2j+1 (high nibble),
+ *   each nibble two's-complement in [-8, 7].  The packed tile is sign-extended to int8
+ *   in shared memory ahead of the int8 tensor-core MMA.
+ * Requires k % 32 == 0, n % 8 == 0, a/w_packed/out 16-byte aligned.
+ * Replaces turing_utils::w4a8_linear (ops.py:8-35; bindings.cpp:167-260;
+ * kernel/csrc/turing/w4a8.cu:1000-1086 with TuringW4ToS8 w4a8.cu:34-72).
+ */
+CTU_API int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                            int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                            void *stream);
+
+/*
  * Raw W8A8 contraction to int32: acc[m, n] (row stride ldc elements) = sum_k a[m,k] * w[n,k].
  * Same alignment rules as ctu_int8_linear; ldc % 4 == 0.
  * Replaces the int32 GEMM the reference takes from comfy-kitchen's cuBLAS binding

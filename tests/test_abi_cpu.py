@@ -47,7 +47,7 @@ def test_reference_c_module_attribute_names():
     # Names probed by the plugin through kernel_extension_has_symbol (kernel_api.py:26-37).
     from comfyui_turing_utils_kernel import _C
 
-    for name in ("turing_int8_linear", "turing_dequantize_int8_bf16", "turing_bf16_int8_convrot_quantize",
+    for name in ("turing_int8_linear", "turing_w4a8_linear", "turing_dequantize_int8_bf16", "turing_bf16_int8_convrot_quantize",
                  "turing_bf16_int4_convrot_quantize", "turing_bf16_gelu_int8_convrot_quantize",
                  "turing_bf16_gelu_int4_convrot_quantize", "turing_swiglu_int8_convrot_quantize",
                  "turing_swiglu_int4_convrot_quantize", "turing_gelu_int8_convrot_quantize",

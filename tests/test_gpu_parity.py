@@ -154,6 +154,44 @@ def test_int8_linear_matches_reference_golden(C, key):
     assert np.array_equal(got, ref)
 
 
+@pytest.mark.parametrize("key", GEMM_KEYS)
+def test_w4a8_linear_matches_reference_golden(C, key):
+    a = torch.from_numpy(GEMM[f"{key}__a"]).cuda()
+    w4 = torch.from_numpy(GEMM[f"{key}__w4_packed"]).cuda()
+    a_s = torch.from_numpy(GEMM[f"{key}__a_scale"]).cuda()
+    w_s = torch.from_numpy(GEMM[f"{key}__w_scale"]).cuda()
+    bias = torch.from_numpy(GEMM[f"{key}__bias"]).cuda() if f"{key}__bias" in GEMM.files else None
+    out = C.turing_w4a8_linear(a, w4, a_s, w_s, bias)
+    torch.cuda.synchronize()
+    got, ref = bf16_bits(out), GEMM[f"{key}__w4a8_linear"]
+    assert ulp_diff(got, ref).max() <= 1
+    assert np.array_equal(got, ref)
+
+
+# kernel/scripts/validate_compatible.py:158-201 edge cases (N and K tails, long M),
+# plus full-width tiles; compared with the oracle (signed int4 unpack + exact GEMM).
+@pytest.mark.parametrize("m,n,k", [(7, 13, 64), (3, 16, 12), (1, 8, 16), (17, 72, 80), (33, 128, 128),
+                                   (129, 264, 256), (513, 520, 508), (513, 520, 64), (8193, 8, 16),
+                                   (300, 512, 1536), (1024, 768, 5120)])
+def test_w4a8_linear_matches_oracle(C, m, n, k):
+    idx = [7, 3, 1, 17, 33, 129, 513, 5130, 8193, 300, 1024].index(m if (m, k) != (513, 64) else 5130)
+    g = torch.Generator().manual_seed(4300 + idx)
+    a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
+    w = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.02 + 0.001
+    w_s = torch.rand((n,), generator=g) * 0.03 + 0.001
+    bias = torch.randn((n,), generator=g) * 0.1 if idx % 2 == 0 else None
+    packed = oracle.pack_int4(w.numpy())
+    out = C.turing_w4a8_linear(a.cuda(), torch.from_numpy(packed).cuda(), a_s.cuda(), w_s.cuda(),
+                               None if bias is None else bias.cuda())
+    torch.cuda.synchronize()
+    ref = oracle.w4a8_linear(a.numpy(), packed, a_s.numpy(), w_s.numpy(), None if bias is None else bias.numpy())
+    got = bf16_bits(out)
+    assert got.shape == (m, n)
+    assert ulp_diff(got, ref).max() <= 1
+    assert np.array_equal(got, ref)
+
+
 @pytest.mark.parametrize("m,n,k", [(1, 8, 16), (7, 16, 64), (33, 72, 128), (127, 264, 144), (129, 256, 512),
                                    (300, 520, 1040), (513, 1024, 5120), (256, 13824 // 54 * 2, 1536)])
 def test_int8_gemm_s32_bit_exact(C, m, n, k):
