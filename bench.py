@@ -235,6 +235,41 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     gemm_tops = sum(o for _, _, o in gemm_ev) / (sum(gemm_ms) * 1e-3) / 1e12
     quant_gbs = sum(o for _, _, o in quant_ev) / (sum(quant_ms) * 1e-3) / 1e9
 
+    # ---------------------------------------------------------------- W4A8 / W4A4 at the same shapes
+    variants = {}
+    if not args.skip_variants:
+        from comfyui_turing_utils_kernel import _C as cabi
+
+        packed = [(k, n, (w[:, 0::2].to(torch.int32) & 7 | ((w[:, 1::2].to(torch.int32) & 7) << 4)).to(torch.int8),
+                   w_s, b) for k, n, w, w_s, b in layers]
+
+        def w4_step(act_bits):
+            for k, n, wp, w_s, b in packed:
+                q, s = (kops.turing_bf16_int8_convrot_quantize if act_bits == 8
+                        else kops.turing_bf16_int4_convrot_quantize)(xs[k], 256)
+                if act_bits == 8:
+                    kops.turing_w4a8_linear(q, wp, s, w_s, b)
+                else:
+                    cabi.int4_linear(q, wp, s, w_s, b)
+
+        for name, bits in (("w4a8", 8), ("w4a4", 4)):
+            for _ in range(3):
+                w4_step(bits)
+            nsteps = max(5, min(args.steps, 50))
+            v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            v0.record(stream)
+            for _ in range(nsteps):
+                w4_step(bits)
+            v1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = v0.elapsed_time(v1) / nsteps
+            variants[name] = {"value": ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+                              "format": "signed int4 weights, per-channel scale" +
+                                        (", int8 activations" if bits == 8 else ", int4 ConvRot activations")}
+        if _lib.device_error(local_rank, clear=True):
+            raise RuntimeError("kernel bounded-wait flags raised during the W4 variants")
+
     # ---------------------------------------------------------------- end-to-end (host buffers)
     e2e_ms, h2d, d2h = float("nan"), 0, 0
     if not args.skip_e2e:
@@ -311,6 +346,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "path": "pinned host activations -> turing_utils ops -> pinned host outputs, one stream"},
         "gpu_launches": 2 * len(SHAPES) * args.steps,
+        "variants_same_shapes": variants or None,
         "cpu_baseline": cpu,
     }
     print(json.dumps(line), flush=True)
@@ -325,6 +361,7 @@ def main():
     ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per GPU")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host round trip")
+    ap.add_argument("--skip-variants", action="store_true", help="skip the W4A8/W4A4 timings")
     # profiles/w8a8_gemm_k5120_n5120_m16384.md: dram read+write of one 5120x5120 launch at
     # M=16384 (240.2 MB), scaled to M=32760 by rows processed.
     ap.add_argument("--gemm-traffic", type=float, default=240.16e6 * 32760 / 16384,

@@ -1,0 +1,156 @@
+"""Plugin-facing ConvRot linear entry points on B200, without comfy-kitchen.
+
+Mirrors the functions of the reference plugin's dispatcher that comfy-kitchen's
+registry and the model adapters call for the ConvRot quantized linear
+(comfyui_turing_utils/quantization/dispatch.py): same names, argument names and
+defaults, same flattening of leading dimensions and scale normalisation.  Where the
+reference delegates to comfy-kitchen (a configuration its fast path does not take:
+non-bf16 input, ConvRot off, group size other than 256, unknown fused activations)
+this module raises NotImplementedError instead, because kitchen is not part of the
+B200 build and there is no CPU or eager fallback.
+"""
+
+from __future__ import annotations
+
+import torch
+
+import comfyui_turing_utils_kernel as ops
+from comfyui_turing_utils_kernel import _C
+
+CONVROT_GROUP = 256
+_FUSED_ACTS = (None, "none", "swiglu", "gelu_tanh")
+
+
+def _require(condition: bool, what: str) -> None:
+    if not condition:
+        raise NotImplementedError(
+            f"{what}: the reference hands this case to comfy-kitchen, which the B200 build does not include")
+
+
+def _quantize_int8(x2d: torch.Tensor, group_size: int, input_act: str | None):
+    """dispatch.py:343-414 without kitchen: every width uses the fused kernel."""
+    if input_act not in _FUSED_ACTS:
+        raise ValueError(f"unsupported fused INT8 activation: {input_act!r}")
+    if input_act == "gelu_tanh":
+        return ops.turing_bf16_gelu_int8_convrot_quantize(x2d, group_size)
+    return ops.turing_bf16_int8_convrot_quantize(x2d, group_size, swiglu=input_act == "swiglu")
+
+
+def _quantize_int4(x2d: torch.Tensor, group_size: int, input_act: str | None):
+    """dispatch.py:468-556 without kitchen."""
+    if input_act not in _FUSED_ACTS:
+        raise ValueError(f"unsupported fused INT4 activation: {input_act!r}")
+    if input_act == "gelu_tanh":
+        return ops.turing_bf16_gelu_int4_convrot_quantize(x2d, group_size)
+    if input_act == "swiglu" and x2d.shape[1] % 2 != 0:
+        raise ValueError("SwiGLU input width must be even")
+    return ops.turing_bf16_int4_convrot_quantize(x2d, group_size, swiglu=input_act == "swiglu")
+
+
+def quantize_convrot_int8_activation(x: torch.Tensor, group_size: int = 256):
+    """dispatch.py:417-429: quantize a 2D bf16 activation once for reuse by several GEMMs."""
+    if x.ndim != 2:
+        raise ValueError("ConvRot W8 activation must be two-dimensional")
+    if x.dtype is not torch.bfloat16:
+        raise ValueError("ConvRot W8 activation must use BF16 storage")
+    if not x.is_cuda:
+        raise ValueError("ConvRot W8 activation must be on CUDA")
+    return _quantize_int8(x.contiguous(), int(group_size), None)
+
+
+def quantize_convrot_swiglu_activation(x: torch.Tensor, group_size: int = 256):
+    """dispatch.py:432-446: fused SwiGLU + ConvRot quantization of a [M, 2K] tile."""
+    if x.ndim != 2 or x.shape[1] % 2:
+        raise ValueError("SwiGLU ConvRot input must be 2D [M, 2K]")
+    if x.dtype is not torch.bfloat16:
+        raise ValueError("SwiGLU ConvRot input must use BF16 storage")
+    if not x.is_cuda:
+        raise ValueError("SwiGLU ConvRot input must be on CUDA")
+    return ops.turing_bf16_int8_convrot_quantize(x.contiguous(), int(group_size), swiglu=True)
+
+
+def _int8_gemm(qactivation, weight, activation_scale, weight_scale, bias, output_dtype):
+    """dispatch.py:616-720: normalise scales, then the fused tcgen05 GEMM (no int32
+    workspace at any size; the reference's cuBLAS/kitchen branches are not needed)."""
+    m, k = qactivation.shape
+    n = weight.shape[0]
+    activation_scale = activation_scale.to(device=qactivation.device, dtype=torch.float32).reshape(-1).contiguous()
+    weight_scale = weight_scale.to(device=qactivation.device, dtype=torch.float32).reshape(-1).contiguous()
+    if activation_scale.numel() != m:
+        raise ValueError(f"W8A8 activation scale must have {m} values, got {activation_scale.numel()}")
+    if weight_scale.numel() not in (1, n):
+        raise ValueError(f"W8A8 weight scale must be scalar or have {n} values, got {weight_scale.numel()}")
+    if weight_scale.numel() == 1:
+        weight_scale = weight_scale.expand(n).contiguous()
+    if bias is not None:
+        bias = bias.to(device=qactivation.device, dtype=torch.float32)
+    output = ops.turing_int8_linear(qactivation, weight, activation_scale, weight_scale, bias)
+    return output if output_dtype == torch.bfloat16 else output.to(output_dtype)
+
+
+def int8_linear_from_quantized(
+    qactivation: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> torch.Tensor:
+    """dispatch.py:723-745: W8 GEMM from an activation quantized once by the caller."""
+    if qactivation.ndim != 2 or weight.ndim != 2:
+        raise ValueError("quantized W8 linear expects two-dimensional tensors")
+    if qactivation.dtype is not torch.int8 or weight.dtype is not torch.int8:
+        raise ValueError("quantized W8 linear expects INT8 activation and weight")
+    if qactivation.shape[1] != weight.shape[1]:
+        raise ValueError("quantized W8 activation and weight widths differ")
+    return _int8_gemm(qactivation, weight.contiguous(), activation_scale, weight_scale, bias, out_dtype)
+
+
+def int8_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    out_dtype: torch.dtype | None = None,
+    convrot: bool = False,
+    convrot_groupsize: int = 256,
+    input_act: str | None = None,
+) -> torch.Tensor:
+    """dispatch.py:748-800: ConvRot W8A8 linear over [..., K] bf16 activations."""
+    _require(x.dtype == torch.bfloat16, "non-bf16 activations")
+    _require(bool(convrot), "INT8 linear without ConvRot")
+    _require(convrot_groupsize == CONVROT_GROUP, f"ConvRot group size {convrot_groupsize}")
+    _require(input_act in _FUSED_ACTS, f"input activation {input_act!r}")
+    original_shape = x.shape
+    x2d = x.reshape(-1, original_shape[-1]).contiguous()
+    qactivation, activation_scale = _quantize_int8(x2d, convrot_groupsize, input_act)
+    output = _int8_gemm(qactivation, weight.contiguous(), activation_scale, weight_scale, bias,
+                        out_dtype or x.dtype)
+    return output.reshape(*original_shape[:-1], weight.shape[0])
+
+
+def convrot_w4a4_linear(
+    x: torch.Tensor,
+    qweight: torch.Tensor,
+    wscales: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    convrot_groupsize: int = 256,
+    quant_group_size: int = 64,
+    linear_dtype: str = "int4",
+    input_act: str | None = None,
+) -> torch.Tensor:
+    """dispatch.py:876-936: W4 weights with int8 (W4A8) or int4 (W4A4) activations."""
+    _require(linear_dtype in {"int4", "int8"}, f"linear_dtype {linear_dtype!r}")
+    _require(convrot_groupsize == CONVROT_GROUP, f"ConvRot group size {convrot_groupsize}")
+    _require(quant_group_size == 64, f"quant_group_size {quant_group_size}")
+    _require(x.dtype == torch.bfloat16, "non-bf16 activations")
+    _require(input_act in _FUSED_ACTS, f"input activation {input_act!r}")
+    original_shape = x.shape
+    x2d = x.reshape(-1, original_shape[-1]).contiguous()
+    if linear_dtype == "int8":
+        qactivation, activation_scale = _quantize_int8(x2d, convrot_groupsize, input_act)
+        output = ops.turing_w4a8_linear(qactivation, qweight, activation_scale, wscales, bias)
+    else:
+        qactivation, activation_scale = _quantize_int4(x2d, convrot_groupsize, input_act)
+        output = _C.int4_linear(qactivation, qweight.contiguous(), activation_scale, wscales, bias, out_dtype=x.dtype)
+    return output.reshape(*original_shape[:-1], qweight.shape[0])

@@ -254,6 +254,56 @@ def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, out
 
 
 # ----------------------------------------------------------------------------- B200 extras
+def int4_linear(qactivation, qweight, activation_scale, wscales, bias=None, out_dtype=torch.bfloat16):
+    """W4A4 GEMM: packed signed-int4 ConvRot codes [M, K/2] x packed signed-int4 weights
+    [N, K/2], per-token activation scale, per-channel weight scale (the 1-D ``wscales``
+    the plugin registry requires, dispatch.py:1031-1034), optional bias; same fused
+    epilogue as int8_linear.  Stands in for comfy-kitchen's ``int4_linear`` that
+    ``convrot_w4a4_linear(linear_dtype="int4")`` calls (dispatch.py:927-934)."""
+    qactivation = qactivation.contiguous()
+    qweight = qweight.contiguous()
+    activation_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
+    wscales = wscales.reshape(-1).to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.float32).contiguous()
+    _check_cuda_2d(qactivation, "activation")
+    _check_cuda_2d(qweight, "weight")
+    if qactivation.dtype != torch.int8 or qweight.dtype != torch.int8:
+        raise RuntimeError("W4A4 activation and weight must use packed int8 storage")
+    dev = qactivation.device
+    m, kp = qactivation.shape
+    n = qweight.shape[0]
+    k = 2 * kp
+    if qweight.shape[1] != kp:
+        raise RuntimeError("W4A4 packed K dimensions must match")
+    if activation_scale.numel() != m:
+        raise RuntimeError("activation_scale must contain one value per row")
+    if wscales.numel() not in (1, n):
+        raise RuntimeError("wscales must be scalar or contain one value per output channel")
+    if bias is not None and bias.numel() != n:
+        raise RuntimeError("bias must contain one value per output channel")
+    k_pad = -(-k // 32) * 32
+    n_pad = -(-n // 8) * 8
+    if k_pad != k:
+        qactivation = torch.nn.functional.pad(qactivation, (0, (k_pad - k) // 2))
+        qweight = torch.nn.functional.pad(qweight, (0, (k_pad - k) // 2))
+    if wscales.numel() == 1:
+        wscales = wscales.expand(n).contiguous()
+    if n_pad != n:
+        qweight = torch.nn.functional.pad(qweight, (0, 0, 0, n_pad - n))
+        wscales = torch.nn.functional.pad(wscales, (0, n_pad - n))
+        if bias is not None:
+            bias = torch.nn.functional.pad(bias, (0, n_pad - n))
+    out = torch.empty((m, n_pad), dtype=torch.bfloat16, device=dev)
+    if m > 0 and n > 0:
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().ctu_w4a4_linear(
+                _ptr(_aligned(qactivation)), _ptr(_aligned(qweight)), _ptr(activation_scale), _ptr(wscales), n_pad,
+                _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+    out = out if n_pad == n else out[:, :n].contiguous()
+    return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
+
+
 def int8_gemm_s32(activation, weight, out=None):
     """Exact int32 accumulators ``activation @ weight.T`` (no epilogue)."""
     _check_cuda_2d(activation, "activation")

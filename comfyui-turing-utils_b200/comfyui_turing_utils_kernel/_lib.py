@@ -33,6 +33,7 @@ SIGNATURES = {
     "ctu_convrot_quantize": (_i32, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
     "ctu_int8_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_w4a8_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ctu_w4a4_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int8_gemm_s32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ctu_dequantize_int8_bf16": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
     "ctu_debug_gemm_injected_timeout": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _u64, _vp]),

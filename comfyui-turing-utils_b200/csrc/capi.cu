@@ -193,43 +193,53 @@ int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const 
 }
 
 // ---------------------------------------------------------------------------- GEMM launch
-template <bool kW4>
+template <int kMode>
 int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms,
                   cudaStream_t stream) {
+    using ctu::gemm::kBK;
+    using ctu::gemm::kBM;
+    using ctu::gemm::kBN;
+    constexpr bool a_packed = kMode == ctu::gemm::kModeW4A4;
+    constexpr bool w_packed = kMode != ctu::gemm::kModeW8A8;
+    // Packed int4 tiles are read by the converter warps with plain loads (no swizzle);
+    // int8 tiles feed the MMA directly (128-byte swizzle).
     CUtensorMap map_a, map_b;
-    if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, args.k, args.m, ctu::gemm::kBK,
-                           ctu::gemm::kBM, CU_TENSOR_MAP_SWIZZLE_128B))
+    if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, a_packed ? args.k / 2 : args.k, args.m,
+                           a_packed ? kBK / 2 : kBK, kBM,
+                           a_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
-    if (kW4) {
-        // Packed weights [n, k/2]: the converters read them with plain loads, no swizzle.
-        if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k / 2, args.n, ctu::gemm::kBK / 2,
-                               ctu::gemm::kBN, CU_TENSOR_MAP_SWIZZLE_NONE))
-            return rc;
-    } else {
-        if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, ctu::gemm::kBK,
-                               ctu::gemm::kBN, CU_TENSOR_MAP_SWIZZLE_128B))
-            return rc;
-    }
-    constexpr int smem = kW4 ? ctu::gemm::kSmemBytesW4 : ctu::gemm::kSmemBytes;
-    constexpr int threads = kW4 ? ctu::gemm::kThreadsW4 : ctu::gemm::kThreads;
+    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, w_packed ? args.k / 2 : args.k, args.n,
+                           w_packed ? kBK / 2 : kBK, kBN,
+                           w_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    constexpr int smem = kMode == ctu::gemm::kModeW8A8   ? ctu::gemm::kSmemBytes
+                         : kMode == ctu::gemm::kModeW4A8 ? ctu::gemm::kSmemBytesW4
+                                                         : ctu::gemm::kSmemBytesW4A4;
+    constexpr int threads = kMode == ctu::gemm::kModeW8A8 ? ctu::gemm::kThreads : ctu::gemm::kThreadsW4;
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
     std::call_once(once, [] {
-        attr_status = cudaFuncSetAttribute(ctu::gemm::int8_gemm_kernel<kW4>,
+        attr_status = cudaFuncSetAttribute(ctu::gemm::int8_gemm_kernel<kMode>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     CTU_CUDA(attr_status);
-    const int64_t tiles = ((args.m + ctu::gemm::kBM - 1) / ctu::gemm::kBM) *
-                          static_cast<int64_t>((args.n + ctu::gemm::kBN - 1) / ctu::gemm::kBN);
+    const int64_t tiles = ((args.m + kBM - 1) / kBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
     const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
-    ctu::gemm::int8_gemm_kernel<kW4><<<grid, threads, smem, stream>>>(map_a, map_b, args);
+    ctu::gemm::int8_gemm_kernel<kMode><<<grid, threads, smem, stream>>>(map_a, map_b, args);
     CTU_CUDA(cudaGetLastError());
     return CTU_OK;
 }
 
 int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms, cudaStream_t stream,
-                bool w4 = false) {
-    return w4 ? launch_gemm_t<true>(a, w, args, num_sms, stream) : launch_gemm_t<false>(a, w, args, num_sms, stream);
+                int mode = ctu::gemm::kModeW8A8) {
+    switch (mode) {
+    case ctu::gemm::kModeW4A8:
+        return launch_gemm_t<ctu::gemm::kModeW4A8>(a, w, args, num_sms, stream);
+    case ctu::gemm::kModeW4A4:
+        return launch_gemm_t<ctu::gemm::kModeW4A4>(a, w, args, num_sms, stream);
+    default:
+        return launch_gemm_t<ctu::gemm::kModeW8A8>(a, w, args, num_sms, stream);
+    }
 }
 
 int check_gemm_shapes(const int8_t *a, const int8_t *w, const void *out, int64_t m, int64_t n, int64_t k) {
@@ -380,14 +390,15 @@ int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
                            static_cast<cudaStream_t>(stream));
 }
 
-int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
-                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
-                    void *stream) {
+static int int4_linear(int mode, const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                       int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                       void *stream) {
+    const char *name = mode == ctu::gemm::kModeW4A4 ? "W4A4" : "W4A8";
     if (m < 0 || n < 0 || k < 0) return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions must be non-negative");
     if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
         return fail(CTU_ERR_INVALID_ARGUMENT, "GEMM dimensions exceed the kernel range");
     if (k % 32 != 0 || n % 8 != 0)
-        return fail(CTU_ERR_INVALID_ARGUMENT, "W4A8 linear requires K%%32=0 and N%%8=0 (got K=%lld, N=%lld)",
+        return fail(CTU_ERR_INVALID_ARGUMENT, "%s linear requires K%%32=0 and N%%8=0 (got K=%lld, N=%lld)", name,
                     static_cast<long long>(k), static_cast<long long>(n));
     if (m == 0 || n == 0) return CTU_OK;
     if (k == 0) return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
@@ -410,7 +421,21 @@ int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scal
     args.ldc = static_cast<int>(n);
     args.w_scale_count = static_cast<int>(w_scale_count);
     args.out_mode = ctu::gemm::kOutBf16;
-    return launch_gemm(a, w_packed, args, dev.num_sms, static_cast<cudaStream_t>(stream), true);
+    return launch_gemm(a, w_packed, args, dev.num_sms, static_cast<cudaStream_t>(stream), mode);
+}
+
+int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    void *stream) {
+    return int4_linear(ctu::gemm::kModeW4A8, a, w_packed, a_scale, w_scale, w_scale_count, bias, out, m, n, k,
+                       stream);
+}
+
+int ctu_w4a4_linear(const int8_t *a_packed, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                    int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                    void *stream) {
+    return int4_linear(ctu::gemm::kModeW4A4, a_packed, w_packed, a_scale, w_scale, w_scale_count, bias, out, m, n,
+                       k, stream);
 }
 
 int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,

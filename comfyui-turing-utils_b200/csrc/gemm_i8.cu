@@ -4,10 +4,11 @@
 //   out[m, n] = bf16( ((float(acc[m, n]) * a_scale[m]) * w_scale[n]) + bias[n] )
 //   acc[m, n] = sum_k a[m, k] * w[n, k]          (exact int32)
 //
-// W8A8 (kW4 = false) replaces the reference's CUTLASS SM75 mma.sync GEMM
-// (kernel/csrc/turing/w4a8.cu:376-618, entry w4a8.cu:1185-1219); W4A8 (kW4 = true)
+// W8A8 (kModeW8A8) replaces the reference's CUTLASS SM75 mma.sync GEMM
+// (kernel/csrc/turing/w4a8.cu:376-618, entry w4a8.cu:1185-1219); W4A8 (kModeW4A8)
 // replaces its signed packed-int4 variant (w4a8.cu:34-72, 1000-1086): weights hold
-// two signed 4-bit values per byte, the even k in the low nibble.  Both keep the
+// two signed 4-bit values per byte, the even k in the low nibble.  W4A4 (kModeW4A4)
+// packs the activations the same way (the int4 ConvRot codes).  All keep the
 // reference's epilogue order (w4a8.cu:474-525: activation scale, weight scale, bias,
 // round to bf16).
 //
@@ -21,7 +22,7 @@
 //   warps 2..5  epilogue: tcgen05.ld 32 columns at a time, fused scale/bias/bf16,
 //               16-byte global stores; releases the accumulator buffer so the next
 //               tile's MMAs overlap this tile's epilogue
-//   warps 6..9  (W4 only) converters: sign-extend each packed weight tile into a
+//   warps 6..9  (int4 modes) converters: sign-extend each packed tile into a
 //               double-buffered int8 tile in the same 128-byte-swizzled layout the
 //               MMA reads, then fence the generic writes for the async proxy
 // Tiles are visited n-fastest so the CTAs resident at one time share the same A
@@ -53,12 +54,18 @@ struct Smem {
     float col_bias[kBN];
 };
 
-template <bool kW4>
+template <int kMode>
 struct Layout {
-    static constexpr int kBStageBytes = kW4 ? kBPackedBytes : kBBytes;  // weight bytes per ring stage
-    static constexpr int kRingBytes = kStages * (kABytes + kBStageBytes);
-    static constexpr int kConvBytes = kW4 ? 2 * kBBytes : 0;             // W4: two unpacked tiles
-    static constexpr int kSmemStructOffset = kRingBytes + kConvBytes;
+    static constexpr bool kAPacked = kMode == kModeW4A4;
+    static constexpr bool kBPacked = kMode != kModeW8A8;
+    static constexpr bool kConvert = kAPacked || kBPacked;
+    static constexpr int kAStageBytes = kAPacked ? kAPackedBytes : kABytes;  // activation bytes per ring stage
+    static constexpr int kBStageBytes = kBPacked ? kBPackedBytes : kBBytes;  // weight bytes per ring stage
+    static constexpr int kRingBytes = kStages * (kAStageBytes + kBStageBytes);
+    // Converted (int8, 128-byte swizzled) tiles, double-buffered: A first, then B.
+    static constexpr int kConvABytes = kAPacked ? 2 * kABytes : 0;
+    static constexpr int kConvBBytes = kBPacked ? 2 * kBBytes : 0;
+    static constexpr int kSmemStructOffset = kRingBytes + kConvABytes + kConvBBytes;
 };
 
 __device__ __forceinline__ void named_barrier(int id, int threads) {
@@ -115,16 +122,39 @@ __device__ __forceinline__ uint2 unpack_s4x8(uint32_t w) {
     return make_uint2(lo, hi);
 }
 
-template <bool kW4>
-__global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
+// Sign-extend `kRows` x 64 packed bytes (ring stage `src`) into `kRows` x 128 int8
+// bytes laid out as a 128-byte-swizzled TMA tile (`dst`).  Thread q of the 128
+// converters takes 16-byte packed chunks q, q+128, ...: row = chunk / 4, chunk % 4 ->
+// k bytes [32c, 32c + 32) = swizzled 16-byte chunks 2c and 2c+1 of the row.
+// Consecutive threads read consecutive 16-byte chunks and write distinct bank groups.
+template <int kRows>
+__device__ __forceinline__ void convert_tile(const uint8_t *src, uint8_t *dst, int cthread) {
+#pragma unroll
+    for (int i = 0; i < kRows * 4 / kConverterThreads; ++i) {
+        const int q = i * kConverterThreads + cthread;
+        const int row = q >> 2;
+        const int c = q & 3;
+        const uint4 p = *reinterpret_cast<const uint4 *>(src + row * 64 + c * 16);
+        const uint2 w0 = unpack_s4x8(p.x), w1 = unpack_s4x8(p.y);
+        const uint2 w2 = unpack_s4x8(p.z), w3 = unpack_s4x8(p.w);
+        const uint32_t r7 = static_cast<uint32_t>(row & 7);
+        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c) ^ r7) << 4)) = make_uint4(w0.x, w0.y, w1.x, w1.y);
+        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c + 1) ^ r7) << 4)) = make_uint4(w2.x, w2.y, w3.x, w3.y);
+    }
+}
+
+template <int kMode>
+__global__ void __launch_bounds__(kMode == kModeW8A8 ? kThreads : kThreadsW4, 1)
     int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const GemmArgs args) {
-    using L = Layout<kW4>;
+    using L = Layout<kMode>;
+    constexpr bool kConvert = L::kConvert;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *sA = smem;
-    uint8_t *sB = smem + kStages * kABytes;                 // ring weight tiles (packed for W4)
-    uint8_t *sBu = smem + L::kRingBytes;                    // W4: unpacked weight tiles
+    uint8_t *sA = smem;                                     // ring activation tiles (packed for W4A4)
+    uint8_t *sB = smem + kStages * L::kAStageBytes;         // ring weight tiles (packed for W4A8/W4A4)
+    uint8_t *sAu = smem + L::kRingBytes;                    // converted activation tiles
+    uint8_t *sBu = sAu + L::kConvABytes;                    // converted weight tiles
     Smem &S = *reinterpret_cast<Smem *>(smem + L::kSmemStructOffset);
 
     const int warp = threadIdx.x >> 5;
@@ -137,8 +167,8 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&S.full[s], 1);
-            // W4: a stage is free once the MMA consumed A and the converters the packed B.
-            mbar_init(&S.empty[s], kW4 ? 2 : 1);
+            // With converters a stage is free once both the MMA and the converters are done.
+            mbar_init(&S.empty[s], kConvert ? 2 : 1);
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&S.acc_full[b], 1);
@@ -180,9 +210,9 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&S.full[s], kABytes + L::kBStageBytes);
-                    tma_load_2d(sA + s * kABytes, &tmap_a, kb * kBK, m0, &S.full[s]);
-                    tma_load_2d(sB + s * L::kBStageBytes, &tmap_b, kb * (kW4 ? kBK / 2 : kBK), n0, &S.full[s]);
+                    mbar_arrive_expect_tx(&S.full[s], L::kAStageBytes + L::kBStageBytes);
+                    tma_load_2d(sA + s * L::kAStageBytes, &tmap_a, kb * (L::kAPacked ? kBK / 2 : kBK), m0, &S.full[s]);
+                    tma_load_2d(sB + s * L::kBStageBytes, &tmap_b, kb * (L::kBPacked ? kBK / 2 : kBK), n0, &S.full[s]);
                     ++fills;
                     if (++s == kStages) {
                         s = 0;
@@ -205,7 +235,7 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
             constexpr uint32_t idesc = idesc_i8(kBM, kBN);
             int s = 0;
             uint32_t ph = 0;
-            uint32_t conv = 0;  // W4: converted tiles consumed so far
+            uint32_t conv = 0;  // converted tiles consumed so far
             int local = 0;
             bool ok = true;
             if (args.inject_timeout) {
@@ -229,20 +259,20 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
                         break;
                     }
                     const int bb = conv & 1;
-                    if (kW4 && !mbar_wait(&S.bu_full[bb], (conv >> 1) & 1u, abort_flag, args.err, kErrTimeoutFull)) {
+                    if (kConvert && !mbar_wait(&S.bu_full[bb], (conv >> 1) & 1u, abort_flag, args.err, kErrTimeoutFull)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + s * kABytes);
-                    const uint32_t b_addr = kW4 ? smem_u32(sBu + bb * kBBytes) : smem_u32(sB + s * kBBytes);
+                    const uint32_t a_addr = L::kAPacked ? smem_u32(sAu + bb * kABytes) : smem_u32(sA + s * kABytes);
+                    const uint32_t b_addr = L::kBPacked ? smem_u32(sBu + bb * kBBytes) : smem_u32(sB + s * kBBytes);
 #pragma unroll
                     for (int k = 0; k < kBK / kUmmaK; ++k) {
                         mma_i8(d_tmem, smem_desc_sw128(a_addr + k * kUmmaK), smem_desc_sw128(b_addr + k * kUmmaK),
                                idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     mma_commit(&S.empty[s]);
-                    if (kW4) {
+                    if (kConvert) {
                         mma_commit(&S.bu_empty[bb]);
                         ++conv;
                     }
@@ -316,15 +346,12 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.acc_empty[ab]);
         }
-    } else if (kW4) {
-        // ------------------------------------------------------------------ W4 converters
-        // 128 threads turn the packed tile of ring stage s ([256 rows x 64 B], k-pairs
-        // per byte) into int8 tile bb ([256 rows x 128 B], 128-byte swizzle).  Thread q
-        // handles 16-byte packed chunks q, q+128, ...: row = chunk / 4, chunk % 4 -> k
-        // bytes [32 c, 32 c + 32) = swizzled 16-byte chunks 2c and 2c+1 of the row.
-        // Consecutive threads read consecutive 16-byte chunks and write distinct bank
-        // groups.  One leader waits on the barriers; the decision is shared through the
-        // converters' named barrier so all 128 threads always take the same path.
+    } else if (kConvert) {
+        // ------------------------------------------------------------------ int4 converters
+        // 128 threads turn the packed tiles of ring stage s (k pairs per byte) into the
+        // int8 tiles of buffer bb.  One leader waits on the barriers; the decision is
+        // shared through the converters' named barrier so all 128 threads always take
+        // the same path.
         const int cthread = threadIdx.x - (2 + kEpilogueWarps) * 32;
         int s = 0;
         uint32_t ph = 0;
@@ -342,22 +369,8 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
                 named_barrier(2, kConverterThreads);
                 alive = S.conv_ok != 0;
                 if (alive) {
-                    const uint8_t *src = sB + s * kBPackedBytes;
-                    uint8_t *dst = sBu + bb * kBBytes;
-#pragma unroll
-                    for (int i = 0; i < kBN * 4 / kConverterThreads; ++i) {
-                        const int q = i * kConverterThreads + cthread;
-                        const int row = q >> 2;
-                        const int c = q & 3;
-                        const uint4 p = *reinterpret_cast<const uint4 *>(src + row * 64 + c * 16);
-                        const uint2 w0 = unpack_s4x8(p.x), w1 = unpack_s4x8(p.y);
-                        const uint2 w2 = unpack_s4x8(p.z), w3 = unpack_s4x8(p.w);
-                        const uint32_t r7 = static_cast<uint32_t>(row & 7);
-                        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c) ^ r7) << 4)) =
-                            make_uint4(w0.x, w0.y, w1.x, w1.y);
-                        *reinterpret_cast<uint4 *>(dst + row * 128 + (((2 * c + 1) ^ r7) << 4)) =
-                            make_uint4(w2.x, w2.y, w3.x, w3.y);
-                    }
+                    if (L::kAPacked) convert_tile<kBM>(sA + s * kAPackedBytes, sAu + bb * kABytes, cthread);
+                    if (L::kBPacked) convert_tile<kBN>(sB + s * kBPackedBytes, sBu + bb * kBBytes, cthread);
                     fence_proxy_async_smem();  // generic writes -> visible to the MMA (async proxy)
                 }
                 named_barrier(2, kConverterThreads);
@@ -382,10 +395,12 @@ __global__ void __launch_bounds__(kW4 ? kThreadsW4 : kThreads, 1)
     }
 }
 
-template __global__ void int8_gemm_kernel<false>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                                 const GemmArgs);
-template __global__ void int8_gemm_kernel<true>(const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap,
-                                                const GemmArgs);
+template __global__ void int8_gemm_kernel<kModeW8A8>(const __grid_constant__ CUtensorMap,
+                                                     const __grid_constant__ CUtensorMap, const GemmArgs);
+template __global__ void int8_gemm_kernel<kModeW4A8>(const __grid_constant__ CUtensorMap,
+                                                     const __grid_constant__ CUtensorMap, const GemmArgs);
+template __global__ void int8_gemm_kernel<kModeW4A4>(const __grid_constant__ CUtensorMap,
+                                                     const __grid_constant__ CUtensorMap, const GemmArgs);
 
 }  // namespace gemm
 }  // namespace ctu

@@ -16,15 +16,21 @@ constexpr int kUmmaK = 32;     // K per tcgen05.mma kind::i8
 constexpr int kStages = 4;     // shared-memory ring depth
 constexpr int kABytes = kBM * kBK;
 constexpr int kBBytes = kBN * kBK;
+constexpr int kAPackedBytes = kBM * kBK / 2;  // W4A4: two signed 4-bit activations per byte
 constexpr int kBPackedBytes = kBN * kBK / 2;  // W4: two signed 4-bit weights per byte
 constexpr int kTmemCols = 512; // two 256-column int32 accumulators
 constexpr int kEpilogueWarps = 4;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
-constexpr int kConverterThreads = 128;  // W4: warps that sign-extend packed weight tiles
+constexpr int kConverterThreads = 128;  // int4 modes: warps that sign-extend packed tiles
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kThreadsW4 = kThreads + kConverterThreads;
 constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes) + 4096;
 constexpr int kSmemBytesW4 = 1024 + kStages * (kABytes + kBPackedBytes) + 2 * kBBytes + 4096;
+constexpr int kSmemBytesW4A4 = 1024 + kStages * (kAPackedBytes + kBPackedBytes) + 2 * (kABytes + kBBytes) + 4096;
+
+// Operand formats: int8 x int8, int8 activations x packed signed int4 weights, packed
+// signed int4 activations x packed signed int4 weights.
+enum Mode : int { kModeW8A8 = 0, kModeW4A8 = 1, kModeW4A4 = 2 };
 
 enum OutMode : int { kOutBf16 = 0, kOutS32 = 1 };
 
@@ -42,8 +48,9 @@ struct GemmArgs {
     unsigned long long inject_timeout_ns;
 };
 
-// kW4 = false: w int8 [n, k]; kW4 = true: w packed signed int4 [n, k/2].
-template <bool kW4>
+// kModeW8A8: a int8 [m, k], w int8 [n, k]; kModeW4A8: w packed signed int4 [n, k/2];
+// kModeW4A4: a and w packed signed int4 ([m, k/2], [n, k/2]).
+template <int kMode>
 __global__ void int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                                  const GemmArgs args);
 

@@ -93,6 +93,21 @@ CTU_API int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float
                             void *stream);
 
 /*
+ * W4A4 linear: both operands signed 4-bit, packed two per byte (even k in the low
+ * nibble): a_packed [m, k/2] (the int4 ConvRot codes of ctu_convrot_quantize(bits=4)),
+ * w_packed [n, k/2]; per-token activation scale [m], per-channel weight scale [n] or
+ * scalar, optional bias; same epilogue as ctu_int8_linear.  Both tiles are
+ * sign-extended to int8 in shared memory ahead of the int8 tensor-core MMA.
+ * Requires k % 32 == 0, n % 8 == 0, 16-byte aligned operands.
+ * Replaces the int4 GEMM the reference takes from comfy-kitchen for
+ * convrot_w4a4_linear(linear_dtype="int4") (comfyui_turing_utils/quantization/
+ * dispatch.py:916-934, kitchen int4_linear; third-party source, not in the reference).
+ */
+CTU_API int ctu_w4a4_linear(const int8_t *a_packed, const int8_t *w_packed, const float *a_scale, const float *w_scale,
+                            int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
+                            void *stream);
+
+/*
  * Raw W8A8 contraction to int32: acc[m, n] (row stride ldc elements) = sum_k a[m,k] * w[n,k].
  * Same alignment rules as ctu_int8_linear; ldc % 4 == 0.
  * Replaces the int32 GEMM the reference takes from comfy-kitchen's cuBLAS binding

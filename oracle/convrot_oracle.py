@@ -188,6 +188,14 @@ def w4a8_linear(a, w_packed, a_scale, w_scale, bias=None, fused=False):
     return epilogue(int8_gemm_s32(a, unpack_int4(w_packed)), a_scale, w_scale, bias, fused=fused)
 
 
+def w4a4_linear(a_packed, w_packed, a_scale, w_scale, bias=None, fused=False):
+    """W4A4: packed signed-int4 activation codes x packed signed-int4 weights, the same
+    epilogue.  The reference's int4 GEMM is comfy-kitchen's (source not available), so
+    this definition -- exact int32 contraction of the sign-extended values, then the
+    bundled kernels' epilogue -- is this build's, not a restatement (parity unpinned)."""
+    return epilogue(int8_gemm_s32(unpack_int4(a_packed), unpack_int4(w_packed)), a_scale, w_scale, bias, fused=fused)
+
+
 def convrot_w8a8_linear(x_bits, w, w_scale, bias=None, fused=False):
     """Whole path: ConvRot quantize, int32 GEMM, dequant+bias epilogue (bf16 bits)."""
     codes, scales = convrot_quantize(x_bits, 8)

@@ -286,3 +286,68 @@ def test_gemm_bounded_wait_reports_and_context_survives(C):
     torch.cuda.synchronize()
     assert torch.all(acc2 == 128)
     assert _lib.device_error(0, clear=True) == 0
+
+
+# ----------------------------------------------------------------------------- W4A4 and dispatch
+@pytest.mark.parametrize("m,n,k", [(1, 8, 32), (33, 72, 256), (130, 264, 1536), (513, 520, 5120), (7, 13, 64)])
+def test_w4a4_linear_matches_oracle(C, m, n, k):
+    g = torch.Generator().manual_seed(m * 3 + n + k)
+    a4 = torch.randint(-7, 8, (m, k), generator=g, dtype=torch.int8)
+    w4 = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.02 + 1e-3
+    w_s = torch.rand((n,), generator=g) * 0.03 + 1e-3
+    bias = torch.randn((n,), generator=g) * 0.05
+    ap, wp = oracle.pack_int4(a4.numpy()), oracle.pack_int4(w4.numpy())
+    out = C.int4_linear(torch.from_numpy(ap).cuda(), torch.from_numpy(wp).cuda(), a_s.cuda(), w_s.cuda(), bias.cuda())
+    torch.cuda.synchronize()
+    ref = oracle.w4a4_linear(ap, wp, a_s.numpy(), w_s.numpy(), bias.numpy())
+    got = bf16_bits(out)
+    assert ulp_diff(got, ref).max() <= 1
+    assert np.array_equal(got, ref)
+
+
+def _dispatch():
+    import comfyui_turing_utils_b200 as d
+
+    return d
+
+
+def test_dispatch_int8_linear_matches_oracle_3d(C):
+    d = _dispatch()
+    b, s, k, n = 2, 97, 1536, 264
+    x = activations(b * s, k, seed=31)
+    g = torch.Generator().manual_seed(32)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    w_s = torch.rand((n,), generator=g) * 0.009 + 1e-3
+    bias = torch.randn((n,), generator=g) * 0.02
+    out = d.int8_linear(x.reshape(b, s, k).cuda(), w.cuda(), w_s.cuda(), bias.cuda(), convrot=True)
+    torch.cuda.synchronize()
+    assert out.shape == (b, s, n) and out.dtype == torch.bfloat16
+    ref = oracle.convrot_w8a8_linear(bf16_bits(x), w.numpy(), w_s.numpy(), bias.numpy())
+    assert np.array_equal(bf16_bits(out.reshape(b * s, n)), ref)
+    # scalar weight scale is expanded like dispatch.py:629-648
+    out1 = d.int8_linear(x.cuda(), w.cuda(), torch.tensor([0.004]).cuda(), None, convrot=True)
+    ref1 = oracle.convrot_w8a8_linear(bf16_bits(x), w.numpy(), np.full((n,), 0.004, np.float32), None)
+    assert np.array_equal(bf16_bits(out1), ref1)
+
+
+@pytest.mark.parametrize("linear_dtype", ["int8", "int4"])
+def test_dispatch_convrot_w4a4_linear(C, linear_dtype):
+    d = _dispatch()
+    m, k, n = 65, 1024, 136
+    x = activations(m, k, seed=41)
+    g = torch.Generator().manual_seed(42)
+    w4 = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    wp = oracle.pack_int4(w4.numpy())
+    w_s = torch.rand((n,), generator=g) * 0.03 + 1e-3
+    bias = torch.randn((n,), generator=g) * 0.05
+    out = d.convrot_w4a4_linear(x.cuda(), torch.from_numpy(wp).cuda(), w_s.cuda(), bias.cuda(),
+                                linear_dtype=linear_dtype)
+    torch.cuda.synchronize()
+    bits = 8 if linear_dtype == "int8" else 4
+    codes, scales = oracle.convrot_quantize(bf16_bits(x), bits)
+    if bits == 8:
+        ref = oracle.w4a8_linear(codes, wp, scales, w_s.numpy(), bias.numpy())
+    else:
+        ref = oracle.w4a4_linear(codes, wp, scales, w_s.numpy(), bias.numpy())
+    assert np.array_equal(bf16_bits(out), ref)
