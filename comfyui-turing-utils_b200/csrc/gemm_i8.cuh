@@ -21,7 +21,7 @@ constexpr int kBPackedBytes = kBN * kBK / 2;  // W4: two signed 4-bit weights pe
 constexpr int kTmemCols = 512; // two 256-column int32 accumulators
 constexpr int kEpilogueWarps = 4;
 constexpr int kEpilogueThreads = kEpilogueWarps * 32;
-constexpr int kConverterThreads = 128;  // int4 modes: warps that sign-extend packed tiles
+constexpr int kConverterThreads = 256;  // int4 modes: 8 warps that sign-extend packed tiles
 constexpr int kThreads = 64 + kEpilogueThreads;
 constexpr int kThreadsW4 = kThreads + kConverterThreads;
 constexpr int kSmemBytes = 1024 + kStages * (kABytes + kBBytes) + 4096;
