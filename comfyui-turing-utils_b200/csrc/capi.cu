@@ -8,6 +8,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -193,14 +194,23 @@ int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const 
 }
 
 // ---------------------------------------------------------------------------- GEMM launch
-template <int kMode>
-int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms,
+// Which GEMM kernel runs: 0 chooses per problem, 1 forces the single-CTA kernel,
+// 2 forces the CTA-pair kernel (test hook ctu_debug_set_gemm_kernel).
+std::atomic<int> g_gemm_kernel{0};
+
+// Clusters of two CTAs that can be resident at once, per device and kernel variant.
+int g_pair_clusters[kMaxDevices][3] = {};
+
+template <int kMode, bool kPair>
+int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int device, int num_sms,
                   cudaStream_t stream) {
     using ctu::gemm::kBK;
     using ctu::gemm::kBM;
     using ctu::gemm::kBN;
     constexpr bool a_packed = kMode == ctu::gemm::kModeW4A4;
     constexpr bool w_packed = kMode != ctu::gemm::kModeW8A8;
+    // The pair kernel stages half of the weight tile in each CTA of the pair.
+    constexpr uint32_t w_box_rows = kPair ? ctu::gemm::kHalfBN : kBN;
     // Packed int4 tiles are read by the converter warps with plain loads (no swizzle);
     // int8 tiles feed the MMA directly (128-byte swizzle).
     CUtensorMap map_a, map_b;
@@ -209,36 +219,86 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
                            a_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
     if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, w_packed ? args.k / 2 : args.k, args.n,
-                           w_packed ? kBK / 2 : kBK, kBN,
+                           w_packed ? kBK / 2 : kBK, w_box_rows,
                            w_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
-    constexpr int smem = kMode == ctu::gemm::kModeW8A8   ? ctu::gemm::kSmemBytes
-                         : kMode == ctu::gemm::kModeW4A8 ? ctu::gemm::kSmemBytesW4
-                                                         : ctu::gemm::kSmemBytesW4A4;
-    constexpr int threads = kMode == ctu::gemm::kModeW8A8 ? ctu::gemm::kThreads : ctu::gemm::kThreadsW4;
+    using PL = ctu::gemm::PairLayout<kMode>;
+    constexpr int smem = kPair                                ? PL::kSmemBytes
+                         : kMode == ctu::gemm::kModeW8A8     ? ctu::gemm::kSmemBytes
+                         : kMode == ctu::gemm::kModeW4A8     ? ctu::gemm::kSmemBytesW4
+                                                             : ctu::gemm::kSmemBytesW4A4;
+    constexpr int threads = kPair ? PL::kThreadCount
+                                  : (kMode == ctu::gemm::kModeW8A8 ? ctu::gemm::kThreads : ctu::gemm::kThreadsW4);
+    constexpr auto kernel = kPair ? ctu::gemm::int8_gemm_pair_kernel<kMode> : ctu::gemm::int8_gemm_kernel<kMode>;
     static std::once_flag once;
     static cudaError_t attr_status = cudaSuccess;
     std::call_once(once, [] {
-        attr_status = cudaFuncSetAttribute(ctu::gemm::int8_gemm_kernel<kMode>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     CTU_CUDA(attr_status);
-    const int64_t tiles = ((args.m + kBM - 1) / kBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
-    const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
-    ctu::gemm::int8_gemm_kernel<kMode><<<grid, threads, smem, stream>>>(map_a, map_b, args);
-    CTU_CUDA(cudaGetLastError());
-    return CTU_OK;
+    if constexpr (!kPair) {
+        const int64_t tiles = ((args.m + kBM - 1) / kBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
+        const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
+        kernel<<<grid, threads, smem, stream>>>(map_a, map_b, args);
+        CTU_CUDA(cudaGetLastError());
+        return CTU_OK;
+    } else {
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg{};
+        cfg.blockDim = dim3(threads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        {
+            std::lock_guard<std::mutex> lock(g_mutex);
+            clusters = g_pair_clusters[device][kMode];
+        }
+        if (clusters == 0) {
+            cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+            CTU_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
+            if (clusters <= 0) return fail(CTU_ERR_UNSUPPORTED, "no CTA pair of the GEMM fits on device %d", device);
+            std::lock_guard<std::mutex> lock(g_mutex);
+            g_pair_clusters[device][kMode] = clusters;
+        }
+        const int64_t tiles =
+            ((args.m + ctu::gemm::kPairBM - 1) / ctu::gemm::kPairBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
+        cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, clusters)), 1, 1);
+        CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, args));
+        return CTU_OK;
+    }
 }
 
-int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int num_sms, cudaStream_t stream,
-                int mode = ctu::gemm::kModeW8A8) {
+// The pair kernel halves the shared-memory traffic of the weight tile per SM; below
+// one pair tile of rows it would leave half of every pair idle.
+bool use_pair_kernel(const ctu::gemm::GemmArgs &args) {
+    const int forced = g_gemm_kernel.load(std::memory_order_relaxed);
+    if (forced == 1) return false;
+    if (forced == 2) return true;
+    return args.m > ctu::gemm::kBM;
+}
+
+template <int kMode>
+int launch_gemm_mode(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int device, int num_sms,
+                     cudaStream_t stream) {
+    return use_pair_kernel(args) ? launch_gemm_t<kMode, true>(a, w, args, device, num_sms, stream)
+                                 : launch_gemm_t<kMode, false>(a, w, args, device, num_sms, stream);
+}
+
+int launch_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int device, int num_sms,
+                cudaStream_t stream, int mode = ctu::gemm::kModeW8A8) {
     switch (mode) {
     case ctu::gemm::kModeW4A8:
-        return launch_gemm_t<ctu::gemm::kModeW4A8>(a, w, args, num_sms, stream);
+        return launch_gemm_mode<ctu::gemm::kModeW4A8>(a, w, args, device, num_sms, stream);
     case ctu::gemm::kModeW4A4:
-        return launch_gemm_t<ctu::gemm::kModeW4A4>(a, w, args, num_sms, stream);
+        return launch_gemm_mode<ctu::gemm::kModeW4A4>(a, w, args, device, num_sms, stream);
     default:
-        return launch_gemm_t<ctu::gemm::kModeW8A8>(a, w, args, num_sms, stream);
+        return launch_gemm_mode<ctu::gemm::kModeW8A8>(a, w, args, device, num_sms, stream);
     }
 }
 
@@ -327,7 +387,7 @@ int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
     args.ldc = static_cast<int>(n);
     args.w_scale_count = static_cast<int>(w_scale_count);
     args.out_mode = ctu::gemm::kOutBf16;
-    return launch_gemm(a, w, args, q.num_sms, stream);
+    return launch_gemm(a, w, args, q.device, q.num_sms, stream);
 }
 
 }  // namespace host
@@ -421,7 +481,7 @@ static int int4_linear(int mode, const int8_t *a, const int8_t *w_packed, const 
     args.ldc = static_cast<int>(n);
     args.w_scale_count = static_cast<int>(w_scale_count);
     args.out_mode = ctu::gemm::kOutBf16;
-    return launch_gemm(a, w_packed, args, dev.num_sms, static_cast<cudaStream_t>(stream), mode);
+    return launch_gemm(a, w_packed, args, dev.device, dev.num_sms, static_cast<cudaStream_t>(stream), mode);
 }
 
 int ctu_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,
@@ -455,7 +515,7 @@ int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ld
     args.ldc = static_cast<int>(ldc);
     args.w_scale_count = 1;
     args.out_mode = ctu::gemm::kOutS32;
-    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+    return launch_gemm(a, w, args, dev.device, dev.num_sms, static_cast<cudaStream_t>(stream));
 }
 
 int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *acc, int64_t m, int64_t n, int64_t k,
@@ -477,7 +537,12 @@ int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *a
     args.out_mode = ctu::gemm::kOutS32;
     args.inject_timeout = 1;
     args.inject_timeout_ns = timeout_ns;
-    return launch_gemm(a, w, args, dev.num_sms, static_cast<cudaStream_t>(stream));
+    return launch_gemm(a, w, args, dev.device, dev.num_sms, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_debug_set_gemm_kernel(int which) {
+    if (which < 0 || which > 2) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1 or 2");
+    return g_gemm_kernel.exchange(which);
 }
 
 int ctu_dequantize_int8_bf16(const int32_t *acc, int64_t acc_stride, const float *a_scale, const float *w_scale,

@@ -54,5 +54,45 @@ template <int kMode>
 __global__ void int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                                  const GemmArgs args);
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant: a cluster of two CTAs computes a 256 x 256 output tile with one
+// tcgen05.mma.cta_group::2 (M = 256) per K step.  Each CTA stages its 128 activation
+// rows and half (128 rows) of the weight tile; the pair's tensor cores read both
+// halves of the weight tile, so every weight byte crosses shared memory once per
+// pair instead of once per CTA.
+constexpr int kPairBM = 2 * kBM;    // output rows per CTA pair
+constexpr int kHalfBN = kBN / 2;    // weight rows staged by each CTA of a pair
+
+template <int kMode>
+struct PairLayout {
+    static constexpr bool kAPacked = kMode == kModeW4A4;
+    static constexpr bool kBPacked = kMode != kModeW8A8;
+    static constexpr bool kConvert = kAPacked || kBPacked;
+    static constexpr int kAStageBytes = kAPacked ? kBM * kBK / 2 : kBM * kBK;          // TMA'd activation tile
+    static constexpr int kBStageBytes = kBPacked ? kHalfBN * kBK / 2 : kHalfBN * kBK;  // TMA'd weight half-tile
+    // int4 modes: every ring stage has its own sign-extended (int8, 128-byte swizzled)
+    // copies, so conversion runs as far ahead of the MMA as the TMA ring does.
+    static constexpr int kAuStageBytes = kAPacked ? kBM * kBK : 0;
+    static constexpr int kBuStageBytes = kBPacked ? kHalfBN * kBK : 0;
+    static constexpr int kStageBytes = kAStageBytes + kBStageBytes + kAuStageBytes + kBuStageBytes;
+    static constexpr int kStages = kMode == kModeW8A8 ? 6 : (kMode == kModeW4A8 ? 5 : 4);
+    static constexpr int kAOffset = 0;
+    static constexpr int kBOffset = kAOffset + kStages * kAStageBytes;
+    static constexpr int kAuOffset = kBOffset + kStages * kBStageBytes;
+    static constexpr int kBuOffset = kAuOffset + kStages * kAuStageBytes;
+    static constexpr int kStructOffset = kBuOffset + kStages * kBuStageBytes;
+    static constexpr int kSmemBytes = 1024 + kStructOffset + 4096;
+    // Converter warps: each owns one ring stage (W4A4: two per stage, one for the
+    // activation tile and one for the weight half-tile).
+    static constexpr int kConvWarpsPerStage = kAPacked ? 2 : 1;
+    static constexpr int kConvWarps = kConvert ? kStages * kConvWarpsPerStage : 0;
+    static constexpr int kThreadCount = kThreads + 32 * kConvWarps;
+    static_assert(kSmemBytes <= 232448, "CTA-pair GEMM exceeds the shared memory of one SM");
+};
+
+template <int kMode>
+__global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                      const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args);
+
 }  // namespace gemm
 }  // namespace ctu

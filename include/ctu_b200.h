@@ -151,6 +151,12 @@ CTU_API int ctu_convrot_w8a8_linear_static_scratch(const void *x, const int8_t *
 CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *acc, int64_t m, int64_t n, int64_t k,
                                     uint64_t timeout_ns, void *stream);
 
+/* Test hook (no counterpart in the reference): choose the integer GEMM kernel for
+ * every later call in this process.  0 = per problem (default: the CTA-pair kernel
+ * when M > 128), 1 = single-CTA kernel, 2 = CTA-pair kernel.  Returns the previous
+ * selector, or a negative error code. */
+CTU_API int ctu_debug_set_gemm_kernel(int which);
+
 #ifdef __cplusplus
 }
 #endif
