@@ -139,6 +139,7 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const 
 
 // ---------------------------------------------------------------------------- quantizer geometry
 struct QuantPlan {
+    bool reg;  // register-resident kernel (whole rows per batch, one lane pair per group)
     int rows_per_batch;
     int warps;
     int box_rows;
@@ -146,7 +147,41 @@ struct QuantPlan {
     size_t smem;
 };
 
+// Which ConvRot quantizer runs: 0 chooses per width, 1 forces the two-pass kernel,
+// 2 forces the register-resident kernel where the width allows it (test hook
+// ctu_debug_set_quant_kernel).
+std::atomic<int> g_quant_kernel{0};
+
+// Register-resident plan: W warps hold 16 W groups, i.e. floor(16 W / groups) whole
+// rows.  At 255 registers a thread, an SM holds floor(8 / W) such CTAs; the plan
+// maximises the share of the SM's 128 lane-pair slots that hold a group.
+bool plan_quant_reg(int64_t k, int act, int smem_optin, QuantPlan *plan) {
+    const int groups = static_cast<int>(k / 256);
+    if (groups > ctu::rot::kRegMaxGroups) return false;
+    double best = -1.0;
+    for (int w = 1; w <= ctu::rot::kRegMaxThreads / 32; ++w) {
+        const int b = 16 * w / groups;
+        if (b < 1) continue;
+        const int ctas = 8 / w;
+        const size_t smem = ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
+        if (smem > static_cast<size_t>(smem_optin) || smem * ctas > 228 * 1024) continue;
+        const double score = static_cast<double>(b * groups) / (16.0 * w) * (ctas * w) / 8.0;
+        if (score > best + 1e-9) {
+            best = score;
+            plan->rows_per_batch = b;
+            plan->warps = w;
+            plan->smem = smem;
+        }
+    }
+    if (best < 0.0) return false;
+    plan->reg = true;
+    ctu::rot::quant_copy_plan(plan->rows_per_batch, static_cast<int>(k), act, &plan->box_rows, &plan->copies);
+    return true;
+}
+
 int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
+    if (g_quant_kernel.load(std::memory_order_relaxed) != 1 && plan_quant_reg(k, act, smem_optin, plan)) return CTU_OK;
+    plan->reg = false;
     const int groups = static_cast<int>(k / 256);
     const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
     // Rows per batch: keep every lane pair busy (a warp owns 16 groups), at most 4
@@ -181,7 +216,7 @@ int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
 template <int Act, int Bits>
 int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan, int num_sms,
                  cudaStream_t stream) {
-    auto kernel = ctu::rot::convrot_quant_kernel<Act, Bits>;
+    auto kernel = plan.reg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits> : ctu::rot::convrot_quant_kernel<Act, Bits>;
     CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem)));
     int per_sm = 0;
     CTU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, plan.warps * 32, plan.smem));
@@ -538,6 +573,11 @@ int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *a
     args.inject_timeout = 1;
     args.inject_timeout_ns = timeout_ns;
     return launch_gemm(a, w, args, dev.device, dev.num_sms, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_debug_set_quant_kernel(int which) {
+    if (which < 0 || which > 2) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1 or 2");
+    return g_quant_kernel.exchange(which);
 }
 
 int ctu_debug_set_gemm_kernel(int which) {

@@ -35,93 +35,12 @@
 
 #include <cstdint>
 
+#include "convrot_math.cuh"
 #include "convrot_quant.cuh"
 #include "ptx.cuh"
 
 namespace ctu {
 namespace rot {
-
-constexpr float kBf16Max = 3.38953139e38f;
-
-// ---------------------------------------------------------------------------
-// Radix-4 butterfly on two independent 4-tuples at once (packed f32x2), with the
-// reference's association: y0 = ((x0+x1)+x2)-x3, y1 = ((x0+x1)-x2)+x3,
-// y2 = ((x0-x1)+x2)+x3, y3 = ((-x0+x1)+x2)+x3, each times 0.5.
-__device__ __forceinline__ void butterfly2(f32x2 &x0, f32x2 &x1, f32x2 &x2, f32x2 &x3, f32x2 half) {
-    const f32x2 t = fadd2(x0, x1);
-    const f32x2 b = fsub2(x0, x1);  // x0 - x1;  (-x0 + x1) == -(x0 - x1) exactly
-    const f32x2 y0 = fmul2(half, fsub2(fadd2(t, x2), x3));
-    const f32x2 y1 = fmul2(half, fadd2(fsub2(t, x2), x3));
-    const f32x2 y2 = fmul2(half, fadd2(fadd2(b, x2), x3));
-    const f32x2 y3 = fmul2(half, fadd2(fsub2(x2, b), x3));  // (-b) + x2 == x2 - b exactly
-    x0 = y0;
-    x1 = y1;
-    x2 = y2;
-    x3 = y3;
-}
-
-// Physical shared-memory byte offset of 16-byte chunk `c` of 128-byte slice `r`
-// as written by a TMA load with CU_TENSOR_MAP_SWIZZLE_128B.
-__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
-
-template <int Act>
-__device__ __forceinline__ float activate(uint32_t gate_bits, uint32_t up_bits);
-
-template <>
-__device__ __forceinline__ float activate<kActNone>(uint32_t x, uint32_t) {
-    return __uint_as_float(x);
-}
-
-// convrot_quant.cu:163-169
-template <>
-__device__ __forceinline__ float activate<kActSwiGLU>(uint32_t gate_bits, uint32_t up_bits) {
-    const float gate = __uint_as_float(gate_bits);
-    const float up = __uint_as_float(up_bits);
-    return (gate / (1.0f + expf(-gate))) * up;
-}
-
-// convrot_quant.cu:171-182 (tanh-GELU, result rounded back to bf16)
-template <>
-__device__ __forceinline__ float activate<kActGelu>(uint32_t x_bits, uint32_t) {
-    const float x = __uint_as_float(x_bits);
-    constexpr float kAlpha = 0.7978845608028654f;
-    constexpr float kBeta = 0.044715f;
-    const float activated = 0.5f * x * (1.0f + tanhf(kAlpha * (x + kBeta * x * x * x)));
-    return __bfloat162float(__float2bfloat16_rn(activated));
-}
-
-// Load one lane's 128 inputs of a group: chunk0 = elements h*64+[0,64) (bit 7 = 0),
-// chunk1 = 128+h*64+[0,64).  `row64` is the 128-byte slice index of chunk0 inside the
-// batch buffer; chunk1 sits two slices later.  For SwiGLU the `up` half of the row
-// starts `up_off` slices after the gate.  v[j] = (chunk0[j], chunk1[j]).
-template <int Act>
-__device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&v)[64]) {
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const uint4 a = *reinterpret_cast<const uint4 *>(buf + sw128(row64, c));
-        const uint4 b = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + 2, c));
-        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
-        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
-        if constexpr (Act == kActSwiGLU) {
-            const uint4 ua = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + up_off, c));
-            const uint4 ub = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + up_off + 2, c));
-            const uint32_t uaw[4] = {ua.x, ua.y, ua.z, ua.w};
-            const uint32_t ubw[4] = {ub.x, ub.y, ub.z, ub.w};
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, uaw[q] << 16), activate<Act>(bw[q] << 16, ubw[q] << 16));
-                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, uaw[q] & 0xFFFF0000u),
-                                           activate<Act>(bw[q] & 0xFFFF0000u, ubw[q] & 0xFFFF0000u));
-            }
-        } else {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, 0), activate<Act>(bw[q] << 16, 0));
-                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, 0), activate<Act>(bw[q] & 0xFFFF0000u, 0));
-            }
-        }
-    }
-}
 
 // Rotate the group held by this lane pair, return this lane's absmax (NaN ignored)
 // and a NaN probe, and write bf16(y) back in place.  All 32 lanes of the warp must
@@ -204,61 +123,6 @@ __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint3
     unpk2(probe, p0, p1);
     absmax = active ? m : 0.0f;
     nan_probe = active ? __fadd_rn(p0, p1) : 0.0f;
-}
-
-// Quantize 8 consecutive bf16(y) values of one row to int8 with the fast chain.
-__device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    int c[8];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float lo, hi;
-        unpk2(fmul2(pk2(bf16lo(ww[i]), bf16hi(ww[i])), rcp2), lo, hi);
-        const uint32_t qb = pack_bf16x2(lo, hi);
-        c[2 * i] = __float2int_rn(bf16lo(qb));
-        c[2 * i + 1] = __float2int_rn(bf16hi(qb));
-    }
-    // cvt.pack.sat.s8.s32.b32 d, a, b, c: d = {sat8(b), sat8(a), c[0:16)} from the low byte up.
-    uint32_t t0, t1, lo, hi;
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(t0) : "r"(c[3]), "r"(c[2]), "r"(0u));
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(lo) : "r"(c[1]), "r"(c[0]), "r"(t0));
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(t1) : "r"(c[7]), "r"(c[6]), "r"(0u));
-    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(hi) : "r"(c[5]), "r"(c[4]), "r"(t1));
-    return make_uint2(lo, hi);
-}
-
-// Exact reference chain including NaN (fmaxf(-128, NaN) == -128) for rows that
-// contain NaN or infinities.
-__device__ __noinline__ uint2 quant8_int8_exact(uint4 w, float rounded_scale) {
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    uint32_t out[2] = {0, 0};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float y = (i & 1) ? bf16hi(ww[i >> 1]) : bf16lo(ww[i >> 1]);
-        const float divided = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(y, rounded_scale)));
-        float qf = nearbyintf(divided);
-        qf = fminf(127.0f, fmaxf(-128.0f, qf));
-        const uint32_t byte = static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu;
-        out[i >> 2] |= byte << (8 * (i & 3));
-    }
-    return make_uint2(out[0], out[1]);
-}
-
-// Quantize 8 consecutive bf16(y) values to packed int4 (exact for every input).
-__device__ __forceinline__ uint32_t quant8_int4(uint4 w, f32x2 inv2) {
-    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    uint32_t out = 0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        float plo, phi;
-        unpk2(fmul2(pk2(bf16lo(ww[i]), bf16hi(ww[i])), inv2), plo, phi);
-        const float lo = fminf(7.0f, fmaxf(-7.0f, plo));
-        const float hi = fminf(7.0f, fmaxf(-7.0f, phi));
-        const uint32_t lb = static_cast<uint32_t>(__float2int_rn(lo)) & 0xFu;
-        const uint32_t hb = static_cast<uint32_t>(__float2int_rn(hi)) & 0xFu;
-        out |= (lb | (hb << 4)) << (8 * i);
-    }
-    return out;
 }
 
 template <int Act, int Bits>

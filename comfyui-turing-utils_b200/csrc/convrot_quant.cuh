@@ -48,5 +48,23 @@ inline size_t quant_smem_bytes(int rows, int k, int act, int bits) {
 template <int Act, int Bits>
 __global__ void convrot_quant_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
+// Register-resident variant: one lane pair per 256-column group and whole rows per
+// batch, so a row may have at most kRegMaxGroups groups (a CTA of at most
+// kRegMaxThreads threads).
+constexpr int kRegMaxThreads = 256;
+constexpr int kRegMaxGroups = kRegMaxThreads / 2;
+
+// Dynamic shared memory of the register-resident variant for a batch of `rows` rows:
+// one input buffer, two slots of per-row absmax and NaN flags, one mbarrier.
+inline size_t quant_reg_smem_bytes(int rows, int k, int act) {
+    int box = 0, copies = 0;
+    quant_copy_plan(rows, k, act, &box, &copies);
+    const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
+    return 1024 + in_bytes + 16 * static_cast<size_t>(rows) + 8;
+}
+
+template <int Act, int Bits>
+__global__ void convrot_quant_reg_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
+
 }  // namespace rot
 }  // namespace ctu

@@ -157,6 +157,12 @@ CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, in
  * selector, or a negative error code. */
 CTU_API int ctu_debug_set_gemm_kernel(int which);
 
+/* Test hook (no counterpart in the reference): choose the ConvRot quantizer for every
+ * later call in this process.  0 = per width (default: the register-resident kernel
+ * when K <= 32768), 1 = two-pass kernel, 2 = register-resident kernel wherever the
+ * width allows it.  Returns the previous selector, or a negative error code. */
+CTU_API int ctu_debug_set_quant_kernel(int which);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,163 @@
+"""Both ConvRot quantizer kernels -- two-pass (bf16(y) back to shared memory, then a
+quantize pass) and register-resident (whole rows per batch, codes from registers) --
+against the reference's golden vectors and the oracle.
+
+By default the library uses the register-resident kernel for K <= 32768;
+``ctu_debug_set_quant_kernel`` forces one kernel so both are checked on every case.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import convrot_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+from pathlib import Path
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+QUANT = np.load(GOLDEN / "convrot_quant.npz")
+QUANT_NAMES = sorted({k.split("__")[0] for k in QUANT.files})
+KERNELS = {"two_pass": 1, "register": 2}
+
+
+@pytest.fixture(scope="module")
+def C():
+    from comfyui_turing_utils_kernel import _C, _lib
+
+    _lib.device_error(0, clear=True)
+    yield _C
+    assert _lib.device_error(0, clear=True) == 0, "a kernel recorded a bounded-wait timeout"
+
+
+@pytest.fixture(params=list(KERNELS))
+def kernel(request):
+    from comfyui_turing_utils_kernel import _lib
+
+    prev = _lib.load().ctu_debug_set_quant_kernel(KERNELS[request.param])
+    assert prev >= 0
+    yield request.param
+    _lib.load().ctu_debug_set_quant_kernel(0)
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def to_bf16_tensor(bits: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(bits).view(np.int16)).view(torch.bfloat16)
+
+
+def activations(rows, width, seed, outlier_scale=30.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn((rows, width), generator=g)
+    idx = torch.randperm(width, generator=g)[: max(1, width // 100)]
+    x[:, idx] *= outlier_scale
+    return x.to(torch.bfloat16)
+
+
+def run_quant(C, x_bits, bits, mode="plain"):
+    x = to_bf16_tensor(x_bits).cuda()
+    if mode == "gelu":
+        fn = C.turing_bf16_gelu_int8_convrot_quantize if bits == 8 else C.turing_bf16_gelu_int4_convrot_quantize
+        codes, scales = fn(x, 256)
+    else:
+        fn = C.turing_bf16_int8_convrot_quantize if bits == 8 else C.turing_bf16_int4_convrot_quantize
+        codes, scales = fn(x, 256, mode == "swiglu")
+    torch.cuda.synchronize()
+    return codes.cpu().numpy(), scales.cpu().numpy().reshape(-1)
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("name", QUANT_NAMES)
+def test_golden(C, kernel, name, bits):
+    mode = "swiglu" if "swiglu" in name else ("gelu" if name.startswith("gelu") else "plain")
+    codes, scales = run_quant(C, QUANT[f"{name}__x"], bits, mode)
+    assert np.array_equal(codes, QUANT[f"{name}__int{bits}_codes"])
+    assert np.array_equal(scales.view(np.uint32), QUANT[f"{name}__int{bits}_scales"].view(np.uint32))
+
+
+# Widths on both sides of every batch plan (one row per batch at 54 groups, several
+# rows at 6 or 20 groups, the register kernel's 128-group limit) and row counts that
+# leave partial last batches.
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(1, 256), (3, 512), (17, 1536), (33, 5120), (5, 13824), (130, 768),
+                                    (7, 2560), (64, 1024), (2, 16384), (3, 32768), (2, 33024), (61, 4096),
+                                    (257, 3072), (1000, 5120)])
+def test_oracle(C, kernel, rows, k, bits):
+    x = activations(rows, k, seed=rows * 131 + k)
+    xb = bf16_bits(x)
+    codes, scales = run_quant(C, xb, bits)
+    ref_codes, ref_scales = oracle.convrot_quantize(xb, bits)
+    assert np.array_equal(codes, ref_codes)
+    assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
+
+
+def special_rows(rows, k, seed):
+    """bf16 rows mixing NaN, +-inf, subnormals, +-0, the largest finite values and
+    ordinary activations, one kind of trouble per row and some rows clean."""
+    rng = np.random.default_rng(seed)
+    x = bf16_bits(activations(rows, k, seed))
+    specials = [0x7FC0, 0xFFC0, 0x7F80, 0xFF80, 0x0001, 0x8001, 0x007F, 0x0000, 0x8000, 0x7F7F, 0xFF7F]
+    for r in range(rows):
+        kind = r % 6
+        cols = rng.choice(k, size=max(1, k // 64), replace=False)
+        if kind == 0:
+            x[r, cols] = rng.choice(specials, size=cols.size)
+        elif kind == 1:
+            x[r, cols] = 0x7F7F  # many maxima: sums overflow to inf
+        elif kind == 2:
+            x[r, :] = rng.choice([0x0001, 0x8001, 0x0003, 0x0000], size=k)  # all subnormal
+        elif kind == 3:
+            x[r, cols[:1]] = 0x7FC0  # a single NaN
+        elif kind == 4:
+            x[r, cols[:2]] = [0x7F80, 0xFF80]  # +inf and -inf: NaN after the rotation
+    return x
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(12, 512), (18, 5120), (7, 13824)])
+def test_special_values(C, kernel, rows, k, bits):
+    xb = special_rows(rows, k, seed=rows + k)
+    codes, scales = run_quant(C, xb, bits)
+    ref_codes, ref_scales = oracle.convrot_quantize(xb, bits)
+    assert np.array_equal(codes, ref_codes)
+    assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("mode", ["swiglu", "gelu"])
+def test_fused_activations_against_each_other(C, mode, bits):
+    # The two kernels share the activation code: their outputs must be identical.
+    from comfyui_turing_utils_kernel import _lib
+
+    width = 2 * 5120 if mode == "swiglu" else 5120
+    xb = bf16_bits(activations(37, width, seed=77))
+    out = {}
+    try:
+        for name, sel in KERNELS.items():
+            _lib.load().ctu_debug_set_quant_kernel(sel)
+            out[name] = run_quant(C, xb, bits, mode)
+    finally:
+        _lib.load().ctu_debug_set_quant_kernel(0)
+    assert np.array_equal(out["two_pass"][0], out["register"][0])
+    assert np.array_equal(out["two_pass"][1].view(np.uint32), out["register"][1].view(np.uint32))
+
+
+def test_full_size_kernels_agree(C):
+    # Wan-14B activation shapes: both kernels give identical codes and scales.
+    from comfyui_turing_utils_kernel import _lib
+
+    for k in (5120, 13824):
+        x = activations(32760, k, seed=k).cuda()
+        res = {}
+        try:
+            for name, sel in KERNELS.items():
+                _lib.load().ctu_debug_set_quant_kernel(sel)
+                res[name] = C.turing_bf16_int8_convrot_quantize(x, 256, False)
+        finally:
+            _lib.load().ctu_debug_set_quant_kernel(0)
+        torch.cuda.synchronize()
+        assert torch.equal(res["two_pass"][0], res["register"][0])
+        assert torch.equal(res["two_pass"][1], res["register"][1])
