@@ -28,6 +28,8 @@ NVCC_FLAGS = [
     "-O3", "-std=c++17", "-lineinfo",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
     "--expt-relaxed-constexpr",
+    # Kernel templates are declared in headers and instantiated in their own .cu files.
+    "-diag-suppress", "20281",
 ]
 
 
