@@ -335,12 +335,17 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    "shapes_kn": SHAPES, "rotation_block": 256, "l2": "inputs (335-906 MB) larger than L2",
                    "parallelism": f"token rows, {world} independent rank(s)"},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": UNIT,
-                     "frac": gemm_tops / peak, "traffic": args.gemm_traffic, "kernel": "ctu::gemm::w8a8_gemm_kernel",
+                     "frac": gemm_tops / peak, "traffic": args.gemm_traffic,
+                     "kernel": "ctu::gemm::int8_gemm_pair_kernel<0> (CTA pair, tcgen05 cta_group::2)",
                      "traffic_note": "dram bytes of one 5120x5120 launch (ncu at M=16384, scaled to M=32760); "
                                      "algorithmic 529 MB",
                      "peak_source": peak_src},
         "quantizer_roofline": {"bound": "hbm", "achieved": quant_gbs, "peak": hbm, "unit": "GB/s",
-                               "frac": quant_gbs / hbm, "kernel": "ctu::rot::convrot_quant_kernel<0,8>"},
+                               "frac": quant_gbs / hbm, "traffic": args.quant_traffic,
+                               "kernel": "ctu::rot::convrot_quant_reg_kernel<0,8> (register-resident)",
+                               "traffic_note": "dram bytes of one K=5120 launch (ncu at M=16384, scaled to "
+                                               "M=32760); algorithmic 503 MB",
+                               "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
         "clocks": clocks.summary(),
         "e2e": None if args.skip_e2e else {
             "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
@@ -366,6 +371,10 @@ def main():
     # M=16384 (240.2 MB), scaled to M=32760 by rows processed.
     ap.add_argument("--gemm-traffic", type=float, default=240.16e6 * 32760 / 16384,
                     help="ncu dram bytes per GEMM launch (profiles/), reported as roofline.traffic")
+    # profiles/convrot_quant_reg_int8_k5120_m16384.md: dram read+write of one K=5120
+    # launch at M=16384, scaled to M=32760.
+    ap.add_argument("--quant-traffic", type=float, default=(168.05e6 + 51.32e6) * 32760 / 16384,
+                    help="ncu dram bytes per quantizer launch (profiles/), reported as quantizer_roofline.traffic")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -8,6 +8,8 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <tuple>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -213,17 +215,33 @@ int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
     return CTU_OK;
 }
 
+// Per (kernel, device, block, shared memory): CTAs per SM.  Filled on first use, so
+// repeated calls of one shape launch without runtime queries (and the first call of a
+// shape should come before any stream capture).
+std::map<std::tuple<const void *, int, int, size_t>, int> g_quant_occupancy;
+
 template <int Act, int Bits>
-int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan, int num_sms,
-                 cudaStream_t stream) {
+int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
+                 const DeviceQuery &q, cudaStream_t stream) {
     auto kernel = plan.reg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits> : ctu::rot::convrot_quant_kernel<Act, Bits>;
-    CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(plan.smem)));
+    const int threads = plan.warps * 32;
+    const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), q.device, threads, plan.smem);
     int per_sm = 0;
-    CTU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, plan.warps * 32, plan.smem));
-    if (per_sm < 1) return fail(CTU_ERR_UNSUPPORTED, "ConvRot quantizer does not fit on an SM");
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        auto it = g_quant_occupancy.find(key);
+        if (it != g_quant_occupancy.end()) per_sm = it->second;
+    }
+    if (per_sm == 0) {
+        CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, q.smem_optin));
+        CTU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, plan.smem));
+        if (per_sm < 1) return fail(CTU_ERR_UNSUPPORTED, "ConvRot quantizer does not fit on an SM");
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_quant_occupancy[key] = per_sm;
+    }
     const int64_t batches = (args.m + plan.rows_per_batch - 1) / plan.rows_per_batch;
-    const int grid = static_cast<int>(std::min<int64_t>(batches, static_cast<int64_t>(num_sms) * per_sm));
-    kernel<<<grid, plan.warps * 32, plan.smem, stream>>>(map, args);
+    const int grid = static_cast<int>(std::min<int64_t>(batches, static_cast<int64_t>(q.num_sms) * per_sm));
+    kernel<<<grid, threads, plan.smem, stream>>>(map, args);
     CTU_CUDA(cudaGetLastError());
     return CTU_OK;
 }
@@ -390,15 +408,15 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
     using ctu::rot::kActNone;
     using ctu::rot::kActSwiGLU;
     if (act == CTU_ACT_NONE) {
-        return bits == 8 ? launch_quant<kActNone, 8>(map, args, plan, q.num_sms, stream)
-                         : launch_quant<kActNone, 4>(map, args, plan, q.num_sms, stream);
+        return bits == 8 ? launch_quant<kActNone, 8>(map, args, plan, q, stream)
+                         : launch_quant<kActNone, 4>(map, args, plan, q, stream);
     }
     if (act == CTU_ACT_SWIGLU) {
-        return bits == 8 ? launch_quant<kActSwiGLU, 8>(map, args, plan, q.num_sms, stream)
-                         : launch_quant<kActSwiGLU, 4>(map, args, plan, q.num_sms, stream);
+        return bits == 8 ? launch_quant<kActSwiGLU, 8>(map, args, plan, q, stream)
+                         : launch_quant<kActSwiGLU, 4>(map, args, plan, q, stream);
     }
-    return bits == 8 ? launch_quant<kActGelu, 8>(map, args, plan, q.num_sms, stream)
-                     : launch_quant<kActGelu, 4>(map, args, plan, q.num_sms, stream);
+    return bits == 8 ? launch_quant<kActGelu, 8>(map, args, plan, q, stream)
+                     : launch_quant<kActGelu, 4>(map, args, plan, q, stream);
 }
 
 int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
