@@ -1,4 +1,5 @@
-"""Kitchen-free mirror of the plugin's ConvRot linear entry points on B200 (see dispatch.py)."""
+"""Kitchen-free mirror of the plugin's ConvRot linear entry points on B200 (see dispatch.py
+and fusions.py)."""
 
 from .dispatch import (
     convrot_w4a4_linear,
@@ -7,11 +8,15 @@ from .dispatch import (
     quantize_convrot_int8_activation,
     quantize_convrot_swiglu_activation,
 )
+from .fusions import convrot_w8_output_slice, convrot_weight_kind, is_turing_convrot_linear
 
 __all__ = [
     "convrot_w4a4_linear",
+    "convrot_w8_output_slice",
+    "convrot_weight_kind",
     "int8_linear",
     "int8_linear_from_quantized",
+    "is_turing_convrot_linear",
     "quantize_convrot_int8_activation",
     "quantize_convrot_swiglu_activation",
 ]

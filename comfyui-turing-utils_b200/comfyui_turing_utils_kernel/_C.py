@@ -119,6 +119,31 @@ def turing_gelu_int4_convrot_quantize(input, group_size=256):
     return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "GELU staged ConvRot")
 
 
+def turing_swiglu_int8_convrot_quantize_scaled(input, scales, group_size=256):
+    """bindings.cpp:512-545: SwiGLU + ConvRot of one channel shard, int8 codes with the
+    caller's whole-row scales (fp32, one per row); returns the codes only."""
+    input = input.contiguous()
+    scales = scales.reshape(-1).to(torch.float32).contiguous()
+    _check_cuda_2d(input, "input")
+    if input.dtype != torch.bfloat16:
+        raise RuntimeError("scaled SwiGLU ConvRot input must be bfloat16")
+    if group_size != 256:
+        raise RuntimeError("scaled SwiGLU ConvRot only supports group_size=256")
+    if input.shape[1] % 2 != 0:
+        raise RuntimeError("scaled SwiGLU input width must be even")
+    rows, hidden = input.shape[0], input.shape[1] // 2
+    if rows <= 0 or hidden <= 0 or hidden % group_size != 0:
+        raise RuntimeError("scaled SwiGLU width must be positive and divisible by 256")
+    if not scales.is_cuda or scales.device != input.device or scales.numel() != rows:
+        raise RuntimeError("scaled SwiGLU requires one FP32 scale per input row")
+    input = _aligned(input)
+    codes = torch.empty((rows, hidden), dtype=torch.int8, device=input.device)
+    with torch.cuda.device(input.device):
+        _lib.check(_lib.load().ctu_swiglu_int8_convrot_quantize_scaled(
+            _ptr(input), rows, hidden, _ptr(scales), _ptr(codes), _stream(input.device)))
+    return codes
+
+
 # ----------------------------------------------------------------------------- GEMMs
 def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=None, tile_policy=0):
     """bindings.cpp:371-421: W8A8 GEMM with the fused dequant + bias epilogue.

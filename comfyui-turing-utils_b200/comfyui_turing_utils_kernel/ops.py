@@ -207,6 +207,27 @@ def _turing_swiglu_int8_convrot_quantize_fake(x, group_size=256):
     )
 
 
+# ops.py:189-219: one channel shard quantized with precomputed whole-row scales.
+@torch.library.custom_op("turing_utils::swiglu_int8_convrot_quantize_scaled", mutates_args=())
+def turing_swiglu_int8_convrot_quantize_scaled(
+    x: torch.Tensor,
+    scales: torch.Tensor,
+    group_size: int = 256,
+) -> torch.Tensor:
+    """Quantize a SwiGLU+ConvRot shard with precomputed whole-row scales."""
+    _require_cuda(x, "scaled Turing SwiGLU ConvRot")
+    if x.dtype != torch.bfloat16 or x.ndim != 2:
+        raise TypeError("scaled SwiGLU ConvRot input must be 2D bfloat16 on the B200 build")
+    if scales.dtype != torch.float32 or scales.numel() != x.shape[0]:
+        raise TypeError("scaled SwiGLU ConvRot requires one FP32 scale per row")
+    return _C.turing_swiglu_int8_convrot_quantize_scaled(x.contiguous(), scales.contiguous(), group_size)
+
+
+@turing_swiglu_int8_convrot_quantize_scaled.register_fake
+def _turing_swiglu_int8_convrot_quantize_scaled_fake(x, scales, group_size=256):
+    return torch.empty((x.size(0), x.size(1) // 2), dtype=torch.int8, device=x.device)
+
+
 @torch.library.custom_op("turing_utils::swiglu_int4_convrot_quantize", mutates_args=())
 def turing_swiglu_int4_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
     """SwiGLU + ConvRot packed-int4 quantization of a [M, 2K] block."""

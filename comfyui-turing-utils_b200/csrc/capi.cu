@@ -385,8 +385,8 @@ int check_quantize_args(const void *x, int64_t rows, int64_t k, int act, int bit
 }
 
 int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
-                 uint32_t *err, const DeviceQuery &q, cudaStream_t stream) {
-    if (int rc = check_quantize_args(x, rows, k, act, bits, codes, scales)) return rc;
+                 uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales) {
+    if (int rc = check_quantize_args(x, rows, k, act, bits, codes, given_scales ? given_scales : scales)) return rc;
     if (rows == 0) return CTU_OK;
     QuantPlan plan;
     if (int rc = plan_quant(k, act, bits, q.smem_optin, &plan)) return rc;
@@ -398,6 +398,7 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
     ctu::rot::QuantArgs args;
     args.codes = codes;
     args.scales = scales;
+    args.given_scales = given_scales;
     args.err = err;
     args.m = static_cast<int>(rows);
     args.k = static_cast<int>(k);
@@ -489,6 +490,18 @@ int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bi
     if (int rc = device_info(&dev)) return rc;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, const float *scales,
+                                            int8_t *codes, void *stream) {
+    if (rows > 0 && scales == nullptr) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (int rc = check_quantize_args(x, rows, k, CTU_ACT_SWIGLU, 8, codes, scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    return run_quantize(x, rows, k, CTU_ACT_SWIGLU, 8, codes, nullptr, dev.err, q, static_cast<cudaStream_t>(stream),
+                        scales);
 }
 
 int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,

@@ -119,6 +119,13 @@ __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
     return make_uint2(lo, hi);
 }
 
+// True when the reciprocal-quotient fast chain reproduces bf16(y / rounded_scale) for
+// every finite y: the rounded scale is a normal, finite bf16 value.
+__device__ __forceinline__ bool fast_chain_scale_ok(float rounded_scale) {
+    const float a = fabsf(rounded_scale);
+    return a >= 1.17549435e-38f && a <= kBf16Max;
+}
+
 // Exact reference chain including NaN (fmaxf(-128, NaN) == -128) for rows that
 // contain NaN or infinities.
 static __device__ __noinline__ uint2 quant8_int8_exact(uint4 w, float rounded_scale) {

@@ -218,7 +218,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         }
 
         // -------------------------------------------------------------- per-row scales
-        for (int r = tid; r < rows; r += nthreads) {
+        const bool given = args.given_scales != nullptr;
+        for (int r = tid; r < rows && !given; r += nthreads) {
             const float amax = __uint_as_float(absmax_rows[r]);
             const float qmax = Bits == 4 ? 7.0f : 127.0f;
             const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
@@ -238,12 +239,13 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 const float amax = __uint_as_float(absmax_rows[r]);
                 const float qmax = Bits == 4 ? 7.0f : 127.0f;
                 const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
-                const float scale = fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
+                const float scale =
+                    given ? args.given_scales[row0 + r] : fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
                 if (Bits == 4) {
                     qparam = __fdiv_rn(1.0f, scale);
                 } else {
                     const float rs = __bfloat162float(__float2bfloat16_rn(scale));
-                    exact = nan_rows[r] != 0u || isinf(amax);
+                    exact = nan_rows[r] != 0u || (given ? !fast_chain_scale_ok(rs) : isinf(amax));
                     qparam = exact ? rs : __frcp_rn(rs);
                 }
             }

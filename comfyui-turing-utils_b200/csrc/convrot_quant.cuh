@@ -16,7 +16,10 @@ constexpr int kMaxBoxRows = 64;    // 128-byte slices per TMA copy (8 KiB)
 
 struct QuantArgs {
     int8_t *codes;       // [m, k] int8 or [m, k/2] packed int4
-    float *scales;       // [m]
+    float *scales;       // [m] (output; unused when given_scales is set)
+    // Optional caller-supplied per-row scales (int8 only): the codes use them instead
+    // of the row's own absmax, and no scale is written.
+    const float *given_scales;
     uint32_t *err;       // device error word
     int m;               // rows
     int k;               // rotated width (the SwiGLU input is 2k wide)

@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
 
     const int pair = tid >> 1;
     const int h = tid & 1;
+    const bool given = args.given_scales != nullptr;  // uniform: a kernel argument
     bool alive = true;
 
     for (int it = 0;; ++it) {
@@ -211,24 +212,26 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
         }
 
         uint32_t wa[32], wb[32];
+        bool group_nan = false;
         if (warp_busy && alive) {
             float amax, probe;
             rotate_to_words(v, h, wa, wb, amax, probe);
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             probe = __fadd_rn(probe, __shfl_xor_sync(0xffffffffu, probe, 1));
-            if (active && h == 0) {
+            if (active && h == 0 && !given) {
                 atomicMax(&row_absmax[par * B + r], __float_as_uint(amax));
                 if (isnan(probe)) atomicOr(&row_nan[par * B + r], 1u);
             }
+            group_nan = isnan(probe);
         }
-        __syncthreads();  // every group of every row has reported its absmax
+        if (!given) __syncthreads();  // every group of every row has reported its absmax
 
         if (active && alive) {
-            const float amax = __uint_as_float(row_absmax[par * B + r]);
+            const float amax = given ? 0.0f : __uint_as_float(row_absmax[par * B + r]);
             const float qmax = Bits == 4 ? 7.0f : 127.0f;
             const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
-            const float scale = fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
-            if (grp == 0 && h == 0) args.scales[row0 + r] = scale;
+            const float scale = given ? args.given_scales[row0 + r] : fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
+            if (grp == 0 && h == 0 && !given) args.scales[row0 + r] = scale;
             int8_t *out = args.codes + static_cast<int64_t>(row0 + r) * Kout;
             if constexpr (Bits == 4) {
                 const float inv = __fdiv_rn(1.0f, scale);
@@ -237,7 +240,10 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
                 store_run_int4(out + 64, wb, inv);
             } else {
                 const float rs = __bfloat162float(__float2bfloat16_rn(scale));
-                const bool exact = row_nan[par * B + r] != 0u || isinf(amax);
+                // Given scales: this group's own NaN probe decides (the exact chain is
+                // correct for any row), plus any scale outside the fast chain's range.
+                const bool exact = given ? (group_nan || !fast_chain_scale_ok(rs))
+                                         : (row_nan[par * B + r] != 0u || isinf(amax));
                 const float qparam = exact ? rs : __frcp_rn(rs);
                 out += grp * 256 + h * 64;
                 store_run_int8(out, wa, exact, qparam);

@@ -66,6 +66,20 @@ CTU_API int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act
                          void *stream);
 
 /*
+ * SwiGLU + ConvRot rotate of one channel shard, quantized to int8 with caller-supplied
+ * per-row scales (the whole row's scales, computed over every shard beforehand):
+ *   x      bf16 [rows, 2k] (gate | up halves of the shard), 16-byte aligned
+ *   scales fp32 [rows], read only
+ *   codes  int8 [rows, k], 16-byte aligned
+ * code = clamp(rint(bf16(bf16(y) / bf16(scale))), -128, 127), as the unscaled op.
+ * k must be a positive multiple of 256.
+ * Replaces turing_utils::swiglu_int8_convrot_quantize_scaled (ops.py:189-219;
+ * bindings.cpp:512-545; convrot_quant.cu:138-161,239-278,591-621).
+ */
+CTU_API int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, const float *scales,
+                                                    int8_t *codes, void *stream);
+
+/*
  * W8A8 linear with the fused dequant + bias epilogue:
  *   out[m, n] = bf16(((float(sum_k a[m,k] * w[n,k]) * a_scale[m]) * w_scale[n]) + bias[n])
  *   a int8 [m, k], w int8 [n, k] (K-contiguous rows), a_scale fp32 [m],

@@ -174,6 +174,37 @@ static void quantize_row_int4(const uint16_t *ybits, int k, float absmax, int8_t
  * bits = 8: codes rows x k int8; bits = 4: rows x k/2 packed int4.  Returns 0, or
  * -1 on an unsupported k.
  */
+/* turing_swiglu_int8_convrot_quantize_scaled (convrot_quant.cu:138-161, 239-278):
+ * rotate each row as ctu_oracle_convrot_quantize does and quantize with the caller's
+ * scale instead of the row's absmax:
+ *   code = clamp(rint(bf16(bf16(y) / bf16(scale))), -128, 127). */
+static void quantize_row_int8_given(const uint16_t *ybits, int k, float scale, int8_t *codes) {
+    const float rounded_scale = round_bf16(scale);
+    for (int c = 0; c < k; ++c) {
+        const float value = bf16_to_f32(ybits[c]);
+        const float divided = round_bf16(value / rounded_scale);
+        float q = nearbyintf(divided);
+        q = fminf(127.0f, fmaxf(-128.0f, q));
+        codes[c] = (int8_t)q;
+    }
+}
+
+int ctu_oracle_convrot_quantize_scaled(const uint16_t *x, const float *scales, int8_t *codes,
+                                       long rows, int k, int mode) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
+    const int width = mode == 1 ? 2 * k : k;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            (void)rotate_row(x + r * width, k, mode, ybits, 0);
+            quantize_row_int8_given(ybits, k, scales[r], codes + r * k);
+        }
+    }
+    return 0;
+}
+
 int ctu_oracle_convrot_quantize(const uint16_t *x, int8_t *codes, float *scales,
                                 long rows, int k, int bits, int mode) {
     if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;

@@ -58,6 +58,8 @@ def _load():
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int
         lib.ctu_oracle_convrot_quantize.argtypes = [vp, vp, vp, i64, i32, i32, i32]
         lib.ctu_oracle_convrot_quantize.restype = i32
+        lib.ctu_oracle_convrot_quantize_scaled.argtypes = [vp, vp, vp, i64, i32, i32]
+        lib.ctu_oracle_convrot_quantize_scaled.restype = i32
         lib.ctu_oracle_rotate.argtypes = [vp, vp, i64, i32, i32]
         lib.ctu_oracle_rotate.restype = None
         lib.ctu_oracle_epilogue.argtypes = [vp, i64, vp, vp, i64, vp, vp, i64, i64, i32, i32]
@@ -116,6 +118,20 @@ def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN):
     if rc != 0:
         raise ValueError(f"unsupported ConvRot width {k}")
     return codes, scales
+
+
+def convrot_quantize_scaled(x_bits: np.ndarray, scales: np.ndarray, mode: int = MODE_SWIGLU) -> np.ndarray:
+    """int8 codes of the rotated rows with caller-supplied per-row scales
+    (``turing_swiglu_int8_convrot_quantize_scaled``, convrot_quant.cu:138-161,239-278)."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, width = x_bits.shape
+    k = width // 2 if mode == MODE_SWIGLU else width
+    scales = np.ascontiguousarray(scales, dtype=np.float32).reshape(-1)
+    codes = np.empty((rows, k), dtype=np.int8)
+    rc = _load().ctu_oracle_convrot_quantize_scaled(_ptr(x_bits), _ptr(scales), _ptr(codes), rows, k, mode)
+    if rc != 0:
+        raise ValueError(f"unsupported ConvRot width {k}")
+    return codes
 
 
 def int8_gemm_s32(a: np.ndarray, w: np.ndarray) -> np.ndarray:

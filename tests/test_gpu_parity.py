@@ -351,3 +351,22 @@ def test_dispatch_convrot_w4a4_linear(C, linear_dtype):
     else:
         ref = oracle.w4a4_linear(codes, wp, scales, w_s.numpy(), bias.numpy())
     assert np.array_equal(bf16_bits(out), ref)
+
+
+def test_w8_output_slices_reassemble_the_linear(C):
+    # fusions.py:56-85: a W8 linear evaluated as contiguous output-channel intervals
+    # from one quantized activation equals the whole linear, for per-channel and
+    # scalar weight scales.
+    d = _dispatch()
+    m, k, n = 300, 1536, 520
+    x = activations(m, k, seed=51).cuda()
+    g = torch.Generator().manual_seed(52)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8).cuda()
+    bias = (torch.randn((n,), generator=g) * 0.02).cuda()
+    q, s = d.quantize_convrot_int8_activation(x)
+    for w_s in ((torch.rand((n,), generator=g) * 0.009 + 1e-3).cuda(), torch.tensor([0.004]).cuda()):
+        full = d.int8_linear_from_quantized(q, s, w, w_s, bias)
+        cuts = [0, 8, 264, 448, n]
+        parts = [d.convrot_w8_output_slice(q, s, w, w_s, bias, a, b, torch.bfloat16) for a, b in zip(cuts, cuts[1:])]
+        torch.cuda.synchronize()
+        assert torch.equal(torch.cat(parts, dim=1), full)

@@ -161,3 +161,49 @@ def test_full_size_kernels_agree(C):
         torch.cuda.synchronize()
         assert torch.equal(res["two_pass"][0], res["register"][0])
         assert torch.equal(res["two_pass"][1], res["register"][1])
+
+
+# ----------------------------------------------------------------------------- scaled SwiGLU shards
+def test_scaled_swiglu_shards_reassemble_the_row(C, kernel):
+    # Exact two-pass channel streaming (dispatch.py:67-69): whole-row scales from the
+    # unscaled op, then each 256-aligned channel shard quantized with them, must give
+    # the unscaled op's codes.
+    rows, k, shards = 37, 5120, 4
+    xb = bf16_bits(activations(rows, 2 * k, seed=91))
+    x = to_bf16_tensor(xb).cuda()
+    codes, scales = C.turing_bf16_int8_convrot_quantize(x, 256, True)
+    width = k // shards
+    parts = []
+    for j in range(shards):
+        gate = x[:, j * width:(j + 1) * width]
+        up = x[:, k + j * width:k + (j + 1) * width]
+        parts.append(C.turing_swiglu_int8_convrot_quantize_scaled(torch.cat([gate, up], dim=1), scales, 256))
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts, dim=1), codes)
+
+
+@pytest.mark.parametrize("rows,k", [(5, 512), (19, 5120), (3, 13824)])
+def test_scaled_swiglu_matches_oracle_with_any_scale(C, kernel, rows, k):
+    rng = np.random.default_rng(rows + k)
+    xb = bf16_bits(activations(rows, 2 * k, seed=rows * 7 + k))
+    if rows > 4:
+        xb[1, rng.choice(2 * k, size=3, replace=False)] = [0x7FC0, 0x7F80, 0xFF80]  # NaN and infinities
+    scales = (rng.random(rows).astype(np.float32) * 0.05 + 1e-3)
+    specials = np.array([0.0, np.nan, np.inf, -0.03, 1e-40, 3e38], dtype=np.float32)
+    scales[: min(rows, specials.size)] = specials[: min(rows, specials.size)]
+    codes = C.turing_swiglu_int8_convrot_quantize_scaled(to_bf16_tensor(xb).cuda(), torch.from_numpy(scales).cuda(), 256)
+    torch.cuda.synchronize()
+    ref = oracle.convrot_quantize_scaled(xb, scales)
+    got = codes.cpu().numpy()
+    # SwiGLU uses expf: CUDA and glibc may differ by one ulp, which can move a code by
+    # one step in rare positions (same tolerance as the unscaled SwiGLU test).
+    assert np.abs(got.astype(np.int32) - ref.astype(np.int32)).max() <= 1
+    assert (got != ref).mean() < 1e-3
+
+
+def test_scaled_swiglu_rejects_bad_scales(C):
+    x = torch.zeros((4, 1024), dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(RuntimeError, match="one FP32 scale per input row"):
+        C.turing_swiglu_int8_convrot_quantize_scaled(x, torch.ones(3, device="cuda"), 256)
+    with pytest.raises(RuntimeError, match="group_size=256"):
+        C.turing_swiglu_int8_convrot_quantize_scaled(x, torch.ones(4, device="cuda"), 128)

@@ -92,3 +92,17 @@ def test_int4_pack_roundtrip():
     rng = np.random.default_rng(0)
     v = rng.integers(-8, 8, size=(5, 64)).astype(np.int8)
     assert np.array_equal(oracle.unpack_int4(oracle.pack_int4(v)), v)
+
+
+def test_scaled_quantizer_oracle_matches_unscaled_with_own_scales():
+    # turing_swiglu_int8_convrot_quantize_scaled with each row's own scale must give the
+    # unscaled quantizer's codes (the two reference kernels share the code chain,
+    # convrot_quant.cu:138-161 and :475-510), including NaN/inf rows.
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((9, 2 * 768)).astype(np.float32)
+    xb = oracle.f32_to_bf16_bits(x)
+    xb[2, 5] = 0x7FC0
+    xb[4, 7] = 0x7F80
+    for mode in (oracle.MODE_SWIGLU, oracle.MODE_PLAIN):
+        codes, scales = oracle.convrot_quantize(xb, 8, mode)
+        assert np.array_equal(oracle.convrot_quantize_scaled(xb, scales, mode), codes)
