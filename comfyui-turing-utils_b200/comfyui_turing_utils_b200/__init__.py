@@ -2,6 +2,7 @@
 and fusions.py)."""
 
 from .dispatch import (
+    codebook_w4a8_linear,
     convrot_w4a4_linear,
     int8_linear,
     int8_linear_from_quantized,
@@ -11,6 +12,7 @@ from .dispatch import (
 from .fusions import convrot_w8_output_slice, convrot_weight_kind, is_turing_convrot_linear
 
 __all__ = [
+    "codebook_w4a8_linear",
     "convrot_w4a4_linear",
     "convrot_w8_output_slice",
     "convrot_weight_kind",

@@ -129,6 +129,40 @@ def int8_linear(
     return output.reshape(*original_shape[:-1], weight.shape[0])
 
 
+def codebook_w4a8_linear(
+    x: torch.Tensor,
+    qdata: torch.Tensor,
+    s_rel: torch.Tensor,
+    s_channel: torch.Tensor,
+    codebook: torch.Tensor | None = None,
+    correction: torch.Tensor | None = None,
+    bias: torch.Tensor | None = None,
+    group_size: int = 16,
+    convrot_groupsize: int = 256,
+    out_dtype: torch.dtype = torch.bfloat16,
+    input_act: str | None = None,
+) -> torch.Tensor:
+    """dispatch.py:803-869: grouped-codebook W4A8 on the fast path's conditions."""
+    _require(x.dtype == torch.bfloat16 and out_dtype == torch.bfloat16, "non-bf16 activations or output")
+    _require(convrot_groupsize == CONVROT_GROUP, f"ConvRot group size {convrot_groupsize}")
+    _require(correction is None, "a codebook correction term")
+    _require(codebook is not None and codebook.numel() == 16, "a codebook without 16 entries")
+    _require(s_rel.dtype == torch.float8_e4m3fn, "non-e4m3 group scales")
+    _require(qdata.ndim == 2 and qdata.shape[0] % 8 == 0 and qdata.shape[1] * 2 == x.shape[-1],
+             "this packed weight shape")
+    _require(input_act in _FUSED_ACTS, f"input activation {input_act!r}")
+    original_shape = x.shape
+    x2d = x.reshape(-1, original_shape[-1]).contiguous()
+    qactivation, activation_scale = _quantize_int8(x2d, convrot_groupsize, input_act)
+    output = ops.turing_codebook_w4a8_linear(qactivation, qdata, activation_scale, s_rel, s_channel, codebook, bias,
+                                             group_size)
+    return output.reshape(*original_shape[:-1], qdata.shape[0])
+
+
+# Kitchen resolves backend implementations by the public capability name (dispatch.py:872-873).
+w4a8_int8_linear = codebook_w4a8_linear
+
+
 def convrot_w4a4_linear(
     x: torch.Tensor,
     qweight: torch.Tensor,

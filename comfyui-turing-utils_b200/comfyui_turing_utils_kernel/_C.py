@@ -247,6 +247,104 @@ def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=
     return out if n_pad == n else out[:, :n].contiguous()
 
 
+# Decoded-weight workspace cap of the B200 codebook path: the whole output dimension is
+# decoded at once (one tensor-core GEMM) whenever its int8 weights fit in this budget.
+CODEBOOK_WORKSPACE_BYTES = 256 << 20
+# Reference chunk of the staged path (dispatch.py TURING_CODEBOOK_W4A8_CHUNK_ROWS).
+TURING_CODEBOOK_W4A8_CHUNK_ROWS = 4096
+
+
+def _codebook_chunk_rows(m: int, n: int, k: int, group_size: int, chunk_rows: int) -> int:
+    """bindings.cpp:328-350 policy, B200 sizes.  -1 (force the inline decode) keeps the
+    reference's precondition; its B200 form decodes all N at once like chunk_rows=0.
+    0 decodes as many channels as the workspace budget allows; a positive multiple of 8
+    forces that chunk."""
+    if chunk_rows < -1:
+        raise RuntimeError("chunk_rows must be -1, 0, or a positive multiple of 8")
+    if chunk_rows == -1 and not (group_size == 16 and m > 8192):
+        raise RuntimeError("forced inline codebook W4A8 requires group_size=16 and M>8192")
+    if chunk_rows > 0:
+        if chunk_rows % 8 != 0:
+            raise RuntimeError("chunk_rows must be divisible by 8")
+        return min(n, chunk_rows)
+    budget_rows = max(8, (CODEBOOK_WORKSPACE_BYTES // max(k, 1)) // 8 * 8)
+    return min(n, budget_rows)
+
+
+def turing_codebook_w4a8_linear(activation, weight, activation_scale, group_scale, channel_scale, codebook,
+                                bias=None, group_size=16, chunk_rows=0, tile_policy=0):
+    """bindings.cpp:262-370: grouped-codebook W4A8 (4-bit codes [N, K/2], e4m3fn group
+    scales [N, K/group_size], 16-entry fp32 codebook, per-channel fp32 scale)."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    activation_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
+    group_scale = group_scale.contiguous()
+    channel_scale = channel_scale.reshape(-1).to(torch.float32).contiguous()
+    codebook = codebook.reshape(-1).to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.float32).contiguous()
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    _check_cuda_2d(group_scale, "group_scale")
+    if activation.dtype != torch.int8:
+        raise RuntimeError("activation must be int8")
+    if weight.dtype != torch.int8:
+        raise RuntimeError("weight must use packed int8 storage")
+    if group_scale.dtype == torch.float8_e4m3fn:
+        group_scale = group_scale.view(torch.uint8)
+    if group_scale.dtype != torch.uint8:
+        raise RuntimeError("group_scale must contain raw float8_e4m3fn bytes")
+    dev = activation.device
+    if any(t.device != dev for t in (weight, group_scale, activation_scale, channel_scale, codebook)):
+        raise RuntimeError("all codebook W4A8 tensors must use the same CUDA device")
+    m, k = activation.shape
+    n = weight.shape[0]
+    if m <= 0 or n <= 0 or k <= 0:
+        raise RuntimeError("codebook W4A8 dimensions must be positive")
+    if k % 16 != 0 or n % 8 != 0:
+        raise RuntimeError("codebook W4A8 requires K divisible by 16 and N divisible by 8")
+    if weight.shape[1] * 2 != k:
+        raise RuntimeError("packed weight K must match activation K")
+    if not (group_size >= 4 and k % group_size == 0 and (16 % group_size == 0 or group_size % 16 == 0)):
+        raise RuntimeError("unsupported codebook W4A8 group_size")
+    if tuple(group_scale.shape) != (n, k // group_size):
+        raise RuntimeError("group_scale must have shape [N, K/group_size]")
+    if activation_scale.numel() != m:
+        raise RuntimeError("activation_scale must contain one value per activation row")
+    if channel_scale.numel() != n:
+        raise RuntimeError("channel_scale must contain one value per output channel")
+    if codebook.numel() != 16:
+        raise RuntimeError("codebook must contain 16 float32 values")
+    if bias is not None and (not bias.is_cuda or bias.device != dev):
+        raise RuntimeError("bias must use the activation CUDA device")
+    if bias is not None and bias.numel() != n:
+        raise RuntimeError("bias must contain one value per output channel")
+    rows = _codebook_chunk_rows(m, n, k, int(group_size), int(chunk_rows))
+    workspace = torch.empty((rows, k), dtype=torch.int8, device=dev)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    activation, weight = _aligned(activation), _aligned(weight)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ctu_codebook_w4a8_linear(
+            _ptr(activation), _ptr(weight), _ptr(activation_scale), _ptr(group_scale), _ptr(channel_scale),
+            _ptr(codebook), _ptr(bias), _ptr(out), _ptr(workspace), rows, m, n, k, int(group_size), _stream(dev)))
+    return out
+
+
+def codebook_decode_s8(weight, group_scale, codebook, group_size=16):
+    """The codebook weight decode alone (w4a8.cu:903-976): int8 [N, K]."""
+    weight = _aligned(weight.contiguous())
+    if group_scale.dtype == torch.float8_e4m3fn:
+        group_scale = group_scale.view(torch.uint8)
+    group_scale = group_scale.contiguous()
+    codebook = codebook.reshape(-1).to(torch.float32).contiguous()
+    n, k = weight.shape[0], 2 * weight.shape[1]
+    out = torch.empty((n, k), dtype=torch.int8, device=weight.device)
+    with torch.cuda.device(weight.device):
+        _lib.check(_lib.load().ctu_codebook_decode_s8(
+            _ptr(weight), _ptr(group_scale), _ptr(codebook), _ptr(out), n, k, int(group_size), _stream(weight.device)))
+    return out
+
+
 def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, output_columns=-1):
     """bindings.cpp:423-472."""
     accumulator = accumulator.contiguous()

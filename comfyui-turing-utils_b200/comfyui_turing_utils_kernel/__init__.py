@@ -11,12 +11,14 @@ from .ops import (
     turing_bf16_gelu_int8_convrot_quantize,
     turing_bf16_int4_convrot_quantize,
     turing_bf16_int8_convrot_quantize,
+    turing_codebook_w4a8_linear,
     turing_dequantize_int8_bf16,
     turing_gelu_int4_convrot_quantize,
     turing_gelu_int8_convrot_quantize,
     turing_int8_linear,
     turing_swiglu_int4_convrot_quantize,
     turing_swiglu_int8_convrot_quantize,
+    turing_swiglu_int8_convrot_quantize_scaled,
     turing_w4a8_linear,
 )
 
@@ -29,11 +31,13 @@ __all__ = [
     "turing_bf16_gelu_int8_convrot_quantize",
     "turing_bf16_int4_convrot_quantize",
     "turing_bf16_int8_convrot_quantize",
+    "turing_codebook_w4a8_linear",
     "turing_dequantize_int8_bf16",
     "turing_gelu_int4_convrot_quantize",
     "turing_gelu_int8_convrot_quantize",
     "turing_int8_linear",
     "turing_swiglu_int4_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize",
+    "turing_swiglu_int8_convrot_quantize_scaled",
     "turing_w4a8_linear",
 ]

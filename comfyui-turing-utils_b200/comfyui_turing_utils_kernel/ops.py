@@ -46,6 +46,42 @@ def _turing_w4a8_linear_fake(activation, weight, activation_scale, weight_scale,
 
 
 # ops.py:96-126
+# ops.py:38-93
+@torch.library.custom_op("turing_utils::codebook_w4a8_linear", mutates_args=())
+def turing_codebook_w4a8_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    group_scale: torch.Tensor,
+    channel_scale: torch.Tensor,
+    codebook: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    group_size: int = 16,
+    chunk_rows: int = 0,
+) -> torch.Tensor:
+    """Grouped-codebook W4A8: codes decoded to int8 ahead of the tcgen05 GEMM.
+
+    ``chunk_rows=0`` selects the production policy, ``-1`` forces the long-sequence
+    policy (group_size 16, M > 8192), and a positive multiple of eight forces that many
+    output channels per decoded chunk.
+    """
+    _require_cuda(activation, "Turing codebook W4A8")
+    if group_scale.dtype == torch.float8_e4m3fn:
+        group_scale = group_scale.view(torch.uint8)
+    if group_scale.dtype != torch.uint8:
+        raise TypeError("group_scale must be float8_e4m3fn or its raw uint8 view")
+    return _C.turing_codebook_w4a8_linear(
+        activation.contiguous(), weight.contiguous(), activation_scale.contiguous(), group_scale.contiguous(),
+        channel_scale.contiguous(), codebook.contiguous(), None if bias is None else bias.contiguous(),
+        group_size, chunk_rows)
+
+
+@turing_codebook_w4a8_linear.register_fake
+def _turing_codebook_w4a8_linear_fake(activation, weight, activation_scale, group_scale, channel_scale, codebook,
+                                      bias=None, group_size=16, chunk_rows=0):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
+
+
 @torch.library.custom_op("turing_utils::int8_linear", mutates_args=())
 def turing_int8_linear(
     activation: torch.Tensor,

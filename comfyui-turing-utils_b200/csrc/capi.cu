@@ -15,6 +15,7 @@
 #include <string>
 
 #include "../../include/ctu_b200.h"
+#include "codebook.cuh"
 #include "convrot_quant.cuh"
 #include "dequant.cuh"
 #include "gemm_i8.cuh"
@@ -562,6 +563,85 @@ int ctu_w4a4_linear(const int8_t *a_packed, const int8_t *w_packed, const float 
                     void *stream) {
     return int4_linear(ctu::gemm::kModeW4A4, a_packed, w_packed, a_scale, w_scale, w_scale_count, bias, out, m, n,
                        k, stream);
+}
+
+// ---------------------------------------------------------------- grouped-codebook W4A8
+static bool codebook_group_size_ok(int64_t k, int64_t group_size) {
+    // bindings.cpp:304-307
+    return group_size >= 4 && k % group_size == 0 && (16 % group_size == 0 || group_size % 16 == 0);
+}
+
+static int launch_codebook_decode(const int8_t *w_packed, const uint8_t *group_scale, const float *codebook,
+                                  int8_t *out, int64_t rows, int64_t k, int64_t group_size, int num_sms,
+                                  cudaStream_t stream) {
+    const int64_t items = rows * (k / 16);
+    if (items == 0) return CTU_OK;
+    const int threads = 256;
+    const int grid = static_cast<int>(std::min<int64_t>((items + threads - 1) / threads, static_cast<int64_t>(num_sms) * 8));
+    ctu::cb::codebook_decode_kernel<<<grid, threads, 0, stream>>>(w_packed, group_scale, codebook, out, items,
+                                                                  static_cast<int>(k), static_cast<int>(group_size));
+    CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
+int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_scale, const float *codebook, int8_t *out,
+                           int64_t rows, int64_t k, int64_t group_size, void *stream) {
+    if (rows < 0 || k < 0 || rows > INT32_MAX || k > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "codebook decode dimensions out of range");
+    if (k % 16 != 0) return fail(CTU_ERR_INVALID_ARGUMENT, "codebook decode requires K divisible by 16");
+    if (!codebook_group_size_ok(k, group_size)) return fail(CTU_ERR_INVALID_ARGUMENT, "unsupported codebook group_size");
+    if (rows == 0 || k == 0) return CTU_OK;
+    if (!w_packed || !group_scale || !codebook || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(w_packed) || !aligned16(out))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "packed weight and output must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    return launch_codebook_decode(w_packed, group_scale, codebook, out, rows, k, group_size, dev.num_sms,
+                                  static_cast<cudaStream_t>(stream));
+}
+
+int ctu_codebook_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale, const uint8_t *group_scale,
+                             const float *channel_scale, const float *codebook, const float *bias, void *out,
+                             int8_t *workspace, int64_t workspace_rows, int64_t m, int64_t n, int64_t k,
+                             int64_t group_size, void *stream) {
+    if (m <= 0 || n <= 0 || k <= 0) return fail(CTU_ERR_INVALID_ARGUMENT, "codebook W4A8 dimensions must be positive");
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "codebook W4A8 dimensions exceed the CUDA kernel range");
+    if (k % 16 != 0 || n % 8 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "codebook W4A8 requires K divisible by 16 and N divisible by 8");
+    if (!codebook_group_size_ok(k, group_size)) return fail(CTU_ERR_INVALID_ARGUMENT, "unsupported codebook W4A8 group_size");
+    if (workspace_rows <= 0 || workspace_rows % 8 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "codebook W4A8 needs an 8-row-aligned workspace");
+    if (!a || !w_packed || !a_scale || !group_scale || !channel_scale || !codebook || !out || !workspace)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(a) || !aligned16(w_packed) || !aligned16(out) || !aligned16(workspace))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "activation, weight, output and workspace must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int64_t groups = k / group_size;
+    // w4a8.cu:1154-1181: decode a chunk of output channels, then the W8A8 GEMM writes
+    // those columns of the output (row stride n).
+    for (int64_t row = 0; row < n; row += workspace_rows) {
+        const int64_t rows = std::min(workspace_rows, n - row);
+        if (int rc = launch_codebook_decode(w_packed + row * (k / 2), group_scale + row * groups, codebook, workspace,
+                                            rows, k, group_size, dev.num_sms, s))
+            return rc;
+        ctu::gemm::GemmArgs args{};
+        args.a_scale = a_scale;
+        args.w_scale = channel_scale + row;
+        args.bias = bias ? bias + row : nullptr;
+        args.out = static_cast<__nv_bfloat16 *>(out) + row;
+        args.err = dev.err;
+        args.m = static_cast<int>(m);
+        args.n = static_cast<int>(rows);
+        args.k = static_cast<int>(k);
+        args.ldc = static_cast<int>(n);
+        args.w_scale_count = static_cast<int>(rows);
+        args.out_mode = ctu::gemm::kOutBf16;
+        if (int rc = launch_gemm(a, workspace, args, dev.device, dev.num_sms, s)) return rc;
+    }
+    return CTU_OK;
 }
 
 int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, int64_t ldc, int64_t m, int64_t n, int64_t k,

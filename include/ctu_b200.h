@@ -131,6 +131,33 @@ CTU_API int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, in
                       void *stream);
 
 /*
+ * Grouped-codebook W4A8 linear:
+ *   w[n, c] = clamp(rint(codebook[code] * e4m3(group_scale[n, c / group_size])), -127, 127)
+ *   out[m, n] = bf16(((float(sum_c a[m, c] * w[n, c]) * a_scale[m]) * channel_scale[n]) + bias[n])
+ *   a            int8 [m, k]; w_packed: 4-bit codes [n, k/2], even column in the low nibble
+ *   group_scale  float8 e4m3fn bytes [n, k / group_size]; codebook fp32 [16]
+ *   channel_scale fp32 [n]; bias fp32 [n] or NULL; out bf16 [m, n]
+ *   workspace    int8 [workspace_rows, k]: output channels are decoded workspace_rows at a
+ *                time (a multiple of 8) and each chunk runs the W8A8 tensor-core GEMM.
+ * Requires k % 16 == 0, n % 8 == 0, group_size >= 4 dividing k with 16 % group_size == 0
+ * or group_size % 16 == 0; a, w_packed, out and workspace 16-byte aligned.
+ * Replaces turing_utils::codebook_w4a8_linear (ops.py:38-93; bindings.cpp:262-370;
+ * kernel/csrc/turing/w4a8.cu:89-242, 903-976, 1088-1182).
+ */
+CTU_API int ctu_codebook_w4a8_linear(const int8_t *a, const int8_t *w_packed, const float *a_scale,
+                                     const uint8_t *group_scale, const float *channel_scale, const float *codebook,
+                                     const float *bias, void *out, int8_t *workspace, int64_t workspace_rows,
+                                     int64_t m, int64_t n, int64_t k, int64_t group_size, void *stream);
+
+/*
+ * The codebook decode alone: int8 [rows, k] from w_packed [rows, k/2], group_scale
+ * [rows, k / group_size] and codebook [16], as in ctu_codebook_w4a8_linear.  Replaces the
+ * reference's internal staged decode (w4a8.cu:903-976), which has no public entry.
+ */
+CTU_API int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_scale, const float *codebook,
+                                   int8_t *out, int64_t rows, int64_t k, int64_t group_size, void *stream);
+
+/*
  * int32 accumulator -> bf16: out[r, c] = bf16((float(acc[r, c]) * a_scale[r]) * w_scale[c]),
  * acc row stride acc_stride (>= cols), w_scale [cols] or scalar (w_scale_count = 1),
  * out bf16 [rows, cols] contiguous.

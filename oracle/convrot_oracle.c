@@ -256,3 +256,44 @@ void ctu_oracle_epilogue(const int32_t *acc, long acc_stride, const float *a_sca
         }
     }
 }
+
+
+/* ---------------------------------------------------------------------------------
+ * Grouped-codebook W4A8 weight decode (kernel/csrc/turing/w4a8.cu:75-80, 903-976 and
+ * the inline iterator :216-240): weight[n][c] = clamp(rint(codebook[code] * s), -127,
+ * 127) with code the 4-bit value of column c (even column in the low nibble of the
+ * packed byte), s the float8 e4m3fn group scale of group c / group_size in row n,
+ * the product in fp32 and rint ties-to-even.  A NaN product decodes to 0 (the device
+ * float-to-int conversion of NaN); +-inf saturates to +-127. */
+static float e4m3fn_to_f32(uint8_t v) {
+    const int sign = v >> 7;
+    const int e = (v >> 3) & 0xF;
+    const int m = v & 0x7;
+    float mag;
+    if (e == 0xF && m == 0x7) return u2f(0x7FC00000u);            /* NaN (no infinities) */
+    if (e == 0) mag = ldexpf((float)m, -9);                          /* subnormal: m * 2^-9 */
+    else mag = ldexpf(1.0f + (float)m / 8.0f, e - 7);
+    return sign ? -mag : mag;
+}
+
+static int8_t decode_weight(float codebook_value, float scale) {
+    const float value = codebook_value * scale;
+    if (value != value) return 0;
+    float q = nearbyintf(value);
+    q = fminf(127.0f, fmaxf(-127.0f, q));
+    return (int8_t)q;
+}
+
+void ctu_oracle_codebook_decode(const int8_t *packed, const uint8_t *group_scale, const float *codebook,
+                                int8_t *out, long rows, int k, int group_size) {
+    const int groups = k / group_size;
+#pragma omp parallel for schedule(static)
+    for (long r = 0; r < rows; ++r) {
+        for (int c = 0; c < k; ++c) {
+            const uint8_t byte = (uint8_t)packed[r * (k / 2) + c / 2];
+            const int code = (c & 1) ? (byte >> 4) : (byte & 0xF);
+            const float scale = e4m3fn_to_f32(group_scale[r * groups + c / group_size]);
+            out[r * k + c] = decode_weight(codebook[code], scale);
+        }
+    }
+}

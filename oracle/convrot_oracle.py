@@ -60,6 +60,8 @@ def _load():
         lib.ctu_oracle_convrot_quantize.restype = i32
         lib.ctu_oracle_convrot_quantize_scaled.argtypes = [vp, vp, vp, i64, i32, i32]
         lib.ctu_oracle_convrot_quantize_scaled.restype = i32
+        lib.ctu_oracle_codebook_decode.argtypes = [vp, vp, vp, vp, i64, i32, i32]
+        lib.ctu_oracle_codebook_decode.restype = None
         lib.ctu_oracle_rotate.argtypes = [vp, vp, i64, i32, i32]
         lib.ctu_oracle_rotate.restype = None
         lib.ctu_oracle_epilogue.argtypes = [vp, i64, vp, vp, i64, vp, vp, i64, i64, i32, i32]
@@ -216,3 +218,27 @@ def convrot_w8a8_linear(x_bits, w, w_scale, bias=None, fused=False):
     """Whole path: ConvRot quantize, int32 GEMM, dequant+bias epilogue (bf16 bits)."""
     codes, scales = convrot_quantize(x_bits, 8)
     return int8_linear(codes, w, scales, w_scale, bias, fused=fused)
+
+
+def codebook_decode(w_packed: np.ndarray, group_scale: np.ndarray, codebook: np.ndarray, group_size: int) -> np.ndarray:
+    """Grouped-codebook W4 weights -> int8 [N, K] (w4a8.cu:903-976): e4m3fn group scale
+    (raw bytes [N, K/group_size]) times a 16-entry fp32 codebook, rint, clamp +-127."""
+    w_packed = np.ascontiguousarray(w_packed).view(np.int8)
+    rows, half = w_packed.shape
+    k = 2 * half
+    group_scale = np.ascontiguousarray(group_scale).view(np.uint8)
+    codebook = np.ascontiguousarray(codebook, dtype=np.float32).reshape(-1)
+    if codebook.size != 16 or group_scale.shape != (rows, k // group_size):
+        raise ValueError("codebook must have 16 entries and group_scale shape [N, K/group_size]")
+    out = np.empty((rows, k), dtype=np.int8)
+    _load().ctu_oracle_codebook_decode(_ptr(w_packed), _ptr(group_scale), _ptr(codebook), _ptr(out), rows, k,
+                                       group_size)
+    return out
+
+
+def codebook_w4a8_linear(a, w_packed, a_scale, group_scale, channel_scale, codebook, bias=None, group_size=16):
+    """``turing_utils::codebook_w4a8_linear`` oracle: decode, exact int32 GEMM, then the
+    W8A8 epilogue with the per-channel scale (w4a8.cu:1088-1182)."""
+    w = codebook_decode(w_packed, group_scale, codebook, group_size)
+    return int8_linear(a, w, a_scale, channel_scale, bias)
+

@@ -132,4 +132,37 @@ int ref_dequantize_int8_bf16(const void *acc, const void *a_scale, const void *w
     });
 }
 
+// kernel/csrc/turing/w4a8.cu:1088-1182 (grouped-codebook W4A8: per-chunk decode to an
+// int8 workspace + W8A8 GEMM, or the inline-decode CUTLASS iterator when
+// inline_decode != 0, which needs group_size 16).
+int ref_codebook_w4a8_linear(const void *a, const void *w_packed, const void *a_scale, const void *group_scale,
+                             const void *channel_scale, const void *codebook, const void *bias, void *workspace,
+                             int workspace_rows, void *out, int m, int n, int k, int group_size, int inline_decode,
+                             int tile_policy, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        ref::turing_codebook_w4a8_linear(
+            view(const_cast<void *>(a), {m, k}, Tensor::INT8),
+            view(const_cast<void *>(w_packed), {n, k / 2}, Tensor::INT8),
+            view(const_cast<void *>(a_scale), {m}, Tensor::FP32),
+            view(const_cast<void *>(group_scale), {n, k / group_size}, Tensor::FP8_E4M3),
+            view(const_cast<void *>(channel_scale), {n}, Tensor::FP32),
+            view(const_cast<void *>(codebook), {16}, Tensor::FP32),
+            bias ? view(const_cast<void *>(bias), {n}, Tensor::FP32) : Tensor{},
+            workspace ? view(workspace, {workspace_rows, k}, Tensor::INT8) : Tensor{},
+            view(out, {m, n}, Tensor::BF16), group_size, inline_decode != 0, tile_policy);
+    });
+}
+
+// kernel/csrc/turing/convrot_quant.cu:591-621 (SwiGLU shard with given row scales).
+int ref_swiglu_int8_convrot_quantize_scaled(const void *x, const void *scales, void *codes, int rows, int k,
+                                            void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        ref::turing_swiglu_int8_convrot_quantize_scaled(view(const_cast<void *>(x), {rows, 2 * k}, Tensor::BF16),
+                                                        view(const_cast<void *>(scales), {rows}, Tensor::FP32),
+                                                        view(codes, {rows, k}, Tensor::INT8));
+    });
+}
+
 }  // extern "C"

@@ -31,8 +31,11 @@ def load_ref():
     lib.ref_int8_linear.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
     lib.ref_w4a8_linear.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
     lib.ref_dequantize_int8_bf16.argtypes = [vp, vp, vp, i32, vp, i32, i32, i32, vp]
+    lib.ref_codebook_w4a8_linear.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp]
+    lib.ref_swiglu_int8_convrot_quantize_scaled.argtypes = [vp, vp, vp, i32, i32, vp]
     for name in ("ref_bf16_convrot_quantize", "ref_bf16_gelu_convrot_quantize", "ref_int8_linear",
-                 "ref_w4a8_linear", "ref_dequantize_int8_bf16"):
+                 "ref_w4a8_linear", "ref_dequantize_int8_bf16", "ref_codebook_w4a8_linear",
+                 "ref_swiglu_int8_convrot_quantize_scaled"):
         getattr(lib, name).restype = i32
     lib.ref_last_error.restype = ctypes.c_char_p
     return lib
@@ -109,14 +112,75 @@ def quant_cases():
     return cases
 
 
+# Grouped-codebook W4A8 cases: (m, n, k, group_size, chunk_rows or 0 for the inline
+# decode).  Inputs come from seeded generators (codebook_inputs), so the large inline
+# case stores only its output.
+CODEBOOK_CASES = [(33, 64, 256, 16, 64), (17, 72, 512, 4, 16), (9, 136, 768, 8, 136), (5, 64, 1024, 32, 32),
+                  (65, 128, 256, 64, 128), (8200, 8, 64, 16, 0)]
+
+
+def codebook_inputs(m, n, k, gs, seed):
+    """Seeded codebook W4A8 operands (numpy), with e4m3 special bytes and tie values."""
+    rng = np.random.default_rng(seed)
+    a = rng.integers(-128, 128, size=(m, k), dtype=np.int8)
+    codes = rng.integers(0, 16, size=(n, k), dtype=np.uint8)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8).view(np.int8)
+    # e4m3fn bytes: mostly moderate scales (exponent 4..9), plus NaN, max, subnormals,
+    # zeros and negative scales.
+    scale = rng.integers(0x20, 0x50, size=(n, k // gs), dtype=np.uint8)
+    special = np.array([0x7F, 0xFF, 0x7E, 0x01, 0x00, 0x80, 0xB8, 0x38], dtype=np.uint8)
+    flat = scale.reshape(-1)
+    flat[rng.choice(flat.size, size=min(flat.size, 8), replace=False)] = special[: min(flat.size, 8)]
+    codebook = np.array([-8.0, -6.5, -4.0, -2.5, -1.5, -0.5, 0.0, 0.5, 1.5, 2.5, 3.25, 4.0, 6.0, 7.5, 64.0, 200.0],
+                        dtype=np.float32)
+    a_s = (rng.random(m, dtype=np.float32) * 0.02 + 0.001).astype(np.float32)
+    c_s = (rng.random(n, dtype=np.float32) * 0.009 + 0.001).astype(np.float32)
+    bias = (rng.standard_normal(n).astype(np.float32) * 0.02) if seed % 2 == 0 else None
+    return a, packed, scale, codebook, a_s, c_s, bias
+
+
+def extra_cases(lib, out):
+    extras = {}
+    for idx, (m, n, k, gs, chunk) in enumerate(CODEBOOK_CASES):
+        a, packed, scale, codebook, a_s, c_s, bias = codebook_inputs(m, n, k, gs, 4500 + idx)
+        dev = [None if t is None else torch.from_numpy(t).cuda() for t in (a, packed, scale, codebook, a_s, c_s, bias)]
+        o = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+        ws = torch.empty((chunk, k), dtype=torch.int8, device="cuda") if chunk else None
+        check(lib, lib.ref_codebook_w4a8_linear(p(dev[0]), p(dev[1]), p(dev[4]), p(dev[2]), p(dev[5]), p(dev[3]),
+                                                p(dev[6]), p(ws), chunk, p(o), m, n, k, gs, 0 if chunk else 1, 0,
+                                                stream()))
+        torch.cuda.synchronize()
+        key = f"codebook_m{m}_n{n}_k{k}_g{gs}"
+        extras[f"{key}__seed"] = np.array([4500 + idx], dtype=np.int64)
+        extras[f"{key}__out"] = o.view(torch.int16).cpu().numpy().view(np.uint16)
+    # SwiGLU shard quantized with caller-supplied row scales (special scales included).
+    rows, k = 8, 512
+    x = torch.cat([special_rows(256), special_rows(256)], dim=1)[:rows].repeat(1, 2)
+    x[6:] = activations(2, 2 * k, 4600)
+    scales = torch.tensor([0.05, 0.0, float("nan"), float("inf"), -0.02, 1e-40, 3e38, 0.013], dtype=torch.float32)
+    codes = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    xd, sd = x.cuda().contiguous(), scales.cuda()
+    check(lib, lib.ref_swiglu_int8_convrot_quantize_scaled(p(xd), p(sd), p(codes), rows, k, stream()))
+    torch.cuda.synchronize()
+    extras["scaled_swiglu__x"] = x.view(torch.int16).numpy().view(np.uint16)
+    extras["scaled_swiglu__scales"] = scales.numpy()
+    extras["scaled_swiglu__codes"] = codes.cpu().numpy()
+    np.savez_compressed(out / "extras.npz", **extras)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
+    ap.add_argument("--only", choices=["all", "extras"], default="all")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     lib = load_ref()
     torch.cuda.init()
+    extra_cases(lib, out)
+    if args.only == "extras":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
 
     # ConvRot rotate + quantize, int8 and int4; every block geometry must agree.
     quant = {}

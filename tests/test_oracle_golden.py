@@ -106,3 +106,25 @@ def test_scaled_quantizer_oracle_matches_unscaled_with_own_scales():
     for mode in (oracle.MODE_SWIGLU, oracle.MODE_PLAIN):
         codes, scales = oracle.convrot_quantize(xb, 8, mode)
         assert np.array_equal(oracle.convrot_quantize_scaled(xb, scales, mode), codes)
+
+
+EXTRAS_PATH = GOLDEN / "extras.npz"
+
+
+@pytest.mark.skipif(not EXTRAS_PATH.exists(), reason="reference fixtures not generated")
+def test_codebook_and_scaled_swiglu_match_reference():
+    import sys
+
+    sys.path.insert(0, str(GOLDEN))
+    import make_golden
+
+    extras = np.load(EXTRAS_PATH)
+    for idx, (m, n, k, gs, _) in enumerate(make_golden.CODEBOOK_CASES):
+        a, packed, scale, codebook, a_s, c_s, bias = make_golden.codebook_inputs(m, n, k, gs, 4500 + idx)
+        ref = extras[f"codebook_m{m}_n{n}_k{k}_g{gs}__out"]
+        assert np.array_equal(oracle.codebook_w4a8_linear(a, packed, a_s, scale, c_s, codebook, bias, gs), ref), idx
+    codes = oracle.convrot_quantize_scaled(extras["scaled_swiglu__x"], extras["scaled_swiglu__scales"])
+    ref = extras["scaled_swiglu__codes"]
+    # expf (glibc vs CUDA) may move a code by one step in rare positions.
+    assert np.abs(codes.astype(np.int32) - ref.astype(np.int32)).max() <= 1
+    assert (codes != ref).mean() < 1e-3
