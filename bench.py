@@ -367,13 +367,13 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host round trip")
     ap.add_argument("--skip-variants", action="store_true", help="skip the W4A8/W4A4 timings")
-    # profiles/w8a8_gemm_k5120_n5120_m16384.md: dram read+write of one 5120x5120 launch at
-    # M=16384 (240.2 MB), scaled to M=32760 by rows processed.
-    ap.add_argument("--gemm-traffic", type=float, default=240.16e6 * 32760 / 16384,
+    # profiles/int8_gemm_pair_k5120_n5120_m16384.md: dram read+write of one 5120x5120 launch
+    # at M=16384 (243.0 MB), scaled to M=32760 by rows processed.
+    ap.add_argument("--gemm-traffic", type=float, default=(111.05e6 + 131.98e6) * 32760 / 16384,
                     help="ncu dram bytes per GEMM launch (profiles/), reported as roofline.traffic")
     # profiles/convrot_quant_reg_int8_k5120_m16384.md: dram read+write of one K=5120
     # launch at M=16384, scaled to M=32760.
-    ap.add_argument("--quant-traffic", type=float, default=(168.05e6 + 51.32e6) * 32760 / 16384,
+    ap.add_argument("--quant-traffic", type=float, default=(168.27e6 + 50.83e6) * 32760 / 16384,
                     help="ncu dram bytes per quantizer launch (profiles/), reported as quantizer_roofline.traffic")
     args = ap.parse_args()
     if args.warmup < 3:
