@@ -137,7 +137,10 @@ def cpu_sample_time(rows: int, threads: int):
     import convrot_oracle as oracle
 
     torch.set_num_threads(threads)
-    os.environ["OMP_NUM_THREADS"] = str(threads)
+    # The OpenMP runtime may already hold a launcher's OMP_NUM_THREADS=1: set the count
+    # explicitly so the reported cores are the threads used.
+    if oracle.set_threads(threads) != threads:
+        raise RuntimeError("could not set the oracle's OpenMP thread count")
     xs, layers = synth_inputs(rows, "cpu", seed=0)
     xbits = {k: x.view(torch.int16).numpy().view(np.uint16) for k, x in xs.items()}
     t0 = time.perf_counter()

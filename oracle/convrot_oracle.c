@@ -22,6 +22,7 @@
  * Python wrapper (torch._int_mm / numpy).
  */
 #include <math.h>
+#include <omp.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -297,3 +298,10 @@ void ctu_oracle_codebook_decode(const int8_t *packed, const uint8_t *group_scale
         }
     }
 }
+
+/* Worker threads of every later OpenMP region of this library, whatever OMP_NUM_THREADS
+ * the process started with (a launcher may pin it to 1 per rank). */
+void ctu_oracle_set_threads(int threads) { omp_set_num_threads(threads > 0 ? threads : 1); }
+
+int ctu_oracle_get_threads(void) { return omp_get_max_threads(); }
+

@@ -60,6 +60,10 @@ def _load():
         lib.ctu_oracle_convrot_quantize.restype = i32
         lib.ctu_oracle_convrot_quantize_scaled.argtypes = [vp, vp, vp, i64, i32, i32]
         lib.ctu_oracle_convrot_quantize_scaled.restype = i32
+        lib.ctu_oracle_set_threads.argtypes = [i32]
+        lib.ctu_oracle_set_threads.restype = None
+        lib.ctu_oracle_get_threads.argtypes = []
+        lib.ctu_oracle_get_threads.restype = i32
         lib.ctu_oracle_codebook_decode.argtypes = [vp, vp, vp, vp, i64, i32, i32]
         lib.ctu_oracle_codebook_decode.restype = None
         lib.ctu_oracle_rotate.argtypes = [vp, vp, i64, i32, i32]
@@ -70,6 +74,13 @@ def _load():
         lib.ctu_oracle_f32_to_bf16.restype = ctypes.c_uint16
         _lib = lib
     return _lib
+
+
+def set_threads(threads: int) -> int:
+    """OpenMP worker threads of the C restatement; returns the count now in effect."""
+    lib = _load()
+    lib.ctu_oracle_set_threads(int(threads))
+    return lib.ctu_oracle_get_threads()
 
 
 def _ptr(a: np.ndarray):
