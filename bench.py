@@ -269,7 +269,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             ms = v0.elapsed_time(v1) / nsteps
             variants[name] = {"value": ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
                               "format": "signed int4 weights, per-channel scale" +
-                                        (", int8 activations" if bits == 8 else ", int4 ConvRot activations")}
+                                        (", int8 activations" if bits == 8 else ", int4 ConvRot activations") +
+                                        "; int4 operands widened to int8 ahead of the W8A8 GEMM (M >= 512)"}
         if _lib.device_error(local_rank, clear=True):
             raise RuntimeError("kernel bounded-wait flags raised during the W4 variants")
 

@@ -185,12 +185,29 @@ def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=
     return out
 
 
+# From this many activation rows on, the W4 linears widen their packed int4 operands to
+# int8 once (a streaming pass) and run the W8A8 tensor-core GEMM, instead of widening every
+# weight tile inside the GEMM for each row block: the pass costs about as much as the GEMM
+# gains at ~500 rows of a 5120x5120 linear.
+W4_WIDEN_MIN_ROWS = 512
+
+
+def _widen_s4(packed: torch.Tensor) -> torch.Tensor:
+    rows, half = packed.shape
+    out = torch.empty((rows, 2 * half), dtype=torch.int8, device=packed.device)
+    with torch.cuda.device(packed.device):
+        _lib.check(_lib.load().ctu_int4_unpack_s8(_ptr(_aligned(packed)), _ptr(out), rows, 2 * half,
+                                                  _stream(packed.device)))
+    return out
+
+
 def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=None, tile_policy=0):
     """bindings.cpp:167-260: signed packed-int4 weights [N, K/2] (even k in the low
     nibble), per-channel weight scale, per-token activation scale, fused epilogue.
     The tcgen05 kernel takes K % 32 == 0 and N % 8 == 0; other shapes allowed by the
     reference (K % 4 == 0, any N) are zero-padded here, as the reference pads its
-    N tail (bindings.cpp:229-255)."""
+    N tail (bindings.cpp:229-255).  From W4_WIDEN_MIN_ROWS rows on, the weight is widened
+    to int8 once and the W8A8 GEMM runs (identical results: the contraction is exact)."""
     activation = activation.contiguous()
     weight = weight.contiguous()
     activation_scale = activation_scale.to(torch.float32).contiguous()
@@ -241,9 +258,15 @@ def turing_w4a8_linear(activation, weight, activation_scale, weight_scale, bias=
         return out[:, :n]
     activation, weight = _aligned(activation), _aligned(weight)
     with torch.cuda.device(dev):
-        _lib.check(_lib.load().ctu_w4a8_linear(
-            _ptr(activation), _ptr(weight), _ptr(activation_scale), _ptr(weight_scale), n_pad,
-            _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+        if m >= W4_WIDEN_MIN_ROWS:
+            wide = _widen_s4(weight)
+            _lib.check(_lib.load().ctu_int8_linear(
+                _ptr(activation), _ptr(wide), _ptr(activation_scale), _ptr(weight_scale), n_pad,
+                _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+        else:
+            _lib.check(_lib.load().ctu_w4a8_linear(
+                _ptr(activation), _ptr(weight), _ptr(activation_scale), _ptr(weight_scale), n_pad,
+                _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
     return out if n_pad == n else out[:, :n].contiguous()
 
 
@@ -382,7 +405,8 @@ def int4_linear(qactivation, qweight, activation_scale, wscales, bias=None, out_
     [N, K/2], per-token activation scale, per-channel weight scale (the 1-D ``wscales``
     the plugin registry requires, dispatch.py:1031-1034), optional bias; same fused
     epilogue as int8_linear.  Stands in for comfy-kitchen's ``int4_linear`` that
-    ``convrot_w4a4_linear(linear_dtype="int4")`` calls (dispatch.py:927-934)."""
+    ``convrot_w4a4_linear(linear_dtype="int4")`` calls (dispatch.py:927-934).  From
+    W4_WIDEN_MIN_ROWS rows on, both operands are widened to int8 and the W8A8 GEMM runs."""
     qactivation = qactivation.contiguous()
     qweight = qweight.contiguous()
     activation_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
@@ -420,9 +444,15 @@ def int4_linear(qactivation, qweight, activation_scale, wscales, bias=None, out_
     out = torch.empty((m, n_pad), dtype=torch.bfloat16, device=dev)
     if m > 0 and n > 0:
         with torch.cuda.device(dev):
-            _lib.check(_lib.load().ctu_w4a4_linear(
-                _ptr(_aligned(qactivation)), _ptr(_aligned(qweight)), _ptr(activation_scale), _ptr(wscales), n_pad,
-                _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+            if m >= W4_WIDEN_MIN_ROWS:
+                a8, w8 = _widen_s4(qactivation), _widen_s4(qweight)
+                _lib.check(_lib.load().ctu_int8_linear(
+                    _ptr(a8), _ptr(w8), _ptr(activation_scale), _ptr(wscales), n_pad,
+                    _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
+            else:
+                _lib.check(_lib.load().ctu_w4a4_linear(
+                    _ptr(_aligned(qactivation)), _ptr(_aligned(qweight)), _ptr(activation_scale), _ptr(wscales),
+                    n_pad, _ptr(bias), _ptr(out), m, n_pad, k_pad, _stream(dev)))
     out = out if n_pad == n else out[:, :n].contiguous()
     return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 

@@ -20,6 +20,7 @@
 #include "dequant.cuh"
 #include "gemm_i8.cuh"
 #include "host.cuh"
+#include "unpack_s4.cuh"
 #include "ptx.cuh"
 
 namespace ctu {
@@ -641,6 +642,22 @@ int ctu_codebook_w4a8_linear(const int8_t *a, const int8_t *w_packed, const floa
         args.out_mode = ctu::gemm::kOutBf16;
         if (int rc = launch_gemm(a, workspace, args, dev.device, dev.num_sms, s)) return rc;
     }
+    return CTU_OK;
+}
+
+int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream) {
+    if (rows < 0 || k < 0) return fail(CTU_ERR_INVALID_ARGUMENT, "int4 unpack dimensions must be non-negative");
+    if (k % 32 != 0) return fail(CTU_ERR_INVALID_ARGUMENT, "int4 unpack requires K divisible by 32");
+    if (rows == 0 || k == 0) return CTU_OK;
+    if (!packed || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(packed) || !aligned16(out)) return fail(CTU_ERR_INVALID_ARGUMENT, "tensors must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    const int64_t items = rows * (k / 32);
+    const int threads = 256;
+    const int grid = static_cast<int>(std::min<int64_t>((items + threads - 1) / threads, static_cast<int64_t>(dev.num_sms) * 8));
+    ctu::w4::unpack_s4_kernel<<<grid, threads, 0, static_cast<cudaStream_t>(stream)>>>(packed, out, items);
+    CTU_CUDA(cudaGetLastError());
     return CTU_OK;
 }
 

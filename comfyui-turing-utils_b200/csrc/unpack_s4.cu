@@ -1,0 +1,30 @@
+// Packed signed int4 -> int8 (sign-extended), for the W4 linears at long sequences: once
+// the weight (and, for W4A4, the activation) is widened, the W8A8 CTA-pair GEMM runs at
+// its full rate, and the widening is a streaming pass of 0.5 byte in + 1 byte out per value
+// (w4a8.cu:34-72 packing: even column in the low nibble, two's complement nibbles).
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gemm_tile.cuh"
+#include "unpack_s4.cuh"
+
+namespace ctu {
+namespace w4 {
+
+__global__ void __launch_bounds__(256) unpack_s4_kernel(const int8_t *packed, int8_t *out, int64_t items) {
+    // One item = 16 packed bytes -> 32 int8 values; rows are contiguous, so the items of
+    // the whole [rows, k/2] tensor are one flat range (k % 32 == 0).
+    for (int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < items;
+         item += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const uint4 p = *reinterpret_cast<const uint4 *>(packed + item * 16);
+        const uint2 w0 = gemm::unpack_s4x8(p.x), w1 = gemm::unpack_s4x8(p.y);
+        const uint2 w2 = gemm::unpack_s4x8(p.z), w3 = gemm::unpack_s4x8(p.w);
+        uint4 *dst = reinterpret_cast<uint4 *>(out + item * 32);
+        dst[0] = make_uint4(w0.x, w0.y, w1.x, w1.y);
+        dst[1] = make_uint4(w2.x, w2.y, w3.x, w3.y);
+    }
+}
+
+}  // namespace w4
+}  // namespace ctu

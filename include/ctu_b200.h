@@ -158,6 +158,14 @@ CTU_API int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_
                                    int8_t *out, int64_t rows, int64_t k, int64_t group_size, void *stream);
 
 /*
+ * Packed signed int4 [rows, k/2] (even column in the low nibble, w4a8.cu:34-72) widened
+ * to int8 [rows, k].  k % 32 == 0; both tensors 16-byte aligned.  The W4 linears of the
+ * op layer use it at long sequences (widen, then ctu_int8_linear).  No reference
+ * counterpart (the reference widens inside its GEMM's shared-memory fill).
+ */
+CTU_API int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream);
+
+/*
  * int32 accumulator -> bf16: out[r, c] = bf16((float(acc[r, c]) * a_scale[r]) * w_scale[c]),
  * acc row stride acc_stride (>= cols), w_scale [cols] or scalar (w_scale_count = 1),
  * out bf16 [rows, cols] contiguous.

@@ -139,3 +139,46 @@ def test_bounded_wait_stops_both_ctas(C, kernel):
     torch.cuda.synchronize()
     assert torch.all(acc2 == k)
     assert _lib.device_error(0, clear=True) == 0
+
+
+def test_int4_unpack_matches_oracle(C):
+    from comfyui_turing_utils_kernel import _C as cabi
+
+    g = torch.Generator().manual_seed(17)
+    v = torch.randint(-8, 8, (67, 1536), generator=g, dtype=torch.int8)
+    packed = oracle.pack_int4(v.numpy())
+    wide = cabi._widen_s4(torch.from_numpy(packed).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(wide.cpu().numpy(), v.numpy())
+
+
+@pytest.mark.parametrize("mode", ["w4a8", "w4a4"])
+def test_fused_w4_kernels_at_long_sequences(C, kernel, mode):
+    # The op layer widens int4 operands from W4_WIDEN_MIN_ROWS rows on; the fused kernels
+    # (int4 widened in shared memory) stay reachable through the C ABI at any M.
+    import ctypes
+
+    from comfyui_turing_utils_kernel import _lib
+
+    m, n, k = 1000, 520, 1536
+    g = torch.Generator().manual_seed(23)
+    a = torch.randint(-128 if mode == "w4a8" else -7, 128 if mode == "w4a8" else 8, (m, k), generator=g,
+                      dtype=torch.int8)
+    w = torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.02 + 1e-3
+    w_s = torch.rand((n,), generator=g) * 0.03 + 1e-3
+    bias = torch.randn((n,), generator=g) * 0.05
+    wp = oracle.pack_int4(w.numpy())
+    act = a.numpy() if mode == "w4a8" else oracle.pack_int4(a.numpy())
+    dev = [torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in (act, wp, a_s.numpy(), w_s.numpy(), bias.numpy())]
+    out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    p = lambda t: ctypes.c_void_p(t.data_ptr())
+    fn = _lib.load().ctu_w4a8_linear if mode == "w4a8" else _lib.load().ctu_w4a4_linear
+    _lib.check(fn(p(dev[0]), p(dev[1]), p(dev[2]), p(dev[3]), n, p(dev[4]), p(out), m, n, k,
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    if mode == "w4a8":
+        ref = oracle.w4a8_linear(a.numpy(), wp, a_s.numpy(), w_s.numpy(), bias.numpy())
+    else:
+        ref = oracle.w4a4_linear(act, wp, a_s.numpy(), w_s.numpy(), bias.numpy())
+    assert np.array_equal(bf16_bits(out), ref)
