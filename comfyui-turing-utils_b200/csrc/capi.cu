@@ -142,8 +142,10 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const 
 }
 
 // ---------------------------------------------------------------------------- quantizer geometry
+enum QuantKind : int { kQuantTwoPass = 0, kQuantReg = 1, kQuantT4 = 2 };
+
 struct QuantPlan {
-    bool reg;  // register-resident kernel (whole rows per batch, one lane pair per group)
+    int kind;  // QuantKind
     int rows_per_batch;
     int warps;
     int box_rows;
@@ -152,24 +154,29 @@ struct QuantPlan {
 };
 
 // Which ConvRot quantizer runs: 0 chooses per width, 1 forces the two-pass kernel,
-// 2 forces the register-resident kernel where the width allows it (test hook
-// ctu_debug_set_quant_kernel).
+// 2 the register-resident (two lanes per group) kernel and 3 the four-lane transpose
+// kernel where the width allows them (test hook ctu_debug_set_quant_kernel).
 std::atomic<int> g_quant_kernel{0};
 
-// Register-resident plan: W warps hold 16 W groups, i.e. floor(16 W / groups) whole
-// rows.  At 255 registers a thread, an SM holds floor(8 / W) such CTAs; the plan
-// maximises the share of the SM's 128 lane-pair slots that hold a group.
-bool plan_quant_reg(int64_t k, int act, int smem_optin, QuantPlan *plan) {
+// Whole-row plans: W warps hold `per_warp` x W groups, i.e. floor(per_warp W / groups)
+// rows; an SM holds floor(max_warps / W) such CTAs (register-limited) when their shared
+// memory fits.  The plan maximises the share of the SM's lane slots holding a group.
+bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *plan) {
     const int groups = static_cast<int>(k / 256);
-    if (groups > ctu::rot::kRegMaxGroups) return false;
+    const int per_warp = kind == kQuantT4 ? 8 : 16;
+    const int max_threads = kind == kQuantT4 ? ctu::rot::kT4MaxThreads : ctu::rot::kRegMaxThreads;
+    const int max_warps = kind == kQuantT4 ? 12 : 8;  // per SM at 168 / 255 registers a thread
+    if (groups > per_warp * max_threads / 32) return false;
     double best = -1.0;
-    for (int w = 1; w <= ctu::rot::kRegMaxThreads / 32; ++w) {
-        const int b = 16 * w / groups;
+    for (int w = 1; w <= max_threads / 32; ++w) {
+        const int b = per_warp * w / groups;
         if (b < 1) continue;
-        const int ctas = 8 / w;
-        const size_t smem = ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
-        if (smem > static_cast<size_t>(smem_optin) || smem * ctas > 228 * 1024) continue;
-        const double score = static_cast<double>(b * groups) / (16.0 * w) * (ctas * w) / 8.0;
+        const size_t smem = kind == kQuantT4 ? ctu::rot::quant_t4_smem_bytes(b, static_cast<int>(k), act, w)
+                                             : ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
+        if (smem > static_cast<size_t>(smem_optin)) continue;
+        const int ctas = std::min(max_warps / w, static_cast<int>((228 * 1024) / (smem + 1024)));
+        if (ctas < 1) continue;
+        const double score = static_cast<double>(b * groups) / (per_warp * w) * (ctas * w) / max_warps;
         if (score > best + 1e-9) {
             best = score;
             plan->rows_per_batch = b;
@@ -178,14 +185,21 @@ bool plan_quant_reg(int64_t k, int act, int smem_optin, QuantPlan *plan) {
         }
     }
     if (best < 0.0) return false;
-    plan->reg = true;
+    plan->kind = kind;
     ctu::rot::quant_copy_plan(plan->rows_per_batch, static_cast<int>(k), act, &plan->box_rows, &plan->copies);
     return true;
 }
 
 int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
-    if (g_quant_kernel.load(std::memory_order_relaxed) != 1 && plan_quant_reg(k, act, smem_optin, plan)) return CTU_OK;
-    plan->reg = false;
+    const int forced = g_quant_kernel.load(std::memory_order_relaxed);
+    // Measured on B200 (M = 32760): the four-lane kernel is 6-37 % faster with a fused
+    // SwiGLU / GELU input and 14-19 % faster for plain rows of K <= 3072; the two-lane
+    // kernel is 1-4 % faster for plain rows of K >= 5120.
+    const bool prefer_t4 = act != CTU_ACT_NONE || k <= 4096;
+    if ((forced == 3 || (forced == 0 && prefer_t4)) && plan_quant_rows(k, act, smem_optin, kQuantT4, plan))
+        return CTU_OK;
+    if (forced != 1 && plan_quant_rows(k, act, smem_optin, kQuantReg, plan)) return CTU_OK;
+    plan->kind = kQuantTwoPass;
     const int groups = static_cast<int>(k / 256);
     const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
     // Rows per batch: keep every lane pair busy (a warp owns 16 groups), at most 4
@@ -225,7 +239,9 @@ std::map<std::tuple<const void *, int, int, size_t>, int> g_quant_occupancy;
 template <int Act, int Bits>
 int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
                  const DeviceQuery &q, cudaStream_t stream) {
-    auto kernel = plan.reg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits> : ctu::rot::convrot_quant_kernel<Act, Bits>;
+    auto kernel = plan.kind == kQuantT4    ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
+                  : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
+                                           : ctu::rot::convrot_quant_kernel<Act, Bits>;
     const int threads = plan.warps * 32;
     const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), q.device, threads, plan.smem);
     int per_sm = 0;
@@ -704,7 +720,7 @@ int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *a
 }
 
 int ctu_debug_set_quant_kernel(int which) {
-    if (which < 0 || which > 2) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1 or 2");
+    if (which < 0 || which > 3) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1, 2 or 3");
     return g_quant_kernel.exchange(which);
 }
 

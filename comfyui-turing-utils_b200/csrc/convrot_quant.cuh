@@ -69,5 +69,23 @@ inline size_t quant_reg_smem_bytes(int rows, int k, int act) {
 template <int Act, int Bits>
 __global__ void convrot_quant_reg_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
+// Four-lane variant with a shared-memory transpose between rotation stages 2 and 3:
+// 8 groups per warp, whole rows per batch, at most kT4MaxThreads threads (168 registers:
+// at 128 it spills).
+constexpr int kT4MaxThreads = 384;
+constexpr int kT4MaxGroups = kT4MaxThreads / 4;
+
+// Dynamic shared memory of the four-lane variant for a batch of `rows` rows and `warps`
+// warps: input buffer, 8 KB of transpose area per warp, row statistics, one mbarrier.
+inline size_t quant_t4_smem_bytes(int rows, int k, int act, int warps) {
+    int box = 0, copies = 0;
+    quant_copy_plan(rows, k, act, &box, &copies);
+    const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
+    return 1024 + in_bytes + 8192 * static_cast<size_t>(warps) + 16 * static_cast<size_t>(rows) + 8;
+}
+
+template <int Act, int Bits>
+__global__ void convrot_quant_t4_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
+
 }  // namespace rot
 }  // namespace ctu

@@ -370,3 +370,39 @@ def test_w8_output_slices_reassemble_the_linear(C):
         parts = [d.convrot_w8_output_slice(q, s, w, w_s, bias, a, b, torch.bfloat16) for a, b in zip(cuts, cuts[1:])]
         torch.cuda.synchronize()
         assert torch.equal(torch.cat(parts, dim=1), full)
+
+
+def test_linears_capture_into_a_cuda_graph(C):
+    # The reference requires capture safety (no sync, no allocation inside capture,
+    # w4a8.cu:308-312).  After a first call per shape (which resolves launch attributes
+    # and the error word), quantize + GEMM for W8A8, widened W4A8 and codebook W4A8
+    # capture into one graph whose replays equal the eager results.
+    d = _dispatch()
+    m, k, n = 600, 1536, 264
+    x = activations(m, k, seed=61).cuda()
+    g = torch.Generator().manual_seed(62)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8).cuda()
+    w4 = torch.from_numpy(oracle.pack_int4(torch.randint(-8, 8, (n, k), generator=g, dtype=torch.int8).numpy())).cuda()
+    w_s = (torch.rand((n,), generator=g) * 0.009 + 1e-3).cuda()
+    bias = (torch.randn((n,), generator=g) * 0.02).cuda()
+
+    def run():
+        q, s = C.turing_bf16_int8_convrot_quantize(x, 256, False)
+        return (C.turing_int8_linear(q, w, s, w_s, bias), C.turing_w4a8_linear(q, w4, s, w_s, bias),
+                d.int8_linear(x, w, w_s, bias, convrot=True))
+
+    eager = run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()  # warm the caching allocator on the capture stream
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(graph):
+        captured = run()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, captured):
+        assert torch.equal(a, b)
