@@ -361,12 +361,144 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- configs[4]
+C4_BLOCKS = 40
+C4_TEXT = 512
+C4_DIM, C4_FFN = 5120, 13824
+
+
+def c4_ops(m_local: int) -> float:
+    """int8 ops of one configs[4] forward on m_local token rows: per block self Q/K/V/O,
+    cross Q/O (m_local rows), cross K/V (512 text rows) and FFN up/down."""
+    d, f = C4_DIM, C4_FFN
+    per_block = 2 * m_local * d * d * 6 + 2 * C4_TEXT * d * d * 2 + 2 * m_local * d * f * 2
+    return float(C4_BLOCKS * per_block)
+
+
+def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
+    """every quantized linear of a 40-block Wan-2.1-14B-shaped DiT forward on
+    one 32760-token sequence, token rows sharded across the ranks (strong scaling).  The
+    only exchange is NCCL's all-gather of the self-attention K and V projections (the
+    attention consumer needs the whole sequence): K's gather overlaps V's GEMM and both
+    complete before the O projection.  Attention and norms are not part of the workload
+    (they stay in bf16 torch in the reference); their outputs are stood in for by fixed
+    synthetic activations of the same shapes, so values do not drift across 40 blocks."""
+    import torch
+    import torch.distributed as dist
+
+    import comfyui_turing_utils_kernel as kops
+    from comfyui_turing_utils_kernel import _lib
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    m_total = args.m
+    per = -(-m_total // world)
+    m_local = max(0, min(per, m_total - rank * per))
+    d, f = C4_DIM, C4_FFN
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+
+    def act(rows, cols):
+        x = torch.randn((rows, cols), generator=g, device=dev)
+        idx = torch.randperm(cols, device=dev, generator=g)[: cols // 100]
+        x[:, idx] *= 30.0
+        return x.to(torch.bfloat16)
+
+    gw = torch.Generator(device=dev).manual_seed(4321)  # the same weights on every rank
+
+    def weight(n, k):
+        return (torch.randint(-127, 128, (n, k), generator=gw, dtype=torch.int8, device=dev),
+                torch.rand((n,), generator=gw, device=dev) * 0.009 + 1e-3,
+                torch.randn((n,), generator=gw, device=dev) * 0.02)
+
+    blocks = [{name: weight(n, k) for name, n, k in (("q", d, d), ("k", d, d), ("v", d, d), ("o", d, d),
+                                                     ("cq", d, d), ("ck", d, d), ("cv", d, d), ("co", d, d),
+                                                     ("up", f, d), ("down", d, f))} for _ in range(C4_BLOCKS)]
+    x_self, attn, x_cross, cross_attn, ffn_in = (act(m_local, d) for _ in range(5))
+    ffn_hidden = act(m_local, f)
+    text = act(C4_TEXT, d)
+    k_full = torch.empty((per * world, d), dtype=torch.bfloat16, device=dev)
+    v_full = torch.empty_like(k_full)
+
+    def linear(q, s, w):
+        return kops.turing_int8_linear(q, w[0], s, w[1], w[2])
+
+    def forward():
+        for blk in blocks:
+            q8, s8 = kops.turing_bf16_int8_convrot_quantize(x_self, 256)  # shared by Q, K, V
+            linear(q8, s8, blk["q"])
+            k = linear(q8, s8, blk["k"])
+            works = []
+            if world > 1:
+                kp = torch.nn.functional.pad(k, (0, 0, 0, per - m_local)) if m_local < per else k
+                works.append(dist.all_gather_into_tensor(k_full, kp, async_op=True))
+            v = linear(q8, s8, blk["v"])
+            if world > 1:
+                vp = torch.nn.functional.pad(v, (0, 0, 0, per - m_local)) if m_local < per else v
+                works.append(dist.all_gather_into_tensor(v_full, vp, async_op=True))
+                for w in works:
+                    w.wait()  # the attention consumer needs the whole sequence
+            linear(*kops.turing_bf16_int8_convrot_quantize(attn, 256), blk["o"])
+            linear(*kops.turing_bf16_int8_convrot_quantize(x_cross, 256), blk["cq"])
+            t8, ts = kops.turing_bf16_int8_convrot_quantize(text, 256)
+            linear(t8, ts, blk["ck"])
+            linear(t8, ts, blk["cv"])
+            linear(*kops.turing_bf16_int8_convrot_quantize(cross_attn, 256), blk["co"])
+            linear(*kops.turing_bf16_int8_convrot_quantize(ffn_in, 256), blk["up"])
+            linear(*kops.turing_bf16_gelu_int8_convrot_quantize(ffn_hidden, 256), blk["down"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        forward()
+    torch.cuda.synchronize(dev)
+    _lib.device_error(local_rank, clear=True)
+    barrier()
+    torch.cuda.synchronize(dev)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            forward()
+        stop.record()
+        torch.cuda.synchronize(dev)
+    barrier()
+    if _lib.device_error(local_rank, clear=True):
+        raise RuntimeError("kernel bounded-wait flags raised during the configs[4] run")
+    (elapsed_ms,) = max_over_ranks([start.elapsed_time(stop)], world, dev)
+    ms = elapsed_ms / args.steps
+    ops_all = torch.tensor([c4_ops(m_local)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ops_all)
+    ops = float(ops_all.item())
+    if rank != 0:
+        return
+    line = {
+        "metric": "configs[4] Wan-14B DiT forward: all ConvRot W8A8 linears, tokens/s", "value": m_total / (ms * 1e-3),
+        "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "tops": ops / (ms * 1e-3) / 1e12,
+        "config": {"workload": "configs[4]: 40 blocks x (self Q/K/V/O, cross Q/O, cross K/V on 512 text rows, "
+                               "FFN up/down with fused tanh-GELU), random-init W8A8 weights",
+                   "tokens": m_total, "tokens_per_rank": per, "blocks": C4_BLOCKS,
+                   "collective": "NCCL all-gather of self-attention K and V (bf16) per block" if world > 1 else None,
+                   "parallelism": f"token rows sharded over {world} rank(s)"},
+        "clocks": clocks.summary(),
+        "gpu_launches": C4_BLOCKS * 17 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["configs1", "configs4"], default="configs1",
+                    help="configs1: the metric's linear sweep (weak scaling); configs4: a whole DiT forward's "
+                         "linears on one sequence sharded over the ranks (strong scaling, K/V all-gather)")
     ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per GPU")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host round trip")
@@ -399,7 +531,10 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        run_b200(args, rank, world, local_rank)
+        if args.workload == "configs4":
+            run_configs4(args, rank, world, local_rank)
+        else:
+            run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist
