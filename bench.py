@@ -453,6 +453,25 @@ def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
     for _ in range(args.warmup):
         forward()
     torch.cuda.synchronize(dev)
+    graph = None
+    if args.graph:
+        # One CUDA graph per forward: 680 kernel launches and 80 collectives replayed
+        # without host work.  Captured after the eager warm-up (communicators, launch
+        # attributes and the error word exist), released before the process group.
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            forward()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        torch.cuda.synchronize(dev)
+        barrier()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            forward()
+        for _ in range(2):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+    run = graph.replay if graph is not None else forward
     _lib.device_error(local_rank, clear=True)
     barrier()
     torch.cuda.synchronize(dev)
@@ -460,9 +479,11 @@ def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
     with ClockSampler(local_rank) as clocks:
         start.record()
         for _ in range(args.steps):
-            forward()
+            run()
         stop.record()
         torch.cuda.synchronize(dev)
+    del graph
+    torch.cuda.synchronize(dev)
     barrier()
     if _lib.device_error(local_rank, clear=True):
         raise RuntimeError("kernel bounded-wait flags raised during the configs[4] run")
@@ -483,6 +504,7 @@ def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
                                "FFN up/down with fused tanh-GELU), random-init W8A8 weights",
                    "tokens": m_total, "tokens_per_rank": per, "blocks": C4_BLOCKS,
                    "collective": "NCCL all-gather of self-attention K and V (bf16) per block" if world > 1 else None,
+                   "launch": "one CUDA graph per forward" if args.graph else "eager",
                    "parallelism": f"token rows sharded over {world} rank(s)"},
         "clocks": clocks.summary(),
         "gpu_launches": C4_BLOCKS * 17 * args.steps,
@@ -496,6 +518,7 @@ def main():
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--graph", action="store_true", help="configs4: replay each forward as one CUDA graph")
     ap.add_argument("--workload", choices=["configs1", "configs4"], default="configs1",
                     help="configs1: the metric's linear sweep (weak scaling); configs4: a whole DiT forward's "
                          "linears on one sequence sharded over the ranks (strong scaling, K/V all-gather)")
