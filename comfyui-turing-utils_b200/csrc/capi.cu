@@ -301,12 +301,18 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
     constexpr int threads = kPair ? PL::kThreadCount
                                   : (kMode == ctu::gemm::kModeW8A8 ? ctu::gemm::kThreads : ctu::gemm::kThreadsW4);
     constexpr auto kernel = kPair ? ctu::gemm::int8_gemm_pair_kernel<kMode> : ctu::gemm::int8_gemm_kernel<kMode>;
-    static std::once_flag once;
-    static cudaError_t attr_status = cudaSuccess;
-    std::call_once(once, [] {
-        attr_status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    });
-    CTU_CUDA(attr_status);
+    // Function attributes belong to a device's context: set once per device.
+    static bool attr_set[kMaxDevices] = {};
+    bool need_attr = false;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        need_attr = !attr_set[device];
+    }
+    if (need_attr) {
+        CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        std::lock_guard<std::mutex> lock(g_mutex);
+        attr_set[device] = true;
+    }
     if constexpr (!kPair) {
         const int64_t tiles = ((args.m + kBM - 1) / kBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
         const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
