@@ -271,8 +271,56 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                               "format": "signed int4 weights, per-channel scale" +
                                         (", int8 activations" if bits == 8 else ", int4 ConvRot activations") +
                                         "; int4 operands widened to int8 ahead of the W8A8 GEMM (M >= 512)"}
+
+        def timed(fn, reps):
+            for _ in range(3):
+                fn()
+            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize(dev)
+            t0.record(stream)
+            for _ in range(reps):
+                fn()
+            t1.record(stream)
+            torch.cuda.synchronize(dev)
+            return t0.elapsed_time(t1) / reps
+
+        # Grouped-codebook W4A8 (group 16, e4m3 scales, 16-entry codebook): decode to int8,
+        # then the W8A8 pair GEMM, per linear.
+        gc = torch.Generator(device=dev).manual_seed(77)
+        book = torch.arange(-8, 8, dtype=torch.float32, device=dev)
+        cb_layers = []
+        for k, n, _, w_s, b in layers:
+            codes = torch.randint(0, 256, (n, k // 2), generator=gc, dtype=torch.int32, device=dev).to(torch.uint8)
+            scales = torch.randint(0x40, 0x58, (n, k // 16), generator=gc, dtype=torch.int32, device=dev).to(torch.uint8)
+            cb_layers.append((k, codes.view(torch.int8), scales, w_s, b))
+
+        def codebook_step():
+            for k, codes, scales, w_s, b in cb_layers:
+                q, s = kops.turing_bf16_int8_convrot_quantize(xs[k], 256)
+                kops.turing_codebook_w4a8_linear(q, codes, s, scales, w_s, book, b, 16)
+
+        ms = timed(codebook_step, max(5, min(args.steps, 30)))
+        variants["codebook_w4a8"] = {"value": ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+                                     "format": "4-bit codes, e4m3 group-16 scales, 16-entry codebook, int8 "
+                                               "activations; decoded to int8 ahead of the W8A8 GEMM"}
+
+        # Fused-activation quantizers at the model's widths (GB/s of algorithmic bytes).
+        x_swiglu = torch.cat([xs[5120], xs[5120]], dim=1)
+        quant_cases = {
+            "swiglu_int8_k5120": (lambda: kops.turing_bf16_int8_convrot_quantize(x_swiglu, 256, swiglu=True),
+                                  m * (2 * 10240 + 5120 + 4)),
+            "gelu_int8_k13824": (lambda: kops.turing_bf16_gelu_int8_convrot_quantize(xs[13824], 256),
+                                 m * (2 * 13824 + 13824 + 4)),
+            "plain_int4_k5120": (lambda: kops.turing_bf16_int4_convrot_quantize(xs[5120], 256),
+                                 m * (2 * 5120 + 2560 + 4)),
+        }
+        qv = {}
+        for name, (fn, nbytes) in quant_cases.items():
+            ms = timed(fn, 20)
+            qv[name] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "us": ms * 1e3}
+        variants["quantizers"] = qv
         if _lib.device_error(local_rank, clear=True):
-            raise RuntimeError("kernel bounded-wait flags raised during the W4 variants")
+            raise RuntimeError("kernel bounded-wait flags raised during the variants")
 
     # ---------------------------------------------------------------- end-to-end (host buffers)
     # Every step copies its activations from pinned host memory and reads every output
