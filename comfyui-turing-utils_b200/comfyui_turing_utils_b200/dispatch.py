@@ -20,6 +20,39 @@ from comfyui_turing_utils_kernel import _C
 CONVROT_GROUP = 256
 _FUSED_ACTS = (None, "none", "swiglu", "gelu_tanh")
 
+BACKEND_NAME = "turing_utils_sm75"  # the registry name the plugin's callers look up (dispatch.py:19)
+# Reference decode chunk of the staged codebook path (dispatch.py:26); kept for planning callers.
+TURING_CODEBOOK_W4A8_CHUNK_ROWS = 4096
+_PREFLIGHTED_DEVICES: set[int] = set()
+_PREFLIGHTED_CODEBOOK_DEVICES: set[int] = set()
+
+
+def turing_int8_workspace_bytes(rows: int, output_channels: int) -> int:
+    """dispatch.py:32-43: global int32 workspace of the selected W8A8 path.  The B200 GEMM
+    fuses the epilogue at every size and never stages int32 accumulators: 0."""
+    return 0
+
+
+def turing_codebook_w4a8_workspace_bytes(input_channels: int, output_channels: int) -> int:
+    """dispatch.py:46-56: decoded-weight workspace of grouped W4A8.  The B200 op decodes
+    all output channels at once while they fit 256 MiB (``_C.CODEBOOK_WORKSPACE_BYTES``),
+    else in 8-row-aligned chunks of that size."""
+    if input_channels <= 0 or output_channels <= 0:
+        return 0
+    rows = _C._codebook_chunk_rows(1, int(output_channels), int(input_channels), 16, 0)
+    return rows * int(input_channels)
+
+
+def convrot_swiglu_channel_sharding_available() -> bool:
+    """dispatch.py:67-69: exact two-pass SwiGLU channel streaming is in the ABI."""
+    return hasattr(_C, "turing_swiglu_int8_convrot_quantize_scaled")
+
+
+def quantize_convrot_swiglu_with_scale(x: torch.Tensor, scale: torch.Tensor, group_size: int = 256) -> torch.Tensor:
+    """dispatch.py:450-465: one SwiGLU channel shard quantized with whole-row scales."""
+    return ops.turing_swiglu_int8_convrot_quantize_scaled(x.contiguous(), scale.reshape(-1).contiguous(),
+                                                          int(group_size))
+
 
 def _require(condition: bool, what: str) -> None:
     if not condition:
@@ -188,3 +221,77 @@ def convrot_w4a4_linear(
         qactivation, activation_scale = _quantize_int4(x2d, convrot_groupsize, input_act)
         output = _C.int4_linear(qactivation, qweight.contiguous(), activation_scale, wscales, bias, out_dtype=x.dtype)
     return output.reshape(*original_shape[:-1], qweight.shape[0])
+
+
+def is_supported_b200_device(device: torch.device) -> bool:
+    """The device check the preflights make (dispatch.py:89 checks for a Turing tensor-core
+    device): a CUDA device of compute capability 10.0, the only arch libctu_b200.so holds."""
+    if device.type != "cuda" or not torch.cuda.is_available():
+        return False
+    return torch.cuda.get_device_capability(device) == (10, 0)
+
+
+def preflight_w4a8(device: torch.device) -> None:
+    """dispatch.py:88-150: once per device, a numerical self-test of the signed W4A8 op and
+    of the ConvRot W4A8 linear (K = 256 and 8192, and a fused SwiGLU input)."""
+    if not is_supported_b200_device(device):
+        raise RuntimeError(f"unsupported device {device}")
+    if not hasattr(_C, "turing_w4a8_linear"):
+        raise RuntimeError("the installed comfyui-turing-utils-kernel does not provide W4A8")
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index in _PREFLIGHTED_DEVICES:
+        return
+    activation = ((torch.arange(3 * 64, device=device) % 23) - 11).to(torch.int8).reshape(3, 64)
+    weight_values = ((torch.arange(5 * 64, device=device) % 15) - 7).to(torch.int8).reshape(5, 64)
+    packed = ((weight_values[:, 0::2].to(torch.int32) & 0x0F) | ((weight_values[:, 1::2].to(torch.int32) & 0x0F) << 4)
+              ).to(torch.int8)
+    a_s = torch.linspace(0.01, 0.03, 3, device=device)
+    w_s = torch.linspace(0.02, 0.06, 5, device=device)
+    bias = torch.linspace(-0.2, 0.2, 5, dtype=torch.bfloat16, device=device)
+    out = ops.turing_w4a8_linear(activation, packed, a_s, w_s, bias)
+    ref = (activation.float() @ weight_values.float().t()) * a_s[:, None] * w_s[None, :] + bias.float()
+    if out.dtype != torch.bfloat16 or not torch.allclose(out.float(), ref, rtol=0.01, atol=0.01):
+        raise RuntimeError("packed W4A8 numerical self-test failed")
+    for hidden in (256, 8192):
+        x = (((torch.arange(3 * hidden, device=device) % 29) - 14).reshape(3, hidden).to(torch.bfloat16) / 16)
+        y = convrot_w4a4_linear(x, torch.zeros((5, hidden // 2), dtype=torch.int8, device=device),
+                                torch.ones((5,), dtype=torch.float32, device=device), linear_dtype="int8")
+        if y.dtype != torch.bfloat16 or not torch.isfinite(y).all():
+            raise RuntimeError(f"BF16 ConvRot W4A8 self-test failed for K={hidden}")
+    y = convrot_w4a4_linear(torch.zeros((3, 512), dtype=torch.bfloat16, device=device),
+                            torch.zeros((5, 128), dtype=torch.int8, device=device),
+                            torch.ones((5,), dtype=torch.float32, device=device), linear_dtype="int8",
+                            input_act="swiglu")
+    if y.dtype != torch.bfloat16 or not torch.isfinite(y).all():
+        raise RuntimeError("SwiGLU W4A8 BF16 self-test failed")
+    torch.cuda.synchronize(device)
+    _PREFLIGHTED_DEVICES.add(index)
+
+
+def preflight_codebook_w4a8(device: torch.device) -> None:
+    """dispatch.py:153-199: once per device, a numerical self-test of grouped-codebook W4A8
+    against a float decode + matmul (the reference's tolerances)."""
+    if not is_supported_b200_device(device):
+        raise RuntimeError(f"unsupported device {device}")
+    if not hasattr(_C, "turing_codebook_w4a8_linear"):
+        raise RuntimeError("the installed comfyui-turing-utils-kernel does not provide codebook W4A8")
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index in _PREFLIGHTED_CODEBOOK_DEVICES:
+        return
+    m, n, k, g = 3, 8, 64, 16
+    activation = ((torch.arange(m * k, device=device) % 23) - 11).to(torch.int8).reshape(m, k)
+    codes = (torch.arange(n * k, device=device) % 16).to(torch.int32).reshape(n, k)
+    packed = ((codes[:, 0::2] & 0x0F) | ((codes[:, 1::2] & 0x0F) << 4)).to(torch.int8)
+    codebook = torch.linspace(-0.95, 0.95, 16, dtype=torch.float32, device=device)
+    group_scale = torch.linspace(8.0, 32.0, n * (k // g), dtype=torch.float32, device=device).reshape(
+        n, k // g).to(torch.float8_e4m3fn)
+    c_s = torch.linspace(0.01, 0.03, n, dtype=torch.float32, device=device)
+    a_s = torch.linspace(0.02, 0.04, m, dtype=torch.float32, device=device)
+    bias = torch.linspace(-0.1, 0.1, n, dtype=torch.bfloat16, device=device)
+    out = ops.turing_codebook_w4a8_linear(activation, packed, a_s, group_scale, c_s, codebook, bias, g)
+    decoded = (codebook[codes] * group_scale.float().repeat_interleave(g, dim=1)).round().clamp(-127, 127)
+    ref = (activation.float() @ decoded.float().t()) * a_s[:, None] * c_s[None, :] + bias.float()
+    if out.dtype is not torch.bfloat16 or not torch.allclose(out.float(), ref, rtol=0.01, atol=0.02):
+        raise RuntimeError("codebook W4A8 numerical self-test failed")
+    _PREFLIGHTED_CODEBOOK_DEVICES.add(index)
+

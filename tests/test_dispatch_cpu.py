@@ -83,3 +83,52 @@ def test_w8_output_slice_rejects_out_of_range_intervals():
     for start, stop in ((-1, 4), (4, 4), (0, 9)):
         with pytest.raises(ValueError, match="outside the weight"):
             convrot_w8_output_slice(q, torch.ones(2), w, torch.ones(8), None, start, stop, torch.bfloat16)
+
+
+def test_workspace_helpers_report_the_b200_workspaces():
+    import comfyui_turing_utils_b200 as d
+
+    # The W8A8 GEMM never stages int32 accumulators (dispatch.py:32-43 returns the
+    # reference's M*N*4 staging size below 64 MiB).
+    assert d.turing_int8_workspace_bytes(4096, 5120) == 0
+    assert d.turing_int8_workspace_bytes(0, 5120) == 0
+    # Grouped W4A8 decodes all channels at once while their int8 weights fit 256 MiB.
+    assert d.turing_codebook_w4a8_workspace_bytes(5120, 5120) == 5120 * 5120
+    assert d.turing_codebook_w4a8_workspace_bytes(5376, 28672) == 28672 * 5376
+    # Above the budget: 8-row-aligned chunks of at most 256 MiB.
+    assert d.turing_codebook_w4a8_workspace_bytes(13824, 28672) == (256 * 2**20 // 13824) // 8 * 8 * 13824
+    assert d.turing_codebook_w4a8_workspace_bytes(13824, 28672) <= 256 * 2**20
+    assert d.turing_codebook_w4a8_workspace_bytes(0, 8) == 0
+    from comfyui_turing_utils_b200 import dispatch
+
+    assert dispatch.TURING_CODEBOOK_W4A8_CHUNK_ROWS == 4096
+
+
+def test_channel_sharding_probe_and_preflight_device_checks():
+    import comfyui_turing_utils_b200 as d
+
+    assert d.convrot_swiglu_channel_sharding_available()
+    # Without a B200 the preflights refuse the device, as the reference's do for
+    # non-Turing devices (dispatch.py:89-90,155-156).
+    if not torch.cuda.is_available():
+        with pytest.raises(RuntimeError, match="unsupported device"):
+            d.preflight_w4a8(torch.device("cuda", 0))
+        with pytest.raises(RuntimeError, match="unsupported device"):
+            d.preflight_codebook_w4a8(torch.device("cuda", 0))
+    with pytest.raises(RuntimeError, match="unsupported device"):
+        d.preflight_w4a8(torch.device("cpu"))
+
+
+def test_preflights_report_missing_kernels(monkeypatch):
+    # Mirrors tests/test_turing_policy.py:359-373 of the reference: a kernel package
+    # without the op fails the preflight with a message naming it.
+    import comfyui_turing_utils_b200 as d
+    from comfyui_turing_utils_b200 import dispatch
+
+    monkeypatch.setattr(dispatch, "is_supported_b200_device", lambda device: True)
+    monkeypatch.delattr(dispatch._C, "turing_w4a8_linear")
+    monkeypatch.delattr(dispatch._C, "turing_codebook_w4a8_linear")
+    with pytest.raises(RuntimeError, match="does not provide W4A8"):
+        d.preflight_w4a8(torch.device("cuda", 0))
+    with pytest.raises(RuntimeError, match="codebook W4A8"):
+        d.preflight_codebook_w4a8(torch.device("cuda", 0))

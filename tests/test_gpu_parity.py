@@ -406,3 +406,21 @@ def test_linears_capture_into_a_cuda_graph(C):
     torch.cuda.synchronize()
     for a, b in zip(eager, captured):
         assert torch.equal(a, b)
+
+
+def test_dispatch_preflights_and_scaled_swiglu_helper(C):
+    # dispatch.py:88-199 self-tests pass on the B200 ops; dispatch.py:450-465 quantizes
+    # a SwiGLU channel shard with whole-row scales, which must reproduce the codes of
+    # the unscaled op for the scales it computed.
+    d = _dispatch()
+    d.preflight_w4a8(torch.device("cuda", 0))
+    d.preflight_codebook_w4a8(torch.device("cuda", 0))
+    assert d.convrot_swiglu_channel_sharding_available()
+    m, half = 37, 1024
+    x = activations(m, 2 * half, seed=71).cuda()
+    q_full, s_full = d.quantize_convrot_swiglu_activation(x)
+    gate, up = x[:, :half], x[:, half:]
+    shard = torch.cat([gate[:, 256:768], up[:, 256:768]], dim=1)
+    q_shard = d.quantize_convrot_swiglu_with_scale(shard, s_full)
+    torch.cuda.synchronize()
+    assert torch.equal(q_shard, q_full[:, 256:768])
