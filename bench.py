@@ -319,6 +319,24 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             ms = timed(fn, 20)
             qv[name] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "us": ms * 1e3}
         variants["quantizers"] = qv
+
+        # Norm + AdaLN ops in front of the linears (MiniMax width 5376, Wan width 5120):
+        # one bf16 read and one bf16 write per element (GB/s of algorithmic bytes).
+        xn = torch.randn((m, 5376), generator=gc, device=dev).to(torch.bfloat16)
+        wn = torch.ones(5376, dtype=torch.bfloat16, device=dev)
+        sn = (torch.randn((1, 5376), generator=gc, device=dev) * 0.02).to(torch.bfloat16)
+        seg = torch.tensor([[0, m, 0]], dtype=torch.int32, device=dev)
+        s3 = (torch.randn((1, 1, 5120), generator=gc, device=dev) * 0.02).to(torch.bfloat16)
+        x3 = xs[5120].view(1, m, 5120)
+        nv = {}
+        for name, fn, nbytes in (
+                ("segmented_rms_adaln_bf16_k5376", lambda: kops.turing_segmented_rms_adaln(xn, wn, sn, sn, seg, 1e-6),
+                 m * 5376 * 4),
+                ("layer_norm_adaln_bf16_k5120", lambda: kops.turing_layer_norm_adaln(x3, s3, s3, 1e-6), m * 5120 * 4)):
+            ms = timed(fn, 20)
+            nv[name] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "us": ms * 1e3}
+        variants["norms"] = nv
+        del xn
         if _lib.device_error(local_rank, clear=True):
             raise RuntimeError("kernel bounded-wait flags raised during the variants")
 

@@ -13,6 +13,7 @@ stay truthful.
 from __future__ import annotations
 
 import ctypes
+import math
 
 import torch
 
@@ -396,6 +397,97 @@ def turing_dequantize_int8_bf16(accumulator, activation_scale, weight_scale, out
         _lib.check(_lib.load().ctu_dequantize_int8_bf16(
             _ptr(accumulator), acc_cols, _ptr(activation_scale), _ptr(weight_scale), weight_scale.numel(),
             _ptr(out), rows, output_columns, _stream(accumulator.device)))
+    return out
+
+
+_NORM_TYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def _check_float_like(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in _NORM_TYPES:
+        raise RuntimeError(f"{name} must be float16, bfloat16, or float32")
+
+
+def turing_segmented_rms_adaln(input, weight, scale, shift, segments, epsilon=1.0e-5):
+    """bindings.cpp:767-834: affine RMSNorm + segmented AdaLN, output like ``input``."""
+    input = input.contiguous()
+    weight = weight.contiguous()
+    segments = segments.contiguous()
+    _check_cuda_2d(input, "input")
+    _check_float_like(input, "input")
+    if not (weight.is_cuda and weight.dim() == 1 and weight.is_contiguous()):
+        raise RuntimeError("weight must be a contiguous 1D CUDA tensor")
+    if not (scale.is_cuda and scale.dim() == 2 and scale.stride(1) == 1):
+        raise RuntimeError("scale must be a CUDA matrix with contiguous rows")
+    if not (shift.is_cuda and shift.dim() == 2 and shift.stride(1) == 1):
+        raise RuntimeError("shift must be a CUDA matrix with contiguous rows")
+    if not (segments.is_cuda and segments.dim() == 2 and segments.is_contiguous()):
+        raise RuntimeError("segments must be a contiguous 2D CUDA tensor")
+    if segments.dtype != torch.int32 or segments.size(1) != 3:
+        raise RuntimeError("segments must be int32 [start, stop, modulation_row] triples")
+    dev = input.device
+    if not (weight.device == dev and scale.device == dev and shift.device == dev and segments.device == dev):
+        raise RuntimeError("all segmented RMSNorm+AdaLN tensors must use the same CUDA device")
+    if not (weight.dtype == input.dtype and scale.dtype == input.dtype and shift.dtype == input.dtype):
+        raise RuntimeError("weight, scale, and shift dtypes must match input")
+    rows, hidden = input.shape
+    if rows <= 0 or hidden <= 0:
+        raise RuntimeError("segmented RMSNorm+AdaLN input dimensions must be positive")
+    if weight.numel() != hidden:
+        raise RuntimeError("RMSNorm weight length must match the input hidden dimension")
+    if scale.size(0) <= 0 or scale.size(1) != hidden:
+        raise RuntimeError("scale must be [modulation_rows, hidden]")
+    if shift.shape != scale.shape:
+        raise RuntimeError("shift shape must match scale shape")
+    if segments.size(0) <= 0:
+        raise RuntimeError("segments must contain at least one row")
+    limit = 2**31 - 1
+    if rows > limit or hidden > limit or scale.stride(0) > limit or shift.stride(0) > limit:
+        raise RuntimeError("segmented RMSNorm+AdaLN dimensions exceed the CUDA kernel range")
+    if not (math.isfinite(epsilon) and epsilon > 0.0):
+        raise RuntimeError("RMSNorm epsilon must be finite and positive")
+    out = torch.empty_like(input)
+    with torch.cuda.device(dev):
+        _lib.check(_lib.load().ctu_segmented_rms_adaln(
+            _ptr(input), _ptr(weight), _ptr(scale), scale.stride(0), _ptr(shift), shift.stride(0), _ptr(segments),
+            segments.size(0), _ptr(out), rows, hidden, scale.size(0), float(epsilon), _NORM_TYPES[input.dtype],
+            _stream(dev)))
+    return out
+
+
+def turing_layer_norm_adaln(input, scale, shift, epsilon=1.0e-5):
+    """bindings.cpp:836-880: LayerNorm (fp32 Welford statistics) + Wan AdaLN."""
+    input = input.contiguous()
+    scale = scale.contiguous()
+    shift = shift.contiguous()
+    if not (input.is_cuda and input.dim() == 3):
+        raise RuntimeError("input must be contiguous CUDA [batch, sequence, hidden]")
+    _check_float_like(input, "input")
+    if not (scale.is_cuda and scale.dim() == 3):
+        raise RuntimeError("scale must be contiguous CUDA [batch, modulation_steps, hidden]")
+    if not (shift.is_cuda and shift.dim() == 3):
+        raise RuntimeError("shift must be contiguous CUDA [batch, modulation_steps, hidden]")
+    if not (input.device == scale.device and input.device == shift.device):
+        raise RuntimeError("LayerNorm+AdaLN tensors must use the same CUDA device")
+    if not (input.dtype == scale.dtype and input.dtype == shift.dtype):
+        raise RuntimeError("LayerNorm+AdaLN tensor dtypes must match")
+    if scale.shape != shift.shape:
+        raise RuntimeError("shift shape must match scale shape")
+    if scale.size(0) != input.size(0) or scale.size(2) != input.size(2):
+        raise RuntimeError("scale must match input batch and hidden dimensions")
+    batch, sequence, hidden = input.shape
+    if batch <= 0 or sequence <= 0 or hidden <= 0 or scale.size(1) <= 0:
+        raise RuntimeError("LayerNorm+AdaLN dimensions must be positive")
+    limit = 2**31 - 1
+    if batch * sequence > limit or sequence > limit or hidden > limit or scale.size(1) > limit:
+        raise RuntimeError("LayerNorm+AdaLN dimensions exceed the CUDA kernel range")
+    if not (math.isfinite(epsilon) and epsilon > 0.0):
+        raise RuntimeError("LayerNorm epsilon must be finite and positive")
+    out = torch.empty_like(input)
+    with torch.cuda.device(input.device):
+        _lib.check(_lib.load().ctu_layer_norm_adaln(
+            _ptr(input), _ptr(scale), _ptr(shift), _ptr(out), batch, sequence, hidden, scale.size(1),
+            float(epsilon), _NORM_TYPES[input.dtype], _stream(input.device)))
     return out
 
 

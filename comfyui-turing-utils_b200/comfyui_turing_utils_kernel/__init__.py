@@ -2,8 +2,8 @@
 
 Exports the ConvRot quantized-linear operations of the reference kernel package
 (kernel/comfyui_turing_utils_kernel/__init__.py:1-39) implemented by hand-written
-tcgen05/TMA CUDA kernels in libctu_b200.so.  Attention (``turing_sage``) and the
-norm kernels of the reference are outside this build's scope.
+tcgen05/TMA CUDA kernels in libctu_b200.so, and the two norm + AdaLN ops that feed
+them.  Attention (``turing_sage``) is outside this build's scope.
 """
 
 from .ops import (
@@ -16,6 +16,8 @@ from .ops import (
     turing_gelu_int4_convrot_quantize,
     turing_gelu_int8_convrot_quantize,
     turing_int8_linear,
+    turing_layer_norm_adaln,
+    turing_segmented_rms_adaln,
     turing_swiglu_int4_convrot_quantize,
     turing_swiglu_int8_convrot_quantize,
     turing_swiglu_int8_convrot_quantize_scaled,
@@ -36,6 +38,8 @@ __all__ = [
     "turing_gelu_int4_convrot_quantize",
     "turing_gelu_int8_convrot_quantize",
     "turing_int8_linear",
+    "turing_layer_norm_adaln",
+    "turing_segmented_rms_adaln",
     "turing_swiglu_int4_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize_scaled",

@@ -25,7 +25,7 @@ ACT_SWIGLU = 1
 ACT_GELU_TANH = 2
 
 # name -> (restype, argtypes)
-_vp, _i64, _i32, _u64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64
+_vp, _i64, _i32, _u64, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64, ctypes.c_float
 SIGNATURES = {
     "ctu_version": (_i32, []),
     "ctu_last_error": (ctypes.c_char_p, []),
@@ -40,6 +40,9 @@ SIGNATURES = {
     "ctu_w4a4_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int8_gemm_s32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
     "ctu_dequantize_int8_bf16": (_i32, [_vp, _i64, _vp, _vp, _i64, _vp, _i64, _i64, _vp]),
+    "ctu_segmented_rms_adaln": (_i32, [_vp, _vp, _vp, _i64, _vp, _i64, _vp, _i64, _vp, _i64, _i64, _i64, _f32, _i32,
+                                       _vp]),
+    "ctu_layer_norm_adaln": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ctu_debug_gemm_injected_timeout": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _u64, _vp]),
     "ctu_debug_set_gemm_kernel": (_i32, [_i32]),
     "ctu_debug_set_quant_kernel": (_i32, [_i32]),

@@ -316,3 +316,64 @@ def _turing_gelu_int4_convrot_quantize_fake(x, group_size=256):
         torch.empty((x.size(0), x.size(1) // 2), dtype=torch.int8, device=x.device),
         torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device),
     )
+
+
+# ops.py:388-425
+@torch.library.custom_op("turing_utils::segmented_rms_adaln", mutates_args=())
+def turing_segmented_rms_adaln(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    segments: torch.Tensor,
+    epsilon: float = 1.0e-5,
+) -> torch.Tensor:
+    """Fused affine RMSNorm and segmented AdaLN modulation."""
+    if x.device.type != "cuda":
+        raise RuntimeError("Segmented RMSNorm+AdaLN requires CUDA tensors")
+    if torch.cuda.get_device_capability(x.device) < (7, 5):
+        raise RuntimeError("Segmented RMSNorm+AdaLN requires sm75 or newer")
+    if x.dtype not in (torch.float16, torch.bfloat16, torch.float32):
+        raise TypeError("segmented RMSNorm+AdaLN input must be float16, bfloat16, or float32")
+    if x.ndim != 2:
+        raise ValueError("segmented RMSNorm+AdaLN input must be 2D [M, K]")
+    if weight.device != x.device or scale.device != x.device or shift.device != x.device:
+        raise ValueError("weight, scale, and shift must be on the input device")
+    weight = weight.to(dtype=x.dtype).contiguous()
+    scale = scale.to(dtype=x.dtype)
+    shift = shift.to(dtype=x.dtype)
+    if scale.stride(-1) != 1:
+        scale = scale.contiguous()
+    if shift.stride(-1) != 1:
+        shift = shift.contiguous()
+    if segments.device != x.device or segments.dtype != torch.int32:
+        raise ValueError("segments must be an int32 tensor on the input device")
+    return _C.turing_segmented_rms_adaln(x.contiguous(), weight, scale, shift, segments.contiguous(), epsilon)
+
+
+@turing_segmented_rms_adaln.register_fake
+def _turing_segmented_rms_adaln_fake(x, weight, scale, shift, segments, epsilon=1.0e-5):
+    return torch.empty_like(x)
+
+
+# ops.py:432-447
+@torch.library.custom_op("turing_utils::layer_norm_adaln", mutates_args=())
+def turing_layer_norm_adaln(
+    x: torch.Tensor,
+    scale: torch.Tensor,
+    shift: torch.Tensor,
+    epsilon: float = 1.0e-5,
+) -> torch.Tensor:
+    """Fused FP32-reduction LayerNorm and Wan AdaLN modulation."""
+    if x.device.type != "cuda" or torch.cuda.get_device_capability(x.device) < (7, 5):
+        raise RuntimeError("LayerNorm+AdaLN requires an sm75-or-newer CUDA tensor")
+    if x.dtype not in (torch.float16, torch.bfloat16, torch.float32) or x.ndim != 3:
+        raise TypeError("LayerNorm+AdaLN input must be 3D float16, bfloat16, or float32")
+    scale = scale.to(device=x.device, dtype=x.dtype).contiguous()
+    shift = shift.to(device=x.device, dtype=x.dtype).contiguous()
+    return _C.turing_layer_norm_adaln(x.contiguous(), scale, shift, epsilon)
+
+
+@turing_layer_norm_adaln.register_fake
+def _turing_layer_norm_adaln_fake(x, scale, shift, epsilon=1.0e-5):
+    return torch.empty_like(x)

@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
@@ -20,6 +21,7 @@
 #include "dequant.cuh"
 #include "gemm_i8.cuh"
 #include "host.cuh"
+#include "norm_adaln.cuh"
 #include "unpack_s4.cuh"
 #include "ptx.cuh"
 
@@ -236,12 +238,10 @@ int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
 // shape should come before any stream capture).
 std::map<std::tuple<const void *, int, int, size_t>, int> g_quant_occupancy;
 
-template <int Act, int Bits>
-int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
-                 const DeviceQuery &q, cudaStream_t stream) {
-    auto kernel = plan.kind == kQuantT4    ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
-                  : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
-                                           : ctu::rot::convrot_quant_kernel<Act, Bits>;
+using QuantKernel = void (*)(const CUtensorMap, const ctu::rot::QuantArgs);
+
+int launch_quant_kernel(QuantKernel kernel, const CUtensorMap &map, const ctu::rot::QuantArgs &args,
+                        const QuantPlan &plan, const DeviceQuery &q, cudaStream_t stream) {
     const int threads = plan.warps * 32;
     const auto key = std::make_tuple(reinterpret_cast<const void *>(kernel), q.device, threads, plan.smem);
     int per_sm = 0;
@@ -262,6 +262,15 @@ int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const 
     kernel<<<grid, threads, plan.smem, stream>>>(map, args);
     CTU_CUDA(cudaGetLastError());
     return CTU_OK;
+}
+
+template <int Act, int Bits>
+int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
+                 const DeviceQuery &q, cudaStream_t stream) {
+    const QuantKernel kernel = plan.kind == kQuantT4    ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
+                               : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
+                                                        : ctu::rot::convrot_quant_kernel<Act, Bits>;
+    return launch_quant_kernel(kernel, map, args, plan, q, stream);
 }
 
 // ---------------------------------------------------------------------------- GEMM launch
@@ -419,7 +428,7 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
     if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k_in / 64, 64,
                            static_cast<uint32_t>(plan.box_rows)))
         return rc;
-    ctu::rot::QuantArgs args;
+    ctu::rot::QuantArgs args{};
     args.codes = codes;
     args.scales = scales;
     args.given_scales = given_scales;
@@ -763,6 +772,70 @@ int ctu_dequantize_int8_bf16(const int32_t *acc, int64_t acc_stride, const float
                                                                   static_cast<__nv_bfloat16 *>(out), rows, cols);
     }
     CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
+int ctu_segmented_rms_adaln(const void *x, const void *weight, const void *scale, int64_t scale_stride,
+                            const void *shift, int64_t shift_stride, const int32_t *segments, int64_t segment_count,
+                            void *out, int64_t rows, int64_t hidden, int64_t param_rows, float epsilon, int dtype,
+                            void *stream) {
+    if (dtype < CTU_DTYPE_BF16 || dtype > CTU_DTYPE_FP32)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "norm input must be float16, bfloat16, or float32");
+    if (rows <= 0 || hidden <= 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "segmented RMSNorm+AdaLN input dimensions must be positive");
+    if (param_rows <= 0) return fail(CTU_ERR_INVALID_ARGUMENT, "scale must be [modulation_rows, hidden]");
+    if (segment_count <= 0) return fail(CTU_ERR_INVALID_ARGUMENT, "segments must contain at least one row");
+    if (rows > INT32_MAX || hidden > INT32_MAX || param_rows > INT32_MAX || segment_count > INT32_MAX ||
+        scale_stride < 0 || shift_stride < 0 || scale_stride > INT32_MAX || shift_stride > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "segmented RMSNorm+AdaLN dimensions exceed the CUDA kernel range");
+    if (!(std::isfinite(epsilon) && epsilon > 0.0f))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "RMSNorm epsilon must be finite and positive");
+    if (!x || !weight || !scale || !shift || !segments || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    ctu::norm::RmsArgs a{};
+    a.x = x;
+    a.weight = weight;
+    a.scale = scale;
+    a.shift = shift;
+    a.segments = segments;
+    a.out = out;
+    a.scale_stride = scale_stride;
+    a.shift_stride = shift_stride;
+    a.rows = static_cast<int>(rows);
+    a.hidden = static_cast<int>(hidden);
+    a.param_rows = static_cast<int>(param_rows);
+    a.segment_count = static_cast<int>(segment_count);
+    a.epsilon = epsilon;
+    CTU_CUDA(ctu::norm::launch_segmented_rms_adaln(a, dtype, static_cast<cudaStream_t>(stream)));
+    return CTU_OK;
+}
+
+int ctu_layer_norm_adaln(const void *x, const void *scale, const void *shift, void *out, int64_t batch,
+                         int64_t sequence, int64_t hidden, int64_t modulation_steps, float epsilon, int dtype,
+                         void *stream) {
+    if (dtype < CTU_DTYPE_BF16 || dtype > CTU_DTYPE_FP32)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "LayerNorm+AdaLN input must be float16, bfloat16, or float32");
+    if (batch <= 0 || sequence <= 0 || hidden <= 0 || modulation_steps <= 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "LayerNorm+AdaLN dimensions must be positive");
+    if (batch * sequence > INT32_MAX || sequence > INT32_MAX || hidden > INT32_MAX || modulation_steps > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "LayerNorm+AdaLN dimensions exceed the CUDA kernel range");
+    if (!(std::isfinite(epsilon) && epsilon > 0.0f))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "LayerNorm epsilon must be finite and positive");
+    if (!x || !scale || !shift || !out) return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    ctu::norm::LnArgs a{};
+    a.x = x;
+    a.scale = scale;
+    a.shift = shift;
+    a.out = out;
+    a.rows = batch * sequence;
+    a.sequence = static_cast<int>(sequence);
+    a.hidden = static_cast<int>(hidden);
+    a.modulation_steps = static_cast<int>(modulation_steps);
+    a.epsilon = epsilon;
+    CTU_CUDA(ctu::norm::launch_layer_norm_adaln(a, dtype, static_cast<cudaStream_t>(stream)));
     return CTU_OK;
 }
 

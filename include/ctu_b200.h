@@ -35,6 +35,11 @@ extern "C" {
 #define CTU_ACT_SWIGLU 1    /* x is [rows, 2k] = [gate | up]; silu(gate) * up */
 #define CTU_ACT_GELU_TANH 2 /* tanh-approximate GELU, rounded to bf16 */
 
+/* Storage types of the norm entry points (every floating tensor of one call). */
+#define CTU_DTYPE_BF16 0
+#define CTU_DTYPE_FP16 1
+#define CTU_DTYPE_FP32 2
+
 /* Library version, (major << 16) | (minor << 8) | patch. */
 CTU_API int ctu_version(void);
 
@@ -164,6 +169,35 @@ CTU_API int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_
  * counterpart (the reference widens inside its GEMM's shared-memory fill).
  */
 CTU_API int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream);
+
+/*
+ * Affine RMSNorm + segmented AdaLN (replaces turing_segmented_rms_adaln,
+ * kernel/csrc/bindings.cpp:767-834 -> kernel/csrc/turing/segmented_rms_adaln.cu:133-232,
+ * 288-340).  out[r, c] = ((x[r, c] * rsqrt(mean(x[r]^2) + epsilon)) * weight[c])
+ * * (1 + scale[m, c]) + shift[m, c], where m is the modulation row of the segment
+ * (start, stop, row) of `segments` that holds r (row 0 when none does or when the row is
+ * outside [0, param_rows)).  x and out are [rows, hidden]; scale and shift rows lie
+ * scale_stride / shift_stride elements apart.  dtype is CTU_DTYPE_*, the type of every
+ * floating tensor.  Bit-identical to the reference for the same inputs, including its
+ * choice between 16-byte vector and per-element order (by alignment and strides).
+ */
+CTU_API int ctu_segmented_rms_adaln(const void *x, const void *weight, const void *scale, int64_t scale_stride,
+                                    const void *shift, int64_t shift_stride, const int32_t *segments,
+                                    int64_t segment_count, void *out, int64_t rows, int64_t hidden,
+                                    int64_t param_rows, float epsilon, int dtype, void *stream);
+
+/*
+ * LayerNorm (no affine) + Wan AdaLN (replaces turing_layer_norm_adaln,
+ * kernel/csrc/bindings.cpp:836-880 -> kernel/csrc/turing/segmented_rms_adaln.cu:234-297,
+ * 365-407).  x and out are [batch, sequence, hidden]; scale and shift are
+ * [batch, modulation_steps, hidden]; token t of a batch uses modulation step
+ * min(t / g, modulation_steps - 1), g = sequence / modulation_steps (integer division),
+ * plus one when that does not divide sequence evenly.  out = round(round(normalized) *
+ * round(1 + scale) + shift), each round to the storage type.
+ */
+CTU_API int ctu_layer_norm_adaln(const void *x, const void *scale, const void *shift, void *out, int64_t batch,
+                                 int64_t sequence, int64_t hidden, int64_t modulation_steps, float epsilon,
+                                 int dtype, void *stream);
 
 /*
  * int32 accumulator -> bf16: out[r, c] = bf16((float(acc[r, c]) * a_scale[r]) * w_scale[c]),

@@ -17,6 +17,18 @@
  *   kernel/csrc/turing/w4a8.cu:474-525            epilogue ((acc*a_s)*w_s)+bias
  *   kernel/csrc/turing/bf16_epilogue.cu:105-113   epilogue (acc*a_s)*w_s
  *   kernel/csrc/turing/w4a8.cu:34-72              signed int4, low nibble first
+ *   kernel/csrc/turing/segmented_rms_adaln.cu:75-232   RMSNorm + segmented AdaLN
+ *   kernel/csrc/turing/segmented_rms_adaln.cu:82-107,234-297  LayerNorm + AdaLN
+ *
+ * The norms reproduce the reference's reduction tree exactly (per-thread
+ * partials over the 256-thread row mapping, the shfl_down warp tree, the
+ * in-order combine of 8 warps) with the contractions nvcc makes by default
+ * (a += b*c -> fma).  The one step this file cannot reproduce bit for bit is
+ * the device rsqrtf (a hardware approximation, max 2 ulp per the CUDA
+ * Programming Guide); here it is the correctly rounded 1/sqrt.  Tests of the
+ * norms against this file therefore allow one output ulp where the inverse
+ * differs, and pin the device kernels bit for bit to fixtures produced by the
+ * reference kernels themselves.
  *
  * The int32 contraction itself is exact integer arithmetic and lives in the
  * Python wrapper (torch._int_mm / numpy).
@@ -304,4 +316,173 @@ void ctu_oracle_codebook_decode(const int8_t *packed, const uint8_t *group_scale
 void ctu_oracle_set_threads(int threads) { omp_set_num_threads(threads > 0 ? threads : 1); }
 
 int ctu_oracle_get_threads(void) { return omp_get_max_threads(); }
+
+/* ---------------------------------------------------------------- norms */
+
+/* Storage types of the norm ops: 0 = bf16, 1 = fp16, 2 = fp32. */
+static inline float load_val(const void *p, long i, int dtype) {
+    if (dtype == 0) return bf16_to_f32(((const uint16_t *)p)[i]);
+    if (dtype == 1) {
+        _Float16 h;
+        memcpy(&h, (const uint16_t *)p + i, 2);
+        return (float)h;
+    }
+    return ((const float *)p)[i];
+}
+
+/* from_float<T> of segmented_rms_adaln.cu:44-60: RNE to the storage type. */
+static inline void store_val(void *p, long i, int dtype, float v) {
+    if (dtype == 0) {
+        ((uint16_t *)p)[i] = ctu_oracle_f32_to_bf16(v);
+    } else if (dtype == 1) {
+        const _Float16 h = (_Float16)v;
+        memcpy((uint16_t *)p + i, &h, 2);
+    } else {
+        ((float *)p)[i] = v;
+    }
+}
+
+static inline float round_to(float v, int dtype) {
+    if (dtype == 0) return round_bf16(v);
+    if (dtype == 1) return (float)(_Float16)v;
+    return v;
+}
+
+static inline float host_rsqrt(float v) { return (float)(1.0 / sqrt((double)v)); }
+
+/* segmented_rms_adaln.cu:114-131: first segment whose stop exceeds the row. */
+static int find_modulation_row(const int32_t *segments, int count, long row) {
+    int low = 0, high = count;
+    while (low < high) {
+        const int mid = low + (high - low) / 2;
+        if (row < segments[mid * 3 + 1]) high = mid; else low = mid + 1;
+    }
+    if (low >= count || row < segments[low * 3]) return -1;
+    return segments[low * 3 + 2];
+}
+
+/* warp_reduce_sum (segmented_rms_adaln.cu:75-81): shfl_down tree; a lane whose
+ * source is past lane 31 reads its own value. */
+static float warp_tree_sum(float *lane_val) {
+    float next[32];
+    for (int off = 16; off > 0; off >>= 1) {
+        for (int l = 0; l < 32; ++l) next[l] = lane_val[l] + (l + off < 32 ? lane_val[l + off] : lane_val[l]);
+        memcpy(lane_val, next, sizeof(next));
+    }
+    return lane_val[0];
+}
+
+/* segmented_rms_adaln.cu:133-232.  `vectorized` selects the reference's per-thread
+ * element order (16-byte vectors t, t+256, ... or columns t, t+256, ...), which the
+ * caller derives from the same alignment rule as the device launch (:308-313). */
+void ctu_oracle_segmented_rms_adaln(const void *x, const void *weight, const void *scale, const void *shift,
+                                    const int32_t *segments, void *out, long rows, int hidden, int param_rows,
+                                    long scale_stride, long shift_stride, int segment_count, float epsilon,
+                                    int dtype, int vectorized) {
+    const int width = dtype == 2 ? 4 : 8;
+#pragma omp parallel for schedule(static)
+    for (long row = 0; row < rows; ++row) {
+        const long base = row * (long)hidden;
+        const int mapped = find_modulation_row(segments, segment_count, row);
+        const int mod_row = mapped >= 0 && mapped < param_rows ? mapped : 0;
+        float warp_sums[8];
+        for (int w = 0; w < 8; ++w) {
+            float lane_sum[32];
+            for (int l = 0; l < 32; ++l) {
+                const int t = w * 32 + l;
+                float acc = 0.0f;
+                if (vectorized) {
+                    for (int j = t; j < hidden / width; j += 256)
+                        for (int item = 0; item < width; ++item) {
+                            const float v = load_val(x, base + (long)j * width + item, dtype);
+                            acc = fmaf(v, v, acc);
+                        }
+                } else {
+                    for (int c = t; c < hidden; c += 256) {
+                        const float v = load_val(x, base + c, dtype);
+                        acc = fmaf(v, v, acc);
+                    }
+                }
+                lane_sum[l] = acc;
+            }
+            warp_sums[w] = warp_tree_sum(lane_sum);
+        }
+        float total = 0.0f;
+        for (int w = 0; w < 8; ++w) total += warp_sums[w];
+        const float inv = host_rsqrt(total / (float)hidden + epsilon);
+        const long srow = (long)mod_row * scale_stride, hrow = (long)mod_row * shift_stride;
+        for (int c = 0; c < hidden; ++c) {
+            const float normalized = load_val(x, base + c, dtype) * inv;
+            const float modulated = normalized * load_val(weight, c, dtype);
+            const float result = fmaf(modulated, 1.0f + load_val(scale, srow + c, dtype), load_val(shift, hrow + c, dtype));
+            store_val(out, base + c, dtype, result);
+        }
+    }
+}
+
+typedef struct { float mean, m2; int count; } welford_t;
+
+/* welford_combine, segmented_rms_adaln.cu:89-105. */
+static welford_t welford_combine(welford_t left, welford_t right) {
+    if (right.count == 0) return left;
+    if (left.count == 0) return right;
+    const int count = left.count + right.count;
+    const float delta = right.mean - left.mean;
+    left.mean += delta * (float)right.count / (float)count;
+    left.m2 += right.m2 + delta * delta * (float)left.count * (float)right.count / (float)count;
+    left.count = count;
+    return left;
+}
+
+/* segmented_rms_adaln.cu:234-297: Welford per thread over columns t, t+256, ...,
+ * the shfl_down Welford tree, the in-order combine of 8 warps, then the
+ * bf16/fp16-rounded normalised value times the rounded (1 + scale) plus shift. */
+void ctu_oracle_layer_norm_adaln(const void *x, const void *scale, const void *shift, void *out, long batch,
+                                 long sequence, int hidden, int modulation_steps, float epsilon, int dtype) {
+    const long rows = batch * sequence;
+#pragma omp parallel for schedule(static)
+    for (long row = 0; row < rows; ++row) {
+        const long b = row / sequence, token = row - b * sequence;
+        long mtoken = 0;
+        if (modulation_steps > 1) {
+            const long repeats = sequence / modulation_steps;
+            const long group = repeats * modulation_steps == sequence ? repeats : repeats + 1;
+            mtoken = token / (group > 1 ? group : 1);
+            if (mtoken > modulation_steps - 1) mtoken = modulation_steps - 1;
+        }
+        const long base = row * (long)hidden;
+        const long mbase = (b * modulation_steps + mtoken) * (long)hidden;
+        welford_t warps[8];
+        for (int w = 0; w < 8; ++w) {
+            welford_t lane[32];
+            for (int l = 0; l < 32; ++l) {
+                welford_t st = {0.0f, 0.0f, 0};
+                for (int c = w * 32 + l; c < hidden; c += 256) {
+                    const float v = load_val(x, base + c, dtype);
+                    ++st.count;
+                    const float delta = v - st.mean;
+                    st.mean += delta / (float)st.count;
+                    st.m2 = fmaf(delta, v - st.mean, st.m2);
+                }
+                lane[l] = st;
+            }
+            welford_t next[32];
+            for (int off = 16; off > 0; off >>= 1) {
+                for (int l = 0; l < 32; ++l) next[l] = welford_combine(lane[l], l + off < 32 ? lane[l + off] : lane[l]);
+                memcpy(lane, next, sizeof(next));
+            }
+            warps[w] = lane[0];
+        }
+        welford_t st = {0.0f, 0.0f, 0};
+        for (int w = 0; w < 8; ++w) st = welford_combine(st, warps[w]);
+        const float mean = st.mean;
+        const float variance = st.m2 / (float)st.count;
+        const float inv = host_rsqrt(variance + epsilon);
+        for (int c = 0; c < hidden; ++c) {
+            const float normalized = round_to((load_val(x, base + c, dtype) - mean) * inv, dtype);
+            const float multiplier = round_to(1.0f + load_val(scale, mbase + c, dtype), dtype);
+            store_val(out, base + c, dtype, fmaf(normalized, multiplier, load_val(shift, mbase + c, dtype)));
+        }
+    }
+}
 

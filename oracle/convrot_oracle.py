@@ -14,6 +14,9 @@ Reference anchors (comfyui-turing-utils, kernel package 0.31.0):
   * epilogue: ``kernel/csrc/turing/w4a8.cu:474-525``, ``bf16_epilogue.cu:105-113``
   * signed int4 packing: ``kernel/csrc/turing/w4a8.cu:34-72``,
     ``kernel/scripts/validate_compatible.py:28-40``
+  * RMSNorm / LayerNorm + AdaLN: ``kernel/csrc/turing/segmented_rms_adaln.cu:75-297``
+    (exact reduction order; the device rsqrtf is replaced by a correctly rounded
+    1/sqrt, so results may differ from the device by one output ulp)
 """
 
 from __future__ import annotations
@@ -70,6 +73,11 @@ def _load():
         lib.ctu_oracle_rotate.restype = None
         lib.ctu_oracle_epilogue.argtypes = [vp, i64, vp, vp, i64, vp, vp, i64, i64, i32, i32]
         lib.ctu_oracle_epilogue.restype = None
+        lib.ctu_oracle_segmented_rms_adaln.argtypes = [vp, vp, vp, vp, vp, vp, i64, i32, i32, i64, i64, i32,
+                                                       ctypes.c_float, i32, i32]
+        lib.ctu_oracle_segmented_rms_adaln.restype = None
+        lib.ctu_oracle_layer_norm_adaln.argtypes = [vp, vp, vp, vp, i64, i64, i32, i32, ctypes.c_float, i32]
+        lib.ctu_oracle_layer_norm_adaln.restype = None
         lib.ctu_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         lib.ctu_oracle_f32_to_bf16.restype = ctypes.c_uint16
         _lib = lib
@@ -252,4 +260,46 @@ def codebook_w4a8_linear(a, w_packed, a_scale, group_scale, channel_scale, codeb
     W8A8 epilogue with the per-channel scale (w4a8.cu:1088-1182)."""
     w = codebook_decode(w_packed, group_scale, codebook, group_size)
     return int8_linear(a, w, a_scale, channel_scale, bias)
+
+
+# Storage-type codes of the norm ops (bf16 and fp16 travel as uint16 bit patterns).
+NORM_BF16, NORM_FP16, NORM_FP32 = 0, 1, 2
+
+
+def _norm_array(a: np.ndarray, dtype: int) -> np.ndarray:
+    want = np.float32 if dtype == NORM_FP32 else np.uint16
+    if a.dtype != want:
+        raise TypeError(f"norm oracle expects {want.__name__} storage for dtype code {dtype}")
+    return np.ascontiguousarray(a)
+
+
+def segmented_rms_adaln(x, weight, scale, shift, segments, epsilon: float, dtype: int, vectorized: bool,
+                        scale_stride: int | None = None, shift_stride: int | None = None,
+                        param_rows: int | None = None) -> np.ndarray:
+    """segmented_rms_adaln.cu:133-232.  x [rows, hidden]; weight [hidden]; scale/shift
+    [param_rows, stride] (rows `*_stride` elements apart, first `hidden` used);
+    segments int32 [S, 3].  ``vectorized`` is the reference launch's choice (:308-313)."""
+    x, weight = _norm_array(x, dtype), _norm_array(weight, dtype)
+    scale, shift = _norm_array(scale, dtype), _norm_array(shift, dtype)
+    segments = np.ascontiguousarray(segments, dtype=np.int32)
+    rows, hidden = x.shape
+    out = np.empty_like(x)
+    _load().ctu_oracle_segmented_rms_adaln(
+        _ptr(x), _ptr(weight), _ptr(scale), _ptr(shift), _ptr(segments), _ptr(out), rows, hidden,
+        param_rows if param_rows is not None else scale.shape[0],
+        scale_stride if scale_stride is not None else scale.shape[1],
+        shift_stride if shift_stride is not None else shift.shape[1], segments.shape[0], float(epsilon), dtype,
+        1 if vectorized else 0)
+    return out
+
+
+def layer_norm_adaln(x, scale, shift, epsilon: float, dtype: int) -> np.ndarray:
+    """segmented_rms_adaln.cu:234-297.  x [batch, sequence, hidden]; scale/shift
+    [batch, modulation_steps, hidden]."""
+    x, scale, shift = _norm_array(x, dtype), _norm_array(scale, dtype), _norm_array(shift, dtype)
+    batch, sequence, hidden = x.shape
+    out = np.empty_like(x)
+    _load().ctu_oracle_layer_norm_adaln(_ptr(x), _ptr(scale), _ptr(shift), _ptr(out), batch, sequence, hidden,
+                                        scale.shape[1], float(epsilon), dtype)
+    return out
 

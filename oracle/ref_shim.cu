@@ -165,4 +165,43 @@ int ref_swiglu_int8_convrot_quantize_scaled(const void *x, const void *scales, v
     });
 }
 
+namespace {
+Tensor::ScalarType float_type(int dtype) {
+    return dtype == 0 ? Tensor::BF16 : dtype == 1 ? Tensor::FP16 : Tensor::FP32;
+}
+}  // namespace
+
+// kernel/csrc/turing/segmented_rms_adaln.cu:288-340 (affine RMSNorm + segmented AdaLN).
+// dtype 0 = bf16, 1 = fp16, 2 = fp32; scale/shift rows are `*_stride` elements apart.
+int ref_segmented_rms_adaln(const void *x, const void *weight, const void *scale, const void *shift,
+                            const void *segments, void *out, int rows, int hidden, int param_rows,
+                            int scale_stride, int shift_stride, int segment_count, float epsilon, int dtype,
+                            void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        const Tensor::ScalarType t = float_type(dtype);
+        Tensor sc = view(const_cast<void *>(scale), {param_rows, hidden}, t);
+        sc.shape.dataStride = {scale_stride, 1};
+        Tensor sh = view(const_cast<void *>(shift), {param_rows, hidden}, t);
+        sh.shape.dataStride = {shift_stride, 1};
+        ref::turing_segmented_rms_adaln(view(const_cast<void *>(x), {rows, hidden}, t),
+                                        view(const_cast<void *>(weight), {hidden}, t), sc, sh,
+                                        view(const_cast<void *>(segments), {segment_count, 3}, Tensor::INT32),
+                                        view(out, {rows, hidden}, t), epsilon);
+    });
+}
+
+// kernel/csrc/turing/segmented_rms_adaln.cu:365-407 (LayerNorm + Wan AdaLN).
+int ref_layer_norm_adaln(const void *x, const void *scale, const void *shift, void *out, int batch, int sequence,
+                         int hidden, int modulation_steps, float epsilon, int dtype, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        const Tensor::ScalarType t = float_type(dtype);
+        ref::turing_layer_norm_adaln(view(const_cast<void *>(x), {batch, sequence, hidden}, t),
+                                     view(const_cast<void *>(scale), {batch, modulation_steps, hidden}, t),
+                                     view(const_cast<void *>(shift), {batch, modulation_steps, hidden}, t),
+                                     view(out, {batch, sequence, hidden}, t), epsilon);
+    });
+}
+
 }  // extern "C"

@@ -1,8 +1,9 @@
 """Generate golden vectors from the REFERENCE kernels (run on a B200 box).
 
 Loads ``oracle/_ref/libctu_ref.so`` -- the reference's own ConvRot quantizers, W8A8
-and W4A8 GEMMs and int32->bf16 epilogue (kernel/csrc/turing/{convrot_quant,w4a8,
-bf16_epilogue}.cu of comfyui-turing-utils 0.31.0), compiled from the reference tree
+and W4A8 GEMMs, int32->bf16 epilogue and norm + AdaLN kernels (kernel/csrc/turing/
+{convrot_quant,w4a8,bf16_epilogue,segmented_rms_adaln}.cu of comfyui-turing-utils
+0.31.0), compiled from the reference tree
 by ``oracle/Makefile`` -- runs them on seeded inputs and writes compressed ``.npz``
 fixtures.  The fixtures are committed under ``tests/golden/`` and pin the CPU oracle
 (``oracle/convrot_oracle.py``) in the CPU test suite.
@@ -33,9 +34,12 @@ def load_ref():
     lib.ref_dequantize_int8_bf16.argtypes = [vp, vp, vp, i32, vp, i32, i32, i32, vp]
     lib.ref_codebook_w4a8_linear.argtypes = [vp, vp, vp, vp, vp, vp, vp, vp, i32, vp, i32, i32, i32, i32, i32, i32, vp]
     lib.ref_swiglu_int8_convrot_quantize_scaled.argtypes = [vp, vp, vp, i32, i32, vp]
+    f32 = ctypes.c_float
+    lib.ref_segmented_rms_adaln.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, i32, vp]
+    lib.ref_layer_norm_adaln.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, vp]
     for name in ("ref_bf16_convrot_quantize", "ref_bf16_gelu_convrot_quantize", "ref_int8_linear",
                  "ref_w4a8_linear", "ref_dequantize_int8_bf16", "ref_codebook_w4a8_linear",
-                 "ref_swiglu_int8_convrot_quantize_scaled"):
+                 "ref_swiglu_int8_convrot_quantize_scaled", "ref_segmented_rms_adaln", "ref_layer_norm_adaln"):
         getattr(lib, name).restype = i32
     lib.ref_last_error.restype = ctypes.c_char_p
     return lib
@@ -168,15 +172,131 @@ def extra_cases(lib, out):
     np.savez_compressed(out / "extras.npz", **extras)
 
 
+# ----------------------------------------------------------------------------- norms
+NORM_TORCH = {0: torch.bfloat16, 1: torch.float16, 2: torch.float32}
+
+# (name, dtype code, rows, hidden, param_rows, scale_stride, x_offset, segments, epsilon)
+# segments: (start, stop, row) triples; rows outside every segment and rows mapped
+# past param_rows fall back to parameter row 0 in the reference kernel.
+RMS_CASES = [
+    ("bf16_h1024", 0, 37, 1024, 3, 1024, 0, [(0, 5, 2), (5, 20, 0), (20, 37, 1)], 1e-5),
+    ("bf16_h5376_minimax", 0, 9, 5376, 2, 5376, 0, [(0, 4, 1), (4, 9, 0)], 1e-6),
+    ("bf16_h200_gap", 0, 12, 200, 2, 200, 0, [(0, 3, 1), (5, 9, 7), (9, 12, 1)], 1e-5),
+    ("bf16_h1001_scalar", 0, 10, 1001, 2, 1001, 0, [(0, 10, 1)], 1e-5),
+    ("bf16_h1024_stride1040", 0, 11, 1024, 3, 1040, 0, [(0, 4, 2), (4, 11, 1)], 1e-5),
+    ("bf16_h1024_stride1036_scalar", 0, 11, 1024, 3, 1036, 0, [(0, 11, 2)], 1e-5),
+    ("bf16_h1024_broadcast", 0, 8, 1024, 4, 0, 0, [(0, 8, 3)], 1e-5),
+    ("bf16_h1024_misaligned", 0, 9, 1024, 2, 1024, 1, [(0, 9, 1)], 1e-5),
+    ("bf16_h20480_tail", 0, 3, 20480, 1, 20480, 0, [(0, 3, 0)], 1e-5),
+    ("fp16_h1024", 1, 13, 1024, 2, 1024, 0, [(0, 6, 1), (6, 13, 0)], 1e-5),
+    ("fp16_h970_scalar", 1, 7, 970, 1, 970, 0, [(0, 7, 0)], 1e-5),
+    ("fp32_h1024", 2, 13, 1024, 2, 1024, 0, [(0, 6, 1), (6, 13, 0)], 1e-5),
+    ("fp32_h1002_scalar", 2, 7, 1002, 1, 1002, 0, [(0, 7, 0)], 1e-5),
+    ("fp32_h9000_tail", 2, 3, 9000, 1, 9000, 0, [(0, 3, 0)], 1e-5),
+]
+
+# (name, dtype code, batch, sequence, hidden, modulation_steps, epsilon, input transform)
+LN_CASES = [
+    ("bf16_b2_s17_h1024", 0, 2, 17, 1024, 4, 1e-6, "plain"),
+    ("bf16_offset100", 0, 2, 17, 1024, 4, 1e-6, "offset100"),
+    ("bf16_offset1000", 0, 2, 17, 1024, 4, 1e-6, "offset1000"),
+    ("bf16_small", 0, 1, 9, 1024, 1, 1e-6, "eighth"),
+    ("bf16_h200", 0, 2, 5, 200, 5, 1e-5, "plain"),
+    ("bf16_h5120_wan", 0, 1, 6, 5120, 1, 1e-6, "plain"),
+    ("bf16_h1001_steps_gt_seq", 0, 1, 3, 1001, 5, 1e-5, "plain"),
+    ("bf16_h20000_tail", 0, 1, 2, 20000, 2, 1e-6, "offset100"),
+    ("fp16_b2_s7_h1024", 1, 2, 7, 1024, 3, 1e-5, "plain"),
+    ("fp32_b2_s7_h1024", 2, 2, 7, 1024, 3, 1e-5, "offset1000"),
+    ("fp32_h300", 2, 1, 4, 300, 2, 1e-5, "plain"),
+]
+
+
+def _norm_np(t: torch.Tensor) -> np.ndarray:
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.float32:
+        return t.numpy()
+    return t.view(torch.int16).numpy().view(np.uint16)
+
+
+def norm_special_rows(x: torch.Tensor) -> torch.Tensor:
+    """Rows 0-3 of a norm input: zeros, a NaN, an infinity, values whose squares overflow."""
+    x = x.clone()
+    if x.shape[0] >= 4:
+        x[0] = 0
+        x[1, 3] = float("nan")
+        x[2, 5] = float("inf")
+        x[3] = x[3].sign() * (3.0e38 if x.dtype != torch.float16 else 6.0e4)
+    return x
+
+
+def norm_cases(lib, out):
+    norms = {}
+    for idx, (name, code, rows, hidden, prow, stride, off, segs, eps) in enumerate(RMS_CASES):
+        dt = NORM_TORCH[code]
+        g = torch.Generator().manual_seed(6000 + idx)
+        x = (torch.randn((rows, hidden), generator=g) * 1.5).to(dt)
+        if idx == 0:
+            x = norm_special_rows(x)
+        w = (torch.randn((hidden,), generator=g) * 0.5 + 1.0).to(dt)
+        width = max(stride, hidden) if stride else hidden
+        scale = (torch.randn((prow if stride else 1, width), generator=g) * 0.1).to(dt)
+        shift = (torch.randn((prow if stride else 1, width), generator=g) * 0.1).to(dt)
+        seg = torch.tensor(segs, dtype=torch.int32)
+        xbuf = torch.zeros(rows * hidden + 8, dtype=dt, device="cuda")
+        xbuf[off:off + rows * hidden] = x.flatten().cuda()
+        xd = xbuf[off:off + rows * hidden]
+        wd, sd, hd, segd = w.cuda(), scale.cuda(), shift.cuda(), seg.cuda()
+        o = torch.empty((rows, hidden), dtype=dt, device="cuda")
+        check(lib, lib.ref_segmented_rms_adaln(p(xd), p(wd), p(sd), p(hd), p(segd), p(o), rows, hidden, prow, stride,
+                                               stride, len(segs), eps, code, stream()))
+        torch.cuda.synchronize()
+        key = f"rms_{name}"
+        norms[f"{key}__meta"] = np.array([code, rows, hidden, prow, stride, off], dtype=np.int64)
+        norms[f"{key}__eps"] = np.array([eps], dtype=np.float32)
+        norms[f"{key}__x"] = _norm_np(x)
+        norms[f"{key}__weight"] = _norm_np(w)
+        norms[f"{key}__scale"] = _norm_np(scale)
+        norms[f"{key}__shift"] = _norm_np(shift)
+        norms[f"{key}__segments"] = seg.numpy()
+        norms[f"{key}__out"] = _norm_np(o)
+    for idx, (name, code, batch, seq, hidden, steps, eps, transform) in enumerate(LN_CASES):
+        dt = NORM_TORCH[code]
+        g = torch.Generator().manual_seed(6500 + idx)
+        x = torch.randn((batch, seq, hidden), generator=g)
+        x = {"plain": x, "offset100": x + 100.0, "offset1000": x + 1000.0, "eighth": x * 0.125}[transform].to(dt)
+        if idx == 0:
+            x = norm_special_rows(x.view(batch * seq, hidden)).view(batch, seq, hidden)
+            x[1, 4] = 2.5  # a constant row: zero variance
+        scale = (torch.randn((batch, steps, hidden), generator=g) * 0.1).to(dt)
+        shift = (torch.randn((batch, steps, hidden), generator=g) * 0.1).to(dt)
+        xd, sd, hd = x.cuda(), scale.cuda(), shift.cuda()
+        o = torch.empty_like(xd)
+        check(lib, lib.ref_layer_norm_adaln(p(xd), p(sd), p(hd), p(o), batch, seq, hidden, steps, eps, code, stream()))
+        torch.cuda.synchronize()
+        key = f"ln_{name}"
+        norms[f"{key}__meta"] = np.array([code, batch, seq, hidden, steps], dtype=np.int64)
+        norms[f"{key}__eps"] = np.array([eps], dtype=np.float32)
+        norms[f"{key}__x"] = _norm_np(x)
+        norms[f"{key}__scale"] = _norm_np(scale)
+        norms[f"{key}__shift"] = _norm_np(shift)
+        norms[f"{key}__out"] = _norm_np(o)
+    np.savez_compressed(out / "norms.npz", **norms)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
-    ap.add_argument("--only", choices=["all", "extras"], default="all")
+    ap.add_argument("--only", choices=["all", "extras", "norms"], default="all")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     lib = load_ref()
     torch.cuda.init()
+    if args.only in ("all", "norms"):
+        norm_cases(lib, out)
+    if args.only == "norms":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
     extra_cases(lib, out)
     if args.only == "extras":
         print("golden vectors written to", out, file=sys.stderr)

@@ -128,3 +128,54 @@ def test_codebook_and_scaled_swiglu_match_reference():
     # expf (glibc vs CUDA) may move a code by one step in rare positions.
     assert np.abs(codes.astype(np.int32) - ref.astype(np.int32)).max() <= 1
     assert (codes != ref).mean() < 1e-3
+
+
+NORMS_PATH = GOLDEN / "norms.npz"
+
+
+def _norm_float(a: np.ndarray, code: int) -> np.ndarray:
+    import torch
+
+    if code == 2:
+        return a.astype(np.float64)
+    t = torch.from_numpy(np.ascontiguousarray(a)).view(torch.int16)
+    t = t.view(torch.bfloat16 if code == 0 else torch.float16)
+    return t.float().numpy().astype(np.float64)
+
+
+def _norm_nan(a: np.ndarray, code: int) -> np.ndarray:
+    if code == 2:
+        return np.isnan(a)
+    return (a.astype(np.uint32) & 0x7FFF) > (0x7F80 if code == 0 else 0x7C00)
+
+
+def _assert_norm_close(got, want, code, atol):
+    # The oracle's 1/sqrt is correctly rounded; the reference's device rsqrtf is within
+    # 2 ulp of it.  Everything else (reduction order, contractions, roundings) is exact.
+    gm, wm = _norm_nan(got, code), _norm_nan(want, code)
+    assert np.array_equal(gm, wm)
+    gf, wf = _norm_float(got, code)[~gm], _norm_float(want, code)[~wm]
+    assert np.all(np.abs(gf - wf) <= atol + 1e-6 * np.abs(wf))
+    if code != 2:
+        assert np.mean(got[~gm] == want[~wm]) >= 0.995
+
+
+@pytest.mark.skipif(not NORMS_PATH.exists(), reason="norm fixtures not generated")
+def test_norm_oracle_matches_reference_kernels():
+    z = np.load(NORMS_PATH)
+    names = sorted({k.split("__")[0] for k in z.files})
+    assert any(n.startswith("rms_") for n in names) and any(n.startswith("ln_") for n in names)
+    for name in names:
+        meta = [int(v) for v in z[f"{name}__meta"]]
+        eps = float(z[f"{name}__eps"][0])
+        code = meta[0]
+        if name.startswith("rms_"):
+            _, rows, hidden, prow, stride, off = meta
+            width = 4 if code == 2 else 8
+            vec = hidden % width == 0 and stride % width == 0 and off == 0
+            got = oracle.segmented_rms_adaln(z[f"{name}__x"], z[f"{name}__weight"], z[f"{name}__scale"],
+                                             z[f"{name}__shift"], z[f"{name}__segments"], eps, code, vec,
+                                             scale_stride=stride, shift_stride=stride, param_rows=prow)
+        else:
+            got = oracle.layer_norm_adaln(z[f"{name}__x"], z[f"{name}__scale"], z[f"{name}__shift"], eps, code)
+        _assert_norm_close(got, z[f"{name}__out"], code, atol={0: 2**-5, 1: 2**-8, 2: 1e-5}[code])
