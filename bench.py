@@ -415,6 +415,9 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     else:
         peak, peak_src = 2.0 * 1400.0, "2x fallback sustained bf16 1.4 PFLOP/s"
     hbm = peaks.get("hbm_gbs", 6650.0)
+    for entry in variants.get("norms", {}).values():
+        entry["frac"] = entry["value"] / hbm
+        entry["peak"] = hbm
 
     cpu = None
     if world == 1 and not args.skip_cpu:

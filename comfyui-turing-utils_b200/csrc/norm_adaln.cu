@@ -321,19 +321,8 @@ __device__ __forceinline__ void welford_push(Welford &s, float v) {
     s.m2 = __fmaf_rn(delta, __fsub_rn(v, s.mean), s.m2);
 }
 
-// Built for 4 resident rows per SM (<= 64 registers): the cache holds the raw storage
-// values, not their fp32 widening.
-template <typename T, int kCache>
-__global__ void __launch_bounds__(kRowThreads, 4) layer_norm_adaln_kernel(const LnArgs a) {
-    using E = Elem<T>;
-    __shared__ float warp_mean[kWarps];
-    __shared__ float warp_m2[kWarps];
-    __shared__ int warp_count[kWarps];
-
-    const int64_t row = blockIdx.x;
-    const int tid = static_cast<int>(threadIdx.x);
-    const int lane = tid & 31;
-    const int warp = tid >> 5;
+// Modulation row offset of token row `row` (segmented_rms_adaln.cu:248-257).
+__device__ __forceinline__ int64_t ln_modulation_offset(const LnArgs &a, int64_t row) {
     const int64_t batch = row / a.sequence;
     const int token = static_cast<int>(row - batch * a.sequence);
     int mtoken = 0;
@@ -342,21 +331,27 @@ __global__ void __launch_bounds__(kRowThreads, 4) layer_norm_adaln_kernel(const 
         const int group = repeats * a.modulation_steps == a.sequence ? repeats : repeats + 1;
         mtoken = min(token / max(group, 1), a.modulation_steps - 1);
     }
-    const T *x = static_cast<const T *>(a.x) + row * a.hidden;
-    const int64_t mod_off = (batch * a.modulation_steps + mtoken) * a.hidden;
+    return (batch * a.modulation_steps + mtoken) * a.hidden;
+}
 
+// Mean and 1/std of the row held in `row_s`, in the reference's order: Welford per
+// thread over columns t, t+256, ... (the first kSteps steps with the compile-time
+// reciprocal of the count), the shfl_down Welford tree, the in-order combine of the
+// 8 warps by warp 0.  Every thread of the CTA must call it.
+template <typename T, int kSteps, typename Load>
+__device__ __forceinline__ void ln_statistics(Load load, int hidden, float epsilon, float *warp_mean,
+                                              float *warp_m2, int *warp_count, float &mean, float &inv) {
+    using E = Elem<T>;
+    const int tid = static_cast<int>(threadIdx.x);
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
     Welford st{0.0f, 0.0f, 0};
-    T cache[kCache];
 #pragma unroll
-    for (int i = 0; i < kCache; ++i) {
+    for (int i = 0; i < kSteps; ++i) {
         const int c = tid + i * kRowThreads;
-        if (c < a.hidden) {
-            cache[i] = x[c];
-            welford_push_fixed(st, E::load(cache[i]), static_cast<float>(i + 1), 1.0f / static_cast<float>(i + 1));
-        }
+        if (c < hidden) welford_push_fixed(st, E::load(load(c)), static_cast<float>(i + 1), 1.0f / static_cast<float>(i + 1));
     }
-    for (int c = tid + kCache * kRowThreads; c < a.hidden; c += kRowThreads) welford_push(st, E::load(x[c]));
-
+    for (int c = tid + kSteps * kRowThreads; c < hidden; c += kRowThreads) welford_push(st, E::load(load(c)));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) {
         const Welford other{__shfl_down_sync(0xffffffffu, st.mean, off), __shfl_down_sync(0xffffffffu, st.m2, off),
@@ -369,8 +364,6 @@ __global__ void __launch_bounds__(kRowThreads, 4) layer_norm_adaln_kernel(const 
         warp_count[warp] = st.count;
     }
     __syncthreads();
-    // The in-order combine of the 8 warp partials is the same for every thread: one warp
-    // forms it and publishes the mean and 1/std.
     if (warp == 0) {
         st = Welford{0.0f, 0.0f, 0};
 #pragma unroll
@@ -378,33 +371,76 @@ __global__ void __launch_bounds__(kRowThreads, 4) layer_norm_adaln_kernel(const 
         __syncwarp();
         if (lane == 0) {
             warp_mean[0] = st.mean;
-            warp_m2[0] = rsqrtf(__fadd_rn(__fdiv_rn(st.m2, static_cast<float>(st.count)), a.epsilon));
+            warp_m2[0] = rsqrtf(__fadd_rn(__fdiv_rn(st.m2, static_cast<float>(st.count)), epsilon));
         }
     }
     __syncthreads();
-    const float mean = warp_mean[0];
-    const float inv = warp_m2[0];
+    mean = warp_mean[0];
+    inv = warp_m2[0];
+}
 
+// Rows of at most kLnSmemBytes: the row is staged in shared memory with 16-byte loads
+// (all of them in flight at once), the strided Welford pass reads it from there, and the
+// output pass reads it back as 16-byte vectors.
+template <typename T, int kSteps>
+__global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnArgs a) {
+    using E = Elem<T>;
+    extern __shared__ uint4 row_v[];
+    __shared__ float warp_mean[kWarps];
+    __shared__ float warp_m2[kWarps];
+    __shared__ int warp_count[kWarps];
+    const T *row_s = reinterpret_cast<const T *>(row_v);
+
+    const int64_t row = blockIdx.x;
+    const int tid = static_cast<int>(threadIdx.x);
+    const T *x = static_cast<const T *>(a.x) + row * a.hidden;
+    constexpr int W = Vec<T>::kWidth;
+    if (a.vector_in) {
+        const uint4 *xv = reinterpret_cast<const uint4 *>(x);
+        for (int j = tid; j < a.hidden / W; j += kRowThreads) row_v[j] = xv[j];
+    } else {
+        T *rw = reinterpret_cast<T *>(row_v);
+        for (int c = tid; c < a.hidden; c += kRowThreads) rw[c] = x[c];
+    }
+    __syncthreads();
+    float mean, inv;
+    ln_statistics<T, kSteps>([&](int c) { return row_s[c]; }, a.hidden, a.epsilon, warp_mean, warp_m2, warp_count,
+                             mean, inv);
+
+    const int64_t mod_off = ln_modulation_offset(a, row);
     const T *scale = static_cast<const T *>(a.scale) + mod_off;
     const T *shift = static_cast<const T *>(a.shift) + mod_off;
     T *out = static_cast<T *>(a.out) + row * a.hidden;
     if (a.vector_out) {
-        // The output is elementwise: 16-byte vectors t, t+256, ... (the row is in L1/L2).
-        const int nvec = a.hidden / Vec<T>::kWidth;
-        const uint4 *xv = reinterpret_cast<const uint4 *>(x);
         const uint4 *sv = reinterpret_cast<const uint4 *>(scale);
         const uint4 *hv = reinterpret_cast<const uint4 *>(shift);
         uint4 *ov = reinterpret_cast<uint4 *>(out);
-        for (int j = tid; j < nvec; j += kRowThreads) ov[j] = ln_vector<T>(xv[j], __ldg(sv + j), __ldg(hv + j), mean, inv);
-        return;
+        for (int j = tid; j < a.hidden / W; j += kRowThreads) ov[j] = ln_vector<T>(row_v[j], __ldg(sv + j), __ldg(hv + j), mean, inv);
+    } else {
+        for (int c = tid; c < a.hidden; c += kRowThreads)
+            out[c] = E::store(ln_output<T>(E::load(row_s[c]), mean, inv, E::load(scale[c]), E::load(shift[c])));
     }
-    auto emit = [&](int c, float v) { out[c] = E::store(ln_output<T>(v, mean, inv, E::load(scale[c]), E::load(shift[c]))); };
-#pragma unroll
-    for (int i = 0; i < kCache; ++i) {
-        const int c = tid + i * kRowThreads;
-        if (c < a.hidden) emit(c, E::load(cache[i]));
-    }
-    for (int c = tid + kCache * kRowThreads; c < a.hidden; c += kRowThreads) emit(c, E::load(x[c]));
+}
+
+// Rows larger than kLnSmemBytes: the same computation reading the row from global memory
+// in both passes.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_wide_kernel(const LnArgs a) {
+    using E = Elem<T>;
+    __shared__ float warp_mean[kWarps];
+    __shared__ float warp_m2[kWarps];
+    __shared__ int warp_count[kWarps];
+    const int64_t row = blockIdx.x;
+    const T *x = static_cast<const T *>(a.x) + row * a.hidden;
+    float mean, inv;
+    ln_statistics<T, 8>([&](int c) { return x[c]; }, a.hidden, a.epsilon, warp_mean, warp_m2, warp_count, mean,
+                        inv);
+    const int64_t mod_off = ln_modulation_offset(a, row);
+    const T *scale = static_cast<const T *>(a.scale) + mod_off;
+    const T *shift = static_cast<const T *>(a.shift) + mod_off;
+    T *out = static_cast<T *>(a.out) + row * a.hidden;
+    for (int c = static_cast<int>(threadIdx.x); c < a.hidden; c += kRowThreads)
+        out[c] = E::store(ln_output<T>(E::load(x[c]), mean, inv, E::load(scale[c]), E::load(shift[c])));
 }
 
 template <typename T, bool kVec>
@@ -427,13 +463,18 @@ cudaError_t launch_rms_t(const RmsArgs &a, cudaStream_t stream) {
 template <typename T>
 cudaError_t launch_ln_t(const LnArgs &a, cudaStream_t stream) {
     const int per_thread = (a.hidden + kRowThreads - 1) / kRowThreads;
+    const size_t bytes = (static_cast<size_t>(a.hidden) * sizeof(T) + 15) & ~size_t(15);
     const dim3 grid(static_cast<unsigned>(a.rows));
-    if (per_thread <= 8) {
-        layer_norm_adaln_kernel<T, 8><<<grid, kRowThreads, 0, stream>>>(a);
+    if (bytes > kLnSmemBytes) {
+        layer_norm_adaln_wide_kernel<T><<<grid, kRowThreads, 0, stream>>>(a);
+    } else if (per_thread <= 8) {
+        layer_norm_adaln_kernel<T, 8><<<grid, kRowThreads, bytes, stream>>>(a);
     } else if (per_thread <= 16) {
-        layer_norm_adaln_kernel<T, 16><<<grid, kRowThreads, 0, stream>>>(a);
+        layer_norm_adaln_kernel<T, 16><<<grid, kRowThreads, bytes, stream>>>(a);
+    } else if (per_thread <= 32) {
+        layer_norm_adaln_kernel<T, 32><<<grid, kRowThreads, bytes, stream>>>(a);
     } else {
-        layer_norm_adaln_kernel<T, kLnCacheValues><<<grid, kRowThreads, 0, stream>>>(a);
+        layer_norm_adaln_kernel<T, kLnSteps><<<grid, kRowThreads, bytes, stream>>>(a);
     }
     return cudaGetLastError();
 }
@@ -467,8 +508,8 @@ cudaError_t launch_segmented_rms_adaln(const RmsArgs &args, int type, cudaStream
 cudaError_t launch_layer_norm_adaln(const LnArgs &args, int type, cudaStream_t stream) {
     LnArgs a = args;
     const int width = type == kNormFp32 ? 4 : 8;
-    a.vector_out = a.hidden % width == 0 && aligned16(a.x) && aligned16(a.scale) && aligned16(a.shift) &&
-                   aligned16(a.out);
+    a.vector_in = a.hidden % width == 0 && aligned16(a.x);
+    a.vector_out = a.hidden % width == 0 && aligned16(a.scale) && aligned16(a.shift) && aligned16(a.out);
     switch (type) {
         case kNormBf16:
             return launch_ln_t<__nv_bfloat16>(a, stream);

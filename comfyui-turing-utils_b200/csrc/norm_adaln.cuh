@@ -14,7 +14,8 @@ enum NormType : int { kNormBf16 = 0, kNormFp16 = 1, kNormFp32 = 2 };
 
 constexpr int kRowThreads = 256;     // threads per row: fixes the reduction order
 constexpr int kRmsCacheVectors = 8;  // 16-byte vectors a thread keeps in registers
-constexpr int kLnCacheValues = 32;   // columns a thread keeps in registers (LayerNorm)
+constexpr int kLnSmemBytes = 48 * 1024;  // LayerNorm rows up to this size are staged in shared memory
+constexpr int kLnSteps = 96;              // Welford steps a thread takes with a compile-time reciprocal
 
 struct RmsArgs {
     const void *x;         // [rows, hidden]
@@ -43,7 +44,8 @@ struct LnArgs {
     int hidden;
     int modulation_steps;
     float epsilon;
-    int vector_out;     // 1 when the output pass may use 16-byte vectors (set by the launcher)
+    int vector_in;      // 1 when x rows may be read as 16-byte vectors (set by the launcher)
+    int vector_out;     // 1 when scale / shift / out may use 16-byte vectors (set by the launcher)
 };
 
 // True when the reference launch takes its 16-byte vector path

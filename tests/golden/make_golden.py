@@ -205,6 +205,7 @@ LN_CASES = [
     ("bf16_h5120_wan", 0, 1, 6, 5120, 1, 1e-6, "plain"),
     ("bf16_h1001_steps_gt_seq", 0, 1, 3, 1001, 5, 1e-5, "plain"),
     ("bf16_h20000_tail", 0, 1, 2, 20000, 2, 1e-6, "offset100"),
+    ("bf16_h30000_wide", 0, 1, 3, 30000, 1, 1e-5, "plain"),
     ("fp16_b2_s7_h1024", 1, 2, 7, 1024, 3, 1e-5, "plain"),
     ("fp32_b2_s7_h1024", 2, 2, 7, 1024, 3, 1e-5, "offset1000"),
     ("fp32_h300", 2, 1, 4, 300, 2, 1e-5, "plain"),

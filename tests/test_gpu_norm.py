@@ -153,7 +153,7 @@ def test_rms_matches_oracle(K, code, rows, hidden):
 
 @pytest.mark.parametrize("code,batch,seq,hidden,steps,offset",
                          [(0, 1, 2048, 5120, 1, 0.0), (0, 2, 300, 1536, 21, 100.0), (1, 2, 129, 2048, 4, 0.0),
-                          (2, 1, 100, 3000, 3, 1000.0)])
+                          (2, 1, 100, 3000, 3, 1000.0), (0, 1, 3, 30000, 1, 0.0), (2, 1, 5, 13000, 2, 10.0)])
 def test_layer_norm_matches_oracle(K, code, batch, seq, hidden, steps, offset):
     dt = TORCH_TYPES[code]
     g = torch.Generator().manual_seed(batch * seq + hidden + code)
