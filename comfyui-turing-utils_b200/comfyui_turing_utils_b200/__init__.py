@@ -16,7 +16,14 @@ from .dispatch import (
     turing_int8_workspace_bytes,
     w4a8_int8_linear,
 )
-from .fusions import convrot_w8_output_slice, convrot_weight_kind, is_turing_convrot_linear
+from .fusions import (
+    convrot_w8_output_slice,
+    convrot_weight_kind,
+    is_turing_convrot_linear,
+    normalized_segments,
+    segment_table,
+    segmented_rms_adaln,
+)
 
 __all__ = [
     "codebook_w4a8_linear",
@@ -27,6 +34,9 @@ __all__ = [
     "int8_linear",
     "int8_linear_from_quantized",
     "is_turing_convrot_linear",
+    "normalized_segments",
+    "segment_table",
+    "segmented_rms_adaln",
     "preflight_codebook_w4a8",
     "preflight_w4a8",
     "quantize_convrot_int8_activation",

@@ -4,12 +4,17 @@ Mirrors the format-level helpers of the reference plugin
 (comfyui_turing_utils/quantization/fusions.py:14-85): the same layout names and
 parameter checks decide which B200 kernel a ComfyUI ``QuantizedTensor`` weight maps
 to, and ``convrot_w8_output_slice`` evaluates a contiguous interval of output
-channels from an activation quantized once.  The helpers read only attributes
+channels from an activation quantized once.  The segmented RMSNorm + AdaLN wrapper
+(fusions.py:198-269) validates and caches the token-to-modulation segment table the
+norm kernel takes.  The helpers read only attributes
 (``_layout_cls`` and ``_params``), so they work on ComfyUI's tensors without
 importing ComfyUI.
 """
 
 from __future__ import annotations
+
+import functools
+import operator
 
 import torch
 
@@ -80,3 +85,59 @@ def convrot_w8_output_slice(
         bias=sliced_bias,
         out_dtype=output_dtype,
     )
+
+
+def normalized_segments(segments, rows: int, parameter_rows: int) -> tuple[int, ...]:
+    """fusions.py:198-222: validate (start, stop, modulation_row) triples that must cover
+    rows 0..rows-1 contiguously with rows inside the scale/shift table; return them flat."""
+    if rows <= 0 or parameter_rows <= 0:
+        raise ValueError("segmented RMSNorm+AdaLN dimensions must be positive")
+    flat: list[int] = []
+    cursor = 0
+    for segment in segments:
+        if len(segment) != 3:
+            raise ValueError("each modulation segment must contain start, stop, and row")
+        try:
+            start, stop, modulation_row = (operator.index(value) for value in segment)
+        except TypeError as exc:
+            raise ValueError("modulation segment values must be integers") from exc
+        if start != cursor or stop <= start:
+            raise ValueError("modulation segments must cover the input contiguously")
+        if modulation_row < 0 or modulation_row >= parameter_rows:
+            raise ValueError("modulation segment row is outside the scale/shift table")
+        flat.extend((start, stop, modulation_row))
+        cursor = stop
+    if cursor != rows:
+        raise ValueError("modulation segments must cover every input row")
+    return tuple(flat)
+
+
+@functools.lru_cache(maxsize=32)
+def _cached_segment_table(flat: tuple[int, ...], device_index: int) -> torch.Tensor:
+    # fusions.py:225-227: one int32 [S, 3] device table per distinct segmentation.
+    return torch.tensor(flat, dtype=torch.int32, device=torch.device("cuda", device_index)).view(-1, 3)
+
+
+def segment_table(segments, rows: int, parameter_rows: int, device: torch.device) -> torch.Tensor:
+    """fusions.py:230-238: the validated, cached device table of ``segments``."""
+    flat = normalized_segments(segments, rows, parameter_rows)
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    return _cached_segment_table(flat, index)
+
+
+def segmented_rms_adaln(norm, x: torch.Tensor, shift: torch.Tensor, scale: torch.Tensor, segments) -> torch.Tensor:
+    """fusions.py:241-269 without ComfyUI's weight casting: the affine RMSNorm ``norm``
+    (its ``weight`` -- ones when None -- and ``eps``; a bias is rejected) followed by
+    the segmented AdaLN modulation, on the B200 norm kernel."""
+    import comfyui_turing_utils_kernel as ops
+
+    weight = getattr(norm, "weight", None)
+    if getattr(norm, "bias", None) is not None:
+        raise RuntimeError("segmented RMSNorm+AdaLN does not support a biased norm")
+    if weight is None:
+        weight = torch.ones(x.shape[-1], dtype=x.dtype, device=x.device)
+    weight = weight.to(device=x.device, dtype=x.dtype)
+    scale = scale.to(device=x.device, dtype=x.dtype)
+    shift = shift.to(device=x.device, dtype=x.dtype)
+    table = segment_table(segments, x.shape[0], scale.shape[0], x.device)
+    return ops.turing_segmented_rms_adaln(x, weight, scale, shift, table, float(norm.eps))

@@ -132,3 +132,32 @@ def test_preflights_report_missing_kernels(monkeypatch):
         d.preflight_w4a8(torch.device("cuda", 0))
     with pytest.raises(RuntimeError, match="codebook W4A8"):
         d.preflight_codebook_w4a8(torch.device("cuda", 0))
+
+
+def test_segment_validation_follows_the_reference_rules():
+    # tests/test_turing_fusions.py:19-33 of the reference.
+    from comfyui_turing_utils_b200 import normalized_segments
+
+    assert normalized_segments([(0, 1, 2), (1, 7, 0), (7, 19, 1)], 19, 3) == (0, 1, 2, 1, 7, 0, 7, 19, 1)
+    with pytest.raises(ValueError, match="contiguously"):
+        normalized_segments([(0, 2, 0), (3, 4, 0)], 4, 1)
+    with pytest.raises(ValueError, match="outside"):
+        normalized_segments([(0, 4, 1)], 4, 1)
+    with pytest.raises(ValueError, match="every input row"):
+        normalized_segments([(0, 3, 0)], 4, 1)
+    with pytest.raises(ValueError, match="start, stop, and row"):
+        normalized_segments([(0, 4)], 4, 1)
+    with pytest.raises(ValueError, match="integers"):
+        normalized_segments([(0, 4.0, 0)], 4, 1)
+    with pytest.raises(ValueError, match="positive"):
+        normalized_segments([(0, 4, 0)], 4, 0)
+
+
+def test_segmented_norm_wrapper_rejects_a_biased_norm():
+    from types import SimpleNamespace
+
+    from comfyui_turing_utils_b200 import segmented_rms_adaln
+
+    norm = SimpleNamespace(weight=None, bias=torch.zeros(8), eps=1e-6)
+    with pytest.raises(RuntimeError, match="biased norm"):
+        segmented_rms_adaln(norm, torch.zeros((2, 8)), torch.zeros((1, 8)), torch.zeros((1, 8)), [(0, 2, 0)])

@@ -203,3 +203,78 @@ def test_norm_ops_reject_bad_arguments(K):
     with pytest.raises(RuntimeError, match="batch and hidden"):
         K.turing_layer_norm_adaln(x.view(1, 4, 256), torch.zeros((2, 1, 256), device="cuda", dtype=x.dtype),
                                   torch.zeros((2, 1, 256), device="cuda", dtype=x.dtype))
+
+
+REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libctu_ref.so"
+
+
+@pytest.mark.skipif(not REF_LIB.exists(), reason="reference kernels not built (make -C oracle ref)")
+def test_norm_kernels_against_reference_kernels_timing(K, capsys):
+    # The reference's own norm kernels (oracle/_ref, built for sm_100a) and the B200 ones on
+    # the same bf16 rows, timed with CUDA events back to back after warm-up: RMS + AdaLN
+    # must be faster, LayerNorm + AdaLN at least on par (both results bit-identical).
+    import sys
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import make_golden as mg
+
+    lib = mg.load_ref()
+    m, h = 32760, 5376
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn((m, h), generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.ones(h, dtype=torch.bfloat16, device="cuda")
+    s = (torch.randn((1, h), generator=g, device="cuda") * 0.02).to(torch.bfloat16)
+    seg = torch.tensor([[0, m, 0]], dtype=torch.int32, device="cuda")
+    out = torch.empty_like(x)
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps
+
+    p = mg.p
+    ours_rms = timed(lambda: K.turing_segmented_rms_adaln(x, w, s, s, seg, 1e-6))
+    ref_rms = timed(lambda: mg.check(lib, lib.ref_segmented_rms_adaln(p(x), p(w), p(s), p(s), p(seg), p(out), m, h, 1,
+                                                                       h, h, 1, 1e-6, 0, mg.stream())))
+    assert torch.equal(K.turing_segmented_rms_adaln(x, w, s, s, seg, 1e-6).view(torch.int16), out.view(torch.int16))
+    x3, s3, o3 = x.view(1, m, h), s.view(1, 1, h), out.view(1, m, h)
+    ours_ln = timed(lambda: K.turing_layer_norm_adaln(x3, s3, s3, 1e-6))
+    ref_ln = timed(lambda: mg.check(lib, lib.ref_layer_norm_adaln(p(x3), p(s3), p(s3), p(o3), 1, m, h, 1, 1e-6, 0,
+                                                                   mg.stream())))
+    assert torch.equal(K.turing_layer_norm_adaln(x3, s3, s3, 1e-6).view(torch.int16), o3.view(torch.int16))
+    with capsys.disabled():
+        print(f"\n[norm timing M={m} K={h} bf16] RMS+AdaLN {ours_rms * 1e3:.1f} us vs reference {ref_rms * 1e3:.1f} us; "
+              f"LayerNorm+AdaLN {ours_ln * 1e3:.1f} us vs reference {ref_ln * 1e3:.1f} us")
+    assert ours_rms < ref_rms
+    assert ours_ln < 1.25 * ref_ln
+
+
+def test_plugin_wrapper_builds_the_segment_table_and_runs_the_kernel(K):
+    # fusions.py:241-269: the norm module's weight / eps, a validated segment table.
+    from types import SimpleNamespace
+
+    import comfyui_turing_utils_b200 as d
+
+    rows, hidden = 19, 1024
+    g = torch.Generator().manual_seed(97)
+    x = torch.randn((rows, hidden), generator=g).to(torch.bfloat16).cuda()
+    w = (torch.randn((hidden,), generator=g) * 0.2 + 1).to(torch.bfloat16).cuda()
+    sc = (torch.randn((3, hidden), generator=g) * 0.1).to(torch.bfloat16).cuda()
+    sh = (torch.randn((3, hidden), generator=g) * 0.1).to(torch.bfloat16).cuda()
+    segs = [(0, 1, 2), (1, 7, 0), (7, rows, 1)]
+    y = d.segmented_rms_adaln(SimpleNamespace(weight=w, bias=None, eps=1e-6), x, sh, sc, segs)
+    table = d.segment_table(segs, rows, 3, x.device)
+    assert table is d.segment_table(segs, rows, 3, x.device)  # cached per segmentation and device
+    ref = K.turing_segmented_rms_adaln(x, w, sc, sh, torch.tensor(segs, dtype=torch.int32, device="cuda"), 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(y, ref)
+    unit = d.segmented_rms_adaln(SimpleNamespace(weight=None, bias=None, eps=1e-6), x, sh, sc, segs)
+    ref1 = K.turing_segmented_rms_adaln(x, torch.ones_like(w), sc, sh, table, 1e-6)
+    assert torch.equal(unit, ref1)
