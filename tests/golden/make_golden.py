@@ -8,7 +8,7 @@ by ``oracle/Makefile`` -- runs them on seeded inputs and writes compressed ``.np
 fixtures.  The fixtures are committed under ``tests/golden/`` and pin the CPU oracle
 (``oracle/convrot_oracle.py``) in the CPU test suite.
 
-Usage (GPU box):  python tests/golden/make_golden.py --out gpurun_out/golden
+Usage (on a B200):  python tests/golden/make_golden.py --out <directory> [--only extras|norms]
 """
 
 from __future__ import annotations
