@@ -417,6 +417,35 @@ int check_quantize_args(const void *x, int64_t rows, int64_t k, int act, int bit
     return CTU_OK;
 }
 
+// Per device: the activation tables of the SwiGLU / GELU quantizers (384 KiB), filled
+// on the first activation call on that device and kept until exit.  That call
+// synchronizes its stream once, so it must not be made during stream capture.
+struct ActTables {
+    float *silu = nullptr;
+    uint16_t *gelu = nullptr;
+};
+ActTables g_act_tables[kMaxDevices];
+
+int act_tables(int device, cudaStream_t stream, ActTables *out) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    ActTables &t = g_act_tables[device];
+    if (t.silu == nullptr) {
+        void *p = nullptr;
+        CTU_CUDA(cudaMalloc(&p, 65536 * (sizeof(float) + sizeof(uint16_t))));
+        ActTables fresh{static_cast<float *>(p), reinterpret_cast<uint16_t *>(static_cast<float *>(p) + 65536)};
+        ctu::rot::act_lut_fill_kernel<<<256, 256, 0, stream>>>(fresh.silu, fresh.gelu);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);  // other streams may read the tables next
+        if (e != cudaSuccess) {
+            cudaFree(p);
+            return cuda_fail(e, "activation table fill");
+        }
+        t = fresh;
+    }
+    *out = t;
+    return CTU_OK;
+}
+
 int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
                  uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales) {
     if (int rc = check_quantize_args(x, rows, k, act, bits, codes, given_scales ? given_scales : scales)) return rc;
@@ -438,6 +467,12 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
     args.rows_per_batch = plan.rows_per_batch;
     args.box_rows = plan.box_rows;
     args.copies = plan.copies;
+    if (act != CTU_ACT_NONE) {
+        ActTables tables;
+        if (int rc = act_tables(q.device, stream, &tables)) return rc;
+        args.silu_lut = tables.silu;
+        args.gelu_lut = tables.gelu;
+    }
     using ctu::rot::kActGelu;
     using ctu::rot::kActNone;
     using ctu::rot::kActSwiGLU;

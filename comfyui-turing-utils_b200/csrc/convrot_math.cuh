@@ -39,30 +39,46 @@ __device__ __forceinline__ void butterfly2(f32x2 &x0, f32x2 &x1, f32x2 &x2, f32x
 // as written by a TMA load with CU_TENSOR_MAP_SWIZZLE_128B.
 __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 128u + ((c ^ (r & 7u)) << 4); }
 
-template <int Act>
-__device__ __forceinline__ float activate(uint32_t gate_bits, uint32_t up_bits);
+// The reference's input activations (convrot_quant.cu:163-182) evaluated on one bf16
+// input given as fp32 bits: the SwiGLU gate factor gate / (1 + exp(-gate)) in fp32,
+// and tanh-GELU rounded back to bf16.  Only act_lut_fill_kernel evaluates them.
+__device__ __forceinline__ float silu_factor(float gate) { return gate / (1.0f + expf(-gate)); }
 
-template <>
-__device__ __forceinline__ float activate<kActNone>(uint32_t x, uint32_t) {
-    return __uint_as_float(x);
-}
-
-// convrot_quant.cu:163-169
-template <>
-__device__ __forceinline__ float activate<kActSwiGLU>(uint32_t gate_bits, uint32_t up_bits) {
-    const float gate = __uint_as_float(gate_bits);
-    const float up = __uint_as_float(up_bits);
-    return (gate / (1.0f + expf(-gate))) * up;
-}
-
-// convrot_quant.cu:171-182 (tanh-GELU, result rounded back to bf16)
-template <>
-__device__ __forceinline__ float activate<kActGelu>(uint32_t x_bits, uint32_t) {
-    const float x = __uint_as_float(x_bits);
+__device__ __forceinline__ float gelu_bf16(float x) {
     constexpr float kAlpha = 0.7978845608028654f;
     constexpr float kBeta = 0.044715f;
     const float activated = 0.5f * x * (1.0f + tanhf(kAlpha * (x + kBeta * x * x * x)));
     return __bfloat162float(__float2bfloat16_rn(activated));
+}
+
+// Both activations take a bf16 input, so each is a function of 65536 bit patterns:
+// act_lut_fill_kernel evaluates them once per device into these tables (the SwiGLU
+// gate factor as fp32, GELU as bf16 bits), and the quantizers look the values up
+// instead of evaluating expf / tanhf per element.  The tables hold exactly the values
+// the expressions give, so the codes are unchanged.
+struct ActLut {
+    const float *silu;     // [65536] gate / (1 + expf(-gate)), indexed by the gate's bf16 bits
+    const uint16_t *gelu;  // [65536] bf16 bits of tanh-GELU, indexed by the input's bf16 bits
+};
+
+template <int Act>
+__device__ __forceinline__ float activate(uint32_t gate_bits, uint32_t up_bits, const ActLut &lut);
+
+template <>
+__device__ __forceinline__ float activate<kActNone>(uint32_t x, uint32_t, const ActLut &) {
+    return __uint_as_float(x);
+}
+
+// (gate / (1 + expf(-gate))) * up (convrot_quant.cu:163-169)
+template <>
+__device__ __forceinline__ float activate<kActSwiGLU>(uint32_t gate_bits, uint32_t up_bits, const ActLut &lut) {
+    return __fmul_rn(__ldg(lut.silu + (gate_bits >> 16)), __uint_as_float(up_bits));
+}
+
+// bf16(tanh-GELU(x)) (convrot_quant.cu:171-182)
+template <>
+__device__ __forceinline__ float activate<kActGelu>(uint32_t x_bits, uint32_t, const ActLut &lut) {
+    return __uint_as_float(static_cast<uint32_t>(__ldg(lut.gelu + (x_bits >> 16))) << 16);
 }
 
 // Load one lane's 128 inputs of a group: chunk0 = elements h*64+[0,64) (bit 7 = 0),
@@ -70,7 +86,8 @@ __device__ __forceinline__ float activate<kActGelu>(uint32_t x_bits, uint32_t) {
 // batch buffer; chunk1 sits two slices later.  For SwiGLU the `up` half of the row
 // starts `up_off` slices after the gate.  v[j] = (chunk0[j], chunk1[j]).
 template <int Act>
-__device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&v)[64]) {
+__device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&v)[64],
+                                           const ActLut &lut) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         const uint4 a = *reinterpret_cast<const uint4 *>(buf + sw128(row64, c));
@@ -84,15 +101,15 @@ __device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, u
             const uint32_t ubw[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, uaw[q] << 16), activate<Act>(bw[q] << 16, ubw[q] << 16));
-                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, uaw[q] & 0xFFFF0000u),
-                                           activate<Act>(bw[q] & 0xFFFF0000u, ubw[q] & 0xFFFF0000u));
+                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, uaw[q] << 16, lut), activate<Act>(bw[q] << 16, ubw[q] << 16, lut));
+                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, uaw[q] & 0xFFFF0000u, lut),
+                                           activate<Act>(bw[q] & 0xFFFF0000u, ubw[q] & 0xFFFF0000u, lut));
             }
         } else {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, 0), activate<Act>(bw[q] << 16, 0));
-                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, 0), activate<Act>(bw[q] & 0xFFFF0000u, 0));
+                v[8 * c + 2 * q] = pk2(activate<Act>(aw[q] << 16, 0, lut), activate<Act>(bw[q] << 16, 0, lut));
+                v[8 * c + 2 * q + 1] = pk2(activate<Act>(aw[q] & 0xFFFF0000u, 0, lut), activate<Act>(bw[q] & 0xFFFF0000u, 0, lut));
             }
         }
     }

@@ -48,9 +48,9 @@ namespace rot {
 // active = false, computes on a valid group and writes nothing.
 template <int Act>
 __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint32_t up_off, int h, bool active,
-                                             float &absmax, float &nan_probe) {
+                                             float &absmax, float &nan_probe, const ActLut &lut) {
     f32x2 v[64];
-    load_group<Act>(buf, row64, up_off, v);
+    load_group<Act>(buf, row64, up_off, v, lut);
     const f32x2 half = pk2(0.5f, 0.5f);
 
     // Stage 1 (stride 1): bits 0-1 of the element index.
@@ -202,7 +202,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             const int grp = task - r * groups;
             const uint32_t row64 = r * slices_per_row + grp * 4 + h;
             float amax, probe;
-            rotate_group<Act>(inbuf[buf], row64, static_cast<uint32_t>(K / 64), h, active, amax, probe);
+            rotate_group<Act>(inbuf[buf], row64, static_cast<uint32_t>(K / 64), h, active, amax, probe,
+                              ActLut{args.silu_lut, args.gelu_lut});
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             probe = __fadd_rn(probe, __shfl_xor_sync(0xffffffffu, probe, 1));
             if (active && h == 0) {
@@ -272,6 +273,16 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         }
     }
     if (tid == 0) bulk_wait_all();
+}
+
+// One thread per bf16 bit pattern: the SwiGLU gate factor and the rounded tanh-GELU
+// of every bf16 value, exactly as the activations define them (silu_factor, gelu_bf16).
+__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= 65536u) return;
+    const float x = __uint_as_float(i << 16);
+    silu[i] = silu_factor(x);
+    gelu[i] = static_cast<uint16_t>(__float_as_uint(gelu_bf16(x)) >> 16);
 }
 
 template __global__ void convrot_quant_kernel<kActNone, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);

@@ -26,7 +26,13 @@ struct QuantArgs {
     int rows_per_batch;  // rows per shared-memory batch
     int box_rows;        // 128-byte slices per TMA copy (a multiple of 8: 1024-byte aligned copies)
     int copies;          // TMA copies per batch; copies * box_rows >= rows_per_batch * k_in / 64
+    // Activation tables (act_lut_fill_kernel), set for the SwiGLU and GELU quantizers.
+    const float *silu_lut;     // [65536] fp32
+    const uint16_t *gelu_lut;  // [65536] bf16 bits
 };
+
+// Fills the activation tables: launch 256 blocks of 256 threads.
+__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu);
 
 // Slices (128 bytes = 64 bf16) per TMA copy and copies per batch.  Every copy
 // starts on a 1024-byte boundary, as the 128-byte swizzle pattern requires.

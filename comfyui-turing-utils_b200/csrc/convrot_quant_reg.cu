@@ -178,6 +178,7 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
     const int pair = tid >> 1;
     const int h = tid & 1;
     const bool given = args.given_scales != nullptr;  // uniform: a kernel argument
+    const ActLut lut{args.silu_lut, args.gelu_lut};
     bool alive = true;
 
     for (int it = 0;; ++it) {
@@ -196,7 +197,7 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
         if (alive) alive = mbar_wait(full, static_cast<uint32_t>(it & 1), nullptr, args.err, kErrTimeoutFull);
         f32x2 v[64];
         if (warp_busy && alive)
-            load_group<Act>(inbuf, r * slices_per_row + grp * 4 + h, static_cast<uint32_t>(K / 64), v);
+            load_group<Act>(inbuf, r * slices_per_row + grp * 4 + h, static_cast<uint32_t>(K / 64), v, lut);
         __syncthreads();  // the batch is in registers: the buffer may be refilled
         if (tid == 0 && alive) {
             const int next = batch + gridDim.x;

@@ -65,7 +65,8 @@ __device__ __forceinline__ float4 ld_shared_f32x4(uint32_t addr) {
 // Phase A load: lane q's 64 inputs of the group (slice row64 of the batch buffer);
 // P[j] = (element j, element j + 32) of the slice.
 template <int Act>
-__device__ __forceinline__ void t4_load(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&P)[32]) {
+__device__ __forceinline__ void t4_load(const uint8_t *buf, uint32_t row64, uint32_t up_off, f32x2 (&P)[32],
+                                        const ActLut &lut) {
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
         const uint4 a = *reinterpret_cast<const uint4 *>(buf + sw128(row64, c));
@@ -79,15 +80,15 @@ __device__ __forceinline__ void t4_load(const uint8_t *buf, uint32_t row64, uint
             const uint32_t ubw[4] = {ub.x, ub.y, ub.z, ub.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, uaw[i] << 16), activate<Act>(bw[i] << 16, ubw[i] << 16));
-                P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, uaw[i] & 0xFFFF0000u),
-                                           activate<Act>(bw[i] & 0xFFFF0000u, ubw[i] & 0xFFFF0000u));
+                P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, uaw[i] << 16, lut), activate<Act>(bw[i] << 16, ubw[i] << 16, lut));
+                P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, uaw[i] & 0xFFFF0000u, lut),
+                                           activate<Act>(bw[i] & 0xFFFF0000u, ubw[i] & 0xFFFF0000u, lut));
             }
         } else {
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, 0), activate<Act>(bw[i] << 16, 0));
-                P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, 0), activate<Act>(bw[i] & 0xFFFF0000u, 0));
+                P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, 0, lut), activate<Act>(bw[i] << 16, 0, lut));
+                P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, 0, lut), activate<Act>(bw[i] & 0xFFFF0000u, 0, lut));
             }
         }
     }
@@ -206,6 +207,7 @@ __global__ void __launch_bounds__(kT4MaxThreads, 1)
     const int num_batches = (args.m + B - 1) / B;
     const uint32_t slices_per_batch = static_cast<uint32_t>(B) * slices_per_row;
     const bool given = args.given_scales != nullptr;  // uniform: a kernel argument
+    const ActLut lut{args.silu_lut, args.gelu_lut};
 
     auto issue_load = [&](int batch) {
         mbar_arrive_expect_tx(full, in_bytes);
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(kT4MaxThreads, 1)
         if (alive) alive = mbar_wait(full, static_cast<uint32_t>(it & 1), nullptr, args.err, kErrTimeoutFull);
         f32x2 P[32];
         if (warp_busy && alive)
-            t4_load<Act>(inbuf, r * slices_per_row + grp * 4 + q, static_cast<uint32_t>(K / 64), P);
+            t4_load<Act>(inbuf, r * slices_per_row + grp * 4 + q, static_cast<uint32_t>(K / 64), P, lut);
         __syncthreads();  // the batch is in registers: the buffer may be refilled
         if (tid == 0 && alive) {
             const int next = batch + gridDim.x;
