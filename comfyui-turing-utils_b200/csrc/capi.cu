@@ -194,10 +194,11 @@ bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *pl
 
 int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
     const int forced = g_quant_kernel.load(std::memory_order_relaxed);
-    // Measured on B200 (M = 32760): the four-lane kernel is 6-37 % faster with a fused
-    // SwiGLU / GELU input and 14-19 % faster for plain rows of K <= 3072; the two-lane
-    // kernel is 1-4 % faster for plain rows of K >= 5120.
-    const bool prefer_t4 = act != CTU_ACT_NONE || k <= 4096;
+    // Measured on B200 (M = 32760, activations from the tables): the four-lane kernel is
+    // 14-19 % faster for plain rows of K <= 3072 and 4-8 % faster with a fused SwiGLU /
+    // GELU input at K = 5120; the two-lane kernel is 1-4 % faster for plain rows of
+    // K >= 5120 and 2-8 % faster with a fused input at K = 13824.
+    const bool prefer_t4 = k <= 4096 || (act != CTU_ACT_NONE && k <= 8192);
     if ((forced == 3 || (forced == 0 && prefer_t4)) && plan_quant_rows(k, act, smem_optin, kQuantT4, plan))
         return CTU_OK;
     if (forced != 1 && plan_quant_rows(k, act, smem_optin, kQuantReg, plan)) return CTU_OK;
