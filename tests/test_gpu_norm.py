@@ -278,3 +278,38 @@ def test_plugin_wrapper_builds_the_segment_table_and_runs_the_kernel(K):
     unit = d.segmented_rms_adaln(SimpleNamespace(weight=None, bias=None, eps=1e-6), x, sh, sc, segs)
     ref1 = K.turing_segmented_rms_adaln(x, torch.ones_like(w), sc, sh, table, 1e-6)
     assert torch.equal(unit, ref1)
+
+
+def test_norms_and_fused_activation_quantizers_capture_into_a_cuda_graph(K):
+    # No allocation and no synchronization inside the calls: after one eager call per
+    # shape (which also fills the activation tables), norm + quantize chains capture.
+    rows, hidden = 300, 5120
+    g = torch.Generator(device="cuda").manual_seed(5)
+    x = torch.randn((rows, hidden), generator=g, device="cuda").to(torch.bfloat16)
+    xs = torch.randn((rows, 2 * hidden), generator=g, device="cuda").to(torch.bfloat16)
+    w = torch.ones(hidden, dtype=torch.bfloat16, device="cuda")
+    s = (torch.randn((2, hidden), generator=g, device="cuda") * 0.05).to(torch.bfloat16)
+    seg = torch.tensor([[0, 100, 1], [100, rows, 0]], dtype=torch.int32, device="cuda")
+
+    def run():
+        h = K.turing_segmented_rms_adaln(x, w, s, s, seg, 1e-6)
+        ln = K.turing_layer_norm_adaln(x.view(1, rows, hidden), s[:1].view(1, 1, hidden), s[1:].view(1, 1, hidden),
+                                       1e-6)
+        return (h, ln, *K.turing_bf16_int8_convrot_quantize(h, 256),
+                *K.turing_bf16_gelu_int8_convrot_quantize(ln.view(rows, hidden), 256),
+                *K.turing_bf16_int8_convrot_quantize(xs, 256, swiglu=True))
+
+    eager = run()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        run()
+    torch.cuda.current_stream().wait_stream(side)
+    with torch.cuda.graph(graph):
+        captured = run()
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b in zip(eager, captured):
+        assert torch.equal(a, b)
