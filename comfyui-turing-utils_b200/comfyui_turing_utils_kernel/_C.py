@@ -50,7 +50,7 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
 
 
 # ----------------------------------------------------------------------------- quantizers
-def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, what: str):
+def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, what: str, staged: bool = False):
     x = x.contiguous()
     _check_cuda_2d(x, "input")
     if x.dtype != torch.bfloat16:
@@ -67,8 +67,8 @@ def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, wha
     codes = torch.empty((rows, hidden // 2 if bits == 4 else hidden), dtype=torch.int8, device=x.device)
     scales = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
-        _lib.check(_lib.load().ctu_convrot_quantize(
-            _ptr(x), rows, hidden, act, bits, _ptr(codes), _ptr(scales), _stream(x.device)))
+        fn = _lib.load().ctu_convrot_quantize_staged if staged else _lib.load().ctu_convrot_quantize
+        _lib.check(fn(_ptr(x), rows, hidden, act, bits, _ptr(codes), _ptr(scales), _stream(x.device)))
     return codes, scales
 
 
@@ -97,27 +97,30 @@ def turing_bf16_gelu_int4_convrot_quantize(input, group_size=256):
     return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "BF16 GELU row-buffer ConvRot")
 
 
-# The reference's staged two-kernel quantizers (convrot_quant.cu:184-358) produce the
-# same codes and scales as the row-buffer kernel (validate_compatible.py:43-64); on
-# B200 both names run the single fused kernel.  The staged entries accept bf16 only.
+# The reference's staged two-kernel quantizers (convrot_quant.cu:184-358) rotate and
+# round exactly like the row-buffer kernel but form the row scale as absmax * (1/qmax)
+# instead of absmax / qmax (their own validation compares the two scales with rtol 1e-6,
+# validate_compatible.py:43-64).  On B200 both names run the same fused kernels, the
+# staged names with the staged scale, so each matches its reference op bit for bit.
+# The staged entries accept bf16 only.
 def turing_swiglu_int8_convrot_quantize(input, group_size=256):
     """bindings.cpp:474-510."""
-    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 8, "SwiGLU staged ConvRot")
+    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 8, "SwiGLU staged ConvRot", staged=True)
 
 
 def turing_swiglu_int4_convrot_quantize(input, group_size=256):
     """bindings.cpp:547-584."""
-    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 4, "SwiGLU staged INT4 ConvRot")
+    return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 4, "SwiGLU staged INT4 ConvRot", staged=True)
 
 
 def turing_gelu_int8_convrot_quantize(input, group_size=256):
     """bindings.cpp:586-633 (int8)."""
-    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 8, "GELU staged ConvRot")
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 8, "GELU staged ConvRot", staged=True)
 
 
 def turing_gelu_int4_convrot_quantize(input, group_size=256):
     """bindings.cpp:586-633 (int4)."""
-    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "GELU staged ConvRot")
+    return _convrot_quantize(input, group_size, _lib.ACT_GELU_TANH, 4, "GELU staged ConvRot", staged=True)
 
 
 def turing_swiglu_int8_convrot_quantize_scaled(input, scales, group_size=256):

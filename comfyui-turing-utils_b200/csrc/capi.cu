@@ -448,7 +448,8 @@ int act_tables(int device, cudaStream_t stream, ActTables *out) {
 }
 
 int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
-                 uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales) {
+                 uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales,
+                 bool staged_scale) {
     if (int rc = check_quantize_args(x, rows, k, act, bits, codes, given_scales ? given_scales : scales)) return rc;
     if (rows == 0) return CTU_OK;
     QuantPlan plan;
@@ -468,6 +469,7 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
     args.rows_per_batch = plan.rows_per_batch;
     args.box_rows = plan.box_rows;
     args.copies = plan.copies;
+    args.scale_mul = staged_scale ? 1 : 0;
     if (act != CTU_ACT_NONE) {
         ActTables tables;
         if (int rc = act_tables(q.device, stream, &tables)) return rc;
@@ -559,6 +561,17 @@ int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bi
     if (int rc = device_info(&dev)) return rc;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes,
+                                float *scales, void *stream) {
+    if (int rc = check_quantize_args(x, rows, k, act, bits, codes, scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream), nullptr,
+                        true);
 }
 
 int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, const float *scales,

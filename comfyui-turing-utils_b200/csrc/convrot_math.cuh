@@ -136,6 +136,18 @@ __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
     return make_uint2(lo, hi);
 }
 
+// Per-row scale from the row's NaN-ignoring absmax.  The row-buffer kernels divide the
+// clamped absmax by qmax (convrot_quant.cu:475-478); the staged kernels multiply it by
+// the fp32 constant 1/qmax (convrot_quant.cu:300-303, 335-338), which rounds differently
+// for some rows.
+template <int Bits>
+__device__ __forceinline__ float row_scale(float amax, bool staged) {
+    constexpr float qmax = Bits == 4 ? 7.0f : 127.0f;
+    constexpr float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
+    const float clamped = fminf(amax, kBf16Max);
+    return fmaxf(staged ? __fmul_rn(clamped, 1.0f / qmax) : __fdiv_rn(clamped, qmax), floor);
+}
+
 // True when the reciprocal-quotient fast chain reproduces bf16(y / rounded_scale) for
 // every finite y: the rounded scale is a normal, finite bf16 value.
 __device__ __forceinline__ bool fast_chain_scale_ok(float rounded_scale) {

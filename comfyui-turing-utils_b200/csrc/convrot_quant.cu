@@ -222,9 +222,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const bool given = args.given_scales != nullptr;
         for (int r = tid; r < rows && !given; r += nthreads) {
             const float amax = __uint_as_float(absmax_rows[r]);
-            const float qmax = Bits == 4 ? 7.0f : 127.0f;
-            const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
-            args.scales[row0 + r] = fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
+            args.scales[row0 + r] = row_scale<Bits>(amax, args.scale_mul != 0);
         }
 
         // -------------------------------------------------------------- quantize
@@ -238,10 +236,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             if (r != cur_row) {
                 cur_row = r;
                 const float amax = __uint_as_float(absmax_rows[r]);
-                const float qmax = Bits == 4 ? 7.0f : 127.0f;
-                const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
                 const float scale =
-                    given ? args.given_scales[row0 + r] : fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
+                    given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0);
                 if (Bits == 4) {
                     qparam = __fdiv_rn(1.0f, scale);
                 } else {

@@ -26,6 +26,7 @@ struct QuantArgs {
     int rows_per_batch;  // rows per shared-memory batch
     int box_rows;        // 128-byte slices per TMA copy (a multiple of 8: 1024-byte aligned copies)
     int copies;          // TMA copies per batch; copies * box_rows >= rows_per_batch * k_in / 64
+    int scale_mul;       // 1: the staged quantizers' scale (absmax * (1/qmax)); 0: absmax / qmax
     // Activation tables (act_lut_fill_kernel), set for the SwiGLU and GELU quantizers.
     const float *silu_lut;     // [65536] fp32
     const uint16_t *gelu_lut;  // [65536] bf16 bits

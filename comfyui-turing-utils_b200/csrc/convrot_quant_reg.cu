@@ -229,9 +229,7 @@ __global__ void __launch_bounds__(kRegMaxThreads, 1)
 
         if (active && alive) {
             const float amax = given ? 0.0f : __uint_as_float(row_absmax[par * B + r]);
-            const float qmax = Bits == 4 ? 7.0f : 127.0f;
-            const float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
-            const float scale = given ? args.given_scales[row0 + r] : fmaxf(__fdiv_rn(fminf(amax, kBf16Max), qmax), floor);
+            const float scale = given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0);
             if (grp == 0 && h == 0 && !given) args.scales[row0 + r] = scale;
             int8_t *out = args.codes + static_cast<int64_t>(row0 + r) * Kout;
             if constexpr (Bits == 4) {

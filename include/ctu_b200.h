@@ -71,6 +71,18 @@ CTU_API int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act
                          void *stream);
 
 /*
+ * The staged quantizers (replace turing_swiglu_int{8,4}_convrot_quantize and
+ * turing_gelu_int{8,4}_convrot_quantize, kernel/csrc/bindings.cpp:474-633 ->
+ * kernel/csrc/turing/convrot_quant.cu:184-358, 577-663): ctu_convrot_quantize with the
+ * staged kernels' per-row scale max(min(absmax, BF16_MAX) * (1/qmax), floor) -- a
+ * multiplication by the fp32 constant 1/qmax where the row-buffer kernel divides, so
+ * some rows' scales (and rarely codes) differ from ctu_convrot_quantize's.  Same
+ * arguments and constraints as ctu_convrot_quantize.
+ */
+CTU_API int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes,
+                                        float *scales, void *stream);
+
+/*
  * SwiGLU + ConvRot rotate of one channel shard, quantized to int8 with caller-supplied
  * per-row scales (the whole row's scales, computed over every shard beforehand):
  *   x      bf16 [rows, 2k] (gate | up halves of the shard), 16-byte aligned

@@ -150,9 +150,19 @@ void ctu_oracle_rotate(const uint16_t *x, float *y, long rows, int k, int mode) 
     }
 }
 
+/* The per-row scale.  The row-buffer kernel divides the clamped absmax by qmax
+ * (convrot_quant.cu:475-478); the staged kernels multiply it by the fp32 constant
+ * 1/qmax (convrot_quant.cu:300-303, 335-338), which can round differently. */
+static float row_scale(float absmax, int bits, int staged) {
+    const float clamped = fminf(absmax, 3.38953139e38f);
+    if (bits == 4) return fmaxf(staged ? clamped * (1.0f / 7.0f) : clamped / 7.0f, 1.0e-10f);
+    return fmaxf(staged ? clamped * (1.0f / 127.0f) : clamped / 127.0f, 1.0e-30f);
+}
+
 /* convrot_quant.cu:475-510, int8 branch. */
-static void quantize_row_int8(const uint16_t *ybits, int k, float absmax, int8_t *codes, float *scale_out) {
-    const float scale = fmaxf(fminf(absmax, 3.38953139e38f) / 127.0f, 1.0e-30f);
+static void quantize_row_int8(const uint16_t *ybits, int k, float absmax, int8_t *codes, float *scale_out,
+                              int staged) {
+    const float scale = row_scale(absmax, 8, staged);
     *scale_out = scale;
     const float rounded_scale = round_bf16(scale);
     for (int c = 0; c < k; ++c) {
@@ -166,8 +176,9 @@ static void quantize_row_int8(const uint16_t *ybits, int k, float absmax, int8_t
 
 /* convrot_quant.cu:475-500, int4 branch: multiply by the fp32 reciprocal of the
  * unrounded scale, clamp to [-7, 7], pack the even column in the low nibble. */
-static void quantize_row_int4(const uint16_t *ybits, int k, float absmax, int8_t *packed, float *scale_out) {
-    const float scale = fmaxf(fminf(absmax, 3.38953139e38f) / 7.0f, 1.0e-10f);
+static void quantize_row_int4(const uint16_t *ybits, int k, float absmax, int8_t *packed, float *scale_out,
+                              int staged) {
+    const float scale = row_scale(absmax, 4, staged);
     *scale_out = scale;
     const float inv_scale = 1.0f / scale;
     for (int p = 0; p < k / 2; ++p) {
@@ -218,8 +229,8 @@ int ctu_oracle_convrot_quantize_scaled(const uint16_t *x, const float *scales, i
     return 0;
 }
 
-int ctu_oracle_convrot_quantize(const uint16_t *x, int8_t *codes, float *scales,
-                                long rows, int k, int bits, int mode) {
+static int convrot_quantize(const uint16_t *x, int8_t *codes, float *scales, long rows, int k, int bits, int mode,
+                            int staged) {
     if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
     const int width = mode == 1 ? 2 * k : k;
     const int out_width = bits == 4 ? k / 2 : k;
@@ -230,13 +241,26 @@ int ctu_oracle_convrot_quantize(const uint16_t *x, int8_t *codes, float *scales,
         for (long r = 0; r < rows; ++r) {
             const float absmax = rotate_row(x + r * width, k, mode, ybits, 0);
             if (bits == 4) {
-                quantize_row_int4(ybits, k, absmax, codes + r * out_width, scales + r);
+                quantize_row_int4(ybits, k, absmax, codes + r * out_width, scales + r, staged);
             } else {
-                quantize_row_int8(ybits, k, absmax, codes + r * out_width, scales + r);
+                quantize_row_int8(ybits, k, absmax, codes + r * out_width, scales + r, staged);
             }
         }
     }
     return 0;
+}
+
+int ctu_oracle_convrot_quantize(const uint16_t *x, int8_t *codes, float *scales,
+                                long rows, int k, int bits, int mode) {
+    return convrot_quantize(x, codes, scales, rows, k, bits, mode, 0);
+}
+
+/* The staged quantizers (turing_swiglu_int{8,4}_convrot_quantize, turing_gelu_int{8,4}_
+ * convrot_quantize; convrot_quant.cu:184-358, 577-663): the same rotation and codes
+ * with the multiply-by-reciprocal row scale. */
+int ctu_oracle_convrot_quantize_staged(const uint16_t *x, int8_t *codes, float *scales,
+                                       long rows, int k, int bits, int mode) {
+    return convrot_quantize(x, codes, scales, rows, k, bits, mode, 1);
 }
 
 /*

@@ -61,6 +61,8 @@ def _load():
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_long, ctypes.c_int
         lib.ctu_oracle_convrot_quantize.argtypes = [vp, vp, vp, i64, i32, i32, i32]
         lib.ctu_oracle_convrot_quantize.restype = i32
+        lib.ctu_oracle_convrot_quantize_staged.argtypes = [vp, vp, vp, i64, i32, i32, i32]
+        lib.ctu_oracle_convrot_quantize_staged.restype = i32
         lib.ctu_oracle_convrot_quantize_scaled.argtypes = [vp, vp, vp, i64, i32, i32]
         lib.ctu_oracle_convrot_quantize_scaled.restype = i32
         lib.ctu_oracle_set_threads.argtypes = [i32]
@@ -122,11 +124,13 @@ def rotate(x_bits: np.ndarray, mode: int = MODE_PLAIN) -> np.ndarray:
     return y
 
 
-def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN):
+def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN, staged: bool = False):
     """Reference ConvRot row quantizer on bf16 bit patterns.
 
     Returns ``(codes, scales)``: int8 ``[M, K]`` (bits=8) or packed int4 ``[M, K/2]``
-    (bits=4), and fp32 ``[M]`` per-token scales.
+    (bits=4), and fp32 ``[M]`` per-token scales.  ``staged`` selects the scale formula
+    of the reference's staged quantizers (absmax times the fp32 reciprocal of qmax,
+    convrot_quant.cu:300-303,335-338) instead of the row-buffer kernel's division.
     """
     x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
     rows, width = x_bits.shape
@@ -135,7 +139,8 @@ def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN):
         raise ValueError("ConvRot requires K divisible by 256")
     codes = np.empty((rows, k // 2 if bits == 4 else k), dtype=np.int8)
     scales = np.empty((rows,), dtype=np.float32)
-    rc = _load().ctu_oracle_convrot_quantize(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k, bits, mode)
+    fn = _load().ctu_oracle_convrot_quantize_staged if staged else _load().ctu_oracle_convrot_quantize
+    rc = fn(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k, bits, mode)
     if rc != 0:
         raise ValueError(f"unsupported ConvRot width {k}")
     return codes, scales

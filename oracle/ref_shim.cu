@@ -165,6 +165,28 @@ int ref_swiglu_int8_convrot_quantize_scaled(const void *x, const void *scales, v
     });
 }
 
+// kernel/csrc/turing/convrot_quant.cu:535-663 (the staged two-kernel quantizers: rotate +
+// per-group absmax into `rotated` / `partial`, then quantize from the partials).
+// act 1 = SwiGLU (x is [rows, 2k]), 2 = tanh-GELU; bf16 input.
+int ref_staged_convrot_quantize(const void *x, void *codes, void *scales, void *rotated, void *partial, int rows,
+                                int k, int bits, int act, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        Tensor in = view(const_cast<void *>(x), {rows, act == 1 ? 2 * k : k}, Tensor::BF16);
+        Tensor rot = view(rotated, {rows, k}, Tensor::BF16);
+        Tensor part = view(partial, {rows, k / 256}, Tensor::FP32);
+        Tensor out = view(codes, {rows, bits == 4 ? k / 2 : k}, Tensor::INT8);
+        Tensor sc = view(scales, {rows, 1}, Tensor::FP32);
+        if (act == 1) {
+            if (bits == 4) ref::turing_swiglu_int4_convrot_quantize(in, rot, part, out, sc);
+            else ref::turing_swiglu_int8_convrot_quantize(in, rot, part, out, sc);
+        } else {
+            if (bits == 4) ref::turing_gelu_int4_convrot_quantize(in, rot, part, out, sc);
+            else ref::turing_gelu_int8_convrot_quantize(in, rot, part, out, sc);
+        }
+    });
+}
+
 namespace {
 Tensor::ScalarType float_type(int dtype) {
     return dtype == 0 ? Tensor::BF16 : dtype == 1 ? Tensor::FP16 : Tensor::FP32;

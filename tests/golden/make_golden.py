@@ -8,7 +8,7 @@ by ``oracle/Makefile`` -- runs them on seeded inputs and writes compressed ``.np
 fixtures.  The fixtures are committed under ``tests/golden/`` and pin the CPU oracle
 (``oracle/convrot_oracle.py``) in the CPU test suite.
 
-Usage (on a B200):  python tests/golden/make_golden.py --out <directory> [--only extras|norms]
+Usage (on a B200):  python tests/golden/make_golden.py --out <directory> [--only extras|norms|staged]
 """
 
 from __future__ import annotations
@@ -37,9 +37,11 @@ def load_ref():
     f32 = ctypes.c_float
     lib.ref_segmented_rms_adaln.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, i32, vp]
     lib.ref_layer_norm_adaln.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, vp]
+    lib.ref_staged_convrot_quantize.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
     for name in ("ref_bf16_convrot_quantize", "ref_bf16_gelu_convrot_quantize", "ref_int8_linear",
                  "ref_w4a8_linear", "ref_dequantize_int8_bf16", "ref_codebook_w4a8_linear",
-                 "ref_swiglu_int8_convrot_quantize_scaled", "ref_segmented_rms_adaln", "ref_layer_norm_adaln"):
+                 "ref_swiglu_int8_convrot_quantize_scaled", "ref_segmented_rms_adaln", "ref_layer_norm_adaln",
+                 "ref_staged_convrot_quantize"):
         getattr(lib, name).restype = i32
     lib.ref_last_error.restype = ctypes.c_char_p
     return lib
@@ -284,15 +286,49 @@ def norm_cases(lib, out):
     np.savez_compressed(out / "norms.npz", **norms)
 
 
+# The reference's staged quantizers (SwiGLU and GELU, int8 and int4) on special and
+# random rows: (name, act, k, rows of special values, random rows).
+STAGED_CASES = [("swiglu_k256", 1, 256), ("swiglu_k5120", 1, 5120), ("swiglu_k13824", 1, 13824),
+                ("gelu_k256", 2, 256), ("gelu_k5120", 2, 5120), ("gelu_k13824", 2, 13824)]
+
+
+def staged_cases(lib, out):
+    staged = {}
+    for idx, (name, act, k) in enumerate(STAGED_CASES):
+        width = 2 * k if act == 1 else k
+        x = activations(24, width, 6900 + idx)
+        special = special_rows(width)
+        x[: special.shape[0]] = special[: x.shape[0]]
+        xd = x.cuda().contiguous()
+        rows = x.shape[0]
+        staged[f"{name}__x"] = x.view(torch.int16).numpy().view(np.uint16)
+        for bits in (8, 4):
+            codes = torch.empty((rows, k // 2 if bits == 4 else k), dtype=torch.int8, device="cuda")
+            scales = torch.empty((rows, 1), dtype=torch.float32, device="cuda")
+            rotated = torch.empty((rows, k), dtype=torch.bfloat16, device="cuda")
+            partial = torch.empty((rows, k // 256), dtype=torch.float32, device="cuda")
+            check(lib, lib.ref_staged_convrot_quantize(p(xd), p(codes), p(scales), p(rotated), p(partial), rows, k,
+                                                       bits, act, stream()))
+            torch.cuda.synchronize()
+            staged[f"{name}__int{bits}_codes"] = codes.cpu().numpy()
+            staged[f"{name}__int{bits}_scales"] = scales.cpu().numpy().reshape(-1)
+    np.savez_compressed(out / "staged.npz", **staged)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", required=True)
-    ap.add_argument("--only", choices=["all", "extras", "norms"], default="all")
+    ap.add_argument("--only", choices=["all", "extras", "norms", "staged"], default="all")
     args = ap.parse_args()
     out = Path(args.out)
     out.mkdir(parents=True, exist_ok=True)
     lib = load_ref()
     torch.cuda.init()
+    if args.only in ("all", "staged"):
+        staged_cases(lib, out)
+    if args.only == "staged":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
     if args.only in ("all", "norms"):
         norm_cases(lib, out)
     if args.only == "norms":

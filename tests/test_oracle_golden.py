@@ -179,3 +179,31 @@ def test_norm_oracle_matches_reference_kernels():
         else:
             got = oracle.layer_norm_adaln(z[f"{name}__x"], z[f"{name}__scale"], z[f"{name}__shift"], eps, code)
         _assert_norm_close(got, z[f"{name}__out"], code, atol={0: 2**-5, 1: 2**-8, 2: 1e-5}[code])
+
+
+STAGED_PATH = GOLDEN / "staged.npz"
+
+
+@pytest.mark.skipif(not STAGED_PATH.exists(), reason="staged fixtures not generated")
+def test_staged_quantizer_oracle_matches_reference():
+    # The reference's staged SwiGLU / GELU quantizers (convrot_quant.cu:184-358) on
+    # special and random rows: codes and scales bit-exact with the staged scale formula.
+    z = np.load(STAGED_PATH)
+    names = sorted({k.split("__")[0] for k in z.files})
+    assert names
+    for name in names:
+        mode = oracle.MODE_SWIGLU if name.startswith("swiglu") else oracle.MODE_GELU
+        for bits in (8, 4):
+            codes, scales = oracle.convrot_quantize(z[f"{name}__x"], bits=bits, mode=mode, staged=True)
+            want = z[f"{name}__int{bits}_scales"]
+            assert np.array_equal(codes, z[f"{name}__int{bits}_codes"]), (name, bits)
+            if mode == oracle.MODE_GELU:
+                assert np.array_equal(scales.view(np.uint32), want.view(np.uint32)), (name, bits)
+                # The row-buffer formula (absmax / qmax) rounds differently in some rows:
+                # the staged ops need their own formula to be bit-exact.
+                _, rb = oracle.convrot_quantize(z[f"{name}__x"], bits=bits, mode=mode, staged=False)
+                if bits == 4 and name != "gelu_k256":
+                    assert not np.array_equal(rb.view(np.uint32), want.view(np.uint32))
+            else:  # glibc's expf vs CUDA's: scales within a few ulps
+                ulps = np.abs(scales.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64))
+                assert ulps.max() <= 4, (name, bits)
