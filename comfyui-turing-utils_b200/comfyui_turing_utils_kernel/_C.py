@@ -53,7 +53,10 @@ def _aligned(t: torch.Tensor) -> torch.Tensor:
 def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, what: str, staged: bool = False):
     x = x.contiguous()
     _check_cuda_2d(x, "input")
-    if x.dtype != torch.bfloat16:
+    if staged:  # the staged quantizers take fp16 rows too (check_half_like, bindings.cpp:95-99)
+        if x.dtype not in (torch.float16, torch.bfloat16):
+            raise RuntimeError("input must be float16 or bfloat16")
+    elif x.dtype != torch.bfloat16:
         raise RuntimeError(f"{what} input must be bfloat16")
     if group_size != 256:
         raise RuntimeError(f"{what} only supports group_size=256")
@@ -67,8 +70,12 @@ def _convrot_quantize(x: torch.Tensor, group_size: int, act: int, bits: int, wha
     codes = torch.empty((rows, hidden // 2 if bits == 4 else hidden), dtype=torch.int8, device=x.device)
     scales = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
-        fn = _lib.load().ctu_convrot_quantize_staged if staged else _lib.load().ctu_convrot_quantize
-        _lib.check(fn(_ptr(x), rows, hidden, act, bits, _ptr(codes), _ptr(scales), _stream(x.device)))
+        if staged:
+            _lib.check(_lib.load().ctu_convrot_quantize_staged(
+                _ptr(x), rows, hidden, act, bits, _NORM_TYPES[x.dtype], _ptr(codes), _ptr(scales), _stream(x.device)))
+        else:
+            _lib.check(_lib.load().ctu_convrot_quantize(
+                _ptr(x), rows, hidden, act, bits, _ptr(codes), _ptr(scales), _stream(x.device)))
     return codes, scales
 
 
@@ -102,7 +109,8 @@ def turing_bf16_gelu_int4_convrot_quantize(input, group_size=256):
 # instead of absmax / qmax (their own validation compares the two scales with rtol 1e-6,
 # validate_compatible.py:43-64).  On B200 both names run the same fused kernels, the
 # staged names with the staged scale, so each matches its reference op bit for bit.
-# The staged entries accept bf16 only.
+# Like the reference, the staged entries also take fp16 rows (rounded to fp16 where the
+# bf16 path rounds to bf16; the two-pass kernel runs them).
 def turing_swiglu_int8_convrot_quantize(input, group_size=256):
     """bindings.cpp:474-510."""
     return _convrot_quantize(input, group_size, _lib.ACT_SWIGLU, 8, "SwiGLU staged ConvRot", staged=True)
@@ -129,8 +137,8 @@ def turing_swiglu_int8_convrot_quantize_scaled(input, scales, group_size=256):
     input = input.contiguous()
     scales = scales.reshape(-1).to(torch.float32).contiguous()
     _check_cuda_2d(input, "input")
-    if input.dtype != torch.bfloat16:
-        raise RuntimeError("scaled SwiGLU ConvRot input must be bfloat16")
+    if input.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("input must be float16 or bfloat16")
     if group_size != 256:
         raise RuntimeError("scaled SwiGLU ConvRot only supports group_size=256")
     if input.shape[1] % 2 != 0:
@@ -144,7 +152,7 @@ def turing_swiglu_int8_convrot_quantize_scaled(input, scales, group_size=256):
     codes = torch.empty((rows, hidden), dtype=torch.int8, device=input.device)
     with torch.cuda.device(input.device):
         _lib.check(_lib.load().ctu_swiglu_int8_convrot_quantize_scaled(
-            _ptr(input), rows, hidden, _ptr(scales), _ptr(codes), _stream(input.device)))
+            _ptr(input), rows, hidden, _NORM_TYPES[input.dtype], _ptr(scales), _ptr(codes), _stream(input.device)))
     return codes
 
 

@@ -229,8 +229,8 @@ def turing_swiglu_int8_convrot_quantize(x: torch.Tensor, group_size: int = 256) 
     _require_cuda(x, "Turing SwiGLU ConvRot")
     if x.ndim != 2:
         raise ValueError("SwiGLU ConvRot input must be 2D [M, 2K]")
-    if x.dtype != torch.bfloat16:
-        raise TypeError("SwiGLU ConvRot input must be bfloat16 on the B200 build")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("SwiGLU ConvRot input must be float16 or bfloat16")
     return _C.turing_swiglu_int8_convrot_quantize(x.contiguous(), group_size)
 
 
@@ -252,8 +252,8 @@ def turing_swiglu_int8_convrot_quantize_scaled(
 ) -> torch.Tensor:
     """Quantize a SwiGLU+ConvRot shard with precomputed whole-row scales."""
     _require_cuda(x, "scaled Turing SwiGLU ConvRot")
-    if x.dtype != torch.bfloat16 or x.ndim != 2:
-        raise TypeError("scaled SwiGLU ConvRot input must be 2D bfloat16 on the B200 build")
+    if x.dtype not in (torch.float16, torch.bfloat16) or x.ndim != 2:
+        raise TypeError("scaled SwiGLU ConvRot input must be 2D float16 or bfloat16")
     if scales.dtype != torch.float32 or scales.numel() != x.shape[0]:
         raise TypeError("scaled SwiGLU ConvRot requires one FP32 scale per row")
     return _C.turing_swiglu_int8_convrot_quantize_scaled(x.contiguous(), scales.contiguous(), group_size)
@@ -270,8 +270,8 @@ def turing_swiglu_int4_convrot_quantize(x: torch.Tensor, group_size: int = 256) 
     _require_cuda(x, "Turing SwiGLU INT4 ConvRot")
     if x.ndim != 2:
         raise ValueError("SwiGLU INT4 ConvRot input must be 2D [M, 2K]")
-    if x.dtype != torch.bfloat16:
-        raise TypeError("SwiGLU INT4 ConvRot input must be bfloat16 on the B200 build")
+    if x.dtype not in (torch.float16, torch.bfloat16):
+        raise TypeError("SwiGLU INT4 ConvRot input must be float16 or bfloat16")
     return _C.turing_swiglu_int4_convrot_quantize(x.contiguous(), group_size)
 
 
@@ -288,8 +288,8 @@ def _turing_swiglu_int4_convrot_quantize_fake(x, group_size=256):
 def turing_gelu_int8_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
     """tanh-GELU + ConvRot int8 quantization."""
     _require_cuda(x, "Turing GELU ConvRot")
-    if x.dtype != torch.bfloat16 or x.ndim != 2:
-        raise TypeError("GELU ConvRot input must be a 2D bfloat16 tensor on the B200 build")
+    if x.dtype not in (torch.float16, torch.bfloat16) or x.ndim != 2:
+        raise TypeError("GELU ConvRot input must be 2D float16 or bfloat16")
     return _C.turing_gelu_int8_convrot_quantize(x.contiguous(), group_size)
 
 
@@ -305,8 +305,8 @@ def _turing_gelu_int8_convrot_quantize_fake(x, group_size=256):
 def turing_gelu_int4_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
     """tanh-GELU + ConvRot packed-int4 quantization."""
     _require_cuda(x, "Turing GELU INT4 ConvRot")
-    if x.dtype != torch.bfloat16 or x.ndim != 2:
-        raise TypeError("GELU INT4 ConvRot input must be a 2D bfloat16 tensor on the B200 build")
+    if x.dtype not in (torch.float16, torch.bfloat16) or x.ndim != 2:
+        raise TypeError("GELU INT4 ConvRot input must be 2D float16 or bfloat16")
     return _C.turing_gelu_int4_convrot_quantize(x.contiguous(), group_size)
 
 

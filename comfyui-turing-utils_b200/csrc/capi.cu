@@ -192,8 +192,8 @@ bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *pl
     return true;
 }
 
-int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan) {
-    const int forced = g_quant_kernel.load(std::memory_order_relaxed);
+int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan, bool two_pass_only = false) {
+    const int forced = two_pass_only ? 1 : g_quant_kernel.load(std::memory_order_relaxed);
     // Measured on B200 (M = 32760, activations from the tables): the four-lane kernel is
     // 14-19 % faster for plain rows of K <= 3072 and 4-8 % faster with a fused SwiGLU /
     // GELU input at K = 5120; the two-lane kernel is 1-4 % faster for plain rows of
@@ -418,12 +418,15 @@ int check_quantize_args(const void *x, int64_t rows, int64_t k, int act, int bit
     return CTU_OK;
 }
 
-// Per device: the activation tables of the SwiGLU / GELU quantizers (384 KiB), filled
-// on the first activation call on that device and kept until exit.  That call
-// synchronizes its stream once, so it must not be made during stream capture.
+// Per device: the activation tables of the SwiGLU / GELU quantizers (bf16- and
+// fp16-indexed, 768 KiB), filled on the first activation call on that device and kept
+// until exit.  That call synchronizes its stream once, so it must not be made during
+// stream capture.
 struct ActTables {
     float *silu = nullptr;
     uint16_t *gelu = nullptr;
+    float *silu16 = nullptr;
+    uint16_t *gelu16 = nullptr;
 };
 ActTables g_act_tables[kMaxDevices];
 
@@ -432,9 +435,11 @@ int act_tables(int device, cudaStream_t stream, ActTables *out) {
     ActTables &t = g_act_tables[device];
     if (t.silu == nullptr) {
         void *p = nullptr;
-        CTU_CUDA(cudaMalloc(&p, 65536 * (sizeof(float) + sizeof(uint16_t))));
-        ActTables fresh{static_cast<float *>(p), reinterpret_cast<uint16_t *>(static_cast<float *>(p) + 65536)};
-        ctu::rot::act_lut_fill_kernel<<<256, 256, 0, stream>>>(fresh.silu, fresh.gelu);
+        CTU_CUDA(cudaMalloc(&p, 2 * 65536 * (sizeof(float) + sizeof(uint16_t))));
+        float *f = static_cast<float *>(p);
+        uint16_t *u = reinterpret_cast<uint16_t *>(f + 2 * 65536);
+        ActTables fresh{f, u, f + 65536, u + 65536};
+        ctu::rot::act_lut_fill_kernel<<<256, 256, 0, stream>>>(fresh.silu, fresh.gelu, fresh.silu16, fresh.gelu16);
         cudaError_t e = cudaGetLastError();
         if (e == cudaSuccess) e = cudaStreamSynchronize(stream);  // other streams may read the tables next
         if (e != cudaSuccess) {
@@ -449,11 +454,13 @@ int act_tables(int device, cudaStream_t stream, ActTables *out) {
 
 int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
                  uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales,
-                 bool staged_scale) {
+                 bool staged_scale, bool half_input) {
     if (int rc = check_quantize_args(x, rows, k, act, bits, codes, given_scales ? given_scales : scales)) return rc;
     if (rows == 0) return CTU_OK;
+    if (half_input && act == CTU_ACT_NONE)
+        return fail(CTU_ERR_UNSUPPORTED, "fp16 rows are taken by the SwiGLU / GELU staged quantizers only");
     QuantPlan plan;
-    if (int rc = plan_quant(k, act, bits, q.smem_optin, &plan)) return rc;
+    if (int rc = plan_quant(k, act, bits, q.smem_optin, &plan, half_input)) return rc;
     const int64_t k_in = act == CTU_ACT_SWIGLU ? 2 * k : k;
     CUtensorMap map;
     if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k_in / 64, 64,
@@ -475,6 +482,18 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
         if (int rc = act_tables(q.device, stream, &tables)) return rc;
         args.silu_lut = tables.silu;
         args.gelu_lut = tables.gelu;
+        args.silu16_lut = tables.silu16;
+        args.gelu16_lut = tables.gelu16;
+    }
+    if (half_input) {  // the two-pass kernel carries the fp16 variant
+        using ctu::rot::convrot_quant_kernel;
+        const QuantKernel kernel =
+            act == CTU_ACT_SWIGLU
+                ? (bits == 8 ? convrot_quant_kernel<ctu::rot::kActSwiGLU, 8, true>
+                             : convrot_quant_kernel<ctu::rot::kActSwiGLU, 4, true>)
+                : (bits == 8 ? convrot_quant_kernel<ctu::rot::kActGelu, 8, true>
+                             : convrot_quant_kernel<ctu::rot::kActGelu, 4, true>);
+        return launch_quant_kernel(kernel, map, args, plan, q, stream);
     }
     using ctu::rot::kActGelu;
     using ctu::rot::kActNone;
@@ -563,19 +582,23 @@ int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bi
     return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
 }
 
-int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes,
+int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int dtype, int8_t *codes,
                                 float *scales, void *stream) {
+    if (dtype != CTU_DTYPE_BF16 && dtype != CTU_DTYPE_FP16)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "staged ConvRot requires float16 or bfloat16 input");
     if (int rc = check_quantize_args(x, rows, k, act, bits, codes, scales)) return rc;
     if (rows == 0) return CTU_OK;
     DeviceInfo dev;
     if (int rc = device_info(&dev)) return rc;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream), nullptr,
-                        true);
+                        true, dtype == CTU_DTYPE_FP16);
 }
 
-int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, const float *scales,
+int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, int dtype, const float *scales,
                                             int8_t *codes, void *stream) {
+    if (dtype != CTU_DTYPE_BF16 && dtype != CTU_DTYPE_FP16)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "scaled SwiGLU ConvRot requires float16 or bfloat16 input");
     if (rows > 0 && scales == nullptr) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
     if (int rc = check_quantize_args(x, rows, k, CTU_ACT_SWIGLU, 8, codes, scales)) return rc;
     if (rows == 0) return CTU_OK;
@@ -583,7 +606,7 @@ int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t
     if (int rc = device_info(&dev)) return rc;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_quantize(x, rows, k, CTU_ACT_SWIGLU, 8, codes, nullptr, dev.err, q, static_cast<cudaStream_t>(stream),
-                        scales);
+                        scales, false, dtype == CTU_DTYPE_FP16);
 }
 
 int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,

@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -44,12 +45,13 @@ __device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t c) { return r * 1
 // and tanh-GELU rounded back to bf16.  Only act_lut_fill_kernel evaluates them.
 __device__ __forceinline__ float silu_factor(float gate) { return gate / (1.0f + expf(-gate)); }
 
-__device__ __forceinline__ float gelu_bf16(float x) {
+__device__ __forceinline__ float gelu_fp32(float x) {
     constexpr float kAlpha = 0.7978845608028654f;
     constexpr float kBeta = 0.044715f;
-    const float activated = 0.5f * x * (1.0f + tanhf(kAlpha * (x + kBeta * x * x * x)));
-    return __bfloat162float(__float2bfloat16_rn(activated));
+    return 0.5f * x * (1.0f + tanhf(kAlpha * (x + kBeta * x * x * x)));
 }
+
+__device__ __forceinline__ float gelu_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(gelu_fp32(x))); }
 
 // Both activations take a bf16 input, so each is a function of 65536 bit patterns:
 // act_lut_fill_kernel evaluates them once per device into these tables (the SwiGLU
@@ -57,8 +59,10 @@ __device__ __forceinline__ float gelu_bf16(float x) {
 // instead of evaluating expf / tanhf per element.  The tables hold exactly the values
 // the expressions give, so the codes are unchanged.
 struct ActLut {
-    const float *silu;     // [65536] gate / (1 + expf(-gate)), indexed by the gate's bf16 bits
-    const uint16_t *gelu;  // [65536] bf16 bits of tanh-GELU, indexed by the input's bf16 bits
+    const float *silu;       // [65536] gate / (1 + expf(-gate)), indexed by the gate's bf16 bits
+    const uint16_t *gelu;    // [65536] bf16 bits of tanh-GELU, indexed by the input's bf16 bits
+    const float *silu16;     // the same two for fp16 inputs (the staged quantizers):
+    const uint16_t *gelu16;  //   indexed by fp16 bits, GELU rounded to fp16
 };
 
 template <int Act>
@@ -115,6 +119,91 @@ __device__ __forceinline__ void load_group(const uint8_t *buf, uint32_t row64, u
     }
 }
 
+// ---------------------------------------------------------------------------
+// fp16 inputs (the staged quantizers' other storage type, convrot_quant.cu:577-663):
+// the values convert with __half2float and the rotated values round to fp16.
+__device__ __forceinline__ float f16_to_f32(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16)));
+}
+__device__ __forceinline__ float f16lo(uint32_t w) { return f16_to_f32(w & 0xFFFFu); }
+__device__ __forceinline__ float f16hi(uint32_t w) { return f16_to_f32(w >> 16); }
+
+// Two fp32 -> packed fp16x2 (round to nearest even); `lo` lands in bits [0,16).
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+template <int Act>
+__device__ __forceinline__ float activate_f16(uint32_t x16, uint32_t up16, const ActLut &lut) {
+    if constexpr (Act == kActSwiGLU) {
+        return __fmul_rn(__ldg(lut.silu16 + x16), f16_to_f32(up16));
+    } else if constexpr (Act == kActGelu) {
+        return f16_to_f32(__ldg(lut.gelu16 + x16));
+    } else {
+        return f16_to_f32(x16);
+    }
+}
+
+// load_group for fp16 rows (same layout: v[j] = (chunk0[j], chunk1[j])).
+template <int Act>
+__device__ __forceinline__ void load_group_f16(const uint8_t *buf, uint32_t row64, uint32_t up_off,
+                                               f32x2 (&v)[64], const ActLut &lut) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(buf + sw128(row64, c));
+        const uint4 b = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + 2, c));
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+        uint32_t uaw[4] = {0, 0, 0, 0}, ubw[4] = {0, 0, 0, 0};
+        if constexpr (Act == kActSwiGLU) {
+            const uint4 ua = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + up_off, c));
+            const uint4 ub = *reinterpret_cast<const uint4 *>(buf + sw128(row64 + up_off + 2, c));
+            uaw[0] = ua.x, uaw[1] = ua.y, uaw[2] = ua.z, uaw[3] = ua.w;
+            ubw[0] = ub.x, ubw[1] = ub.y, ubw[2] = ub.z, ubw[3] = ub.w;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            v[8 * c + 2 * q] = pk2(activate_f16<Act>(aw[q] & 0xFFFFu, uaw[q] & 0xFFFFu, lut),
+                                   activate_f16<Act>(bw[q] & 0xFFFFu, ubw[q] & 0xFFFFu, lut));
+            v[8 * c + 2 * q + 1] = pk2(activate_f16<Act>(aw[q] >> 16, uaw[q] >> 16, lut),
+                                       activate_f16<Act>(bw[q] >> 16, ubw[q] >> 16, lut));
+        }
+    }
+}
+
+// int8 codes of 8 consecutive fp16(y) values, the staged chain for fp16
+// (convrot_quant.cu:66-73,304-310): clamp(rint(fp16(y / fp16(scale))), -128, 127), with
+// the IEEE quotient (NaN -> -128 as fminf/fmaxf give it).
+__device__ __forceinline__ uint2 quant8_int8_f16(uint4 w, float rounded_scale) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float y = (i & 1) ? f16hi(ww[i >> 1]) : f16lo(ww[i >> 1]);
+        const float divided = __half2float(__float2half_rn(__fdiv_rn(y, rounded_scale)));
+        const float qf = fminf(127.0f, fmaxf(-128.0f, nearbyintf(divided)));
+        out[i >> 2] |= (static_cast<uint32_t>(static_cast<int32_t>(qf)) & 0xFFu) << (8 * (i & 3));
+    }
+    return make_uint2(out[0], out[1]);
+}
+
+// Packed int4 codes of 8 consecutive fp16(y) values: clamp(rint(y * inv), -7, 7).
+__device__ __forceinline__ uint32_t quant8_int4_f16(uint4 w, float inv) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    uint32_t out = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float lo = fminf(7.0f, fmaxf(-7.0f, nearbyintf(__fmul_rn(f16lo(ww[i]), inv))));
+        const float hi = fminf(7.0f, fmaxf(-7.0f, nearbyintf(__fmul_rn(f16hi(ww[i]), inv))));
+        const uint32_t lb = static_cast<uint32_t>(static_cast<int32_t>(lo)) & 0xFu;
+        const uint32_t hb = static_cast<uint32_t>(static_cast<int32_t>(hi)) & 0xFu;
+        out |= (lb | (hb << 4)) << (8 * i);
+    }
+    return out;
+}
+
 // Quantize 8 consecutive bf16(y) values of one row to int8 with the fast chain.
 __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
@@ -140,11 +229,12 @@ __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
 // clamped absmax by qmax (convrot_quant.cu:475-478); the staged kernels multiply it by
 // the fp32 constant 1/qmax (convrot_quant.cu:300-303, 335-338), which rounds differently
 // for some rows.
+// The clamp is the input type's largest finite value (bf16, or 65504 for fp16 input).
 template <int Bits>
-__device__ __forceinline__ float row_scale(float amax, bool staged) {
+__device__ __forceinline__ float row_scale(float amax, bool staged, float finite_max = kBf16Max) {
     constexpr float qmax = Bits == 4 ? 7.0f : 127.0f;
     constexpr float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
-    const float clamped = fminf(amax, kBf16Max);
+    const float clamped = fminf(amax, finite_max);
     return fmaxf(staged ? __fmul_rn(clamped, 1.0f / qmax) : __fdiv_rn(clamped, qmax), floor);
 }
 

@@ -31,6 +31,7 @@
 //     (exhaustively re-checked in tests/test_quotient_identity.py).
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -46,11 +47,15 @@ namespace rot {
 // and a NaN probe, and write bf16(y) back in place.  All 32 lanes of the warp must
 // call this together (it shuffles with a full mask); a lane pair without work passes
 // active = false, computes on a valid group and writes nothing.
-template <int Act>
+template <int Act, bool kHalf>
 __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint32_t up_off, int h, bool active,
                                              float &absmax, float &nan_probe, const ActLut &lut) {
     f32x2 v[64];
-    load_group<Act>(buf, row64, up_off, v, lut);
+    if constexpr (kHalf) {
+        load_group_f16<Act>(buf, row64, up_off, v, lut);
+    } else {
+        load_group<Act>(buf, row64, up_off, v, lut);
+    }
     const f32x2 half = pk2(0.5f, 0.5f);
 
     // Stage 1 (stride 1): bits 0-1 of the element index.
@@ -109,8 +114,8 @@ __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint3
         unpk2(yb, yb0, yb1);
         m = max_abs3(m, ya0, ya1);
         m = max_abs3(m, yb0, yb1);
-        wa[(j >> 1) & 3] = pack_bf16x2(ya0, ya1);
-        wb[(j >> 1) & 3] = pack_bf16x2(yb0, yb1);
+        wa[(j >> 1) & 3] = kHalf ? pack_f16x2(ya0, ya1) : pack_bf16x2(ya0, ya1);
+        wb[(j >> 1) & 3] = kHalf ? pack_f16x2(yb0, yb1) : pack_bf16x2(yb0, yb1);
         if ((j & 7) == 6 && active) {
             // bf16(y) of 8 positions back in place over this lane's own (already
             // consumed) input elements.
@@ -125,9 +130,10 @@ __device__ __forceinline__ void rotate_group(uint8_t *buf, uint32_t row64, uint3
     nan_probe = active ? __fadd_rn(p0, p1) : 0.0f;
 }
 
-template <int Act, int Bits>
+template <int Act, int Bits, bool kHalf>
 __global__ void __launch_bounds__(kMaxThreads, 1)
     convrot_quant_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
+    constexpr float kFiniteMax = kHalf ? 65504.0f : kBf16Max;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int K = args.k;
@@ -202,8 +208,8 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             const int grp = task - r * groups;
             const uint32_t row64 = r * slices_per_row + grp * 4 + h;
             float amax, probe;
-            rotate_group<Act>(inbuf[buf], row64, static_cast<uint32_t>(K / 64), h, active, amax, probe,
-                              ActLut{args.silu_lut, args.gelu_lut});
+            rotate_group<Act, kHalf>(inbuf[buf], row64, static_cast<uint32_t>(K / 64), h, active, amax, probe,
+                                     ActLut{args.silu_lut, args.gelu_lut, args.silu16_lut, args.gelu16_lut});
             amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
             probe = __fadd_rn(probe, __shfl_xor_sync(0xffffffffu, probe, 1));
             if (active && h == 0) {
@@ -222,7 +228,7 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
         const bool given = args.given_scales != nullptr;
         for (int r = tid; r < rows && !given; r += nthreads) {
             const float amax = __uint_as_float(absmax_rows[r]);
-            args.scales[row0 + r] = row_scale<Bits>(amax, args.scale_mul != 0);
+            args.scales[row0 + r] = row_scale<Bits>(amax, args.scale_mul != 0, kFiniteMax);
         }
 
         // -------------------------------------------------------------- quantize
@@ -237,9 +243,11 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
                 cur_row = r;
                 const float amax = __uint_as_float(absmax_rows[r]);
                 const float scale =
-                    given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0);
+                    given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0, kFiniteMax);
                 if (Bits == 4) {
                     qparam = __fdiv_rn(1.0f, scale);
+                } else if (kHalf) {
+                    qparam = __half2float(__float2half_rn(scale));
                 } else {
                     const float rs = __bfloat162float(__float2bfloat16_rn(scale));
                     exact = nan_rows[r] != 0u || (given ? !fast_chain_scale_ok(rs) : isinf(amax));
@@ -248,9 +256,12 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
             }
             const uint4 w = *reinterpret_cast<const uint4 *>(inbuf[buf] + sw128(r * slices_per_row + (col8 >> 3), col8 & 7));
             if (Bits == 4) {
-                *reinterpret_cast<uint32_t *>(codebuf + r * Kout + col8 * 4) = quant8_int4(w, pk2(qparam, qparam));
+                *reinterpret_cast<uint32_t *>(codebuf + r * Kout + col8 * 4) =
+                    kHalf ? quant8_int4_f16(w, qparam) : quant8_int4(w, pk2(qparam, qparam));
             } else {
-                const uint2 q = exact ? quant8_int8_exact(w, qparam) : quant8_int8_fast(w, pk2(qparam, qparam));
+                const uint2 q = kHalf   ? quant8_int8_f16(w, qparam)
+                                : exact ? quant8_int8_exact(w, qparam)
+                                        : quant8_int8_fast(w, pk2(qparam, qparam));
                 *reinterpret_cast<uint2 *>(codebuf + r * Kout + col8 * 8) = q;
             }
             col8 += nthreads;
@@ -273,12 +284,15 @@ __global__ void __launch_bounds__(kMaxThreads, 1)
 
 // One thread per bf16 bit pattern: the SwiGLU gate factor and the rounded tanh-GELU
 // of every bf16 value, exactly as the activations define them (silu_factor, gelu_bf16).
-__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu) {
+__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu, float *silu16, uint16_t *gelu16) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= 65536u) return;
     const float x = __uint_as_float(i << 16);
     silu[i] = silu_factor(x);
     gelu[i] = static_cast<uint16_t>(__float_as_uint(gelu_bf16(x)) >> 16);
+    const float xh = f16_to_f32(i);
+    silu16[i] = silu_factor(xh);
+    gelu16[i] = __half_as_ushort(__float2half_rn(gelu_fp32(xh)));
 }
 
 template __global__ void convrot_quant_kernel<kActNone, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
@@ -287,6 +301,12 @@ template __global__ void convrot_quant_kernel<kActSwiGLU, 8>(const __grid_consta
 template __global__ void convrot_quant_kernel<kActSwiGLU, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_kernel<kActGelu, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_kernel<kActGelu, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_kernel<kActSwiGLU, 8, true>(const __grid_constant__ CUtensorMap,
+                                                                    const QuantArgs);
+template __global__ void convrot_quant_kernel<kActSwiGLU, 4, true>(const __grid_constant__ CUtensorMap,
+                                                                    const QuantArgs);
+template __global__ void convrot_quant_kernel<kActGelu, 8, true>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_kernel<kActGelu, 4, true>(const __grid_constant__ CUtensorMap, const QuantArgs);
 
 }  // namespace rot
 }  // namespace ctu

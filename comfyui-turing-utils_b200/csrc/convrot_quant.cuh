@@ -28,12 +28,14 @@ struct QuantArgs {
     int copies;          // TMA copies per batch; copies * box_rows >= rows_per_batch * k_in / 64
     int scale_mul;       // 1: the staged quantizers' scale (absmax * (1/qmax)); 0: absmax / qmax
     // Activation tables (act_lut_fill_kernel), set for the SwiGLU and GELU quantizers.
-    const float *silu_lut;     // [65536] fp32
-    const uint16_t *gelu_lut;  // [65536] bf16 bits
+    const float *silu_lut;       // [65536] fp32, bf16-indexed
+    const uint16_t *gelu_lut;    // [65536] bf16 bits, bf16-indexed
+    const float *silu16_lut;     // [65536] fp32, fp16-indexed
+    const uint16_t *gelu16_lut;  // [65536] fp16 bits, fp16-indexed
 };
 
 // Fills the activation tables: launch 256 blocks of 256 threads.
-__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu);
+__global__ void act_lut_fill_kernel(float *silu, uint16_t *gelu, float *silu16, uint16_t *gelu16);
 
 // Slices (128 bytes = 64 bf16) per TMA copy and copies per batch.  Every copy
 // starts on a 1024-byte boundary, as the 128-byte swizzle pattern requires.
@@ -55,7 +57,9 @@ inline size_t quant_smem_bytes(int rows, int k, int act, int bits) {
     return 1024 + 2 * in_bytes + code_bytes + 16 * static_cast<size_t>(rows) + 64;
 }
 
-template <int Act, int Bits>
+// kHalf: fp16 rows (the staged quantizers' other input type); instantiated for the
+// SwiGLU and GELU activations only.
+template <int Act, int Bits, bool kHalf = false>
 __global__ void convrot_quant_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
 // Register-resident variant: one lane pair per 256-column group and whole rows per

@@ -27,7 +27,7 @@ int device_query(DeviceQuery *q);
 // allocates device memory.
 int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes, float *scales,
                  uint32_t *err, const DeviceQuery &q, cudaStream_t stream, const float *given_scales = nullptr,
-                 bool staged_scale = false);
+                 bool staged_scale = false, bool half_input = false);
 int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
                     int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
                     uint32_t *err, const DeviceQuery &q, cudaStream_t stream);

@@ -76,25 +76,28 @@ CTU_API int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act
  * kernel/csrc/turing/convrot_quant.cu:184-358, 577-663): ctu_convrot_quantize with the
  * staged kernels' per-row scale max(min(absmax, BF16_MAX) * (1/qmax), floor) -- a
  * multiplication by the fp32 constant 1/qmax where the row-buffer kernel divides, so
- * some rows' scales (and rarely codes) differ from ctu_convrot_quantize's.  Same
- * arguments and constraints as ctu_convrot_quantize.
+ * some rows' scales (and rarely codes) differ from ctu_convrot_quantize's.  act must be
+ * CTU_ACT_SWIGLU or CTU_ACT_GELU_TANH for dtype CTU_DTYPE_FP16 (like the reference, fp16
+ * rows round the rotated values, the scale and the quotient to fp16 and clamp at
+ * 65504); otherwise the same arguments and constraints as ctu_convrot_quantize.
  */
-CTU_API int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int8_t *codes,
-                                        float *scales, void *stream);
+CTU_API int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int dtype,
+                                        int8_t *codes, float *scales, void *stream);
 
 /*
  * SwiGLU + ConvRot rotate of one channel shard, quantized to int8 with caller-supplied
  * per-row scales (the whole row's scales, computed over every shard beforehand):
- *   x      bf16 [rows, 2k] (gate | up halves of the shard), 16-byte aligned
+ *   x      bf16 or fp16 (dtype CTU_DTYPE_BF16 / CTU_DTYPE_FP16) [rows, 2k] (gate | up
+ *          halves of the shard), 16-byte aligned
  *   scales fp32 [rows], read only
  *   codes  int8 [rows, k], 16-byte aligned
- * code = clamp(rint(bf16(bf16(y) / bf16(scale))), -128, 127), as the unscaled op.
+ * code = clamp(rint(T(T(y) / T(scale))), -128, 127), T the input type, as the unscaled op.
  * k must be a positive multiple of 256.
  * Replaces turing_utils::swiglu_int8_convrot_quantize_scaled (ops.py:189-219;
  * bindings.cpp:512-545; convrot_quant.cu:138-161,239-278,591-621).
  */
-CTU_API int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, const float *scales,
-                                                    int8_t *codes, void *stream);
+CTU_API int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows, int64_t k, int dtype,
+                                                    const float *scales, int8_t *codes, void *stream);
 
 /*
  * W8A8 linear with the fused dequant + bias epilogue:

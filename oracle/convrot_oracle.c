@@ -88,7 +88,7 @@ static inline float swiglu_value(float gate, float up) {
  * The reference is compiled with nvcc's default FMA contraction; the two
  * products feeding an addition are contracted exactly as written here with
  * fmaf so the C restatement follows the device's evaluation. */
-static inline float gelu_tanh_value(float x, int contract) {
+static inline float gelu_tanh_activated(float x, int contract) {
     const float kAlpha = 0.7978845608028654f;
     const float kBeta = 0.044715f;
     float inner;
@@ -98,9 +98,10 @@ static inline float gelu_tanh_value(float x, int contract) {
         inner = x + ((kBeta * x) * x) * x;
     }
     const float t = tanhf(kAlpha * inner);
-    const float activated = (0.5f * x) * (1.0f + t);
-    return round_bf16(activated);
+    return (0.5f * x) * (1.0f + t);
 }
+
+static inline float gelu_tanh_value(float x, int contract) { return round_bf16(gelu_tanh_activated(x, contract)); }
 
 /*
  * Rotate one activation row and return the fp32 absmax over the rotated
@@ -508,5 +509,99 @@ void ctu_oracle_layer_norm_adaln(const void *x, const void *scale, const void *s
             store_val(out, base + c, dtype, fmaf(normalized, multiplier, load_val(shift, mbase + c, dtype)));
         }
     }
+}
+
+/* ------------------------------------------------------------ fp16 staged rows */
+
+/* The staged quantizers' fp16 instantiation (convrot_quant.cu:184-358 with
+ * InputType = half): values convert exactly to fp32, GELU rounds to fp16, the
+ * rotated values are stored as fp16, the scale clamps at 65504 and is formed with
+ * the reciprocal constant, and the int8 chain rounds the scale and the quotient to
+ * fp16 (convrot_quant.cu:66-73). */
+static inline float f16_to_f32(uint16_t v) {
+    _Float16 h;
+    memcpy(&h, &v, 2);
+    return (float)h;
+}
+static inline uint16_t f32_to_f16(float v) {
+    const _Float16 h = (_Float16)v;
+    uint16_t u;
+    memcpy(&u, &h, 2);
+    return u;
+}
+static inline float round_f16(float v) { return (float)(_Float16)v; }
+
+static float rotate_row_f16(const uint16_t *row, int k, int mode, uint16_t *ybits) {
+    float absmax = 0.0f;
+    float in[KGROUP], out[KGROUP];
+    for (int g = 0; g < k / KGROUP; ++g) {
+        for (int i = 0; i < KGROUP; ++i) {
+            const int col = g * KGROUP + i;
+            in[i] = mode == 1 ? swiglu_value(f16_to_f32(row[col]), f16_to_f32(row[k + col]))
+                              : round_f16(gelu_tanh_activated(f16_to_f32(row[col]), 1));
+        }
+        ctu_oracle_rotate_group(in, out);
+        for (int i = 0; i < KGROUP; ++i) {
+            ybits[g * KGROUP + i] = f32_to_f16(out[i]);
+            absmax = fmaxf(absmax, fabsf(out[i]));
+        }
+    }
+    return absmax;
+}
+
+static void quantize_row_int8_f16(const uint16_t *ybits, int k, float scale, int8_t *codes) {
+    const float rounded_scale = round_f16(scale);
+    for (int c = 0; c < k; ++c) {
+        float q = nearbyintf(round_f16(f16_to_f32(ybits[c]) / rounded_scale));
+        q = fminf(127.0f, fmaxf(-128.0f, q));
+        codes[c] = (int8_t)q;
+    }
+}
+
+/* mode 1 = SwiGLU ([rows, 2k] gate | up), 2 = tanh-GELU; fp16 bit patterns in x. */
+int ctu_oracle_convrot_quantize_staged_f16(const uint16_t *x, int8_t *codes, float *scales, long rows, int k, int bits,
+                                           int mode) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536 || (mode != 1 && mode != 2)) return -1;
+    const int width = mode == 1 ? 2 * k : k;
+    const int out_width = bits == 4 ? k / 2 : k;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            const float clamped = fminf(rotate_row_f16(x + r * width, k, mode, ybits), 65504.0f);
+            if (bits == 4) {
+                const float scale = fmaxf(clamped * (1.0f / 7.0f), 1.0e-10f);
+                scales[r] = scale;
+                const float inv_scale = 1.0f / scale;
+                int8_t *packed = codes + r * out_width;
+                for (int p = 0; p < k / 2; ++p) {
+                    const float lo = fminf(7.0f, fmaxf(-7.0f, nearbyintf(f16_to_f32(ybits[2 * p]) * inv_scale)));
+                    const float hi = fminf(7.0f, fmaxf(-7.0f, nearbyintf(f16_to_f32(ybits[2 * p + 1]) * inv_scale)));
+                    packed[p] = (int8_t)(((uint8_t)(int8_t)lo & 0x0f) | (((uint8_t)(int8_t)hi & 0x0f) << 4));
+                }
+            } else {
+                const float scale = fmaxf(clamped * (1.0f / 127.0f), 1.0e-30f);
+                scales[r] = scale;
+                quantize_row_int8_f16(ybits, k, scale, codes + r * out_width);
+            }
+        }
+    }
+    return 0;
+}
+
+/* turing_swiglu_int8_convrot_quantize_scaled on fp16 rows (convrot_quant.cu:239-278). */
+int ctu_oracle_convrot_quantize_scaled_f16(const uint16_t *x, const float *scales, int8_t *codes, long rows, int k) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            (void)rotate_row_f16(x + r * 2 * k, k, 1, ybits);
+            quantize_row_int8_f16(ybits, k, scales[r], codes + r * k);
+        }
+    }
+    return 0;
 }
 

@@ -63,6 +63,10 @@ def _load():
         lib.ctu_oracle_convrot_quantize.restype = i32
         lib.ctu_oracle_convrot_quantize_staged.argtypes = [vp, vp, vp, i64, i32, i32, i32]
         lib.ctu_oracle_convrot_quantize_staged.restype = i32
+        lib.ctu_oracle_convrot_quantize_staged_f16.argtypes = [vp, vp, vp, i64, i32, i32, i32]
+        lib.ctu_oracle_convrot_quantize_staged_f16.restype = i32
+        lib.ctu_oracle_convrot_quantize_scaled_f16.argtypes = [vp, vp, vp, i64, i32]
+        lib.ctu_oracle_convrot_quantize_scaled_f16.restype = i32
         lib.ctu_oracle_convrot_quantize_scaled.argtypes = [vp, vp, vp, i64, i32, i32]
         lib.ctu_oracle_convrot_quantize_scaled.restype = i32
         lib.ctu_oracle_set_threads.argtypes = [i32]
@@ -144,6 +148,33 @@ def convrot_quantize(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_PLAIN, 
     if rc != 0:
         raise ValueError(f"unsupported ConvRot width {k}")
     return codes, scales
+
+
+def convrot_quantize_staged_f16(x_bits: np.ndarray, bits: int = 8, mode: int = MODE_SWIGLU):
+    """The staged SwiGLU / GELU quantizers on fp16 bit patterns (convrot_quant.cu:184-358
+    with InputType = half): ``(codes, scales)`` like convrot_quantize."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, width = x_bits.shape
+    k = width // 2 if mode == MODE_SWIGLU else width
+    codes = np.empty((rows, k // 2 if bits == 4 else k), dtype=np.int8)
+    scales = np.empty((rows,), dtype=np.float32)
+    rc = _load().ctu_oracle_convrot_quantize_staged_f16(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k, bits,
+                                                        1 if mode == MODE_SWIGLU else 2)
+    if rc != 0:
+        raise ValueError(f"unsupported ConvRot width {k} or mode {mode}")
+    return codes, scales
+
+
+def convrot_quantize_scaled_f16(x_bits: np.ndarray, scales: np.ndarray) -> np.ndarray:
+    """turing_swiglu_int8_convrot_quantize_scaled on fp16 bit patterns."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, width = x_bits.shape
+    k = width // 2
+    scales = np.ascontiguousarray(scales, dtype=np.float32).reshape(-1)
+    codes = np.empty((rows, k), dtype=np.int8)
+    if _load().ctu_oracle_convrot_quantize_scaled_f16(_ptr(x_bits), _ptr(scales), _ptr(codes), rows, k) != 0:
+        raise ValueError(f"unsupported ConvRot width {k}")
+    return codes
 
 
 def convrot_quantize_scaled(x_bits: np.ndarray, scales: np.ndarray, mode: int = MODE_SWIGLU) -> np.ndarray:

@@ -165,15 +165,27 @@ int ref_swiglu_int8_convrot_quantize_scaled(const void *x, const void *scales, v
     });
 }
 
-// kernel/csrc/turing/convrot_quant.cu:535-663 (the staged two-kernel quantizers: rotate +
-// per-group absmax into `rotated` / `partial`, then quantize from the partials).
-// act 1 = SwiGLU (x is [rows, 2k]), 2 = tanh-GELU; bf16 input.
-int ref_staged_convrot_quantize(const void *x, void *codes, void *scales, void *rotated, void *partial, int rows,
-                                int k, int bits, int act, void *stream) {
+// The same on fp16 rows.
+int ref_swiglu_int8_convrot_quantize_scaled_f16(const void *x, const void *scales, void *codes, int rows, int k,
+                                                void *stream) {
     return guarded([&] {
         StreamScope scope(stream);
-        Tensor in = view(const_cast<void *>(x), {rows, act == 1 ? 2 * k : k}, Tensor::BF16);
-        Tensor rot = view(rotated, {rows, k}, Tensor::BF16);
+        ref::turing_swiglu_int8_convrot_quantize_scaled(view(const_cast<void *>(x), {rows, 2 * k}, Tensor::FP16),
+                                                        view(const_cast<void *>(scales), {rows}, Tensor::FP32),
+                                                        view(codes, {rows, k}, Tensor::INT8));
+    });
+}
+
+// kernel/csrc/turing/convrot_quant.cu:535-663 (the staged two-kernel quantizers: rotate +
+// per-group absmax into `rotated` / `partial`, then quantize from the partials).
+// act 1 = SwiGLU (x is [rows, 2k]), 2 = tanh-GELU; bf16 input, or fp16 when fp16 != 0.
+int ref_staged_convrot_quantize(const void *x, void *codes, void *scales, void *rotated, void *partial, int rows,
+                                int k, int bits, int act, int fp16, void *stream) {
+    return guarded([&] {
+        StreamScope scope(stream);
+        const Tensor::ScalarType t = fp16 ? Tensor::FP16 : Tensor::BF16;
+        Tensor in = view(const_cast<void *>(x), {rows, act == 1 ? 2 * k : k}, t);
+        Tensor rot = view(rotated, {rows, k}, t);
         Tensor part = view(partial, {rows, k / 256}, Tensor::FP32);
         Tensor out = view(codes, {rows, bits == 4 ? k / 2 : k}, Tensor::INT8);
         Tensor sc = view(scales, {rows, 1}, Tensor::FP32);

@@ -37,11 +37,12 @@ def load_ref():
     f32 = ctypes.c_float
     lib.ref_segmented_rms_adaln.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, i32, vp]
     lib.ref_layer_norm_adaln.argtypes = [vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, vp]
-    lib.ref_staged_convrot_quantize.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
+    lib.ref_staged_convrot_quantize.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]
+    lib.ref_swiglu_int8_convrot_quantize_scaled_f16.argtypes = [vp, vp, vp, i32, i32, vp]
     for name in ("ref_bf16_convrot_quantize", "ref_bf16_gelu_convrot_quantize", "ref_int8_linear",
                  "ref_w4a8_linear", "ref_dequantize_int8_bf16", "ref_codebook_w4a8_linear",
                  "ref_swiglu_int8_convrot_quantize_scaled", "ref_segmented_rms_adaln", "ref_layer_norm_adaln",
-                 "ref_staged_convrot_quantize"):
+                 "ref_staged_convrot_quantize", "ref_swiglu_int8_convrot_quantize_scaled_f16"):
         getattr(lib, name).restype = i32
     lib.ref_last_error.restype = ctypes.c_char_p
     return lib
@@ -294,24 +295,43 @@ STAGED_CASES = [("swiglu_k256", 1, 256), ("swiglu_k5120", 1, 5120), ("swiglu_k13
 
 def staged_cases(lib, out):
     staged = {}
-    for idx, (name, act, k) in enumerate(STAGED_CASES):
-        width = 2 * k if act == 1 else k
-        x = activations(24, width, 6900 + idx)
-        special = special_rows(width)
-        x[: special.shape[0]] = special[: x.shape[0]]
-        xd = x.cuda().contiguous()
-        rows = x.shape[0]
-        staged[f"{name}__x"] = x.view(torch.int16).numpy().view(np.uint16)
-        for bits in (8, 4):
-            codes = torch.empty((rows, k // 2 if bits == 4 else k), dtype=torch.int8, device="cuda")
-            scales = torch.empty((rows, 1), dtype=torch.float32, device="cuda")
-            rotated = torch.empty((rows, k), dtype=torch.bfloat16, device="cuda")
-            partial = torch.empty((rows, k // 256), dtype=torch.float32, device="cuda")
-            check(lib, lib.ref_staged_convrot_quantize(p(xd), p(codes), p(scales), p(rotated), p(partial), rows, k,
-                                                       bits, act, stream()))
-            torch.cuda.synchronize()
-            staged[f"{name}__int{bits}_codes"] = codes.cpu().numpy()
-            staged[f"{name}__int{bits}_scales"] = scales.cpu().numpy().reshape(-1)
+    for fp16 in (False, True):
+        for idx, (name, act, k) in enumerate(STAGED_CASES):
+            if fp16 and k == 13824:
+                continue
+            width = 2 * k if act == 1 else k
+            x = activations(24, width, 6900 + idx).float()
+            special = special_rows(width).float()
+            x[: special.shape[0]] = special[: x.shape[0]]
+            if fp16:
+                x[4:8] = x[4:8].clamp(-7e4, 7e4)  # values past 65504 become infinities in fp16
+                x[11] = x[11] * 2.0e-6             # fp16 subnormal range
+            x = x.to(torch.float16 if fp16 else torch.bfloat16)
+            xd = x.cuda().contiguous()
+            rows = x.shape[0]
+            key = f"{'f16_' if fp16 else ''}{name}"
+            staged[f"{key}__x"] = x.view(torch.int16).numpy().view(np.uint16)
+            for bits in (8, 4):
+                codes = torch.empty((rows, k // 2 if bits == 4 else k), dtype=torch.int8, device="cuda")
+                scales = torch.empty((rows, 1), dtype=torch.float32, device="cuda")
+                rotated = torch.empty((rows, k), dtype=x.dtype, device="cuda")
+                partial = torch.empty((rows, k // 256), dtype=torch.float32, device="cuda")
+                check(lib, lib.ref_staged_convrot_quantize(p(xd), p(codes), p(scales), p(rotated), p(partial), rows,
+                                                           k, bits, act, 1 if fp16 else 0, stream()))
+                torch.cuda.synchronize()
+                staged[f"{key}__int{bits}_codes"] = codes.cpu().numpy()
+                staged[f"{key}__int{bits}_scales"] = scales.cpu().numpy().reshape(-1)
+    # fp16 SwiGLU shard with caller-supplied scales (special scales included).
+    rows, k = 8, 512
+    x = activations(rows, 2 * k, 6990).float().to(torch.float16)
+    scales = torch.tensor([0.05, 0.0, float("nan"), float("inf"), -0.02, 1e-9, 7e4, 0.013], dtype=torch.float32)
+    codes = torch.empty((rows, k), dtype=torch.int8, device="cuda")
+    check(lib, lib.ref_swiglu_int8_convrot_quantize_scaled_f16(p(x.cuda()), p(scales.cuda()), p(codes), rows, k,
+                                                               stream()))
+    torch.cuda.synchronize()
+    staged["scaled_f16__x"] = x.view(torch.int16).numpy().view(np.uint16)
+    staged["scaled_f16__scales"] = scales.numpy()
+    staged["scaled_f16__codes"] = codes.cpu().numpy()
     np.savez_compressed(out / "staged.npz", **staged)
 
 

@@ -221,10 +221,12 @@ def test_staged_ops_match_reference_staged_kernels(C, kernel):
     # turing_swiglu_int{8,4}_convrot_quantize / turing_gelu_int{8,4}_convrot_quantize keep the
     # staged kernels' scale formula (absmax * (1/qmax)); bit-exact against those kernels.
     z = np.load(STAGED_PATH)
-    for name in sorted({k.split("__")[0] for k in z.files}):
-        x = torch.from_numpy(z[f"{name}__x"].astype(np.int16)).view(torch.bfloat16).cuda()
+    for name in sorted({k.split("__")[0] for k in z.files} - {"scaled_f16"}):
+        fp16 = name.startswith("f16_")
+        x = torch.from_numpy(z[f"{name}__x"].astype(np.int16)).view(torch.float16 if fp16 else torch.bfloat16).cuda()
+        act = "swiglu" if "swiglu" in name else "gelu"
         for bits in (8, 4):
-            fn = getattr(C, f"turing_{name.split('_')[0]}_int{bits}_convrot_quantize")
+            fn = getattr(C, f"turing_{act}_int{bits}_convrot_quantize")
             codes, scales = fn(x, 256)
             torch.cuda.synchronize()
             assert np.array_equal(codes.cpu().numpy(), z[f"{name}__int{bits}_codes"]), (name, bits)
@@ -260,3 +262,21 @@ def test_staged_ops_match_oracle(C, kernel, act, k):
             want = want_codes
         diff = np.abs(got.astype(np.int32) - want.astype(np.int32))
         assert diff.max() <= 1 and np.mean(diff != 0) < (1e-2 if act == "swiglu" else 1e-3)
+
+
+@pytest.mark.skipif(not STAGED_PATH.exists(), reason="staged fixtures not generated")
+def test_scaled_swiglu_fp16_matches_reference(C):
+    z = np.load(STAGED_PATH)
+    x = torch.from_numpy(z["scaled_f16__x"].astype(np.int16)).view(torch.float16).cuda()
+    codes = C.turing_swiglu_int8_convrot_quantize_scaled(x, torch.from_numpy(z["scaled_f16__scales"]).cuda(), 256)
+    torch.cuda.synchronize()
+    assert np.array_equal(codes.cpu().numpy(), z["scaled_f16__codes"])
+
+
+def test_row_buffer_names_reject_fp16(C):
+    x = torch.zeros((4, 512), dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        C.turing_bf16_int8_convrot_quantize(x, 256)
+    with pytest.raises(RuntimeError, match="bfloat16"):
+        C.turing_bf16_gelu_int8_convrot_quantize(x, 256)
+
