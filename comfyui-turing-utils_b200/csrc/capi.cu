@@ -907,7 +907,8 @@ int ctu_layer_norm_adaln(const void *x, const void *scale, const void *shift, vo
     a.hidden = static_cast<int>(hidden);
     a.modulation_steps = static_cast<int>(modulation_steps);
     a.epsilon = epsilon;
-    CTU_CUDA(ctu::norm::launch_layer_norm_adaln(a, dtype, static_cast<cudaStream_t>(stream)));
+    a.err = dev.err;
+    CTU_CUDA(ctu::norm::launch_layer_norm_adaln(a, dtype, dev.num_sms, static_cast<cudaStream_t>(stream)));
     return CTU_OK;
 }
 

@@ -16,7 +16,11 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "norm_adaln.cuh"
 #include "norm_math.cuh"
@@ -249,13 +253,16 @@ __device__ __forceinline__ uint4 ln_vector(const uint4 x, const uint4 s, const u
         };
         return make_uint4(f(x.x, s.x, h.x), f(x.y, s.y, h.y), f(x.z, s.z, h.z), f(x.w, s.w, h.w));
     } else {
+        // ln_output on two values per packed instruction; each rounding to the storage
+        // type is the pack of the pair (round to nearest even per lane).
         using Wd = Words<T>;
+        const f32x2 mean2 = pk2(mean, mean);
+        const f32x2 inv2 = pk2(inv, inv);
+        const f32x2 one2 = pk2(1.0f, 1.0f);
         auto f = [&](uint32_t xw, uint32_t sw, uint32_t hw) {
-            float x0, x1, s0, s1, h0, h1;
-            unpk2(Wd::unpack(xw), x0, x1);
-            unpk2(Wd::unpack(sw), s0, s1);
-            unpk2(Wd::unpack(hw), h0, h1);
-            return Wd::pack(pk2(ln_output<T>(x0, mean, inv, s0, h0), ln_output<T>(x1, mean, inv, s1, h1)));
+            const f32x2 normalized = Wd::unpack(Wd::pack(fmul2(fsub2(Wd::unpack(xw), mean2), inv2)));
+            const f32x2 multiplier = Wd::unpack(Wd::pack(fadd2(one2, Wd::unpack(sw))));
+            return Wd::pack(ffma2(normalized, multiplier, Wd::unpack(hw)));
         };
         (void)sizeof(E);
         return make_uint4(f(x.x, s.x, h.x), f(x.y, s.y, h.y), f(x.z, s.z, h.z), f(x.w, s.w, h.w));
@@ -268,58 +275,125 @@ struct Welford {
     int count;
 };
 
-__device__ __noinline__ float ieee_div(float a, float b) { return __fdiv_rn(a, b); }
-
-// a / count with IEEE round-to-nearest, for a positive integer count: the correction
-// step of Markstein's division with rcp = RN(1 / count) -- q0 = a * rcp,
-// r = fma(-q0, count, a) (exact), q = fma(r, rcp, q0) -- which equals the IEEE quotient
-// for every count <= kMaxMarksteinCount and every a with 2^-96 <= |a| <= FLT_MAX (checked
-// over every significand by tests/native/division_check.c); the IEEE division otherwise.
-constexpr int kMaxMarksteinCount = 16384;
-
-__device__ __forceinline__ float div_by_count(float a, float count, float rcp, bool count_ok) {
-    const float mag = fabsf(a);
-    if (count_ok && mag >= 0x1p-96f && mag <= 3.40282347e38f) {
-        const float q0 = __fmul_rn(a, rcp);
-        return __fmaf_rn(__fmaf_rn(-q0, count, a), rcp, q0);
-    }
-    return ieee_div(a, count);
-}
-
-// welford_combine, segmented_rms_adaln.cu:89-105 (same operation order).
-__device__ __forceinline__ Welford combine(Welford l, const Welford r) {
-    if (r.count == 0) return l;
-    if (l.count == 0) return r;
-    const int count = l.count + r.count;
-    const float c = static_cast<float>(count);
-    const float lc = static_cast<float>(l.count);
-    const float rc = static_cast<float>(r.count);
-    const bool ok = count <= kMaxMarksteinCount;
-    const float rcp = ok ? __frcp_rn(c) : 0.0f;
-    const float delta = __fsub_rn(r.mean, l.mean);
-    l.mean = __fadd_rn(l.mean, div_by_count(__fmul_rn(delta, rc), c, rcp, ok));
-    l.m2 = __fadd_rn(l.m2, __fadd_rn(r.m2, div_by_count(__fmul_rn(__fmul_rn(__fmul_rn(delta, delta), lc), rc), c,
-                                                        rcp, ok)));
-    l.count = count;
-    return l;
-}
-
-// Welford step of the register-cached pass, where the count is the compile-time `count`
-// (every earlier cached column of the thread was pushed) and `rcp` = RN(1 / count) is a
-// compile-time constant; the division is div_by_count's.
-__device__ __forceinline__ void welford_push_fixed(Welford &s, float v, float count, float rcp) {
-    ++s.count;
-    const float delta = __fsub_rn(v, s.mean);
-    s.mean = __fadd_rn(s.mean, div_by_count(delta, count, rcp, true));
-    s.m2 = __fmaf_rn(delta, __fsub_rn(v, s.mean), s.m2);
-}
-
+// Welford step with IEEE division by the new count (segmented_rms_adaln.cu:74-78).
 __device__ __forceinline__ void welford_push(Welford &s, float v) {
     ++s.count;
     const float delta = __fsub_rn(v, s.mean);
     s.mean = __fadd_rn(s.mean, __fdiv_rn(delta, static_cast<float>(s.count)));
     s.m2 = __fmaf_rn(delta, __fsub_rn(v, s.mean), s.m2);
 }
+
+// welford_combine, segmented_rms_adaln.cu:86-100 (same operation order, IEEE division).
+__device__ __forceinline__ Welford combine_ieee(Welford l, const Welford r) {
+    if (r.count == 0) return l;
+    if (l.count == 0) return r;
+    const int count = l.count + r.count;
+    const float c = static_cast<float>(count);
+    const float delta = __fsub_rn(r.mean, l.mean);
+    l.mean = __fadd_rn(l.mean, __fdiv_rn(__fmul_rn(delta, static_cast<float>(r.count)), c));
+    l.m2 = __fadd_rn(l.m2, __fadd_rn(r.m2, __fdiv_rn(__fmul_rn(__fmul_rn(__fmul_rn(delta, delta),
+                                                                        static_cast<float>(l.count)),
+                                                               static_cast<float>(r.count)),
+                                                      c)));
+    l.count = count;
+    return l;
+}
+
+// a / c for a positive integer c by the correction step of Markstein's division with
+// rcp = RN(1 / c): q0 = a * rcp, r = fma(-q0, c, a) (exact), q = fma(r, rcp, q0).  It
+// equals the IEEE quotient for every c <= kMaxMarksteinCount and every a with
+// 2^-96 <= |a| <= FLT_MAX (checked over every significand by
+// tests/native/division_check.c), and is NaN for a NaN a as the IEEE one is.  For a == 0
+// it returns +0 where IEEE gives the sign of a; that cannot change any sum below, because
+// no running mean or m2 is ever -0 (they start at +0, and a round-to-nearest sum is -0
+// only when both terms are), so x + (+-0) == x.
+constexpr int kMaxMarksteinCount = 16384;
+
+__device__ __forceinline__ float markstein_div(float a, float c, float rcp) {
+    const float q0 = __fmul_rn(a, rcp);
+    return __fmaf_rn(__fmaf_rn(-q0, c, a), rcp, q0);
+}
+
+// False when markstein_div(a, ...) may differ from the IEEE quotient: 0 < |a| < 2^-96 or
+// |a| infinite.
+__device__ __forceinline__ bool markstein_safe(float a) {
+    const float mag = fabsf(a);
+    return !(mag > 3.40282347e38f) && !(mag < 0x1p-96f && mag != 0.0f);
+}
+
+// Reciprocal of the count of Welford step I (the count is I + 1), a compile-time constant.
+template <int I>
+struct StepRcp {
+    static constexpr float value = 1.0f / static_cast<float>(I + 1);
+};
+
+// Welford step I of one thread (column tid + I * 256), count and reciprocal constants.
+template <int I, typename T, typename Load>
+__device__ __forceinline__ void welford_step(Welford &st, Load load, int tid, bool &exact) {
+    const float v = Elem<T>::load(load(tid + I * kRowThreads));
+    const float delta = __fsub_rn(v, st.mean);
+    exact = exact && markstein_safe(delta);
+    st.mean = __fadd_rn(st.mean, markstein_div(delta, static_cast<float>(I + 1), StepRcp<I>::value));
+    st.m2 = __fmaf_rn(delta, __fsub_rn(v, st.mean), st.m2);
+}
+
+// Welford steps I..N-1 of one thread (columns tid + I * 256, ...).  Steps that every
+// thread takes run unguarded; the first one that not every thread takes is the last and
+// is guarded per thread (the tests on I are uniform).  `exact` is cleared when a step's
+// quotient may differ from the IEEE one; the caller then redoes the chain.
+template <int I, int N, typename T, typename Load>
+__device__ __forceinline__ void welford_steps(Welford &st, Load load, int hidden, int tid, bool &exact) {
+    if constexpr (I < N) {
+        if ((I + 1) * kRowThreads <= hidden) {
+            welford_step<I, T>(st, load, tid, exact);
+            welford_steps<I + 1, N, T>(st, load, hidden, tid, exact);
+        } else if (tid + I * kRowThreads < hidden) {
+            welford_step<I, T>(st, load, tid, exact);
+        }
+    }
+}
+
+// The counts of one combine are fixed by the row length alone, so each CTA works them
+// out once: (left count, right count, total, RN(1 / total)) as floats (rcp 0 when the
+// total is 0 or above kMaxMarksteinCount).
+__device__ __forceinline__ float4 combine_plan(int lc, int rc) {
+    const int c = lc + rc;
+    const float rcp = (c > 0 && c <= kMaxMarksteinCount) ? __frcp_rn(static_cast<float>(c)) : 0.0f;
+    return make_float4(static_cast<float>(lc), static_cast<float>(rc), static_cast<float>(c), rcp);
+}
+
+// welford_combine on (mean, m2) for two positive counts with a total of at most
+// kMaxMarksteinCount, taken from `plan`.  Returns false when a quotient may differ from
+// the IEEE one (the caller redoes the reduction with IEEE division).  Both quotients are
+// exact when delta == 0 or 2^-96 <= |a2| <= FLT_MAX, a2 = delta^2 * lc * rc: then
+// a1 = delta * rc is in that range too (with lc * rc <= 2^28, a2 >= 2^-96 needs
+// |delta| >= 2^-62, and |delta| >= 1 gives |a1| <= |a2|).  A NaN stays NaN on both paths.
+__device__ __forceinline__ bool combine_fast(float &mean, float &m2, float rmean, float rm2, const float4 plan) {
+    const float delta = __fsub_rn(rmean, mean);
+    const float a1 = __fmul_rn(delta, plan.y);
+    const float a2 = __fmul_rn(__fmul_rn(__fmul_rn(delta, delta), plan.x), plan.y);
+    mean = __fadd_rn(mean, markstein_div(a1, plan.z, plan.w));
+    m2 = __fadd_rn(m2, __fadd_rn(rm2, markstein_div(a2, plan.z, plan.w)));
+    const float mag = fabsf(a2);
+    return delta == 0.0f || !(mag < 0x1p-96f || mag > 3.40282347e38f);
+}
+
+// combine_fast where either count may be 0 (rows shorter than 256 columns): a right
+// count of 0 keeps the left state and a left count of 0 takes the right one, as
+// welford_combine's early returns do.
+__device__ __forceinline__ bool combine_general(float &mean, float &m2, float rmean, float rm2, const float4 plan) {
+    float nmean = mean, nm2 = m2;
+    const bool ok = combine_fast(nmean, nm2, rmean, rm2, plan);
+    const bool keep = plan.y == 0.0f;
+    const bool take = plan.x == 0.0f;
+    mean = keep ? mean : (take ? rmean : nmean);
+    m2 = keep ? m2 : (take ? rm2 : nm2);
+    return keep || take || ok;
+}
+
+constexpr int kTreeLevels = 5;  // shfl_down offsets 16, 8, 4, 2, 1
+enum TreeMode : int { kTreeFast = 0, kTreeGeneral = 1, kTreeIeee = 2 };
+constexpr size_t kTreePlanBytes = static_cast<size_t>(kTreeLevels) * kRowThreads * sizeof(float4);
 
 // Modulation row offset of token row `row` (segmented_rms_adaln.cu:248-257).
 __device__ __forceinline__ int64_t ln_modulation_offset(const LnArgs &a, int64_t row) {
@@ -334,113 +408,215 @@ __device__ __forceinline__ int64_t ln_modulation_offset(const LnArgs &a, int64_t
     return (batch * a.modulation_steps + mtoken) * a.hidden;
 }
 
-// Mean and 1/std of the row held in `row_s`, in the reference's order: Welford per
-// thread over columns t, t+256, ... (the first kSteps steps with the compile-time
-// reciprocal of the count), the shfl_down Welford tree, the in-order combine of the
-// 8 warps by warp 0.  Every thread of the CTA must call it.
-template <typename T, int kSteps, typename Load>
-__device__ __forceinline__ void ln_statistics(Load load, int hidden, float epsilon, float *warp_mean,
-                                              float *warp_m2, int *warp_count, float &mean, float &inv) {
+// LayerNorm + AdaLN over rows blockIdx.x, blockIdx.x + gridDim.x, ... (persistent CTAs of
+// 256 threads).  Statistics in the reference's order: Welford per thread over columns t,
+// t+256, ..., the shfl_down Welford tree in each warp, then warp 0 combines the 8 warp
+// partials in order; every division by a count is the Markstein step with the count's
+// reciprocal worked out in advance, and a row whose operands leave markstein_safe's
+// range is redone with IEEE division.
+// kStaged: the row (at most kLnSmemBytes) is copied into one of two shared-memory
+// buffers -- a bulk copy issued one row ahead when rows are 16-byte aligned, plain loads
+// otherwise -- and both passes read it from there.  Otherwise both passes read HBM.
+template <typename T, bool kStaged>
+__global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnArgs a) {
     using E = Elem<T>;
+    constexpr int W = Vec<T>::kWidth;
+    extern __shared__ float4 ln_smem[];
+    float4 *tree_plan = ln_smem;  // [level][thread]
+    uint8_t *bufs = reinterpret_cast<uint8_t *>(ln_smem + kTreeLevels * kRowThreads);
+    __shared__ float4 warp_plan[kWarps];
+    __shared__ int warp_count[kWarps];
+    __shared__ float warp_mean[kWarps];
+    __shared__ float warp_m2[kWarps];
+    __shared__ float row_mean;
+    __shared__ float row_inv;
+    __shared__ long long row_mod;
+    __shared__ __align__(8) uint64_t full[2];
+
     const int tid = static_cast<int>(threadIdx.x);
     const int lane = tid & 31;
     const int warp = tid >> 5;
-    Welford st{0.0f, 0.0f, 0};
+    const int hidden = a.hidden;
+    const uint32_t row_bytes = static_cast<uint32_t>(hidden) * static_cast<uint32_t>(sizeof(T));
+    const uint32_t buf_bytes = (row_bytes + 15u) & ~15u;
+    const bool bulk = kStaged && a.vector_in;
+
+    // Counts of every combine of this CTA's rows.
+    {
+        int count = hidden > tid ? (hidden - 1 - tid) / kRowThreads + 1 : 0;
 #pragma unroll
-    for (int i = 0; i < kSteps; ++i) {
-        const int c = tid + i * kRowThreads;
-        if (c < hidden) welford_push_fixed(st, E::load(load(c)), static_cast<float>(i + 1), 1.0f / static_cast<float>(i + 1));
+        for (int k = 0; k < kTreeLevels; ++k) {
+            const int off = 16 >> k;
+            const int right = __shfl_down_sync(0xffffffffu, count, off);
+            const int rc = lane + off < 32 ? right : 0;  // lanes past the warp end are discarded
+            tree_plan[k * kRowThreads + tid] = combine_plan(count, rc);
+            count += rc;
+        }
+        if (lane == 0) warp_count[warp] = count;
     }
-    for (int c = tid + kSteps * kRowThreads; c < hidden; c += kRowThreads) welford_push(st, E::load(load(c)));
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) {
-        const Welford other{__shfl_down_sync(0xffffffffu, st.mean, off), __shfl_down_sync(0xffffffffu, st.m2, off),
-                            __shfl_down_sync(0xffffffffu, st.count, off)};
-        st = combine(st, other);
-    }
-    if (lane == 0) {
-        warp_mean[warp] = st.mean;
-        warp_m2[warp] = st.m2;
-        warp_count[warp] = st.count;
+    if (tid == 0 && bulk) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
     }
     __syncthreads();
-    if (warp == 0) {
-        st = Welford{0.0f, 0.0f, 0};
-#pragma unroll
-        for (int w = 0; w < kWarps; ++w) st = combine(st, Welford{warp_mean[w], warp_m2[w], warp_count[w]});
-        __syncwarp();
-        if (lane == 0) {
-            warp_mean[0] = st.mean;
-            warp_m2[0] = rsqrtf(__fadd_rn(__fdiv_rn(st.m2, static_cast<float>(st.count)), epsilon));
+    if (tid == 0) {
+        int total = 0;
+        for (int w = 0; w < kWarps; ++w) {
+            warp_plan[w] = combine_plan(total, warp_count[w]);
+            total += warp_count[w];
+        }
+        if (bulk && static_cast<int64_t>(blockIdx.x) < a.rows) {
+            mbar_arrive_expect_tx(&full[0], row_bytes);
+            bulk_load(bufs, static_cast<const T *>(a.x) + static_cast<int64_t>(blockIdx.x) * hidden, row_bytes,
+                      &full[0]);
         }
     }
     __syncthreads();
-    mean = warp_mean[0];
-    inv = warp_m2[0];
-}
+    // Which combines take the Markstein path: every tree count and total is at most
+    // kMaxMarksteinCount (warp 0 holds the most columns), and (fast) every count is
+    // positive.  Warp 0's partial always has a count, so the in-order combine of the
+    // warps starts from it (welford_combine with an empty left state returns the right).
+    const int tree_mode = warp_count[0] > kMaxMarksteinCount ? kTreeIeee
+                          : hidden >= kRowThreads            ? kTreeFast
+                                                             : kTreeGeneral;
+    const int final_mode = hidden > kMaxMarksteinCount      ? kTreeIeee
+                           : hidden > (kWarps - 1) * 32      ? kTreeFast
+                                                             : kTreeGeneral;
 
-// Rows of at most kLnSmemBytes: the row is staged in shared memory with 16-byte loads
-// (all of them in flight at once), the strided Welford pass reads it from there, and the
-// output pass reads it back as 16-byte vectors.
-template <typename T, int kSteps>
-__global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnArgs a) {
-    using E = Elem<T>;
-    extern __shared__ uint4 row_v[];
-    __shared__ float warp_mean[kWarps];
-    __shared__ float warp_m2[kWarps];
-    __shared__ int warp_count[kWarps];
-    const T *row_s = reinterpret_cast<const T *>(row_v);
+    int it = 0;
+    for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x, ++it) {
+        const T *x = static_cast<const T *>(a.x) + row * hidden;
+        const int b = it & 1;
+        const T *row_s = reinterpret_cast<const T *>(bufs + b * buf_bytes);
+        bool ok = true;
+        if constexpr (kStaged) {
+            if (bulk) {
+                ok = mbar_wait(&full[b], static_cast<uint32_t>(it >> 1) & 1u, nullptr, a.err, kErrTimeoutFull);
+            } else {
+                // Buffer b was last read two rows ago, before the previous row's barriers.
+                T *rw = reinterpret_cast<T *>(bufs + b * buf_bytes);
+                for (int c = tid; c < hidden; c += kRowThreads) rw[c] = x[c];
+                __syncthreads();
+            }
+        }
+        auto load = [&](int c) -> T {
+            if constexpr (kStaged) {
+                return row_s[c];
+            } else {
+                return x[c];
+            }
+        };
 
-    const int64_t row = blockIdx.x;
-    const int tid = static_cast<int>(threadIdx.x);
-    const T *x = static_cast<const T *>(a.x) + row * a.hidden;
-    constexpr int W = Vec<T>::kWidth;
-    if (a.vector_in) {
-        const uint4 *xv = reinterpret_cast<const uint4 *>(x);
-        for (int j = tid; j < a.hidden / W; j += kRowThreads) row_v[j] = xv[j];
-    } else {
-        T *rw = reinterpret_cast<T *>(row_v);
-        for (int c = tid; c < a.hidden; c += kRowThreads) rw[c] = x[c];
+        // Per-thread Welford chain.
+        Welford st{0.0f, 0.0f, 0};
+        bool exact = true;
+        welford_steps<0, kLnSteps, T>(st, load, hidden, tid, exact);
+        st.count = hidden > tid ? min(kLnSteps, (hidden - 1 - tid) / kRowThreads + 1) : 0;
+        if (!exact) {
+            st = Welford{0.0f, 0.0f, 0};
+#pragma unroll 1
+            for (int c = tid; c < min(hidden, kLnSteps * kRowThreads); c += kRowThreads)
+                welford_push(st, E::load(load(c)));
+        }
+#pragma unroll 1
+        for (int c = tid + kLnSteps * kRowThreads; c < hidden; c += kRowThreads) welford_push(st, E::load(load(c)));
+
+        // Warp tree.  Lanes whose partner lies past the warp end read their own state
+        // (delta 0); their results, like those of every lane >= off, are discarded.
+        {
+            const float mean0 = st.mean, m20 = st.m2;
+            bool good = tree_mode != kTreeIeee;
+            if (tree_mode == kTreeFast) {
+#pragma unroll
+                for (int k = 0; k < kTreeLevels; ++k) {
+                    const float rmean = __shfl_down_sync(0xffffffffu, st.mean, 16 >> k);
+                    const float rm2 = __shfl_down_sync(0xffffffffu, st.m2, 16 >> k);
+                    good = combine_fast(st.mean, st.m2, rmean, rm2, tree_plan[k * kRowThreads + tid]) && good;
+                }
+            } else if (tree_mode == kTreeGeneral) {
+#pragma unroll
+                for (int k = 0; k < kTreeLevels; ++k) {
+                    const float rmean = __shfl_down_sync(0xffffffffu, st.mean, 16 >> k);
+                    const float rm2 = __shfl_down_sync(0xffffffffu, st.m2, 16 >> k);
+                    good = combine_general(st.mean, st.m2, rmean, rm2, tree_plan[k * kRowThreads + tid]) && good;
+                }
+            }
+            if (!__all_sync(0xffffffffu, good)) {
+                Welford w{mean0, m20, hidden > tid ? (hidden - 1 - tid) / kRowThreads + 1 : 0};
+#pragma unroll 1
+                for (int off = 16; off > 0; off >>= 1) {
+                    const Welford other{__shfl_down_sync(0xffffffffu, w.mean, off),
+                                        __shfl_down_sync(0xffffffffu, w.m2, off),
+                                        __shfl_down_sync(0xffffffffu, w.count, off)};
+                    w = combine_ieee(w, other);
+                }
+                st.mean = w.mean;
+                st.m2 = w.m2;
+            }
+        }
+        if (lane == 0) {
+            warp_mean[warp] = st.mean;
+            warp_m2[warp] = st.m2;
+        }
+        if (__syncthreads_or(!ok)) {
+            // A row copy did not arrive in time: wait (bounded) for it, then stop.
+            if (tid == 0 && bulk) (void)mbar_wait(&full[b], static_cast<uint32_t>(it >> 1) & 1u, nullptr, a.err,
+                                                  kErrTimeoutDrain);
+            return;
+        }
+        if (tid == 0 && bulk && row + gridDim.x < a.rows) {
+            // Prefetch the CTA's next row into the other buffer, last read one row ago.
+            const int nb = b ^ 1;
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&full[nb], row_bytes);
+            bulk_load(bufs + nb * buf_bytes, x + static_cast<int64_t>(gridDim.x) * hidden, row_bytes, &full[nb]);
+        }
+        if (warp == 0) {
+            float mean = warp_mean[0], m2 = warp_m2[0];
+            bool good = final_mode != kTreeIeee;
+            if (final_mode == kTreeFast) {
+#pragma unroll
+                for (int w = 1; w < kWarps; ++w)
+                    good = combine_fast(mean, m2, warp_mean[w], warp_m2[w], warp_plan[w]) && good;
+            } else if (final_mode == kTreeGeneral) {
+#pragma unroll
+                for (int w = 1; w < kWarps; ++w)
+                    good = combine_general(mean, m2, warp_mean[w], warp_m2[w], warp_plan[w]) && good;
+            }
+            if (!good) {
+                Welford s{0.0f, 0.0f, 0};
+#pragma unroll 1
+                for (int w = 0; w < kWarps; ++w) s = combine_ieee(s, Welford{warp_mean[w], warp_m2[w], warp_count[w]});
+                mean = s.mean;
+                m2 = s.m2;
+            }
+            if (lane == 0) {
+                row_mean = mean;
+                row_inv = rsqrtf(__fadd_rn(__fdiv_rn(m2, static_cast<float>(hidden)), a.epsilon));
+                row_mod = ln_modulation_offset(a, row);
+            }
+        }
+        __syncthreads();
+        const float mean = row_mean;
+        const float inv = row_inv;
+        const int64_t mod_off = row_mod;
+
+        const T *scale = static_cast<const T *>(a.scale) + mod_off;
+        const T *shift = static_cast<const T *>(a.shift) + mod_off;
+        T *out = static_cast<T *>(a.out) + row * hidden;
+        if (a.vector_out && (kStaged || a.vector_in)) {
+            const uint4 *xv = kStaged ? reinterpret_cast<const uint4 *>(row_s) : reinterpret_cast<const uint4 *>(x);
+            const uint4 *sv = reinterpret_cast<const uint4 *>(scale);
+            const uint4 *hv = reinterpret_cast<const uint4 *>(shift);
+            uint4 *ov = reinterpret_cast<uint4 *>(out);
+            for (int j = tid; j < hidden / W; j += kRowThreads)
+                ov[j] = ln_vector<T>(xv[j], __ldg(sv + j), __ldg(hv + j), mean, inv);
+        } else {
+            for (int c = tid; c < hidden; c += kRowThreads)
+                out[c] = E::store(ln_output<T>(E::load(load(c)), mean, inv, E::load(scale[c]), E::load(shift[c])));
+        }
     }
-    __syncthreads();
-    float mean, inv;
-    ln_statistics<T, kSteps>([&](int c) { return row_s[c]; }, a.hidden, a.epsilon, warp_mean, warp_m2, warp_count,
-                             mean, inv);
-
-    const int64_t mod_off = ln_modulation_offset(a, row);
-    const T *scale = static_cast<const T *>(a.scale) + mod_off;
-    const T *shift = static_cast<const T *>(a.shift) + mod_off;
-    T *out = static_cast<T *>(a.out) + row * a.hidden;
-    if (a.vector_out) {
-        const uint4 *sv = reinterpret_cast<const uint4 *>(scale);
-        const uint4 *hv = reinterpret_cast<const uint4 *>(shift);
-        uint4 *ov = reinterpret_cast<uint4 *>(out);
-        for (int j = tid; j < a.hidden / W; j += kRowThreads) ov[j] = ln_vector<T>(row_v[j], __ldg(sv + j), __ldg(hv + j), mean, inv);
-    } else {
-        for (int c = tid; c < a.hidden; c += kRowThreads)
-            out[c] = E::store(ln_output<T>(E::load(row_s[c]), mean, inv, E::load(scale[c]), E::load(shift[c])));
-    }
-}
-
-// Rows larger than kLnSmemBytes: the same computation reading the row from global memory
-// in both passes.
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_wide_kernel(const LnArgs a) {
-    using E = Elem<T>;
-    __shared__ float warp_mean[kWarps];
-    __shared__ float warp_m2[kWarps];
-    __shared__ int warp_count[kWarps];
-    const int64_t row = blockIdx.x;
-    const T *x = static_cast<const T *>(a.x) + row * a.hidden;
-    float mean, inv;
-    ln_statistics<T, 8>([&](int c) { return x[c]; }, a.hidden, a.epsilon, warp_mean, warp_m2, warp_count, mean,
-                        inv);
-    const int64_t mod_off = ln_modulation_offset(a, row);
-    const T *scale = static_cast<const T *>(a.scale) + mod_off;
-    const T *shift = static_cast<const T *>(a.shift) + mod_off;
-    T *out = static_cast<T *>(a.out) + row * a.hidden;
-    for (int c = static_cast<int>(threadIdx.x); c < a.hidden; c += kRowThreads)
-        out[c] = E::store(ln_output<T>(E::load(x[c]), mean, inv, E::load(scale[c]), E::load(shift[c])));
 }
 
 template <typename T, bool kVec>
@@ -460,21 +636,49 @@ cudaError_t launch_rms_t(const RmsArgs &a, cudaStream_t stream) {
     return cudaGetLastError();
 }
 
+// CTAs per SM of one LayerNorm kernel at one shared-memory size, per device.  Filled on
+// first use, so the first call of a shape should come before any stream capture.
+std::mutex g_ln_mutex;
+std::map<std::tuple<const void *, int, size_t>, int> g_ln_occupancy;
+
+cudaError_t ln_ctas_per_sm(const void *kernel, size_t smem, int *per_sm) {
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return e;
+    const auto key = std::make_tuple(kernel, device, smem);
+    {
+        std::lock_guard<std::mutex> lock(g_ln_mutex);
+        auto it = g_ln_occupancy.find(key);
+        if (it != g_ln_occupancy.end()) {
+            *per_sm = it->second;
+            return cudaSuccess;
+        }
+    }
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kTreePlanBytes + 2 * kLnSmemBytes));
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kernel, kRowThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (*per_sm < 1) return cudaErrorInvalidConfiguration;
+    std::lock_guard<std::mutex> lock(g_ln_mutex);
+    g_ln_occupancy[key] = *per_sm;
+    return cudaSuccess;
+}
+
 template <typename T>
-cudaError_t launch_ln_t(const LnArgs &a, cudaStream_t stream) {
-    const int per_thread = (a.hidden + kRowThreads - 1) / kRowThreads;
-    const size_t bytes = (static_cast<size_t>(a.hidden) * sizeof(T) + 15) & ~size_t(15);
-    const dim3 grid(static_cast<unsigned>(a.rows));
-    if (bytes > kLnSmemBytes) {
-        layer_norm_adaln_wide_kernel<T><<<grid, kRowThreads, 0, stream>>>(a);
-    } else if (per_thread <= 8) {
-        layer_norm_adaln_kernel<T, 8><<<grid, kRowThreads, bytes, stream>>>(a);
-    } else if (per_thread <= 16) {
-        layer_norm_adaln_kernel<T, 16><<<grid, kRowThreads, bytes, stream>>>(a);
-    } else if (per_thread <= 32) {
-        layer_norm_adaln_kernel<T, 32><<<grid, kRowThreads, bytes, stream>>>(a);
+cudaError_t launch_ln_t(const LnArgs &a, int num_sms, cudaStream_t stream) {
+    const size_t row_bytes = (static_cast<size_t>(a.hidden) * sizeof(T) + 15) & ~size_t(15);
+    const bool staged = row_bytes <= static_cast<size_t>(kLnSmemBytes);
+    const void *kernel = staged ? reinterpret_cast<const void *>(layer_norm_adaln_kernel<T, true>)
+                                : reinterpret_cast<const void *>(layer_norm_adaln_kernel<T, false>);
+    const size_t smem = kTreePlanBytes + (staged ? 2 * row_bytes : 0);
+    int per_sm = 0;
+    cudaError_t e = ln_ctas_per_sm(kernel, smem, &per_sm);
+    if (e != cudaSuccess) return e;
+    const dim3 grid(static_cast<unsigned>(std::min<int64_t>(a.rows, static_cast<int64_t>(num_sms) * per_sm)));
+    if (staged) {
+        layer_norm_adaln_kernel<T, true><<<grid, kRowThreads, smem, stream>>>(a);
     } else {
-        layer_norm_adaln_kernel<T, kLnSteps><<<grid, kRowThreads, bytes, stream>>>(a);
+        layer_norm_adaln_kernel<T, false><<<grid, kRowThreads, smem, stream>>>(a);
     }
     return cudaGetLastError();
 }
@@ -505,18 +709,18 @@ cudaError_t launch_segmented_rms_adaln(const RmsArgs &args, int type, cudaStream
     }
 }
 
-cudaError_t launch_layer_norm_adaln(const LnArgs &args, int type, cudaStream_t stream) {
+cudaError_t launch_layer_norm_adaln(const LnArgs &args, int type, int num_sms, cudaStream_t stream) {
     LnArgs a = args;
     const int width = type == kNormFp32 ? 4 : 8;
     a.vector_in = a.hidden % width == 0 && aligned16(a.x);
     a.vector_out = a.hidden % width == 0 && aligned16(a.scale) && aligned16(a.shift) && aligned16(a.out);
     switch (type) {
         case kNormBf16:
-            return launch_ln_t<__nv_bfloat16>(a, stream);
+            return launch_ln_t<__nv_bfloat16>(a, num_sms, stream);
         case kNormFp16:
-            return launch_ln_t<__half>(a, stream);
+            return launch_ln_t<__half>(a, num_sms, stream);
         case kNormFp32:
-            return launch_ln_t<float>(a, stream);
+            return launch_ln_t<float>(a, num_sms, stream);
         default:
             return cudaErrorInvalidValue;
     }

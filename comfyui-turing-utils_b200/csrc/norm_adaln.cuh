@@ -16,6 +16,7 @@ constexpr int kRowThreads = 256;     // threads per row: fixes the reduction ord
 constexpr int kRmsCacheVectors = 8;  // 16-byte vectors a thread keeps in registers
 constexpr int kLnSmemBytes = 48 * 1024;  // LayerNorm rows up to this size are staged in shared memory
 constexpr int kLnSteps = 96;              // Welford steps a thread takes with a compile-time reciprocal
+                                          // (every step of a staged row)
 
 struct RmsArgs {
     const void *x;         // [rows, hidden]
@@ -46,6 +47,7 @@ struct LnArgs {
     float epsilon;
     int vector_in;      // 1 when x rows may be read as 16-byte vectors (set by the launcher)
     int vector_out;     // 1 when scale / shift / out may use 16-byte vectors (set by the launcher)
+    uint32_t *err;      // device error word (bounded-wait timeouts)
 };
 
 // True when the reference launch takes its 16-byte vector path
@@ -53,7 +55,7 @@ struct LnArgs {
 bool rms_vectorized(const RmsArgs &a, int type);
 
 cudaError_t launch_segmented_rms_adaln(const RmsArgs &a, int type, cudaStream_t stream);
-cudaError_t launch_layer_norm_adaln(const LnArgs &a, int type, cudaStream_t stream);
+cudaError_t launch_layer_norm_adaln(const LnArgs &a, int type, int num_sms, cudaStream_t stream);
 
 }  // namespace norm
 }  // namespace ctu

@@ -256,6 +256,40 @@ def test_norm_kernels_against_reference_kernels_timing(K, capsys):
     assert ours_ln < 1.25 * ref_ln
 
 
+@pytest.mark.skipif(not REF_LIB.exists(), reason="reference kernels not built (make -C oracle ref)")
+@pytest.mark.parametrize("code,batch,seq,hidden,steps", [
+    (0, 2, 3000, 5120, 1), (0, 1, 4096, 1001, 3), (1, 3, 700, 3072, 2), (2, 1, 2500, 4096, 5),
+    (0, 1, 5000, 24, 1), (0, 1, 300, 20000, 2), (0, 1, 200, 30000, 1), (2, 2, 400, 12288, 1),
+])
+def test_layer_norm_many_rows_bit_exact_against_reference_kernel(K, code, batch, seq, hidden, steps):
+    # Thousands of rows, so that every persistent CTA takes several rows (and the one-row
+    # -ahead copies), with rows that leave the fast division range: zeros, a constant row,
+    # NaN / infinity, and values near 1e-30 whose deltas fall below 2^-96.
+    import sys
+
+    sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
+    import make_golden as mg
+
+    lib = mg.load_ref()
+    dt = TORCH_TYPES[code]
+    g = torch.Generator(device="cuda").manual_seed(hidden + seq + code)
+    x = torch.randn((batch * seq, hidden), generator=g, device="cuda") * 3.0
+    x[5] = 0.0
+    x[17] = 1.5
+    x[40, hidden // 2] = float("nan")
+    x[41, 0] = float("inf")
+    x[90] = x[90] * (1e-4 if code == 1 else 1e-30)  # fp16 cannot hold 1e-30
+    x = x.to(dt).view(batch, seq, hidden)
+    sc = (torch.randn((batch, steps, hidden), generator=g, device="cuda") * 0.1).to(dt)
+    sh = (torch.randn((batch, steps, hidden), generator=g, device="cuda") * 0.1).to(dt)
+    want = torch.empty_like(x)
+    mg.check(lib, lib.ref_layer_norm_adaln(mg.p(x), mg.p(sc), mg.p(sh), mg.p(want), batch, seq, hidden, steps, 1e-6,
+                                           code, mg.stream()))
+    got = K.turing_layer_norm_adaln(x, sc, sh, 1e-6)
+    torch.cuda.synchronize()
+    assert_same(to_np(got), to_np(want), code)
+
+
 def test_plugin_wrapper_builds_the_segment_table_and_runs_the_kernel(K):
     # fusions.py:241-269: the norm module's weight / eps, a validated segment table.
     from types import SimpleNamespace
