@@ -1,14 +1,16 @@
 // Affine RMSNorm + segmented AdaLN, and LayerNorm + Wan AdaLN, for bf16 / fp16 / fp32
 // rows (reference: kernel/csrc/turing/segmented_rms_adaln.cu:133-297).
 //
-// Both norms are HBM-streaming: one CTA of 256 threads per row reads the row from HBM
-// once with 16-byte coalesced loads (vector path) and keeps it in registers for the
-// output pass; the reference reads it twice.  The thread-to-column mapping and the
-// reduction tree are the reference's, because they fix the fp32 rounding of the
-// statistics and so the output bits:
+// Both norms are HBM-streaming and read each row from HBM once (the reference reads it
+// twice): RMS with one CTA of 256 threads per row that keeps its 16-byte vectors in
+// registers for the output pass; LayerNorm with persistent 256-thread CTAs that bring
+// each row into shared memory by a bulk copy issued one row ahead.  The thread-to-column
+// mapping and the reduction tree are the reference's, because they fix the fp32
+// rounding of the statistics and so the output bits:
 //   * RMS: thread t accumulates fma(v, v, s) over 16-byte vectors t, t+256, ... in
 //     order (or columns t, t+256, ... when the reference launch is not vectorized);
-//   * LayerNorm: thread t runs Welford over columns t, t+256, ... with IEEE division;
+//   * LayerNorm: thread t runs Welford over columns t, t+256, ..., every quotient equal
+//     to the reference's IEEE division by the count;
 //   * a shfl_down tree inside each warp, then the 8 warp partials combined in order.
 // Every arithmetic step is written with round-to-nearest intrinsics so that the
 // compiler cannot contract or reorder it differently from the reference's build.
