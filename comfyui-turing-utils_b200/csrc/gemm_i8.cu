@@ -1,7 +1,7 @@
 // Integer GEMMs on the 5th-generation tensor cores (tcgen05, kind::i8) with the
 // ConvRot dequant + bias epilogue fused:
 //
-//   out[m, n] = bf16( ((float(acc[m, n]) * a_scale[m]) * w_scale[n]) + bias[n] )
+//   out[m, n] = bf16( fma(float(acc[m, n]) * a_scale[m], w_scale[n], bias[n]) )
 //   acc[m, n] = sum_k a[m, k] * w[n, k]          (exact int32)
 //
 // W8A8 (kModeW8A8) replaces the reference's CUTLASS SM75 mma.sync GEMM

@@ -1,7 +1,7 @@
 // CTA-pair integer GEMMs (tcgen05.mma.cta_group::2, kind::i8) with the same fused
 // ConvRot epilogue as the single-CTA kernel:
 //
-//   out[m, n] = bf16( ((float(acc[m, n]) * a_scale[m]) * w_scale[n]) + bias[n] )
+//   out[m, n] = bf16( fma(float(acc[m, n]) * a_scale[m], w_scale[n], bias[n]) )
 //
 // A cluster of two CTAs (one per SM) owns a 256 x 256 output tile.  CTA r of the pair
 // stages activation rows [128 r, 128 r + 128) and weight rows [128 r, 128 r + 128) of

@@ -16,6 +16,12 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// 32 columns of one row: bf16(fma(float(acc) * a_s, w_s, bias)).  The reference's
+// epilogue visitor tree (w4a8.cu:474-525: activation scale, weight scale, bias add, each
+// rounded to nearest) is built without -fmad=false, and nvcc contracts the weight-scale
+// multiply and the bias add into one fma; its outputs match this form on every element
+// (about 2 in 10^5 differ from a separately rounded multiply and add).  A null bias is
+// +0.0 here as in the reference, and fma(x, w, +0) equals the rounded product.
 __device__ __forceinline__ void store_chunk_bf16(__nv_bfloat16 *dst, const uint32_t (&acc)[32], float a_s,
                                                  const float *ws, const float *bs, int valid_cols) {
     uint32_t packed[16];
@@ -23,8 +29,8 @@ __device__ __forceinline__ void store_chunk_bf16(__nv_bfloat16 *dst, const uint3
     for (int j = 0; j < 16; ++j) {
         float v0 = __fmul_rn(__int2float_rn(static_cast<int>(acc[2 * j])), a_s);
         float v1 = __fmul_rn(__int2float_rn(static_cast<int>(acc[2 * j + 1])), a_s);
-        v0 = __fadd_rn(__fmul_rn(v0, ws[2 * j]), bs[2 * j]);
-        v1 = __fadd_rn(__fmul_rn(v1, ws[2 * j + 1]), bs[2 * j + 1]);
+        v0 = __fmaf_rn(v0, ws[2 * j], bs[2 * j]);
+        v1 = __fmaf_rn(v1, ws[2 * j + 1], bs[2 * j + 1]);
         packed[j] = pack_bf16x2(v0, v1);
     }
     uint4 *d = reinterpret_cast<uint4 *>(dst);

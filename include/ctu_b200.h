@@ -101,7 +101,9 @@ CTU_API int ctu_swiglu_int8_convrot_quantize_scaled(const void *x, int64_t rows,
 
 /*
  * W8A8 linear with the fused dequant + bias epilogue:
- *   out[m, n] = bf16(((float(sum_k a[m,k] * w[n,k]) * a_scale[m]) * w_scale[n]) + bias[n])
+ *   out[m, n] = bf16(fma(float(sum_k a[m,k] * w[n,k]) * a_scale[m], w_scale[n], bias[n]))
+ * (the weight-scale multiply and the bias add as one fma, as the reference's build
+ * contracts them; a null bias adds +0)
  *   a int8 [m, k], w int8 [n, k] (K-contiguous rows), a_scale fp32 [m],
  *   w_scale fp32 [n] (w_scale_count = n) or a scalar (w_scale_count = 1),
  *   bias fp32 [n] or NULL, out bf16 [m, n].
@@ -153,7 +155,7 @@ CTU_API int ctu_int8_gemm_s32(const int8_t *a, const int8_t *w, int32_t *acc, in
 /*
  * Grouped-codebook W4A8 linear:
  *   w[n, c] = clamp(rint(codebook[code] * e4m3(group_scale[n, c / group_size])), -127, 127)
- *   out[m, n] = bf16(((float(sum_c a[m, c] * w[n, c]) * a_scale[m]) * channel_scale[n]) + bias[n])
+ *   out[m, n] = bf16(fma(float(sum_c a[m, c] * w[n, c]) * a_scale[m], channel_scale[n], bias[n]))
  *   a            int8 [m, k]; w_packed: 4-bit codes [n, k/2], even column in the low nibble
  *   group_scale  float8 e4m3fn bytes [n, k / group_size]; codebook fp32 [16]
  *   channel_scale fp32 [n]; bias fp32 [n] or NULL; out bf16 [m, n]

@@ -8,7 +8,7 @@ by ``oracle/Makefile`` -- runs them on seeded inputs and writes compressed ``.np
 fixtures.  The fixtures are committed under ``tests/golden/`` and pin the CPU oracle
 (``oracle/convrot_oracle.py``) in the CPU test suite.
 
-Usage (on a B200):  python tests/golden/make_golden.py --out <directory> [--only extras|norms|staged]
+Usage (on a B200):  python tests/golden/make_golden.py --out <directory> [--only extras|norms|staged|gemm]
 """
 
 from __future__ import annotations
@@ -335,47 +335,13 @@ def staged_cases(lib, out):
     np.savez_compressed(out / "staged.npz", **staged)
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--out", required=True)
-    ap.add_argument("--only", choices=["all", "extras", "norms", "staged"], default="all")
-    args = ap.parse_args()
-    out = Path(args.out)
-    out.mkdir(parents=True, exist_ok=True)
-    lib = load_ref()
-    torch.cuda.init()
-    if args.only in ("all", "staged"):
-        staged_cases(lib, out)
-    if args.only == "staged":
-        print("golden vectors written to", out, file=sys.stderr)
-        return
-    if args.only in ("all", "norms"):
-        norm_cases(lib, out)
-    if args.only == "norms":
-        print("golden vectors written to", out, file=sys.stderr)
-        return
-    extra_cases(lib, out)
-    if args.only == "extras":
-        print("golden vectors written to", out, file=sys.stderr)
-        return
-
-    # ConvRot rotate + quantize, int8 and int4; every block geometry must agree.
-    quant = {}
-    for name, mode, x, k in quant_cases():
-        quant[f"{name}__x"] = x.view(torch.int16).numpy().view(np.uint16)
-        for bits in (8, 4):
-            results = [run_quant(lib, x, k, bits, mode, t) for t in (512, 768, 1024)]
-            for codes, scales in results[1:]:
-                assert np.array_equal(codes, results[0][0]), (name, bits)
-                assert np.array_equal(scales.view(np.uint32), results[0][1].view(np.uint32)), (name, bits)
-            quant[f"{name}__int{bits}_codes"] = results[0][0]
-            quant[f"{name}__int{bits}_scales"] = results[0][1]
-    np.savez_compressed(out / "convrot_quant.npz", **quant)
-
-    # W8A8 / W4A8 GEMMs and the int32 epilogue.
+def gemm_cases(lib, out: Path) -> None:
+    """W8A8 / W4A8 GEMMs (w4a8.cu:1000-1086, 1185-1219) and the int32 epilogue
+    (bf16_epilogue.cu:146-217) -> gemm.npz."""
     gemm = {}
     for idx, (m, n, k, with_bias) in enumerate([(33, 64, 256, True), (17, 72, 128, False),
-                                                (130, 136, 512, True), (1, 16, 64, False)]):
+                                                (130, 136, 512, True), (1, 16, 64, False),
+                                                (64, 128, 256, "cancel")]):
         g = torch.Generator().manual_seed(4300 + idx)
         a = torch.randint(-128, 128, (m, k), generator=g, dtype=torch.int8)
         w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
@@ -383,6 +349,13 @@ def main():
         a_s = torch.rand((m,), generator=g) * 0.02 + 0.001
         w_s = torch.rand((n,), generator=g) * 0.009 + 0.001
         bias = (torch.randn((n,), generator=g) * 0.02) if with_bias else None
+        if with_bias == "cancel":
+            # Column j's bias cancels the separately rounded product of row j % m, so
+            # that output is the product's rounding error under a fused multiply-add
+            # and zero without one: the case pins the epilogue's contraction.
+            acc = (a.to(torch.int64) @ w.to(torch.int64).t()).numpy().astype(np.float32)
+            prod = (acc * a_s.numpy()[:, None]) * w_s.numpy()[None, :]
+            bias = torch.from_numpy(-prod[np.arange(n) % m, np.arange(n)].astype(np.float32))
         packed = ((w4[:, 0::2].to(torch.int32) & 0xF) | ((w4[:, 1::2].to(torch.int32) & 0xF) << 4)).to(torch.uint8).view(torch.int8)
         dev = [t.cuda() if t is not None else None for t in (a, w, packed, a_s, w_s, bias)]
         out8 = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
@@ -417,6 +390,50 @@ def main():
     gemm["dequant__acc"] = acc.numpy()
     gemm["dequant__a_scale"] = a_s.numpy()
     np.savez_compressed(out / "gemm.npz", **gemm)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--only", choices=["all", "extras", "norms", "staged", "gemm"], default="all")
+    args = ap.parse_args()
+    out = Path(args.out)
+    out.mkdir(parents=True, exist_ok=True)
+    lib = load_ref()
+    torch.cuda.init()
+    if args.only == "gemm":
+        gemm_cases(lib, out)
+        print("golden vectors written to", out, file=sys.stderr)
+        return
+    if args.only in ("all", "staged"):
+        staged_cases(lib, out)
+    if args.only == "staged":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
+    if args.only in ("all", "norms"):
+        norm_cases(lib, out)
+    if args.only == "norms":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
+    extra_cases(lib, out)
+    if args.only == "extras":
+        print("golden vectors written to", out, file=sys.stderr)
+        return
+
+    # ConvRot rotate + quantize, int8 and int4; every block geometry must agree.
+    quant = {}
+    for name, mode, x, k in quant_cases():
+        quant[f"{name}__x"] = x.view(torch.int16).numpy().view(np.uint16)
+        for bits in (8, 4):
+            results = [run_quant(lib, x, k, bits, mode, t) for t in (512, 768, 1024)]
+            for codes, scales in results[1:]:
+                assert np.array_equal(codes, results[0][0]), (name, bits)
+                assert np.array_equal(scales.view(np.uint32), results[0][1].view(np.uint32)), (name, bits)
+            quant[f"{name}__int{bits}_codes"] = results[0][0]
+            quant[f"{name}__int{bits}_scales"] = results[0][1]
+    np.savez_compressed(out / "convrot_quant.npz", **quant)
+
+    gemm_cases(lib, out)
     print("golden vectors written to", out, file=sys.stderr)
 
 

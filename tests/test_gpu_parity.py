@@ -1,8 +1,10 @@
 """Parity of the B200 CUDA path with the reference (golden vectors) and the CPU oracle.
 
 All calls go through the drop-in ``_C`` module, i.e. through libctu_b200.so's C ABI.
-Integer outputs (codes, int32 accumulators) must be bit-exact; the bf16 GEMM output is
-held to at most 1 bf16 ulp against the oracle (observed: exact).
+Integer outputs (codes, int32 accumulators) and the bf16 GEMM outputs must be bit-exact.
+The GEMM epilogue is the reference build's fma(acc * a_s, w_s, bias) (the golden case
+m64_n128_k256 pins the contraction); the 1-ulp bound checked before equality only makes
+a failure's report say how far off it is.
 """
 
 from pathlib import Path

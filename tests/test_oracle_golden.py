@@ -62,6 +62,20 @@ def test_int8_and_w4a8_linear_match_reference(key):
     assert np.array_equal(oracle.w4a8_linear(a, w4, a_s, w_s, bias), GEMM[f"{key}__w4a8_linear"])
 
 
+def test_reference_epilogue_fuses_the_bias_add():
+    # m64_n128_k256: column j's bias cancels the separately rounded product of row j % 64,
+    # so the reference's output there is the product's rounding error (fma) rather than 0.
+    key = "m64_n128_k256"
+    a, w = GEMM[f"{key}__a"], GEMM[f"{key}__w"]
+    a_s, w_s, bias = GEMM[f"{key}__a_scale"], GEMM[f"{key}__w_scale"], GEMM[f"{key}__bias"]
+    ref = GEMM[f"{key}__int8_linear"]
+    rows, cols = np.arange(128) % 64, np.arange(128)
+    separate = oracle.int8_linear(a, w, a_s, w_s, bias, fused=False)
+    assert np.all((separate[rows, cols] & 0x7FFF) == 0)
+    assert np.count_nonzero(ref[rows, cols] & 0x7FFF) >= 100
+    assert np.array_equal(oracle.int8_linear(a, w, a_s, w_s, bias, fused=True), ref)
+
+
 @pytest.mark.parametrize("tag", ["vec", "scalar"])
 def test_dequantize_matches_reference(tag):
     out = oracle.epilogue(GEMM["dequant__acc"], GEMM["dequant__a_scale"], GEMM[f"dequant_{tag}__w_scale"],
