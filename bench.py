@@ -444,7 +444,8 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                      "peak_source": peak_src},
         "quantizer_roofline": {"bound": "hbm", "achieved": quant_gbs, "peak": hbm, "unit": "GB/s",
                                "frac": quant_gbs / hbm, "traffic": args.quant_traffic,
-                               "kernel": "ctu::rot::convrot_quant_reg_kernel<0,8> (register-resident)",
+                               "kernel": "ctu::rot::convrot_quant_k8_kernel<0,8> (eight-lane, K=5120 x5) and "
+                                         "convrot_quant_reg_kernel<0,8> (register-resident, K=13824)",
                                "traffic_note": "dram bytes of one K=5120 launch (ncu at M=16384, scaled to "
                                                "M=32760); algorithmic 503 MB",
                                "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
@@ -631,7 +632,7 @@ def main():
                     help="ncu dram bytes per GEMM launch (profiles/), reported as roofline.traffic")
     # profiles/convrot_quant_reg_int8_k5120_m16384.md: dram read+write of one K=5120
     # launch at M=16384, scaled to M=32760.
-    ap.add_argument("--quant-traffic", type=float, default=(168.27e6 + 50.83e6) * 32760 / 16384,
+    ap.add_argument("--quant-traffic", type=float, default=(167.84e6 + 55.16e6) * 32760 / 16384,
                     help="ncu dram bytes per quantizer launch (profiles/), reported as quantizer_roofline.traffic")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -144,7 +144,7 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const 
 }
 
 // ---------------------------------------------------------------------------- quantizer geometry
-enum QuantKind : int { kQuantTwoPass = 0, kQuantReg = 1, kQuantT4 = 2 };
+enum QuantKind : int { kQuantTwoPass = 0, kQuantReg = 1, kQuantT4 = 2, kQuantK8 = 3 };
 
 struct QuantPlan {
     int kind;  // QuantKind
@@ -156,8 +156,9 @@ struct QuantPlan {
 };
 
 // Which ConvRot quantizer runs: 0 chooses per width, 1 forces the two-pass kernel,
-// 2 the register-resident (two lanes per group) kernel and 3 the four-lane transpose
-// kernel where the width allows them (test hook ctu_debug_set_quant_kernel).
+// 2 the register-resident (two lanes per group) kernel, 3 the four-lane and 4 the
+// eight-lane transpose kernel where the width allows them (test hook
+// ctu_debug_set_quant_kernel).
 std::atomic<int> g_quant_kernel{0};
 
 // Whole-row plans: W warps hold `per_warp` x W groups, i.e. floor(per_warp W / groups)
@@ -165,16 +166,20 @@ std::atomic<int> g_quant_kernel{0};
 // memory fits.  The plan maximises the share of the SM's lane slots holding a group.
 bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *plan) {
     const int groups = static_cast<int>(k / 256);
-    const int per_warp = kind == kQuantT4 ? 8 : 16;
-    const int max_threads = kind == kQuantT4 ? ctu::rot::kT4MaxThreads : ctu::rot::kRegMaxThreads;
-    const int max_warps = kind == kQuantT4 ? 12 : 8;  // per SM at 168 / 255 registers a thread
+    const int per_warp = kind == kQuantK8 ? 4 : (kind == kQuantT4 ? 8 : 16);
+    const int max_threads = kind == kQuantK8  ? ctu::rot::kK8MaxThreads
+                            : kind == kQuantT4 ? ctu::rot::kT4MaxThreads
+                                               : ctu::rot::kRegMaxThreads;
+    // Warps per SM at 96 / 168 / 255 registers a thread.
+    const int max_warps = kind == kQuantK8 ? 65536 / (ctu::rot::kK8Registers * 32) : (kind == kQuantT4 ? 12 : 8);
     if (groups > per_warp * max_threads / 32) return false;
     double best = -1.0;
     for (int w = 1; w <= max_threads / 32; ++w) {
         const int b = per_warp * w / groups;
         if (b < 1) continue;
-        const size_t smem = kind == kQuantT4 ? ctu::rot::quant_t4_smem_bytes(b, static_cast<int>(k), act, w)
-                                             : ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
+        const size_t smem = kind == kQuantK8  ? ctu::rot::quant_k8_smem_bytes(b, static_cast<int>(k), act, w)
+                            : kind == kQuantT4 ? ctu::rot::quant_t4_smem_bytes(b, static_cast<int>(k), act, w)
+                                               : ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
         if (smem > static_cast<size_t>(smem_optin)) continue;
         const int ctas = std::min(max_warps / w, static_cast<int>((228 * 1024) / (smem + 1024)));
         if (ctas < 1) continue;
@@ -194,11 +199,14 @@ bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *pl
 
 int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan, bool two_pass_only = false) {
     const int forced = two_pass_only ? 1 : g_quant_kernel.load(std::memory_order_relaxed);
-    // Measured on B200 (M = 32760, activations from the tables): the four-lane kernel is
-    // 14-19 % faster for plain rows of K <= 3072 and 4-8 % faster with a fused SwiGLU /
-    // GELU input at K = 5120; the two-lane kernel is 1-4 % faster for plain rows of
-    // K >= 5120 and 2-8 % faster with a fused input at K = 13824.
-    const bool prefer_t4 = k <= 4096 || (act != CTU_ACT_NONE && k <= 8192);
+    // Measured on B200 (M = 32760, activations from the tables, int8 and int4, plain and
+    // fused): the eight-lane kernel is fastest at K = 5120 (20 groups: one row per 5-warp
+    // CTA, 20 warps per SM; 2-11 % ahead), the four-lane kernel at K <= 4096 and K = 8192
+    // (5-11 % ahead), the two-lane kernel at K = 13824 (9-13 % ahead of the others).
+    const bool prefer_k8 = k > 4096 && k <= 6144;
+    const bool prefer_t4 = k <= 8192;
+    if ((forced == 4 || (forced == 0 && prefer_k8)) && plan_quant_rows(k, act, smem_optin, kQuantK8, plan))
+        return CTU_OK;
     if ((forced == 3 || (forced == 0 && prefer_t4)) && plan_quant_rows(k, act, smem_optin, kQuantT4, plan))
         return CTU_OK;
     if (forced != 1 && plan_quant_rows(k, act, smem_optin, kQuantReg, plan)) return CTU_OK;
@@ -268,7 +276,8 @@ int launch_quant_kernel(QuantKernel kernel, const CUtensorMap &map, const ctu::r
 template <int Act, int Bits>
 int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
                  const DeviceQuery &q, cudaStream_t stream) {
-    const QuantKernel kernel = plan.kind == kQuantT4    ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
+    const QuantKernel kernel = plan.kind == kQuantK8    ? ctu::rot::convrot_quant_k8_kernel<Act, Bits>
+                               : plan.kind == kQuantT4  ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
                                : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
                                                         : ctu::rot::convrot_quant_kernel<Act, Bits>;
     return launch_quant_kernel(kernel, map, args, plan, q, stream);
@@ -807,7 +816,7 @@ int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *a
 }
 
 int ctu_debug_set_quant_kernel(int which) {
-    if (which < 0 || which > 3) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1, 2 or 3");
+    if (which < 0 || which > 4) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1, 2, 3 or 4");
     return g_quant_kernel.exchange(which);
 }
 

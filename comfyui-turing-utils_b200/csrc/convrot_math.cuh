@@ -230,12 +230,20 @@ __device__ __forceinline__ uint2 quant8_int8_fast(uint4 w, f32x2 rcp2) {
 // the fp32 constant 1/qmax (convrot_quant.cu:300-303, 335-338), which rounds differently
 // for some rows.
 // The clamp is the input type's largest finite value (bf16, or 65504 for fp16 input).
+// The row-buffer quotient clamped / qmax is formed by the correction step of Markstein's
+// division with r = RN(1 / qmax): q0 = clamped * r, q = fma(fma(-q0, qmax, clamped), r, q0)
+// equals the IEEE quotient for every dividend in [2^-96, FLT_MAX] and integer divisors up
+// to 16384 (tests/native/division_check.c); a smaller dividend gives a quotient far below
+// the floor on both paths, so the scale is the floor either way.
 template <int Bits>
 __device__ __forceinline__ float row_scale(float amax, bool staged, float finite_max = kBf16Max) {
     constexpr float qmax = Bits == 4 ? 7.0f : 127.0f;
+    constexpr float rcp = 1.0f / qmax;
     constexpr float floor = Bits == 4 ? 1.0e-10f : 1.0e-30f;
     const float clamped = fminf(amax, finite_max);
-    return fmaxf(staged ? __fmul_rn(clamped, 1.0f / qmax) : __fdiv_rn(clamped, qmax), floor);
+    if (staged) return fmaxf(__fmul_rn(clamped, rcp), floor);
+    const float q0 = __fmul_rn(clamped, rcp);
+    return fmaxf(__fmaf_rn(__fmaf_rn(-q0, qmax, clamped), rcp, q0), floor);
 }
 
 // True when the reciprocal-quotient fast chain reproduces bf16(y / rounded_scale) for

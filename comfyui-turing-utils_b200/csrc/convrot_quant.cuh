@@ -98,5 +98,26 @@ inline size_t quant_t4_smem_bytes(int rows, int k, int act, int warps) {
 template <int Act, int Bits>
 __global__ void convrot_quant_t4_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
+// Eight-lane variant: 32 values per lane, a 1 KB shared-memory transpose per group between
+// rotation stages 2 and 3, 4 groups per warp, whole rows per batch, at most kK8MaxThreads
+// threads.
+constexpr int kK8MaxThreads = 512;
+constexpr int kK8Registers = 96;
+constexpr int kK8MaxGroups = kK8MaxThreads / 8;
+constexpr int kK8GroupBytes = 1024;
+constexpr int kK8WarpBytes = 4 * kK8GroupBytes;
+
+// Dynamic shared memory of the eight-lane variant for a batch of `rows` rows and `warps`
+// warps: input buffer, 4 KB of transpose area per warp, row statistics, one mbarrier.
+inline size_t quant_k8_smem_bytes(int rows, int k, int act, int warps) {
+    int box = 0, copies = 0;
+    quant_copy_plan(rows, k, act, &box, &copies);
+    const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
+    return 1024 + in_bytes + static_cast<size_t>(kK8WarpBytes) * warps + 16 * static_cast<size_t>(rows) + 8;
+}
+
+template <int Act, int Bits>
+__global__ void convrot_quant_k8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
+
 }  // namespace rot
 }  // namespace ctu

@@ -258,11 +258,12 @@ CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, in
 CTU_API int ctu_debug_set_gemm_kernel(int which);
 
 /* Test hook (no counterpart in the reference): choose the ConvRot quantizer for every
- * later call in this process.  0 = per width and activation (default: the four-lane
- * transpose kernel for fused activations and K <= 4096, the register-resident kernel for
- * other K <= 32768, the two-pass kernel beyond), 1 = two-pass kernel, 2 =
- * register-resident kernel, 3 = four-lane kernel, the last two wherever the width allows
- * them.  Returns the previous selector, or a negative error code. */
+ * later call in this process.  0 = per width (default: the eight-lane kernel for
+ * 4096 < K <= 6144, the four-lane kernel for other K <= 8192, the register-resident
+ * kernel for other K <= 32768, the two-pass kernel beyond), 1 = two-pass kernel, 2 =
+ * register-resident kernel, 3 = four-lane kernel, 4 = eight-lane kernel, the last three
+ * wherever the width allows them.  Returns the previous selector, or a negative error
+ * code. */
 CTU_API int ctu_debug_set_quant_kernel(int which);
 
 #ifdef __cplusplus

@@ -1,7 +1,8 @@
 """The LayerNorm kernels replace the per-element IEEE division delta / count of the
 Welford mean update (segmented_rms_adaln.cu:262-265) by Markstein's correction step with
 a correctly rounded reciprocal of the integer count (compile-time for the per-element
-step, rounded at run time for the combine steps).  tests/native/division_check.c
+step, planned per CTA for the combine steps), and the quantizers form the row scale
+absmax / qmax (convrot_quant.cu:475-478, qmax = 127 or 7) the same way.  tests/native/division_check.c
 compares the two against C's IEEE division and fmaf -- every significand of two binades
 of delta, both signs, every count 1..128, and a sample of the counts up to 16384."""
 

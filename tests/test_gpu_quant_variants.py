@@ -1,10 +1,10 @@
 """The ConvRot quantizer kernels -- two-pass (bf16(y) back to shared memory, then a
 quantize pass), register-resident (two lanes per group, whole rows per batch, codes from
-registers) and four-lane transpose (stages 3-4 after a shared-memory transpose) --
-against the reference's golden vectors and the oracle.
+registers), four-lane and eight-lane transpose (stages 3-4 after a shared-memory
+transpose) -- against the reference's golden vectors and the oracle.
 
-By default the library uses the register-resident kernel for K <= 32768;
-``ctu_debug_set_quant_kernel`` forces one kernel so both are checked on every case.
+The library picks a kernel per width; ``ctu_debug_set_quant_kernel`` forces one kernel
+so every kernel is checked on every case.
 """
 
 import numpy as np
@@ -20,7 +20,7 @@ from pathlib import Path
 GOLDEN = Path(__file__).resolve().parent / "golden"
 QUANT = np.load(GOLDEN / "convrot_quant.npz")
 QUANT_NAMES = sorted({k.split("__")[0] for k in QUANT.files})
-KERNELS = {"two_pass": 1, "register": 2, "t4": 3}
+KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4}
 
 
 @pytest.fixture(scope="module")
@@ -142,7 +142,7 @@ def test_fused_activations_against_each_other(C, mode, bits):
             out[name] = run_quant(C, xb, bits, mode)
     finally:
         _lib.load().ctu_debug_set_quant_kernel(0)
-    for name in ("register", "t4"):
+    for name in ("register", "t4", "k8"):
         assert np.array_equal(out["two_pass"][0], out[name][0])
         assert np.array_equal(out["two_pass"][1].view(np.uint32), out[name][1].view(np.uint32))
 
@@ -161,7 +161,7 @@ def test_full_size_kernels_agree(C):
         finally:
             _lib.load().ctu_debug_set_quant_kernel(0)
         torch.cuda.synchronize()
-        for name in ("register", "t4"):
+        for name in ("register", "t4", "k8"):
             assert torch.equal(res["two_pass"][0], res[name][0])
             assert torch.equal(res["two_pass"][1], res[name][1])
 
