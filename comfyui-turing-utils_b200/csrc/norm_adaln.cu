@@ -271,6 +271,42 @@ __device__ __forceinline__ uint4 ln_vector(const uint4 x, const uint4 s, const u
     }
 }
 
+// store(1 + s) for the values of one 16-byte vector (the multiplier of ln_output).
+template <typename T>
+__device__ __forceinline__ uint4 ln_multiplier(const uint4 s) {
+    if constexpr (sizeof(T) == 4) {
+        auto f = [](uint32_t v) { return __float_as_uint(__fadd_rn(1.0f, __uint_as_float(v))); };
+        return make_uint4(f(s.x), f(s.y), f(s.z), f(s.w));
+    } else {
+        using Wd = Words<T>;
+        const f32x2 one2 = pk2(1.0f, 1.0f);
+        auto f = [&](uint32_t w) { return Wd::pack(fadd2(one2, Wd::unpack(w))); };
+        return make_uint4(f(s.x), f(s.y), f(s.z), f(s.w));
+    }
+}
+
+// ln_vector with the multiplier already rounded to the storage type (m = store(1 + s)).
+template <typename T>
+__device__ __forceinline__ uint4 ln_vector_mult(const uint4 x, const uint4 m, const uint4 h, float mean, float inv) {
+    using E = Elem<T>;
+    if constexpr (sizeof(T) == 4) {
+        auto f = [&](uint32_t xv, uint32_t mv, uint32_t hv) {
+            const float normalized = E::load(E::store(__fmul_rn(__fsub_rn(__uint_as_float(xv), mean), inv)));
+            return __float_as_uint(__fmaf_rn(normalized, __uint_as_float(mv), __uint_as_float(hv)));
+        };
+        return make_uint4(f(x.x, m.x, h.x), f(x.y, m.y, h.y), f(x.z, m.z, h.z), f(x.w, m.w, h.w));
+    } else {
+        using Wd = Words<T>;
+        const f32x2 mean2 = pk2(mean, mean);
+        const f32x2 inv2 = pk2(inv, inv);
+        auto f = [&](uint32_t xw, uint32_t mw, uint32_t hw) {
+            const f32x2 normalized = Wd::unpack(Wd::pack(fmul2(fsub2(Wd::unpack(xw), mean2), inv2)));
+            return Wd::pack(ffma2(normalized, Wd::unpack(mw), Wd::unpack(hw)));
+        };
+        return make_uint4(f(x.x, m.x, h.x), f(x.y, m.y, h.y), f(x.z, m.z, h.z), f(x.w, m.w, h.w));
+    }
+}
+
 struct Welford {
     float mean;
     float m2;
@@ -395,7 +431,8 @@ __device__ __forceinline__ bool combine_general(float &mean, float &m2, float rm
 
 constexpr int kTreeLevels = 5;  // shfl_down offsets 16, 8, 4, 2, 1
 enum TreeMode : int { kTreeFast = 0, kTreeGeneral = 1, kTreeIeee = 2 };
-constexpr size_t kTreePlanBytes = static_cast<size_t>(kTreeLevels) * kRowThreads * sizeof(float4);
+constexpr int kPlanKinds = 3;  // warps whose lanes hold base + 1, base, or both column counts
+constexpr size_t kTreePlanBytes = static_cast<size_t>(kPlanKinds) * kTreeLevels * 32 * sizeof(float4);
 
 // Modulation row offset of token row `row` (segmented_rms_adaln.cu:248-257).
 __device__ __forceinline__ int64_t ln_modulation_offset(const LnArgs &a, int64_t row) {
@@ -424,8 +461,8 @@ __global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnA
     using E = Elem<T>;
     constexpr int W = Vec<T>::kWidth;
     extern __shared__ float4 ln_smem[];
-    float4 *tree_plan = ln_smem;  // [level][thread]
-    uint8_t *bufs = reinterpret_cast<uint8_t *>(ln_smem + kTreeLevels * kRowThreads);
+    float4 *tree_plan = ln_smem;  // [warp kind][level][lane]
+    uint8_t *bufs = reinterpret_cast<uint8_t *>(ln_smem + kPlanKinds * kTreeLevels * 32);
     __shared__ float4 warp_plan[kWarps];
     __shared__ int warp_count[kWarps];
     __shared__ float warp_mean[kWarps];
@@ -443,19 +480,27 @@ __global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnA
     const uint32_t buf_bytes = (row_bytes + 15u) & ~15u;
     const bool bulk = kStaged && a.vector_in;
 
-    // Counts of every combine of this CTA's rows.
-    {
-        int count = hidden > tid ? (hidden - 1 - tid) / kRowThreads + 1 : 0;
+    // Counts of every combine of this CTA's rows.  Thread t holds base + (t < rem)
+    // columns, so a warp's lanes hold base + 1 columns (kind 0), base (kind 1), or base + 1
+    // below lane rem % 32 (kind 2, the one warp that straddles rem); warp k < 3 works out
+    // the tree counts of kind k.
+    const int base = hidden / kRowThreads;
+    const int rem = hidden % kRowThreads;
+    const int kind = 32 * (warp + 1) <= rem ? 0 : (32 * warp >= rem ? 1 : 2);
+    if (warp < kPlanKinds) {
+        const int high_lanes = warp == 0 ? 32 : (warp == 1 ? 0 : rem % 32);
+        int count = base + (lane < high_lanes ? 1 : 0);
 #pragma unroll
         for (int k = 0; k < kTreeLevels; ++k) {
             const int off = 16 >> k;
             const int right = __shfl_down_sync(0xffffffffu, count, off);
             const int rc = lane + off < 32 ? right : 0;  // lanes past the warp end are discarded
-            tree_plan[k * kRowThreads + tid] = combine_plan(count, rc);
+            tree_plan[(warp * kTreeLevels + k) * 32 + lane] = combine_plan(count, rc);
             count += rc;
         }
-        if (lane == 0) warp_count[warp] = count;
     }
+    if (lane == 0) warp_count[warp] = 32 * base + min(max(rem - 32 * warp, 0), 32);
+    const float4 *my_plan = tree_plan + kind * kTreeLevels * 32 + lane;
     if (tid == 0 && bulk) {
         mbar_init(&full[0], 1);
         mbar_init(&full[1], 1);
@@ -486,6 +531,7 @@ __global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnA
                            : hidden > (kWarps - 1) * 32      ? kTreeFast
                                                              : kTreeGeneral;
 
+    int64_t mult_off = -1;  // modulation offset whose multiplier row is in shared memory
     int it = 0;
     for (int64_t row = blockIdx.x; row < a.rows; row += gridDim.x, ++it) {
         const T *x = static_cast<const T *>(a.x) + row * hidden;
@@ -534,14 +580,14 @@ __global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnA
                 for (int k = 0; k < kTreeLevels; ++k) {
                     const float rmean = __shfl_down_sync(0xffffffffu, st.mean, 16 >> k);
                     const float rm2 = __shfl_down_sync(0xffffffffu, st.m2, 16 >> k);
-                    good = combine_fast(st.mean, st.m2, rmean, rm2, tree_plan[k * kRowThreads + tid]) && good;
+                    good = combine_fast(st.mean, st.m2, rmean, rm2, my_plan[k * 32]) && good;
                 }
             } else if (tree_mode == kTreeGeneral) {
 #pragma unroll
                 for (int k = 0; k < kTreeLevels; ++k) {
                     const float rmean = __shfl_down_sync(0xffffffffu, st.mean, 16 >> k);
                     const float rm2 = __shfl_down_sync(0xffffffffu, st.m2, 16 >> k);
-                    good = combine_general(st.mean, st.m2, rmean, rm2, tree_plan[k * kRowThreads + tid]) && good;
+                    good = combine_general(st.mean, st.m2, rmean, rm2, my_plan[k * 32]) && good;
                 }
             }
             if (!__all_sync(0xffffffffu, good)) {
@@ -607,7 +653,22 @@ __global__ void __launch_bounds__(kRowThreads) layer_norm_adaln_kernel(const LnA
         const T *scale = static_cast<const T *>(a.scale) + mod_off;
         const T *shift = static_cast<const T *>(a.shift) + mod_off;
         T *out = static_cast<T *>(a.out) + row * hidden;
-        if (a.vector_out && (kStaged || a.vector_in)) {
+        if (kStaged && a.vector_out) {
+            // store(1 + scale) of the row's modulation row, kept in shared memory while
+            // consecutive rows of the CTA share it (mod_off is uniform across the CTA).
+            uint4 *mult = reinterpret_cast<uint4 *>(bufs + 2 * buf_bytes);
+            const uint4 *sv = reinterpret_cast<const uint4 *>(scale);
+            if (mod_off != mult_off) {
+                for (int j = tid; j < hidden / W; j += kRowThreads) mult[j] = ln_multiplier<T>(__ldg(sv + j));
+                __syncthreads();
+                mult_off = mod_off;
+            }
+            const uint4 *xv = reinterpret_cast<const uint4 *>(row_s);
+            const uint4 *hv = reinterpret_cast<const uint4 *>(shift);
+            uint4 *ov = reinterpret_cast<uint4 *>(out);
+            for (int j = tid; j < hidden / W; j += kRowThreads)
+                ov[j] = ln_vector_mult<T>(xv[j], mult[j], __ldg(hv + j), mean, inv);
+        } else if (a.vector_out && (kStaged || a.vector_in)) {
             const uint4 *xv = kStaged ? reinterpret_cast<const uint4 *>(row_s) : reinterpret_cast<const uint4 *>(x);
             const uint4 *sv = reinterpret_cast<const uint4 *>(scale);
             const uint4 *hv = reinterpret_cast<const uint4 *>(shift);
@@ -657,7 +718,7 @@ cudaError_t ln_ctas_per_sm(const void *kernel, size_t smem, int *per_sm) {
         }
     }
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kTreePlanBytes + 2 * kLnSmemBytes));
+                             static_cast<int>(kTreePlanBytes + 3 * kLnSmemBytes));
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kernel, kRowThreads, smem);
     if (e != cudaSuccess) return e;
     if (*per_sm < 1) return cudaErrorInvalidConfiguration;
@@ -672,7 +733,7 @@ cudaError_t launch_ln_t(const LnArgs &a, int num_sms, cudaStream_t stream) {
     const bool staged = row_bytes <= static_cast<size_t>(kLnSmemBytes);
     const void *kernel = staged ? reinterpret_cast<const void *>(layer_norm_adaln_kernel<T, true>)
                                 : reinterpret_cast<const void *>(layer_norm_adaln_kernel<T, false>);
-    const size_t smem = kTreePlanBytes + (staged ? 2 * row_bytes : 0);
+    const size_t smem = kTreePlanBytes + (staged ? 3 * row_bytes : 0);  // two row buffers + the multiplier row
     int per_sm = 0;
     cudaError_t e = ln_ctas_per_sm(kernel, smem, &per_sm);
     if (e != cudaSuccess) return e;
