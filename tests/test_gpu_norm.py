@@ -211,8 +211,8 @@ REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libctu_ref.
 @pytest.mark.skipif(not REF_LIB.exists(), reason="reference kernels not built (make -C oracle ref)")
 def test_norm_kernels_against_reference_kernels_timing(K, capsys):
     # The reference's own norm kernels (oracle/_ref, built for sm_100a) and the B200 ones on
-    # the same bf16 rows, timed with CUDA events back to back after warm-up: RMS + AdaLN
-    # must be faster, LayerNorm + AdaLN at least on par (both results bit-identical).
+    # the same bf16 rows, timed with CUDA events back to back after warm-up: both B200
+    # kernels must be faster (measured: 1.5x RMS, 2.4x LayerNorm), results bit-identical.
     import sys
 
     sys.path.insert(0, str(Path(__file__).resolve().parent / "golden"))
@@ -253,7 +253,7 @@ def test_norm_kernels_against_reference_kernels_timing(K, capsys):
         print(f"\n[norm timing M={m} K={h} bf16] RMS+AdaLN {ours_rms * 1e3:.1f} us vs reference {ref_rms * 1e3:.1f} us; "
               f"LayerNorm+AdaLN {ours_ln * 1e3:.1f} us vs reference {ref_ln * 1e3:.1f} us")
     assert ours_rms < ref_rms
-    assert ours_ln < 1.25 * ref_ln
+    assert ours_ln < ref_ln
 
 
 @pytest.mark.skipif(not REF_LIB.exists(), reason="reference kernels not built (make -C oracle ref)")
