@@ -84,7 +84,6 @@ __global__ void convrot_quant_reg_kernel(const __grid_constant__ CUtensorMap tma
 // 8 groups per warp, whole rows per batch, at most kT4MaxThreads threads (168 registers:
 // at 128 it spills).
 constexpr int kT4MaxThreads = 384;
-constexpr int kT4MaxGroups = kT4MaxThreads / 4;
 
 // Dynamic shared memory of the four-lane variant for a batch of `rows` rows and `warps`
 // warps: input buffer, 8 KB of transpose area per warp, row statistics, one mbarrier.
@@ -103,7 +102,6 @@ __global__ void convrot_quant_t4_kernel(const __grid_constant__ CUtensorMap tmap
 // threads.
 constexpr int kK8MaxThreads = 512;
 constexpr int kK8Registers = 96;
-constexpr int kK8MaxGroups = kK8MaxThreads / 8;
 constexpr int kK8GroupBytes = 1024;
 constexpr int kK8WarpBytes = 4 * kK8GroupBytes;
 
