@@ -352,11 +352,16 @@ __device__ __forceinline__ float markstein_div(float a, float c, float rcp) {
     return __fmaf_rn(__fmaf_rn(-q0, c, a), rcp, q0);
 }
 
-// False when markstein_div(a, ...) may differ from the IEEE quotient: 0 < |a| < 2^-96 or
-// |a| infinite.
+// False when a Welford step's quotient markstein_div(delta, ...) may differ from the IEEE
+// one in a way that can reach the output: 0 < |delta| < 2^-96.  An infinite delta (an
+// infinite input, or an overflowing difference of finite ones) gives NaN here and +-inf
+// in the reference, but either way that thread's m2 becomes NaN or -inf for good (the
+// step's fma(delta, v - mean, m2) meets inf - inf or inf * -inf), no later combine can
+// turn that into a finite or positive value, and rsqrtf of the row's variance is NaN on
+// both paths, so every output of the row is NaN on both.
 __device__ __forceinline__ bool markstein_safe(float a) {
     const float mag = fabsf(a);
-    return !(mag > 3.40282347e38f) && !(mag < 0x1p-96f && mag != 0.0f);
+    return !(mag < 0x1p-96f && mag != 0.0f);
 }
 
 // Reciprocal of the count of Welford step I (the count is I + 1), a compile-time constant.
