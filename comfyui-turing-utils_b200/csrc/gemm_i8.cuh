@@ -61,7 +61,6 @@ __global__ void int8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, con
 // halves of the weight tile, so every weight byte crosses shared memory once per
 // pair instead of once per CTA.
 constexpr int kPairBM = 2 * kBM;    // output rows per CTA pair
-constexpr int kPairStructBytes = 1536;  // barriers, TMEM address, abort flag, the tile's weight scales
 constexpr int kHalfBN = kBN / 2;    // weight rows staged by each CTA of a pair
 
 template <int kMode>
@@ -76,13 +75,13 @@ struct PairLayout {
     static constexpr int kAuStageBytes = kAPacked ? kBM * kBK : 0;
     static constexpr int kBuStageBytes = kBPacked ? kHalfBN * kBK : 0;
     static constexpr int kStageBytes = kAStageBytes + kBStageBytes + kAuStageBytes + kBuStageBytes;
-    static constexpr int kStages = kMode == kModeW8A8 ? 7 : (kMode == kModeW4A8 ? 5 : 4);
+    static constexpr int kStages = kMode == kModeW8A8 ? 6 : (kMode == kModeW4A8 ? 5 : 4);
     static constexpr int kAOffset = 0;
     static constexpr int kBOffset = kAOffset + kStages * kAStageBytes;
     static constexpr int kAuOffset = kBOffset + kStages * kBStageBytes;
     static constexpr int kBuOffset = kAuOffset + kStages * kAuStageBytes;
     static constexpr int kStructOffset = kBuOffset + kStages * kBuStageBytes;
-    static constexpr int kSmemBytes = 1024 + kStructOffset + kPairStructBytes;
+    static constexpr int kSmemBytes = 1024 + kStructOffset + 4096;
     // Converter warps: each owns one ring stage (W4A4: two per stage, one for the
     // activation tile and one for the weight half-tile).
     static constexpr int kConvWarpsPerStage = kAPacked ? 2 : 1;

@@ -51,9 +51,9 @@ struct PairSmem {
     uint64_t drain;
     uint32_t tmem_base;
     int abort_flag;
-    float col_scale[kBN];  // the tile's weight scales (the biases are read from global memory)
+    float col_scale[kBN];
+    float col_bias[kBN];
 };
-static_assert(sizeof(PairSmem) <= kPairStructBytes, "CTA-pair GEMM control block outgrew its reservation");
 
 __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
     asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
@@ -279,6 +279,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                     const int n = n0 + c;
                     const bool in = n < args.n;
                     S.col_scale[c] = in ? args.w_scale[args.w_scale_count == 1 ? 0 : n] : 0.0f;
+                    S.col_bias[c] = (in && args.bias != nullptr) ? args.bias[n] : 0.0f;
                 }
             }
             named_barrier(1, kEpilogueThreads);
@@ -305,8 +306,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                 if (row_ok && valid > 0) {
                     if (args.out_mode == kOutBf16) {
                         __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(args.out) + static_cast<int64_t>(m) * args.ldc + n;
-                        store_chunk_bf16(dst, acc, a_s, &S.col_scale[c * 32],
-                                         args.bias != nullptr ? args.bias + n : nullptr, valid);
+                        store_chunk_bf16(dst, acc, a_s, &S.col_scale[c * 32], &S.col_bias[c * 32], valid);
                     } else {
                         int32_t *dst = static_cast<int32_t *>(args.out) + static_cast<int64_t>(m) * args.ldc + n;
                         store_chunk_s32(dst, acc, valid);
