@@ -820,6 +820,19 @@ int ctu_debug_set_quant_kernel(int which) {
     return g_quant_kernel.exchange(which);
 }
 
+int ctu_debug_quant_plan(int64_t k, int act, int bits, int smem_optin, int *kind, int *warps, int *rows_per_batch) {
+    if (!kind || !warps || !rows_per_batch) return fail(CTU_ERR_INVALID_ARGUMENT, "null output pointer");
+    if (k <= 0 || k % 256 != 0) return fail(CTU_ERR_INVALID_ARGUMENT, "width must be a positive multiple of 256");
+    if (act < CTU_ACT_NONE || act > CTU_ACT_GELU_TANH || (bits != 4 && bits != 8))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "invalid activation or bit width");
+    QuantPlan plan{};
+    if (int rc = plan_quant(k, act, bits, smem_optin, &plan)) return rc;
+    *kind = plan.kind;
+    *warps = plan.warps;
+    *rows_per_batch = plan.rows_per_batch;
+    return CTU_OK;
+}
+
 int ctu_debug_set_gemm_kernel(int which) {
     if (which < 0 || which > 2) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1 or 2");
     return g_gemm_kernel.exchange(which);

@@ -266,6 +266,13 @@ CTU_API int ctu_debug_set_gemm_kernel(int which);
  * code. */
 CTU_API int ctu_debug_set_quant_kernel(int which);
 
+/* Test hook (host only, no GPU needed): the quantizer plan a call of width k would use on a
+ * device with `smem_optin` bytes of opt-in shared memory per block, under the current
+ * selector: kind 0 = two-pass, 1 = register-resident, 2 = four-lane, 3 = eight-lane; the
+ * CTA's warps and rows per batch. */
+CTU_API int ctu_debug_quant_plan(int64_t k, int act, int bits, int smem_optin, int *kind, int *warps,
+                                 int *rows_per_batch);
+
 #ifdef __cplusplus
 }
 #endif
