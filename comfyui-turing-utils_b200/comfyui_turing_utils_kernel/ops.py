@@ -45,7 +45,6 @@ def _turing_w4a8_linear_fake(activation, weight, activation_scale, weight_scale,
     return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
 
 
-# ops.py:96-126
 # ops.py:38-93
 @torch.library.custom_op("turing_utils::codebook_w4a8_linear", mutates_args=())
 def turing_codebook_w4a8_linear(
