@@ -16,8 +16,8 @@
 //   * every call on a device uses the same array: calls that may overlap on the
 //     GPU (different streams without ordering) race on it and must be serialized;
 //   * the first call on each device resolves the array's address with
-//     cudaGetSymbolAddress and clears the error word; make that first call before
-//     any stream capture.
+//     cudaGetSymbolAddress and clears the error word on the caller's stream; make
+//     that first call before any stream capture.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
@@ -34,6 +34,9 @@ constexpr int64_t kMaxRows = 65536;
 constexpr size_t kScaleOffset = kCodeBytes;
 constexpr size_t kErrOffset = kScaleOffset + kMaxRows * sizeof(float);
 constexpr size_t kScratchBytes = kErrOffset + 256;
+// The narrowest accepted width (256) at the row limit fills the code area exactly.
+static_assert(kCodeBytes == static_cast<size_t>(kMaxRows) * 256, "code area = row limit x narrowest width");
+static_assert(kScaleOffset % 256 == 0 && kErrOffset % 256 == 0, "scale and error areas start 256-byte aligned");
 
 // Codes [m, k] int8 | scales [m] fp32 | error word.
 static __device__ __align__(256) uint8_t g_static_scratch[kScratchBytes];
@@ -43,14 +46,18 @@ std::mutex g_setup_mutex;
 uint8_t *g_scratch_ptr[kMaxDevices] = {};
 
 // Resolve the array's device address once per device (the host-side symbol is not
-// a device address).  Clears the error word.  Must run with `device` current.
-int setup(int device, uint8_t **out) {
+// a device address).  Clears the error word on the caller's stream, so the clear is
+// ordered before the kernels this call launches next on that stream (a memset on the
+// legacy default stream would not be ordered against a non-blocking stream).  Must
+// run with `device` current.
+int setup(int device, cudaStream_t stream, uint8_t **out) {
     std::lock_guard<std::mutex> lock(g_setup_mutex);
     if (g_scratch_ptr[device] == nullptr) {
         void *ptr = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
         if (e != cudaSuccess) return ctu::host::cuda_fail(e, "cudaGetSymbolAddress(static scratch)");
-        const cudaError_t z = cudaMemset(static_cast<uint8_t *>(ptr) + kErrOffset, 0, sizeof(uint32_t));
+        const cudaError_t z =
+            cudaMemsetAsync(static_cast<uint8_t *>(ptr) + kErrOffset, 0, sizeof(uint32_t), stream);
         if (z != cudaSuccess) return ctu::host::cuda_fail(z, "clearing the static-scratch error word");
         g_scratch_ptr[device] = static_cast<uint8_t *>(ptr);
     }
@@ -105,12 +112,12 @@ int ctu_convrot_w8a8_linear_static_scratch(const void *x, const int8_t *w, const
     ctu::host::DeviceQuery q;
     if (int rc = ctu::host::device_query(&q)) return rc;
     if (q.device < 0 || q.device >= kMaxDevices) return fail(CTU_ERR_UNSUPPORTED, "device index out of range");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t *base = nullptr;
-    if (int rc = setup(q.device, &base)) return rc;
+    if (int rc = setup(q.device, s, &base)) return rc;
     int8_t *codes = reinterpret_cast<int8_t *>(base);
     float *scales = reinterpret_cast<float *>(base + kScaleOffset);
     uint32_t *err = reinterpret_cast<uint32_t *>(base + kErrOffset);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
     // The codes and scales are rewritten in full by the quantizer on every call; the
     // error word keeps flags until ctu_get_device_error reads and clears it.
     if (int rc = ctu::host::run_quantize(x, m, k, CTU_ACT_NONE, 8, codes, scales, err, q, s)) return rc;

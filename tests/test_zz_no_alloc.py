@@ -89,3 +89,29 @@ def test_static_scratch_linear_rejects_oversized_problems():
         None, ctypes.c_void_p(out.data_ptr()), 32768, 8, 1024, None)
     assert rc == _lib.CTU_ERR_INVALID_ARGUMENT
     assert "at most" in _lib.load().ctu_last_error().decode()
+
+
+def test_static_scratch_linear_at_the_exact_limits():
+    """m = 65536, k = 256 fills the code area to its last byte and uses every scale
+    slot: the output must still equal the two-step path bit for bit, with no kernel
+    flag raised.  One more row (m = 65537) must be refused before any launch."""
+    from comfyui_turing_utils_kernel import _lib
+
+    dev = torch.cuda.current_device()
+    _lib.device_error(dev, clear=True)
+    m, k, n = 65536, 256, 16
+    x, w, w_s, bias = _problem(m, k, n, 3)
+    got = _static_scratch_linear(x, w, w_s, bias)
+    ref = _two_step_linear(x, w, w_s, bias)
+    torch.cuda.synchronize()
+    assert np.array_equal(_bits(got), _bits(ref))
+    assert _lib.device_error(dev, clear=True) == 0
+
+    x1 = torch.zeros((m + 1, k), dtype=torch.bfloat16, device="cuda")
+    out = torch.empty((m + 1, n), dtype=torch.bfloat16, device="cuda")
+    rc = _lib.load().ctu_convrot_w8a8_linear_static_scratch(
+        ctypes.c_void_p(x1.data_ptr()), ctypes.c_void_p(w.data_ptr()), ctypes.c_void_p(w_s.data_ptr()), n,
+        ctypes.c_void_p(bias.data_ptr()), ctypes.c_void_p(out.data_ptr()), m + 1, n, k,
+        ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT
+    assert "at most" in _lib.load().ctu_last_error().decode()
