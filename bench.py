@@ -3,14 +3,18 @@
 One step = the configs[1] sweep: six ConvRot W8A8 linears on M = 32760 tokens,
 (K, N) in {(5120, 5120) x 4 (Q, K, V, O), (5120, 13824) (FFN up), (13824, 5120)
 (FFN down)}; each linear is the fused rotate+quantize kernel followed by the
-tcgen05 GEMM with the dequant+bias epilogue.  Metric: int8 tera-ops per second
+tcgen05 GEMM with the dequant+bias epilogue, and each has its own input, so no
+activation is re-read from L2 within a step.  Metric: int8 tera-ops per second
 (2*M*N*K per linear) summed over all GPUs.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--scaling strong|weak] [--workload configs1|configs4]
 
-N > 1 is launched by torchrun, one process per GPU; every rank runs its own full
-configs[1] workload (weak scaling: token rows of independent sequences never cross
-GPUs, so there is no collective on the data path).
+N > 1 is launched by torchrun, one process per GPU.  Default (--scaling strong): the
+32760 token rows are sharded over the ranks, ceil(M/N) rows each, weights replicated;
+rows are independent through rotation, quantization and the GEMM, so no collective
+runs on the data path, and the step time is the maximum over ranks.  --scaling weak
+gives every rank its own full 32760-row workload instead.
 """
 
 from __future__ import annotations
@@ -32,31 +36,81 @@ M_TOKENS = 32760
 SHAPES = [(5120, 5120)] * 4 + [(5120, 13824), (13824, 5120)]  # (K, N)
 METRIC = "ConvRot W8A8 linear TOPS at Wan-14B shapes (configs[1] sweep)"
 UNIT = "TOPS"
+# one Wan-1.3B FFN-up linear (M, K, N).
+CFG0 = (1024, 1536, 8960)
+# Token rows of each configs[1] linear that the CPU baseline times in full.
+CPU_ROWS = 1024
 
 
 def ops_per_step(m: int) -> float:
     return float(sum(2 * m * n * k for k, n in SHAPES))
 
 
-def synth_inputs(m, device, seed=0):
-    """Seeded synthetic inputs with the BASELINE distributions (random weights)."""
+def shard_rows(m_total: int, world: int, rank: int):
+    """Row range [start, start + rows) of `rank` when m_total token rows are split
+    into ceil(m_total / world) rows per rank (the last ranks may hold fewer, or none)."""
+    per = -(-m_total // world)
+    start = min(rank * per, m_total)
+    return start, max(0, min(per, m_total - start))
+
+
+def padded_shard(local, per: int):
+    """`local` ([rows, cols], rows <= per) with zero rows appended up to `per` rows: the
+    all-gather exchanges equal-sized shards, so a short last shard is padded."""
     import torch
 
-    g = torch.Generator(device="cpu").manual_seed(seed)
-    xs = {}
-    for k in sorted({k for k, _ in SHAPES}):
-        x = torch.randn((m, k), generator=g, dtype=torch.float32)
-        idx = torch.randperm(k, generator=g)[: k // 100]
-        x[:, idx] *= 30.0
-        xs[k] = x.to(torch.bfloat16).to(device)
+    rows = local.shape[0]
+    if rows == per:
+        return local
+    return torch.nn.functional.pad(local, (0, 0, 0, per - rows))
+
+
+def gather_rows(local, per: int, full, async_op: bool = False):
+    """All-gather every rank's row shard, padded to `per` rows, into `full`
+    ([per * world, cols], in rank order).  With the rows split by shard_rows, rows
+    [0, m_total) of `full` are the whole sequence in order; the rest is padding."""
+    import torch.distributed as dist
+
+    return dist.all_gather_into_tensor(full, padded_shard(local, per), async_op=async_op)
+
+
+def synth_activation(m, k, generator):
+    """bf16 [m, k] N(0,1) with 1 % of the channels scaled x30 (the BASELINE outliers)."""
+    import torch
+
+    x = torch.randn((m, k), generator=generator, dtype=torch.float32)
+    idx = torch.randperm(k, generator=generator)[: k // 100]
+    x[:, idx] *= 30.0
+    return x.to(torch.bfloat16)
+
+
+def synth_weight(n, k, seed):
+    """int8 [n, k] U[-127, 127], fp32 per-channel scale U(1e-3, 1e-2), fp32 bias N(0, 0.02)."""
+    import torch
+
+    gw = torch.Generator(device="cpu").manual_seed(seed)
+    w = torch.randint(-127, 128, (n, k), generator=gw, dtype=torch.int8)
+    w_s = torch.rand((n,), generator=gw) * 0.009 + 1e-3
+    b = torch.randn((n,), generator=gw) * 0.02
+    return w, w_s, b
+
+
+def synth_inputs(m, device, seed=0):
+    """Seeded synthetic inputs with the BASELINE distributions (random weights): one
+    activation per linear of the sweep (xs[i] for SHAPES[i]) and its weights."""
+    g = torch_generator(seed)
+    xs = [synth_activation(m, k, g).to(device) for k, _ in SHAPES]
     layers = []
     for i, (k, n) in enumerate(SHAPES):
-        gw = torch.Generator(device="cpu").manual_seed(1000 + i)
-        w = torch.randint(-127, 128, (n, k), generator=gw, dtype=torch.int8)
-        w_s = torch.rand((n,), generator=gw) * 0.009 + 1e-3
-        b = torch.randn((n,), generator=gw) * 0.02
+        w, w_s, b = synth_weight(n, k, 1000 + i)
         layers.append((k, n, w.to(device), w_s.to(device), b.to(device)))
     return xs, layers
+
+
+def torch_generator(seed):
+    import torch
+
+    return torch.Generator(device="cpu").manual_seed(seed)
 
 
 def max_over_ranks(values, world: int, device=None):
@@ -127,10 +181,7 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------- CPU arm
-def cpu_sample_time(rows: int, threads: int):
-    """Time the CPU oracle port (rotate+quantize in C/OpenMP, torch int32 GEMM on CPU,
-    C epilogue) on `rows` tokens of every configs[1] linear.  Returns seconds."""
-    import numpy as np
+def _cpu_oracle(threads: int):
     import torch
 
     sys.path.insert(0, str(ROOT / "oracle"))
@@ -141,22 +192,49 @@ def cpu_sample_time(rows: int, threads: int):
     # explicitly so the reported cores are the threads used.
     if oracle.set_threads(threads) != threads:
         raise RuntimeError("could not set the oracle's OpenMP thread count")
+    return oracle
+
+
+def cpu_sample_time(rows: int, threads: int):
+    """Time the CPU oracle port (rotate+quantize in C/OpenMP, torch int32 GEMM on CPU,
+    C epilogue) on `rows` tokens of every configs[1] linear.  Returns seconds."""
+    import numpy as np
+    import torch
+
+    oracle = _cpu_oracle(threads)
     xs, layers = synth_inputs(rows, "cpu", seed=0)
-    xbits = {k: x.view(torch.int16).numpy().view(np.uint16) for k, x in xs.items()}
+    xbits = [x.view(torch.int16).numpy().view(np.uint16) for x in xs]
     t0 = time.perf_counter()
-    for k, n, w, w_s, b in layers:
-        codes, scales = oracle.convrot_quantize(xbits[k], 8)
+    for xb, (k, n, w, w_s, b) in zip(xbits, layers):
+        codes, scales = oracle.convrot_quantize(xb, 8)
         oracle.int8_linear(codes, w.numpy(), scales, w_s.numpy(), b.numpy())
+    return time.perf_counter() - t0
+
+
+def cpu_cfg0_time(threads: int):
+    """The whole configs[0] linear (M=1024, K=1536, N=8960) on the CPU oracle port."""
+    import numpy as np
+    import torch
+
+    oracle = _cpu_oracle(threads)
+    m, k, n = CFG0
+    x = synth_activation(m, k, torch_generator(7))
+    w, w_s, b = synth_weight(n, k, 2000)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    t0 = time.perf_counter()
+    codes, scales = oracle.convrot_quantize(xb, 8)
+    oracle.int8_linear(codes, w.numpy(), scales, w_s.numpy(), b.numpy())
     return time.perf_counter() - t0
 
 
 def run_reference_arm(args, rank: int) -> None:
     """`--impl reference`: the reference has no CPU path of its own for this op, so the
-    arm times the oracle's CPU restatement of its arithmetic (kind "port")."""
+    arm times the oracle's CPU restatement of its arithmetic (kind "port") on CPU_ROWS
+    token rows of every configs[1] linear per step."""
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    rows = 64
+    rows = CPU_ROWS
     for _ in range(max(args.warmup, 1)):
         cpu_sample_time(rows, threads)
     times = [cpu_sample_time(rows, threads) for _ in range(args.steps)]
@@ -164,13 +242,14 @@ def run_reference_arm(args, rank: int) -> None:
     value = ops_per_step(rows) / t / 1e12
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3 * (M_TOKENS / rows),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "configs[1] Wan-14B W8A8 sweep, M=32760, rows sampled on CPU", "m": M_TOKENS,
-                   "shapes_kn": SHAPES},
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "configs[1] Wan-14B W8A8 sweep (six linears), a slice of the M=32760 tokens on CPU",
+                   "m": M_TOKENS, "rows_per_step": rows, "shapes_kn": SHAPES},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{rows} token rows of each of the 6 configs[1] linears per step, "
-                                   f"extrapolated linearly in M (rows are independent)"},
+                         "sample": f"{rows} token rows of each of the 6 configs[1] linears per step (rows are "
+                                   f"independent, so TOPS on the slice is the rate on the whole M; "
+                                   f"ms_per_step is the slice's own time)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -186,7 +265,13 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
-    m = args.m
+    if args.scaling == "strong":
+        m_total = args.m
+        _, m = shard_rows(m_total, world, rank)
+    else:
+        m = args.m
+        m_total = args.m * world
+    # Seeded per rank: rank r's rows are its own slice of the token sequence.
     xs, layers = synth_inputs(m, dev, seed=rank)
     stream = torch.cuda.current_stream(dev)
 
@@ -194,11 +279,13 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 
     def step(record=False):
         outs = []
-        for k, n, w, w_s, b in layers:
+        for x, (k, n, w, w_s, b) in zip(xs, layers):
+            if m == 0:
+                continue
             if record:
                 e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 e0.record(stream)
-            q, s = kops.turing_bf16_int8_convrot_quantize(xs[k], 256)
+            q, s = kops.turing_bf16_int8_convrot_quantize(x, 256)
             if record:
                 e1.record(stream)
             outs.append(kops.turing_int8_linear(q, w, s, w_s, b))
@@ -233,56 +320,48 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     if flags:
         raise RuntimeError(f"kernel bounded-wait flags {flags:#x} during the timed region")
 
-    gemm_ms = [a.elapsed_time(b) for a, b, _ in gemm_ev]
-    quant_ms = [a.elapsed_time(b) for a, b, _ in quant_ev]
-    gemm_tops = sum(o for _, _, o in gemm_ev) / (sum(gemm_ms) * 1e-3) / 1e12
-    quant_gbs = sum(o for _, _, o in quant_ev) / (sum(quant_ms) * 1e-3) / 1e9
+    gemm_ms = sum(a.elapsed_time(b) for a, b, _ in gemm_ev)
+    quant_ms = sum(a.elapsed_time(b) for a, b, _ in quant_ev)
+    gemm_tops = sum(o for _, _, o in gemm_ev) / (gemm_ms * 1e-3) / 1e12 if gemm_ms else float("nan")
+    quant_gbs = sum(o for _, _, o in quant_ev) / (quant_ms * 1e-3) / 1e9 if quant_ms else float("nan")
+    x_rep = {k: x for x, (k, _) in zip(xs, SHAPES)}  # one input per width for the variants
 
-    # ---------------------------------------------------------------- W4A8 / W4A4 at the same shapes
+    def timed(fn, reps):
+        for _ in range(3):
+            fn()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        t0.record(stream)
+        for _ in range(reps):
+            fn()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        return t0.elapsed_time(t1) / reps
+
+    # ---------------------------------------------------------------- variants at the same shapes
     variants = {}
-    if not args.skip_variants:
+    if not args.skip_variants and m > 0:
         from comfyui_turing_utils_kernel import _C as cabi
 
         packed = [(k, n, (w[:, 0::2].to(torch.int32) & 7 | ((w[:, 1::2].to(torch.int32) & 7) << 4)).to(torch.int8),
                    w_s, b) for k, n, w, w_s, b in layers]
 
         def w4_step(act_bits):
-            for k, n, wp, w_s, b in packed:
+            for x, (k, n, wp, w_s, b) in zip(xs, packed):
                 q, s = (kops.turing_bf16_int8_convrot_quantize if act_bits == 8
-                        else kops.turing_bf16_int4_convrot_quantize)(xs[k], 256)
+                        else kops.turing_bf16_int4_convrot_quantize)(x, 256)
                 if act_bits == 8:
                     kops.turing_w4a8_linear(q, wp, s, w_s, b)
                 else:
                     cabi.int4_linear(q, wp, s, w_s, b)
 
         for name, bits in (("w4a8", 8), ("w4a4", 4)):
-            for _ in range(3):
-                w4_step(bits)
-            nsteps = max(5, min(args.steps, 50))
-            v0, v1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize(dev)
-            v0.record(stream)
-            for _ in range(nsteps):
-                w4_step(bits)
-            v1.record(stream)
-            torch.cuda.synchronize(dev)
-            ms = v0.elapsed_time(v1) / nsteps
-            variants[name] = {"value": ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            ms = timed(lambda: w4_step(bits), max(5, min(args.steps, 50)))
+            variants[name] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,
+                              "ms_per_step": ms,
                               "format": "signed int4 weights, per-channel scale" +
                                         (", int8 activations" if bits == 8 else ", int4 ConvRot activations") +
                                         "; int4 operands widened to int8 ahead of the W8A8 GEMM (M >= 512)"}
-
-        def timed(fn, reps):
-            for _ in range(3):
-                fn()
-            t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize(dev)
-            t0.record(stream)
-            for _ in range(reps):
-                fn()
-            t1.record(stream)
-            torch.cuda.synchronize(dev)
-            return t0.elapsed_time(t1) / reps
 
         # Grouped-codebook W4A8 (group 16, e4m3 scales, 16-entry codebook): decode to int8,
         # then the W8A8 pair GEMM, per linear.
@@ -295,23 +374,36 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             cb_layers.append((k, codes.view(torch.int8), scales, w_s, b))
 
         def codebook_step():
-            for k, codes, scales, w_s, b in cb_layers:
-                q, s = kops.turing_bf16_int8_convrot_quantize(xs[k], 256)
+            for x, (k, codes, scales, w_s, b) in zip(xs, cb_layers):
+                q, s = kops.turing_bf16_int8_convrot_quantize(x, 256)
                 kops.turing_codebook_w4a8_linear(q, codes, s, scales, w_s, book, b, 16)
 
         ms = timed(codebook_step, max(5, min(args.steps, 30)))
-        variants["codebook_w4a8"] = {"value": ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+        variants["codebook_w4a8"] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,
+                                     "ms_per_step": ms,
                                      "format": "4-bit codes, e4m3 group-16 scales, 16-entry codebook, int8 "
                                                "activations; decoded to int8 ahead of the W8A8 GEMM"}
 
+        # the Wan-1.3B FFN-up linear, timed whole (quantize + GEMM).
+        c0m, c0k, c0n = CFG0
+        x0 = synth_activation(c0m, c0k, torch_generator(7)).to(dev)
+        w0, ws0, b0 = (t.to(dev) for t in synth_weight(c0n, c0k, 2000))
+        ms = timed(lambda: kops.turing_int8_linear(*kops.turing_bf16_int8_convrot_quantize(x0, 256), w0, ws0, b0),
+                   50)
+        variants["cfg0"] = {"value": 2.0 * c0m * c0n * c0k / (ms * 1e-3) / 1e12, "unit": UNIT, "us": ms * 1e3,
+                            "shape_mkn": list(CFG0),
+                            "note": "configs[0] (Wan-1.3B FFN up) on one GPU: rotate+quantize + W8A8 GEMM; "
+                                    "inputs 3 MB fit in L2"}
+        del x0, w0
+
         # Fused-activation quantizers at the model's widths (GB/s of algorithmic bytes).
-        x_swiglu = torch.cat([xs[5120], xs[5120]], dim=1)
+        x_swiglu = torch.cat([x_rep[5120], x_rep[5120]], dim=1)
         quant_cases = {
             "swiglu_int8_k5120": (lambda: kops.turing_bf16_int8_convrot_quantize(x_swiglu, 256, swiglu=True),
                                   m * (2 * 10240 + 5120 + 4)),
-            "gelu_int8_k13824": (lambda: kops.turing_bf16_gelu_int8_convrot_quantize(xs[13824], 256),
+            "gelu_int8_k13824": (lambda: kops.turing_bf16_gelu_int8_convrot_quantize(x_rep[13824], 256),
                                  m * (2 * 13824 + 13824 + 4)),
-            "plain_int4_k5120": (lambda: kops.turing_bf16_int4_convrot_quantize(xs[5120], 256),
+            "plain_int4_k5120": (lambda: kops.turing_bf16_int4_convrot_quantize(x_rep[5120], 256),
                                  m * (2 * 5120 + 2560 + 4)),
         }
         qv = {}
@@ -319,6 +411,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             ms = timed(fn, 20)
             qv[name] = {"value": nbytes / (ms * 1e-3) / 1e9, "unit": "GB/s", "us": ms * 1e3}
         variants["quantizers"] = qv
+        del x_swiglu
 
         # Norm + AdaLN ops in front of the linears (MiniMax width 5376, Wan width 5120):
         # one bf16 read and one bf16 write per element (GB/s of algorithmic bytes).
@@ -327,7 +420,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         sn = (torch.randn((1, 5376), generator=gc, device=dev) * 0.02).to(torch.bfloat16)
         seg = torch.tensor([[0, m, 0]], dtype=torch.int32, device=dev)
         s3 = (torch.randn((1, 1, 5120), generator=gc, device=dev) * 0.02).to(torch.bfloat16)
-        x3 = xs[5120].view(1, m, 5120)
+        x3 = x_rep[5120].view(1, m, 5120)
         nv = {}
         for name, fn, nbytes in (
                 ("segmented_rms_adaln_bf16_k5376", lambda: kops.turing_segmented_rms_adaln(xn, wn, sn, sn, seg, 1e-6),
@@ -341,37 +434,36 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             raise RuntimeError("kernel bounded-wait flags raised during the variants")
 
     # ---------------------------------------------------------------- end-to-end (host buffers)
-    # Every step copies its activations from pinned host memory and reads every output
-    # back.  The copies run on their own streams (PCIe is full duplex): a linear starts
-    # when its input has landed, and its output streams back while later linears compute
-    # and the next step's inputs stream in.
+    # Every step copies each linear's activation from pinned host memory and reads every
+    # output back.  The copies run on their own streams (PCIe is full duplex): a linear
+    # starts when its input has landed, and its output streams back while later linears
+    # compute and the next step's inputs stream in.
     e2e_ms, h2d, d2h = float("nan"), 0, 0
-    if not args.skip_e2e:
-        host_x = {k: x.cpu().pin_memory() for k, x in xs.items()}
+    if not args.skip_e2e and m > 0:
+        host_x = [x.cpu().pin_memory() for x in xs]
         host_out = [torch.empty((m, n), dtype=torch.bfloat16).pin_memory() for _, n, _, _, _ in layers]
-        h2d = sum(x.numel() * x.element_size() for x in host_x.values())
+        h2d = sum(x.numel() * x.element_size() for x in host_x)
         d2h = sum(o.numel() * o.element_size() for o in host_out)
-        dev_x = {k: torch.empty_like(x) for k, x in xs.items()}
+        dev_x = [torch.empty_like(x) for x in xs]
         s_h2d, s_d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        consumed = {k: torch.cuda.Event() for k in dev_x}
-        for ev in consumed.values():
+        consumed = [torch.cuda.Event() for _ in dev_x]
+        for ev in consumed:
             ev.record(stream)
-        last_use = {k: i for i, (k, _, _, _, _) in enumerate(layers)}
 
         def e2e_step():
-            ready = {}
-            for k in dev_x:  # inputs in first-use order
-                s_h2d.wait_event(consumed[k])  # the previous step's last reader is done
+            ready = []
+            for i in range(len(dev_x)):  # inputs in use order
+                s_h2d.wait_event(consumed[i])  # the previous step's reader is done
                 with torch.cuda.stream(s_h2d):
-                    dev_x[k].copy_(host_x[k], non_blocking=True)
-                    ready[k] = torch.cuda.Event()
-                    ready[k].record(s_h2d)
+                    dev_x[i].copy_(host_x[i], non_blocking=True)
+                    ev = torch.cuda.Event()
+                    ev.record(s_h2d)
+                    ready.append(ev)
             for i, (k, n, w, w_s, b) in enumerate(layers):
-                stream.wait_event(ready[k])
-                q, s = kops.turing_bf16_int8_convrot_quantize(dev_x[k], 256)
+                stream.wait_event(ready[i])
+                q, s = kops.turing_bf16_int8_convrot_quantize(dev_x[i], 256)
+                consumed[i].record(stream)
                 out = kops.turing_int8_linear(q, w, s, w_s, b)
-                if last_use[k] == i:
-                    consumed[k].record(stream)
                 done = torch.cuda.Event()
                 done.record(stream)
                 s_d2h.wait_event(done)
@@ -396,12 +488,16 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         torch.cuda.synchronize(dev)
         barrier()
         e2e_ms = e_start.elapsed_time(e_stop) / e2e_steps
+    elif not args.skip_e2e:
+        barrier()
+        barrier()
+        e2e_ms = 0.0
 
     # ---------------------------------------------------------------- reduce over ranks (max time)
-    elapsed_ms, e2e_ms = max_over_ranks([elapsed_ms, e2e_ms], world, dev)
+    elapsed_ms, e2e_ms, h2d_all, d2h_all = max_over_ranks([elapsed_ms, e2e_ms, h2d, d2h], world, dev)
     ms_per_step = elapsed_ms / args.steps
-    value = world * ops_per_step(m) / (ms_per_step * 1e-3) / 1e12
-    e2e_value = None if args.skip_e2e else world * ops_per_step(m) / (e2e_ms * 1e-3) / 1e12
+    value = ops_per_step(m_total) / (ms_per_step * 1e-3) / 1e12
+    e2e_value = None if args.skip_e2e else ops_per_step(m_total) / (e2e_ms * 1e-3) / 1e12
 
     if rank != 0:
         return
@@ -409,39 +505,66 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
     peaks_path = ROOT / "MEASURED_PEAKS.json"
     if peaks_path.exists():
         peaks = json.loads(peaks_path.read_text())
-    bf16_sus = peaks.get("bf16_tflops_sustained")
-    if bf16_sus:
-        peak, peak_src = 2.0 * bf16_sus, "2x measured sustained cuBLAS bf16 (MEASURED_PEAKS.json); int8 dense = 2x bf16 on B200"
+    # The GEMM launches last 0.5-1.9 ms each, so the burst figure is the comparable one.
+    # MEASURED_PEAKS.json has no int8 entry: int8 dense = 2x bf16 dense on B200 (4.5 vs
+    # 2.25 POPS nominal) is assumed.
+    bf16_burst = peaks.get("bf16_tflops")
+    if bf16_burst:
+        peak = 2.0 * bf16_burst
+        peak_src = ("2x measured burst cuBLAS bf16 (MEASURED_PEAKS.json bf16_tflops); int8 dense = 2x bf16 "
+                    "dense assumed (no measured int8 figure); nominal int8 dense 4500 TOPS")
     else:
-        peak, peak_src = 2.0 * 1400.0, "2x fallback sustained bf16 1.4 PFLOP/s"
+        peak, peak_src = 2.0 * 1590.0, "2x fallback burst bf16 1.59 PFLOP/s (int8 = 2x bf16 assumed)"
     hbm = peaks.get("hbm_gbs", 6650.0)
     for entry in variants.get("norms", {}).values():
         entry["frac"] = entry["value"] / hbm
         entry["peak"] = hbm
+    frac = gemm_tops / peak
+    if frac > 1.0:
+        raise RuntimeError(f"GEMM roofline fraction {frac:.3f} > 1 against {peak:.0f} TOPS: the denominator "
+                           "or the timing is wrong")
 
     cpu = None
     if world == 1 and not args.skip_cpu:
         threads = os.cpu_count() or 1
-        rows = 64
+        rows = CPU_ROWS
         cpu_sample_time(rows, threads)
         tcpu = statistics.median(cpu_sample_time(rows, threads) for _ in range(3))
         cpu = {"value": ops_per_step(rows) / tcpu / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{rows} token rows of each configs[1] linear, oracle C/OpenMP rotate+quantize + "
-                         f"torch CPU int32 GEMM + C epilogue, extrapolated linearly in M"}
+               "sample": f"{rows} token rows of each of the six configs[1] linears ({tcpu:.2f} s), oracle "
+                         f"C/OpenMP rotate+quantize + torch CPU int32 GEMM + C epilogue; rows are independent, "
+                         f"so TOPS on the slice is the rate on the whole M"}
+        if "cfg0" in variants:
+            cpu_cfg0_time(threads)
+            t0 = statistics.median(cpu_cfg0_time(threads) for _ in range(3))
+            c0m, c0k, c0n = CFG0
+            variants["cfg0"]["cpu_baseline"] = {
+                "value": 2.0 * c0m * c0n * c0k / t0 / 1e12, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"the whole configs[0] linear ({t0 * 1e3:.1f} ms)"}
 
+    per_gpu = value / world
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "configs[1]: ConvRot W8A8 linear sweep at Wan-2.1-14B shapes", "m_per_gpu": m,
-                   "shapes_kn": SHAPES, "rotation_block": 256, "l2": "inputs (335-906 MB) larger than L2",
-                   "parallelism": f"token rows, {world} independent rank(s)"},
+        "config": {"workload": "configs[1]: ConvRot W8A8 linear sweep at Wan-2.1-14B shapes (six linears, each "
+                               "with its own input)",
+                   "m_total": m_total, "m_per_gpu": shard_rows(m_total, world, 0)[1] if args.scaling == "strong"
+                   else args.m,
+                   "shapes_kn": SHAPES, "rotation_block": 256,
+                   "l2": "no L2 flush: every linear reads its own input and weights once per step; the "
+                         "per-step working set (%.2f GB per GPU) is far larger than L2 (126 MB)" % (
+                             sum(2 * m * k + k * n + 2 * m * n + m * k for k, n in SHAPES) / 1e9),
+                   "parallelism": (f"token rows sharded over {world} rank(s), weights replicated, no collective"
+                                   if args.scaling == "strong" else f"{world} independent full-M rank(s)")},
         "roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": peak, "unit": UNIT,
-                     "frac": gemm_tops / peak, "traffic": args.gemm_traffic,
+                     "frac": frac, "traffic": args.gemm_traffic,
                      "kernel": "ctu::gemm::int8_gemm_pair_kernel<0> (CTA pair, tcgen05 cta_group::2)",
                      "traffic_note": "dram bytes of one 5120x5120 launch (ncu at M=16384, scaled to M=32760); "
                                      "algorithmic 529 MB",
-                     "peak_source": peak_src},
+                     "peak_source": peak_src,
+                     "linear_frac": per_gpu / peak,
+                     "linear_frac_note": "whole linear (quantize + GEMM) per GPU: value / n_gpus / peak"},
         "quantizer_roofline": {"bound": "hbm", "achieved": quant_gbs, "peak": hbm, "unit": "GB/s",
                                "frac": quant_gbs / hbm, "traffic": args.quant_traffic,
                                "kernel": "ctu::rot::convrot_quant_k8_kernel<0,8> (eight-lane, K=5120 x5) and "
@@ -451,10 +574,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                                "peak_source": "measured copy bandwidth (MEASURED_PEAKS.json hbm_gbs)"},
         "clocks": clocks.summary(),
         "e2e": None if args.skip_e2e else {
-            "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": int(h2d_all), "d2h_bytes_per_step": int(d2h_all),
+            "bytes_note": "per rank (the largest shard); every rank copies its own rows",
             "path": "pinned host activations -> turing_utils ops -> pinned host outputs; copies on their own "
                     "streams, overlapped with compute (PCIe full duplex)"},
-        "gpu_launches": 2 * len(SHAPES) * args.steps,
+        "gpu_launches": 2 * len(SHAPES) * args.steps if m > 0 else 0,
         "variants_same_shapes": variants or None,
         "cpu_baseline": cpu,
     }
@@ -493,7 +617,7 @@ def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(dev)
     m_total = args.m
     per = -(-m_total // world)
-    m_local = max(0, min(per, m_total - rank * per))
+    _, m_local = shard_rows(m_total, world, rank)
     d, f = C4_DIM, C4_FFN
     g = torch.Generator(device=dev).manual_seed(1234 + rank)
 
@@ -529,12 +653,10 @@ def run_configs4(args, rank: int, world: int, local_rank: int) -> None:
             k = linear(q8, s8, blk["k"])
             works = []
             if world > 1:
-                kp = torch.nn.functional.pad(k, (0, 0, 0, per - m_local)) if m_local < per else k
-                works.append(dist.all_gather_into_tensor(k_full, kp, async_op=True))
+                works.append(gather_rows(k, per, k_full, async_op=True))
             v = linear(q8, s8, blk["v"])
             if world > 1:
-                vp = torch.nn.functional.pad(v, (0, 0, 0, per - m_local)) if m_local < per else v
-                works.append(dist.all_gather_into_tensor(v_full, vp, async_op=True))
+                works.append(gather_rows(v, per, v_full, async_op=True))
                 for w in works:
                     w.wait()  # the attention consumer needs the whole sequence
             linear(*kops.turing_bf16_int8_convrot_quantize(attn, 256), blk["o"])
@@ -620,9 +742,13 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--graph", action="store_true", help="configs4: replay each forward as one CUDA graph")
     ap.add_argument("--workload", choices=["configs1", "configs4"], default="configs1",
-                    help="configs1: the metric's linear sweep (weak scaling); configs4: a whole DiT forward's "
-                         "linears on one sequence sharded over the ranks (strong scaling, K/V all-gather)")
-    ap.add_argument("--m", type=int, default=M_TOKENS, help="tokens per GPU")
+                    help="configs1: the metric's linear sweep; configs4: a whole DiT forward's linears on one "
+                         "sequence sharded over the ranks (strong scaling, K/V all-gather)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="configs1: strong = the M tokens sharded over the ranks (default); weak = every rank "
+                         "runs its own M tokens")
+    ap.add_argument("--m", type=int, default=M_TOKENS,
+                    help="tokens: the whole sequence (strong scaling, configs4) or per GPU (weak scaling)")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true", help="profiling runs: no host round trip")
     ap.add_argument("--skip-variants", action="store_true", help="skip the W4A8/W4A4 timings")
