@@ -144,7 +144,7 @@ int encode_2d(CUtensorMap *map, CUtensorMapDataType type, int elem_bytes, const 
 }
 
 // ---------------------------------------------------------------------------- quantizer geometry
-enum QuantKind : int { kQuantTwoPass = 0, kQuantReg = 1, kQuantT4 = 2, kQuantK8 = 3 };
+enum QuantKind : int { kQuantTwoPass = 0, kQuantReg = 1, kQuantT4 = 2, kQuantK8 = 3, kQuantG8 = 4 };
 
 struct QuantPlan {
     int kind;  // QuantKind
@@ -153,31 +153,41 @@ struct QuantPlan {
     int box_rows;
     int copies;
     size_t smem;
+    int groups_per_team = 1;  // kQuantG8: groups each 8-lane team rotates per batch
 };
+
+// Registers a thread of the multi-group eight-lane kernel uses, by groups per team
+// (ptxas, no spills).
+constexpr int kG8Registers[3] = {100, 128, 128};
 
 // Which ConvRot quantizer runs: 0 chooses per width, 1 forces the two-pass kernel,
 // 2 the register-resident (two lanes per group) kernel, 3 the four-lane and 4 the
-// eight-lane transpose kernel where the width allows them (test hook
-// ctu_debug_set_quant_kernel).
+// eight-lane transpose kernel, 5 the multi-group eight-lane kernel (groups per team
+// chosen per width), 6 / 7 that kernel with 1 / 2 groups per team, where the width
+// allows them (test hook ctu_debug_set_quant_kernel).
 std::atomic<int> g_quant_kernel{0};
 
 // Whole-row plans: W warps hold `per_warp` x W groups, i.e. floor(per_warp W / groups)
 // rows; an SM holds floor(max_warps / W) such CTAs (register-limited) when their shared
 // memory fits.  The plan maximises the share of the SM's lane slots holding a group.
-bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *plan) {
+bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *plan, int g8_groups = 1) {
     const int groups = static_cast<int>(k / 256);
-    const int per_warp = kind == kQuantK8 ? 4 : (kind == kQuantT4 ? 8 : 16);
-    const int max_threads = kind == kQuantK8  ? ctu::rot::kK8MaxThreads
+    const int per_warp = kind == kQuantG8 ? 4 * g8_groups : kind == kQuantK8 ? 4 : (kind == kQuantT4 ? 8 : 16);
+    const int max_threads = kind == kQuantG8   ? ctu::rot::kG8MaxThreads
+                            : kind == kQuantK8 ? ctu::rot::kK8MaxThreads
                             : kind == kQuantT4 ? ctu::rot::kT4MaxThreads
                                                : ctu::rot::kRegMaxThreads;
-    // Warps per SM at 96 / 168 / 255 registers a thread.
-    const int max_warps = kind == kQuantK8 ? 65536 / (ctu::rot::kK8Registers * 32) : (kind == kQuantT4 ? 12 : 8);
+    // Warps per SM at 96 / 168 / 255 registers a thread (multi-group: per groups per team).
+    const int max_warps = kind == kQuantG8   ? 65536 / (kG8Registers[g8_groups - 1] * 32)
+                          : kind == kQuantK8 ? 65536 / (ctu::rot::kK8Registers * 32)
+                                             : (kind == kQuantT4 ? 12 : 8);
     if (groups > per_warp * max_threads / 32) return false;
     double best = -1.0;
     for (int w = 1; w <= max_threads / 32; ++w) {
         const int b = per_warp * w / groups;
         if (b < 1) continue;
-        const size_t smem = kind == kQuantK8  ? ctu::rot::quant_k8_smem_bytes(b, static_cast<int>(k), act, w)
+        const size_t smem = kind == kQuantG8   ? ctu::rot::quant_g8_smem_bytes(b, static_cast<int>(k), act, w)
+                            : kind == kQuantK8 ? ctu::rot::quant_k8_smem_bytes(b, static_cast<int>(k), act, w)
                             : kind == kQuantT4 ? ctu::rot::quant_t4_smem_bytes(b, static_cast<int>(k), act, w)
                                                : ctu::rot::quant_reg_smem_bytes(b, static_cast<int>(k), act);
         if (smem > static_cast<size_t>(smem_optin)) continue;
@@ -193,6 +203,7 @@ bool plan_quant_rows(int64_t k, int act, int smem_optin, int kind, QuantPlan *pl
     }
     if (best < 0.0) return false;
     plan->kind = kind;
+    plan->groups_per_team = kind == kQuantG8 ? g8_groups : 1;
     ctu::rot::quant_copy_plan(plan->rows_per_batch, static_cast<int>(k), act, &plan->box_rows, &plan->copies);
     return true;
 }
@@ -205,6 +216,16 @@ int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan, bo
     // (5-11 % ahead), the two-lane kernel at K = 13824 (9-13 % ahead of the others).
     const bool prefer_k8 = k > 4096 && k <= 6144;
     const bool prefer_t4 = k <= 8192;
+    // The multi-group eight-lane kernel for plain and GELU rows (whose rotation folds the
+    // halvings): one group per team up to 24 groups a row, two beyond.  Measured at
+    // M = 32760: K = 5120 164 us against 197 us for the eight-lane kernel, K = 13824
+    // 498 us against 573 us for the two-lane kernel (GELU 648 against 838 us).
+    const int g8_default = k / 256 <= 24 ? 1 : 2;
+    const bool prefer_g8 = act != CTU_ACT_SWIGLU && k > 4096;
+    if ((forced >= 5 && forced <= 7) || (forced == 0 && prefer_g8)) {
+        const int g8_groups = forced == 6 ? 1 : forced == 7 ? 2 : g8_default;
+        if (plan_quant_rows(k, act, smem_optin, kQuantG8, plan, g8_groups)) return CTU_OK;
+    }
     if ((forced == 4 || (forced == 0 && prefer_k8)) && plan_quant_rows(k, act, smem_optin, kQuantK8, plan))
         return CTU_OK;
     if ((forced == 3 || (forced == 0 && prefer_t4)) && plan_quant_rows(k, act, smem_optin, kQuantT4, plan))
@@ -276,10 +297,13 @@ int launch_quant_kernel(QuantKernel kernel, const CUtensorMap &map, const ctu::r
 template <int Act, int Bits>
 int launch_quant(const CUtensorMap &map, const ctu::rot::QuantArgs &args, const QuantPlan &plan,
                  const DeviceQuery &q, cudaStream_t stream) {
-    const QuantKernel kernel = plan.kind == kQuantK8    ? ctu::rot::convrot_quant_k8_kernel<Act, Bits>
-                               : plan.kind == kQuantT4  ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
-                               : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
-                                                        : ctu::rot::convrot_quant_kernel<Act, Bits>;
+    const QuantKernel kernel =
+        plan.kind == kQuantG8    ? (plan.groups_per_team == 2 ? ctu::rot::convrot_quant_g8_kernel<Act, Bits, 2>
+                                                              : ctu::rot::convrot_quant_g8_kernel<Act, Bits, 1>)
+        : plan.kind == kQuantK8  ? ctu::rot::convrot_quant_k8_kernel<Act, Bits>
+        : plan.kind == kQuantT4  ? ctu::rot::convrot_quant_t4_kernel<Act, Bits>
+        : plan.kind == kQuantReg ? ctu::rot::convrot_quant_reg_kernel<Act, Bits>
+                                 : ctu::rot::convrot_quant_kernel<Act, Bits>;
     return launch_quant_kernel(kernel, map, args, plan, q, stream);
 }
 
@@ -816,7 +840,7 @@ int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, int32_t *a
 }
 
 int ctu_debug_set_quant_kernel(int which) {
-    if (which < 0 || which > 4) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be 0, 1, 2, 3 or 4");
+    if (which < 0 || which > 7) return fail(CTU_ERR_INVALID_ARGUMENT, "kernel selector must be between 0 and 7");
     return g_quant_kernel.exchange(which);
 }
 

@@ -117,5 +117,23 @@ inline size_t quant_k8_smem_bytes(int rows, int k, int act, int warps) {
 template <int Act, int Bits>
 __global__ void convrot_quant_k8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
+// Multi-group eight-lane variant: each 8-lane team rotates G groups per batch, the batch
+// input is double-buffered (one CTA barrier per batch), and plain / GELU rows run the
+// rotation with the per-stage halvings folded into the quantization.
+constexpr int kG8MaxThreads = 512;
+
+// Dynamic shared memory of the multi-group variant for a batch of `rows` rows and `warps`
+// warps: two input buffers, 4 KB of transpose area per warp, three slots of row
+// statistics, two mbarriers.
+inline size_t quant_g8_smem_bytes(int rows, int k, int act, int warps) {
+    int box = 0, copies = 0;
+    quant_copy_plan(rows, k, act, &box, &copies);
+    const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
+    return 1024 + 2 * in_bytes + static_cast<size_t>(kK8WarpBytes) * warps + 24 * static_cast<size_t>(rows) + 24;
+}
+
+template <int Act, int Bits, int G>
+__global__ void convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
+
 }  // namespace rot
 }  // namespace ctu

@@ -297,12 +297,357 @@ __global__ void __maxnreg__(kK8Registers)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Multi-group eight-lane kernel (convrot_quant_g8_kernel): the eight-lane layout above,
+// with each 8-lane team rotating G groups per batch, the batch input double-buffered
+// so it stays in shared memory until the batch's single CTA barrier, and -- for
+// bf16-valued inputs (plain rows and tanh-GELU, whose table values are bf16) -- the
+// four per-stage halvings folded into the quantization.
+//
+// Why the fold is exact.  Every bf16 value is a multiple of 2^-133 (the bf16
+// subnormal spacing), so every intermediate of the reference's rotation is a multiple
+// of 2^-137: sums of multiples of a power of two stay multiples of it (a sum is
+// rounded only when it needs more than 24 significant bits, and then onto a coarser
+// grid that is itself a multiple), and each halving step removes one factor of two.
+// 2^-137 is far above the fp32 subnormal spacing 2^-149, so no halving ever rounds and
+// no sum in the subnormal range is inexact.  Rounding to nearest commutes with scaling
+// by powers of two when nothing overflows, so the rotation without the halvings gives
+// z = 16 y exactly, sum by sum, unless z overflows.  An overflow leaves an infinity or
+// NaN in some output (neither ever turns finite again), so a group whose folded
+// outputs are all finite has y = z / 16 exactly; a group with a non-finite output is
+// recomputed in the reference's order from the still-resident input.  The codes then
+// take the folded factor 1/16 in the reciprocal: bf16(z) * (r / 16) equals
+// bf16(y) * r as exact products (r / 16 stays a normal fp32 value), and outputs small
+// enough to fall below the normal range quantize to 0 on both paths.  SwiGLU inputs
+// are fp32 products with spacings down to 2^-149, so they keep the halvings.
+namespace {
+
+// Radix-4 butterfly without the halving (the reference's association otherwise).
+__device__ __forceinline__ void butterfly2_unscaled(f32x2 &x0, f32x2 &x1, f32x2 &x2, f32x2 &x3) {
+    const f32x2 t = fadd2(x0, x1);
+    const f32x2 b = fsub2(x0, x1);
+    const f32x2 y0 = fsub2(fadd2(t, x2), x3);
+    const f32x2 y1 = fadd2(fsub2(t, x2), x3);
+    const f32x2 y2 = fadd2(fadd2(b, x2), x3);
+    const f32x2 y3 = fadd2(fsub2(x2, b), x3);
+    x0 = y0;
+    x1 = y1;
+    x2 = y2;
+    x3 = y3;
+}
+
+// max(a, |b|, |c|) propagating NaN (any NaN operand gives NaN).
+__device__ __forceinline__ float max_abs3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(fabsf(b)), "f"(fabsf(c)));
+    return r;
+}
+
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+// The folded rotation of the team's group: W[u] = bf16(z) words of columns
+// (2q + 16u, 2q + 16u + 1) with z = 16 y, and the team's NaN-propagating absmax of z.
+__device__ __forceinline__ void g8_rotate_folded(f32x2 (&P)[16], uint32_t garea, uint32_t g, uint32_t q,
+                                                 uint32_t (&W)[16], float &absmax) {
+#pragma unroll
+    for (int a = 0; a < 4; ++a) butterfly2_unscaled(P[4 * a], P[4 * a + 1], P[4 * a + 2], P[4 * a + 3]);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) butterfly2_unscaled(P[p], P[p + 4], P[p + 8], P[p + 12]);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float lo, hi;
+                unpk2(P[4 * c + i], lo, hi);
+                v[i] = h ? hi : lo;
+            }
+            const uint32_t t = 4u * q + static_cast<uint32_t>(c) + 32u * static_cast<uint32_t>(h);
+            st_shared_v4(garea + 16u * k8_slot(g, t), v[0], v[1], v[2], v[3]);
+        }
+    }
+    __syncwarp();
+    f32x2 R[16];
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+        const uint32_t t = 4u * static_cast<uint32_t>(u) + (q >> 1);
+        const float2 v = ld_shared_v2(garea + 16u * k8_slot(g, t) + 8u * (q & 1u));
+        R[u] = pk2(v.x, v.y);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int v = 0; v < 4; ++v) butterfly2_unscaled(R[4 * v], R[4 * v + 1], R[4 * v + 2], R[4 * v + 3]);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
+    float m = 0.0f;
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+        float lo, hi;
+        unpk2(R[u], lo, hi);
+        m = max_abs3_nan(m, lo, hi);
+        W[u] = pack_bf16x2(lo, hi);
+    }
+#pragma unroll
+    for (int d = 1; d < 8; d <<= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, d));
+    absmax = m;
+}
+
+// Two int8 codes of one bf16 word (columns c, c + 1) with the reciprocal chain, in the
+// low 16 bits (byte 0 = column c).
+__device__ __forceinline__ uint32_t quant2_int8_fast(uint32_t w, f32x2 rcp2) {
+    float lo, hi;
+    unpk2(fmul2(pk2(bf16lo(w), bf16hi(w)), rcp2), lo, hi);
+    const uint32_t qb = pack_bf16x2(lo, hi);
+    const int c0 = __float2int_rn(bf16lo(qb));
+    const int c1 = __float2int_rn(bf16hi(qb));
+    uint32_t d;
+    asm("cvt.pack.sat.s8.s32.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(c1), "r"(c0), "r"(0u));
+    return d;
+}
+
+// Packed int4 codes of 8 values whose folded words must first be scaled by 1/16 (rows
+// whose reciprocal is too small to take the factor without leaving the normal range).
+static __device__ __noinline__ uint32_t quant8_int4_prescaled(uint4 w, float inv) {
+    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    const f32x2 pre = pk2(0.0625f, 0.0625f);
+    const f32x2 inv2 = pk2(inv, inv);
+    uint32_t out = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float plo, phi;
+        unpk2(fmul2(fmul2(pk2(bf16lo(ww[i]), bf16hi(ww[i])), pre), inv2), plo, phi);
+        const uint32_t lb = static_cast<uint32_t>(__float2int_rn(fminf(7.0f, fmaxf(-7.0f, plo)))) & 0xFu;
+        const uint32_t hb = static_cast<uint32_t>(__float2int_rn(fminf(7.0f, fmaxf(-7.0f, phi)))) & 0xFu;
+        out |= (lb | (hb << 4)) << (8 * i);
+    }
+    return out;
+}
+
+}  // namespace
+
+template <int Act, int Bits, int G>
+__global__ void __launch_bounds__(kG8MaxThreads)
+    convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
+    constexpr bool kFold = Act != kActSwiGLU;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int K = args.k;
+    const int B = args.rows_per_batch;
+    const int Kin = Act == kActSwiGLU ? 2 * K : K;
+    const int Kout = Bits == 4 ? K / 2 : K;
+    const int groups = K / 256;
+    const int nwarps = blockDim.x >> 5;
+    const int teams = 4 * nwarps;
+    const uint32_t in_bytes = static_cast<uint32_t>(args.box_rows) * args.copies * 128u;  // multiple of 1024
+    const uint32_t slices_per_row = Kin / 64;
+    uint8_t *inbuf = smem;                                    // [2][in_bytes]
+    uint8_t *xbase = smem + 2 * in_bytes;                     // nwarps x 4 KB
+    uint32_t *row_absmax = reinterpret_cast<uint32_t *>(xbase + nwarps * kK8WarpBytes);  // [3][B]
+    uint32_t *row_flag = row_absmax + 3 * B;                                              // [3][B]
+    uint64_t *full = reinterpret_cast<uint64_t *>(row_flag + 3 * B);  // [2]: 24 B bytes in, 8-byte aligned
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const uint32_t g = static_cast<uint32_t>(lane >> 3);
+    const uint32_t q = static_cast<uint32_t>(lane & 7);
+    const uint32_t garea = smem_u32(xbase + warp * kK8WarpBytes) + g * kK8GroupBytes;
+    const int team = warp * 4 + static_cast<int>(g);
+    const int num_batches = (args.m + B - 1) / B;
+    const uint32_t slices_per_batch = static_cast<uint32_t>(B) * slices_per_row;
+    const bool given = args.given_scales != nullptr;
+    const ActLut lut{args.silu_lut, args.gelu_lut};
+
+    auto issue_load = [&](int batch, int buf) {
+        mbar_arrive_expect_tx(&full[buf], in_bytes);
+        for (int c = 0; c < args.copies; ++c) {
+            const uint32_t s0 = static_cast<uint32_t>(c * args.box_rows);
+            tma_load_2d(inbuf + buf * in_bytes + s0 * 128u, &tmap_x, 0, static_cast<int>(batch * slices_per_batch + s0),
+                        &full[buf]);
+        }
+    };
+
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_mbar_init();
+    }
+    for (int i = tid; i < 6 * B; i += blockDim.x) row_absmax[i] = 0u;  // also clears row_flag
+    __syncthreads();
+    uint32_t issued[2] = {0, 0};
+    if (tid == 0) {
+        prefetch_tmap(&tmap_x);
+        for (int b = 0; b < 2; ++b) {
+            const int batch = blockIdx.x + b * gridDim.x;
+            if (batch < num_batches) {
+                issue_load(batch, b);
+                issued[b] = 1;
+            }
+        }
+    }
+
+    bool alive = true;
+    for (int it = 0;; ++it) {
+        const int batch = blockIdx.x + it * gridDim.x;
+        if (batch >= num_batches) break;
+        const int buf = it & 1;
+        const int par = it % 3;
+        const int row0 = batch * B;
+        const int rows = min(B, args.m - row0);
+        const int tasks = rows * groups;
+        const uint8_t *in = inbuf + buf * in_bytes;
+
+        if (alive) alive = mbar_wait(&full[buf], static_cast<uint32_t>((it >> 1) & 1), nullptr, args.err,
+                                     kErrTimeoutFull);
+        alive = __all_sync(0xffffffffu, alive);  // the rotation's shuffles need every lane of the warp
+        uint32_t W[G][16];
+        bool folded[G];
+        bool group_nan[G];
+#pragma unroll
+        for (int s = 0; s < G; ++s) {
+            folded[s] = false;
+            group_nan[s] = false;
+            const int task = team + s * teams;
+            if (!alive || warp * 4 + s * teams >= tasks) continue;  // warp-uniform
+            const bool active = task < tasks;
+            const int r = active ? task / groups : 0;
+            const int grp = active ? task - r * groups : 0;
+            const uint32_t slice0 = r * slices_per_row + grp * 4;
+            float amax = 0.0f;
+            bool exact = true;
+            if constexpr (kFold) {
+                f32x2 P[16];
+                k8_load<Act>(in, slice0, q, 0u, P, lut);
+                g8_rotate_folded(P, garea, g, q, W[s], amax);
+                exact = __any_sync(0xffffffffu, !(amax <= 3.40282347e38f));
+                if (!exact) {
+                    folded[s] = true;
+                    amax *= 0.0625f;
+                }
+            }
+            if (exact) {  // warp-uniform: the reference's order, halvings included
+                f32x2 P[16];
+                float probe;
+                k8_load<Act>(in, slice0, q, static_cast<uint32_t>(K / 64), P, lut);
+                k8_rotate(P, garea, g, q, W[s], amax, probe);
+                group_nan[s] = isnan(probe);
+            }
+            if (active && q == 0 && !given) {
+                atomicMax(&row_absmax[par * B + r], __float_as_uint(amax));
+                if (group_nan[s]) atomicOr(&row_flag[par * B + r], 1u);
+            }
+        }
+        __syncthreads();  // every group has reported its absmax; buffer `buf` is consumed
+        if (tid == 0 && alive) {
+            const int next = batch + 2 * gridDim.x;
+            if (next < num_batches) {
+                issue_load(next, buf);
+                ++issued[buf];
+            }
+        }
+        {
+            const int clear = (it + 2) % 3;  // read two batches ago, written again next batch
+            for (int i = tid; i < B; i += blockDim.x) {
+                row_absmax[clear * B + i] = 0u;
+                row_flag[clear * B + i] = 0u;
+            }
+        }
+
+#pragma unroll
+        for (int s = 0; s < G; ++s) {
+            const int task = team + s * teams;
+            if (!alive || task >= tasks) continue;
+            const int r = task / groups;
+            const int grp = task - r * groups;
+            const float amax = given ? 0.0f : __uint_as_float(row_absmax[par * B + r]);
+            const float scale = given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0);
+            if (grp == 0 && q == 0 && !given) args.scales[row0 + r] = scale;
+            int8_t *out = args.codes + static_cast<int64_t>(row0 + r) * Kout;
+            if constexpr (Bits == 4) {
+                const float inv = __fdiv_rn(1.0f, scale);
+                out += grp * 128 + q;
+                if (folded[s] && !(inv >= 0x1p-100f)) {
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint32_t c = quant8_int4_prescaled(
+                            make_uint4(W[s][u], W[s][u + 1], W[s][u + 2], W[s][u + 3]), inv);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) out[8 * (u + i)] = static_cast<int8_t>((c >> (8 * i)) & 0xFFu);
+                    }
+                } else {
+                    const float iv = folded[s] ? inv * 0.0625f : inv;
+                    const f32x2 i2 = pk2(iv, iv);
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint32_t c = quant8_int4(make_uint4(W[s][u], W[s][u + 1], W[s][u + 2], W[s][u + 3]), i2);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) out[8 * (u + i)] = static_cast<int8_t>((c >> (8 * i)) & 0xFFu);
+                    }
+                }
+            } else {
+                const float rs = __bfloat162float(__float2bfloat16_rn(scale));
+                const bool exact_chain = given ? (group_nan[s] || !fast_chain_scale_ok(rs))
+                                               : (row_flag[par * B + r] != 0u || isinf(amax));
+                uint16_t *o16 = reinterpret_cast<uint16_t *>(out + grp * 256 + 2 * q);
+                if (exact_chain) {
+                    const float divisor = folded[s] ? rs * 16.0f : rs;
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint2 c = quant8_int8_exact(make_uint4(W[s][u], W[s][u + 1], W[s][u + 2], W[s][u + 3]),
+                                                          divisor);
+                        o16[8 * u] = static_cast<uint16_t>(c.x & 0xFFFFu);
+                        o16[8 * u + 8] = static_cast<uint16_t>(c.x >> 16);
+                        o16[8 * u + 16] = static_cast<uint16_t>(c.y & 0xFFFFu);
+                        o16[8 * u + 24] = static_cast<uint16_t>(c.y >> 16);
+                    }
+                } else {
+                    const float rc = __frcp_rn(rs) * (folded[s] ? 0.0625f : 1.0f);
+                    const f32x2 r2 = pk2(rc, rc);
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) o16[8 * u] = static_cast<uint16_t>(quant2_int8_fast(W[s][u], r2));
+                }
+            }
+        }
+    }
+    if (tid == 0 && !alive) {
+        // A wait gave up: let the copies still in flight land before the CTA exits.
+        for (int b = 0; b < 2; ++b) {
+            if (issued[b] > 0) mbar_wait(&full[b], (issued[b] - 1) & 1u, nullptr, args.err, kErrTimeoutDrain);
+        }
+    }
+}
+
 template __global__ void convrot_quant_k8_kernel<kActNone, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActNone, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActSwiGLU, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActSwiGLU, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActGelu, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActGelu, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+
+template __global__ void convrot_quant_g8_kernel<kActNone, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 
 }  // namespace rot
 }  // namespace ctu

@@ -261,15 +261,16 @@ CTU_API int ctu_debug_set_gemm_kernel(int which);
  * later call in this process.  0 = per width (default: the eight-lane kernel for
  * 4096 < K <= 6144, the four-lane kernel for other K <= 8192, the register-resident
  * kernel for other K <= 32768, the two-pass kernel beyond), 1 = two-pass kernel, 2 =
- * register-resident kernel, 3 = four-lane kernel, 4 = eight-lane kernel, the last three
- * wherever the width allows them.  Returns the previous selector, or a negative error
- * code. */
+ * register-resident kernel, 3 = four-lane kernel, 4 = eight-lane kernel, 5 = multi-group
+ * eight-lane kernel (groups per team chosen per width), 6 / 7 = multi-group eight-lane
+ * kernel with 1 / 2 groups per team, all but the first wherever the width allows them.
+ * Returns the previous selector, or a negative error code. */
 CTU_API int ctu_debug_set_quant_kernel(int which);
 
 /* Test hook (host only, no GPU needed): the quantizer plan a call of width k would use on a
  * device with `smem_optin` bytes of opt-in shared memory per block, under the current
- * selector: kind 0 = two-pass, 1 = register-resident, 2 = four-lane, 3 = eight-lane; the
- * CTA's warps and rows per batch. */
+ * selector: kind 0 = two-pass, 1 = register-resident, 2 = four-lane, 3 = eight-lane,
+ * 4 = multi-group eight-lane; the CTA's warps and rows per batch. */
 CTU_API int ctu_debug_quant_plan(int64_t k, int act, int bits, int smem_optin, int *kind, int *warps,
                                  int *rows_per_batch);
 

@@ -86,15 +86,16 @@ def test_ops_refuse_cpu_tensors():
 
 def test_quantizer_selection_per_width():
     # The per-width choice the measurements in the kernel sources justify, evaluated on the
-    # host for B200's 227 KB of opt-in shared memory: eight lanes at K = 5120 (one row per
-    # 5-warp CTA), four lanes at K <= 4096 and K = 8192, two lanes at K = 13824, and the
-    # two-pass kernel beyond K = 32768.
+    # host for B200's 227 KB of opt-in shared memory: the multi-group eight-lane kernel for
+    # plain and GELU rows wider than 4096 (one group per team at K = 5120, two at K = 13824),
+    # eight lanes for SwiGLU at K = 5120, four lanes at K <= 4096, and the two-pass kernel
+    # beyond K = 32768.
     import ctypes
 
     from comfyui_turing_utils_kernel import _lib
 
     lib = _lib.load()
-    two_pass, reg, t4, k8 = 0, 1, 2, 3
+    two_pass, reg, t4, k8, g8 = 0, 1, 2, 3, 4
 
     def plan(k, act=0, bits=8):
         kind, warps, rows = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
@@ -102,11 +103,13 @@ def test_quantizer_selection_per_width():
         assert rc == 0, lib.ctu_last_error().decode()
         return kind.value, warps.value, rows.value
 
-    assert plan(5120) == (k8, 5, 1)
-    assert plan(5120, act=1)[0] == k8 and plan(5120, act=2)[0] == k8 and plan(5120, bits=4)[0] == k8
-    for k in (256, 1536, 3072, 4096, 8192):
+    assert plan(5120) == (g8, 5, 1)
+    assert plan(5120, act=2)[0] == g8 and plan(5120, bits=4)[0] == g8
+    assert plan(5120, act=1)[0] == k8
+    for k in (256, 1536, 3072, 4096):
         assert plan(k)[0] == t4, k
-    assert plan(13824)[0] == reg and plan(13824, act=2)[0] == reg
+    assert plan(13824) == (g8, 7, 1) and plan(13824, act=2)[0] == g8
+    assert plan(13824, act=1)[0] == reg
     assert plan(33024)[0] == two_pass
     # The selector hook forces one kernel wherever the width allows it.
     prev = lib.ctu_debug_set_quant_kernel(2)

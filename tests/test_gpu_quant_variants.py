@@ -20,7 +20,7 @@ from pathlib import Path
 GOLDEN = Path(__file__).resolve().parent / "golden"
 QUANT = np.load(GOLDEN / "convrot_quant.npz")
 QUANT_NAMES = sorted({k.split("__")[0] for k in QUANT.files})
-KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4}
+KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6}
 
 
 @pytest.fixture(scope="module")
@@ -117,6 +117,32 @@ def special_rows(rows, k, seed):
     return x
 
 
+def large_rows(rows, k, seed):
+    """Rows scaled to magnitudes where the kernels' scaling shortcuts meet their limits:
+    1e31 and 1e36 (the int4 reciprocal falls below 2^-100; the rotation stays finite
+    without its halvings), 2^120 to 2^124 (finite in the reference's order, overflowing
+    without the halvings), and rows mixing such groups with ordinary ones."""
+    x = activations(rows, k, seed).float()
+    mags = [1e31, 1e36, 2.0 ** 120, 2.0 ** 122, 2.0 ** 124, 1e30, 3e37]
+    for r in range(rows):
+        m = mags[r % len(mags)]
+        if r % 2 == 0:
+            x[r] = x[r] / x[r].abs().max() * m
+        else:  # only the first group of the row is large
+            x[r, :256] = x[r, :256] / x[r, :256].abs().max() * m
+    return bf16_bits(x.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(14, 512), (14, 5120), (7, 13824)])
+def test_large_magnitudes(C, kernel, rows, k, bits):
+    xb = large_rows(rows, k, seed=rows * 3 + k)
+    codes, scales = run_quant(C, xb, bits)
+    ref_codes, ref_scales = oracle.convrot_quantize(xb, bits)
+    assert np.array_equal(codes, ref_codes)
+    assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
+
+
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("rows,k", [(12, 512), (18, 5120), (7, 13824)])
 def test_special_values(C, kernel, rows, k, bits):
@@ -142,7 +168,7 @@ def test_fused_activations_against_each_other(C, mode, bits):
             out[name] = run_quant(C, xb, bits, mode)
     finally:
         _lib.load().ctu_debug_set_quant_kernel(0)
-    for name in ("register", "t4", "k8"):
+    for name in [n for n in KERNELS if n != "two_pass"]:
         assert np.array_equal(out["two_pass"][0], out[name][0])
         assert np.array_equal(out["two_pass"][1].view(np.uint32), out[name][1].view(np.uint32))
 
@@ -161,7 +187,7 @@ def test_full_size_kernels_agree(C):
         finally:
             _lib.load().ctu_debug_set_quant_kernel(0)
         torch.cuda.synchronize()
-        for name in ("register", "t4", "k8"):
+        for name in [n for n in KERNELS if n != "two_pass"]:
             assert torch.equal(res["two_pass"][0], res[name][0])
             assert torch.equal(res["two_pass"][1], res[name][1])
 
