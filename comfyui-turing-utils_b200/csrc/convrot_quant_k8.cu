@@ -300,7 +300,8 @@ __global__ void __maxnreg__(kK8Registers)
 // ---------------------------------------------------------------------------
 // Multi-group eight-lane kernel (convrot_quant_g8_kernel): the eight-lane layout above,
 // with each 8-lane team rotating G groups per batch, the batch input double-buffered
-// so it stays in shared memory until the batch's single CTA barrier, and -- for
+// so it stays in shared memory until the batch's single CTA barrier, every per-lane
+// address and the team's row/group assignment computed once per launch, and -- for
 // bf16-valued inputs (plain rows and tanh-GELU, whose table values are bf16) -- the
 // four per-stage halvings folded into the quantization.
 //
@@ -320,6 +321,14 @@ __global__ void __maxnreg__(kK8Registers)
 // bf16(y) * r as exact products (r / 16 stays a normal fp32 value), and outputs small
 // enough to fall below the normal range quantize to 0 on both paths.  SwiGLU inputs
 // are fp32 products with spacings down to 2^-149, so they keep the halvings.
+//
+// Transpose addresses.  With garea 1024-byte aligned, the eight-lane placement
+// k8_slot reduces to XORs of one per-lane base with constants:
+//   write (c, h): garea + 16 k8_slot(g, 4q + c + 32h) = wbase ^ 16c            (h = 0)
+//                                                    = (wbase ^ 16c ^ 64) + 512 (h = 1)
+//   read u:       garea + 8 (q % 2) + 16 k8_slot(g, 4u + q / 2) = rbase ^ 16 (4u ^ u / 2)
+// with wbase = garea + 16 (4q ^ q / 2 ^ 4 (g % 2)) and
+// rbase = garea + 8 (q % 2) + 16 (q / 2 ^ 4 (g % 2)).
 namespace {
 
 // Radix-4 butterfly without the halving (the reference's association otherwise).
@@ -349,14 +358,94 @@ __device__ __forceinline__ float max_nan(float a, float b) {
     return r;
 }
 
-// The folded rotation of the team's group: W[u] = bf16(z) words of columns
-// (2q + 16u, 2q + 16u + 1) with z = 16 y, and the team's NaN-propagating absmax of z.
-__device__ __forceinline__ void g8_rotate_folded(f32x2 (&P)[16], uint32_t garea, uint32_t g, uint32_t q,
-                                                 uint32_t (&W)[16], float &absmax) {
+__device__ __forceinline__ uint4 ld_shared_v4u(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+                 : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint32_t ld_shared_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_shared_u32(uint32_t addr, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void atom_max_shared(uint32_t addr, uint32_t v) {
+    asm volatile("red.shared.max.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void atom_or_shared(uint32_t addr, uint32_t v) {
+    asm volatile("red.shared.or.b32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+// bf16 words of one lane's 32 inputs, unpacked to the phase A pairs (element 16q + j,
+// element 16q + j + 128); `ld[c]` / `ld[2 + c]` are the shared addresses of chunk c of
+// the lane's slice and of the slice 2 later (the h = 1 half).
+template <int Act>
+__device__ __forceinline__ void g8_load(uint32_t base, const uint32_t (&ld)[4], f32x2 (&P)[16], const ActLut &lut) {
 #pragma unroll
-    for (int a = 0; a < 4; ++a) butterfly2_unscaled(P[4 * a], P[4 * a + 1], P[4 * a + 2], P[4 * a + 3]);
+    for (int c = 0; c < 2; ++c) {
+        const uint4 a = ld_shared_v4u(base + ld[c]);
+        const uint4 b = ld_shared_v4u(base + ld[2 + c]);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int p = 0; p < 4; ++p) butterfly2_unscaled(P[p], P[p + 4], P[p + 8], P[p + 12]);
+        for (int i = 0; i < 4; ++i) {
+            P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, 0, lut), activate<Act>(bw[i] << 16, 0, lut));
+            P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, 0, lut),
+                                       activate<Act>(bw[i] & 0xFFFF0000u, 0, lut));
+        }
+    }
+}
+
+// SwiGLU inputs: the gate chunks at `ld`, the up chunks `up_bytes` later (not 1024-byte
+// periodic, so their swizzled addresses are formed here from the slice index).
+__device__ __forceinline__ void g8_load_swiglu(uint32_t base, uint32_t slice, uint32_t q, uint32_t up_slices,
+                                               f32x2 (&P)[16], const ActLut &lut) {
+    const uint32_t s = slice + (q >> 2);
+    const uint32_t c0 = 2u * (q & 3u);
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const uint4 a = ld_shared_v4u(base + sw128(s, c0 + c));
+        const uint4 b = ld_shared_v4u(base + sw128(s + 2, c0 + c));
+        const uint4 ua = ld_shared_v4u(base + sw128(s + up_slices, c0 + c));
+        const uint4 ub = ld_shared_v4u(base + sw128(s + up_slices + 2, c0 + c));
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+        const uint32_t uaw[4] = {ua.x, ua.y, ua.z, ua.w};
+        const uint32_t ubw[4] = {ub.x, ub.y, ub.z, ub.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            P[8 * c + 2 * i] = pk2(activate<kActSwiGLU>(aw[i] << 16, uaw[i] << 16, lut),
+                                   activate<kActSwiGLU>(bw[i] << 16, ubw[i] << 16, lut));
+            P[8 * c + 2 * i + 1] = pk2(activate<kActSwiGLU>(aw[i] & 0xFFFF0000u, uaw[i] & 0xFFFF0000u, lut),
+                                       activate<kActSwiGLU>(bw[i] & 0xFFFF0000u, ubw[i] & 0xFFFF0000u, lut));
+        }
+    }
+}
+
+// Rotation of the team's group.  kHalve: the reference's order with the per-stage
+// halvings (W = bf16(y), NaN-ignoring absmax, NaN probe); otherwise unscaled (W = bf16(z),
+// z = 16 y, NaN-propagating absmax of z).  All 32 lanes of the warp take part.
+template <bool kHalve>
+__device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32_t rbase, uint32_t (&W)[16],
+                                          float &absmax, float &nan_probe) {
+    const f32x2 half = pk2(0.5f, 0.5f);
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        if constexpr (kHalve) butterfly2(P[4 * a], P[4 * a + 1], P[4 * a + 2], P[4 * a + 3], half);
+        else butterfly2_unscaled(P[4 * a], P[4 * a + 1], P[4 * a + 2], P[4 * a + 3]);
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        if constexpr (kHalve) butterfly2(P[p], P[p + 4], P[p + 8], P[p + 12], half);
+        else butterfly2_unscaled(P[p], P[p + 4], P[p + 8], P[p + 12]);
+    }
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
 #pragma unroll
@@ -368,34 +457,59 @@ __device__ __forceinline__ void g8_rotate_folded(f32x2 (&P)[16], uint32_t garea,
                 unpk2(P[4 * c + i], lo, hi);
                 v[i] = h ? hi : lo;
             }
-            const uint32_t t = 4u * q + static_cast<uint32_t>(c) + 32u * static_cast<uint32_t>(h);
-            st_shared_v4(garea + 16u * k8_slot(g, t), v[0], v[1], v[2], v[3]);
+            const uint32_t addr = h ? ((wbase ^ (16u * c) ^ 64u) + 512u) : (wbase ^ (16u * c));
+            st_shared_v4(addr, v[0], v[1], v[2], v[3]);
         }
     }
     __syncwarp();
     f32x2 R[16];
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
-        const uint32_t t = 4u * static_cast<uint32_t>(u) + (q >> 1);
-        const float2 v = ld_shared_v2(garea + 16u * k8_slot(g, t) + 8u * (q & 1u));
+        const float2 v = ld_shared_v2(rbase ^ (16u * ((4u * u) ^ (u >> 1))));
         R[u] = pk2(v.x, v.y);
     }
-    __syncwarp();
+    __syncwarp();  // the area is rewritten by the next group only after these reads
 #pragma unroll
-    for (int v = 0; v < 4; ++v) butterfly2_unscaled(R[4 * v], R[4 * v + 1], R[4 * v + 2], R[4 * v + 3]);
+    for (int v = 0; v < 4; ++v) {
+        if constexpr (kHalve) butterfly2(R[4 * v], R[4 * v + 1], R[4 * v + 2], R[4 * v + 3], half);
+        else butterfly2_unscaled(R[4 * v], R[4 * v + 1], R[4 * v + 2], R[4 * v + 3]);
+    }
 #pragma unroll
-    for (int w = 0; w < 4; ++w) butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
+    for (int w = 0; w < 4; ++w) {
+        if constexpr (kHalve) butterfly2(R[w], R[w + 4], R[w + 8], R[w + 12], half);
+        else butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
+    }
     float m = 0.0f;
+    f32x2 probe = pk2(0.0f, 0.0f);
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
         float lo, hi;
         unpk2(R[u], lo, hi);
-        m = max_abs3_nan(m, lo, hi);
+        if constexpr (kHalve) {
+            probe = fadd2(probe, R[u]);
+            m = max_abs3(m, lo, hi);
+        } else {
+            m = max_abs3_nan(m, lo, hi);
+        }
         W[u] = pack_bf16x2(lo, hi);
     }
+    float pr = 0.0f;
+    if constexpr (kHalve) {
+        float p0, p1;
+        unpk2(probe, p0, p1);
+        pr = __fadd_rn(p0, p1);
+    }
 #pragma unroll
-    for (int d = 1; d < 8; d <<= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, d));
+    for (int d = 1; d < 8; d <<= 1) {
+        if constexpr (kHalve) {
+            m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));  // NaN-ignoring, as the reference's fmaxf
+            pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, d));
+        } else {
+            m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, d));
+        }
+    }
     absmax = m;
+    nan_probe = pr;
 }
 
 // Two int8 codes of one bf16 word (columns c, c + 1) with the reciprocal chain, in the
@@ -436,39 +550,60 @@ __global__ void __launch_bounds__(kG8MaxThreads)
     convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
     constexpr bool kFold = Act != kActSwiGLU;
     extern __shared__ uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    // Shared-space addresses (32-bit), 1024-byte aligned as the 128-byte swizzle needs.
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (sbase - raw);
     const int K = args.k;
     const int B = args.rows_per_batch;
-    const int Kin = Act == kActSwiGLU ? 2 * K : K;
     const int Kout = Bits == 4 ? K / 2 : K;
     const int groups = K / 256;
     const int nwarps = blockDim.x >> 5;
     const int teams = 4 * nwarps;
     const uint32_t in_bytes = static_cast<uint32_t>(args.box_rows) * args.copies * 128u;  // multiple of 1024
-    const uint32_t slices_per_row = Kin / 64;
-    uint8_t *inbuf = smem;                                    // [2][in_bytes]
-    uint8_t *xbase = smem + 2 * in_bytes;                     // nwarps x 4 KB
-    uint32_t *row_absmax = reinterpret_cast<uint32_t *>(xbase + nwarps * kK8WarpBytes);  // [3][B]
-    uint32_t *row_flag = row_absmax + 3 * B;                                              // [3][B]
-    uint64_t *full = reinterpret_cast<uint64_t *>(row_flag + 3 * B);  // [2]: 24 B bytes in, 8-byte aligned
+    const uint32_t slices_per_row = (Act == kActSwiGLU ? 2 * K : K) / 64;
+    const uint32_t xarea = sbase + 2 * in_bytes;                         // nwarps x 4 KB
+    const uint32_t stats = xarea + static_cast<uint32_t>(nwarps) * kK8WarpBytes;  // absmax [3][B], flags [3][B]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + 2 * in_bytes + nwarps * kK8WarpBytes + 24 * B);  // [2]
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
     const int lane = tid & 31;
     const uint32_t g = static_cast<uint32_t>(lane >> 3);
     const uint32_t q = static_cast<uint32_t>(lane & 7);
-    const uint32_t garea = smem_u32(xbase + warp * kK8WarpBytes) + g * kK8GroupBytes;
     const int team = warp * 4 + static_cast<int>(g);
     const int num_batches = (args.m + B - 1) / B;
     const uint32_t slices_per_batch = static_cast<uint32_t>(B) * slices_per_row;
     const bool given = args.given_scales != nullptr;
     const ActLut lut{args.silu_lut, args.gelu_lut};
 
+    // Per-lane constants.  Every batch holds B whole rows, so slot s of this team always
+    // takes row r[s], group grp[s] of the batch (or nothing, where task >= B * groups).
+    const uint32_t garea = xarea + static_cast<uint32_t>(warp) * kK8WarpBytes + g * kK8GroupBytes;
+    const uint32_t wbase = garea + 16u * ((4u * q) ^ (q >> 1) ^ (4u * (g & 1u)));
+    const uint32_t rbase = garea + 8u * (q & 1u) + 16u * ((q >> 1) ^ (4u * (g & 1u)));
+    int r_of[G], grp_of[G];
+    uint32_t slice_of[G];
+    uint32_t ld[G][4];
+#pragma unroll
+    for (int s = 0; s < G; ++s) {
+        const int task = team + s * teams;
+        r_of[s] = task / groups;
+        grp_of[s] = task - r_of[s] * groups;
+        slice_of[s] = static_cast<uint32_t>(r_of[s]) * slices_per_row + static_cast<uint32_t>(grp_of[s]) * 4u;
+        const uint32_t sl = slice_of[s] + (q >> 2);
+        const uint32_t c0 = 2u * (q & 3u);
+        ld[s][0] = sw128(sl, c0);
+        ld[s][1] = sw128(sl, c0 + 1);
+        ld[s][2] = sw128(sl + 2, c0);
+        ld[s][3] = sw128(sl + 2, c0 + 1);
+    }
+
     auto issue_load = [&](int batch, int buf) {
         mbar_arrive_expect_tx(&full[buf], in_bytes);
         for (int c = 0; c < args.copies; ++c) {
             const uint32_t s0 = static_cast<uint32_t>(c * args.box_rows);
-            tma_load_2d(inbuf + buf * in_bytes + s0 * 128u, &tmap_x, 0, static_cast<int>(batch * slices_per_batch + s0),
+            tma_load_2d(smem + buf * in_bytes + s0 * 128u, &tmap_x, 0, static_cast<int>(batch * slices_per_batch + s0),
                         &full[buf]);
         }
     };
@@ -478,7 +613,7 @@ __global__ void __launch_bounds__(kG8MaxThreads)
         mbar_init(&full[1], 1);
         fence_mbar_init();
     }
-    for (int i = tid; i < 6 * B; i += blockDim.x) row_absmax[i] = 0u;  // also clears row_flag
+    for (int i = tid; i < 6 * B; i += blockDim.x) st_shared_u32(stats + 4u * i, 0u);
     __syncthreads();
     uint32_t issued[2] = {0, 0};
     if (tid == 0) {
@@ -493,15 +628,16 @@ __global__ void __launch_bounds__(kG8MaxThreads)
     }
 
     bool alive = true;
-    for (int it = 0;; ++it) {
+    int par = 0;  // statistics slot of this batch: it % 3
+    for (int it = 0;; ++it, par = par == 2 ? 0 : par + 1) {
         const int batch = blockIdx.x + it * gridDim.x;
         if (batch >= num_batches) break;
         const int buf = it & 1;
-        const int par = it % 3;
         const int row0 = batch * B;
-        const int rows = min(B, args.m - row0);
-        const int tasks = rows * groups;
-        const uint8_t *in = inbuf + buf * in_bytes;
+        const int tasks = min(B, args.m - row0) * groups;
+        const uint32_t in = sbase + static_cast<uint32_t>(buf) * in_bytes;
+        const uint32_t amax_slot = stats + 4u * static_cast<uint32_t>(par * B);
+        const uint32_t flag_slot = amax_slot + 12u * static_cast<uint32_t>(B);
 
         if (alive) alive = mbar_wait(&full[buf], static_cast<uint32_t>((it >> 1) & 1), nullptr, args.err,
                                      kErrTimeoutFull);
@@ -513,18 +649,14 @@ __global__ void __launch_bounds__(kG8MaxThreads)
         for (int s = 0; s < G; ++s) {
             folded[s] = false;
             group_nan[s] = false;
-            const int task = team + s * teams;
             if (!alive || warp * 4 + s * teams >= tasks) continue;  // warp-uniform
-            const bool active = task < tasks;
-            const int r = active ? task / groups : 0;
-            const int grp = active ? task - r * groups : 0;
-            const uint32_t slice0 = r * slices_per_row + grp * 4;
-            float amax = 0.0f;
+            const bool active = team + s * teams < tasks;
+            float amax = 0.0f, probe = 0.0f;
             bool exact = true;
             if constexpr (kFold) {
                 f32x2 P[16];
-                k8_load<Act>(in, slice0, q, 0u, P, lut);
-                g8_rotate_folded(P, garea, g, q, W[s], amax);
+                g8_load<Act>(in, ld[s], P, lut);
+                g8_rotate<false>(P, wbase, rbase, W[s], amax, probe);
                 exact = __any_sync(0xffffffffu, !(amax <= 3.40282347e38f));
                 if (!exact) {
                     folded[s] = true;
@@ -533,14 +665,14 @@ __global__ void __launch_bounds__(kG8MaxThreads)
             }
             if (exact) {  // warp-uniform: the reference's order, halvings included
                 f32x2 P[16];
-                float probe;
-                k8_load<Act>(in, slice0, q, static_cast<uint32_t>(K / 64), P, lut);
-                k8_rotate(P, garea, g, q, W[s], amax, probe);
+                if constexpr (Act == kActSwiGLU) g8_load_swiglu(in, slice_of[s], q, static_cast<uint32_t>(K / 64), P, lut);
+                else g8_load<Act>(in, ld[s], P, lut);
+                g8_rotate<true>(P, wbase, rbase, W[s], amax, probe);
                 group_nan[s] = isnan(probe);
             }
             if (active && q == 0 && !given) {
-                atomicMax(&row_absmax[par * B + r], __float_as_uint(amax));
-                if (group_nan[s]) atomicOr(&row_flag[par * B + r], 1u);
+                atom_max_shared(amax_slot + 4u * r_of[s], __float_as_uint(amax));
+                if (group_nan[s]) atom_or_shared(flag_slot + 4u * r_of[s], 1u);
             }
         }
         __syncthreads();  // every group has reported its absmax; buffer `buf` is consumed
@@ -552,20 +684,20 @@ __global__ void __launch_bounds__(kG8MaxThreads)
             }
         }
         {
-            const int clear = (it + 2) % 3;  // read two batches ago, written again next batch
+            // Slot (it + 2) % 3 was read two batches ago and is written again next batch.
+            const uint32_t clear = stats + 4u * static_cast<uint32_t>((par == 0 ? 2 : par - 1) * B);
             for (int i = tid; i < B; i += blockDim.x) {
-                row_absmax[clear * B + i] = 0u;
-                row_flag[clear * B + i] = 0u;
+                st_shared_u32(clear + 4u * i, 0u);
+                st_shared_u32(clear + 12u * B + 4u * i, 0u);
             }
         }
 
 #pragma unroll
         for (int s = 0; s < G; ++s) {
-            const int task = team + s * teams;
-            if (!alive || task >= tasks) continue;
-            const int r = task / groups;
-            const int grp = task - r * groups;
-            const float amax = given ? 0.0f : __uint_as_float(row_absmax[par * B + r]);
+            if (!alive || team + s * teams >= tasks) continue;
+            const int r = r_of[s];
+            const int grp = grp_of[s];
+            const float amax = given ? 0.0f : __uint_as_float(ld_shared_u32(amax_slot + 4u * r));
             const float scale = given ? args.given_scales[row0 + r] : row_scale<Bits>(amax, args.scale_mul != 0);
             if (grp == 0 && q == 0 && !given) args.scales[row0 + r] = scale;
             int8_t *out = args.codes + static_cast<int64_t>(row0 + r) * Kout;
@@ -593,7 +725,7 @@ __global__ void __launch_bounds__(kG8MaxThreads)
             } else {
                 const float rs = __bfloat162float(__float2bfloat16_rn(scale));
                 const bool exact_chain = given ? (group_nan[s] || !fast_chain_scale_ok(rs))
-                                               : (row_flag[par * B + r] != 0u || isinf(amax));
+                                               : (ld_shared_u32(flag_slot + 4u * r) != 0u || isinf(amax));
                 uint16_t *o16 = reinterpret_cast<uint16_t *>(out + grp * 256 + 2 * q);
                 if (exact_chain) {
                     const float divisor = folded[s] ? rs * 16.0f : rs;
@@ -632,22 +764,16 @@ template __global__ void convrot_quant_k8_kernel<kActGelu, 4>(const __grid_const
 
 template __global__ void convrot_quant_g8_kernel<kActNone, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActNone, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActNone, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActSwiGLU, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
-template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
 
 }  // namespace rot
 }  // namespace ctu
