@@ -46,6 +46,7 @@ SIGNATURES = {
     "ctu_layer_norm_adaln": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ctu_debug_gemm_injected_timeout": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _u64, _vp]),
     "ctu_debug_set_gemm_kernel": (_i32, [_i32]),
+    "ctu_debug_set_gemm_split": (_i32, [_i32]),
     "ctu_debug_set_quant_kernel": (_i32, [_i32]),
     "ctu_debug_quant_plan": (_i32, [_i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "ctu_convrot_w8a8_linear_static_scratch": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),

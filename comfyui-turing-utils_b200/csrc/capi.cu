@@ -315,6 +315,21 @@ std::atomic<int> g_gemm_kernel{0};
 // Clusters of two CTAs that can be resident at once, per device and kernel variant.
 int g_pair_clusters[kMaxDevices][3] = {};
 
+// Tiles of the CTA-pair W8A8 kernel that run as two 128-column halves.  With P pairs
+// resident, T tiles take ceil(T / P) rounds; when the last round holds r = T mod P
+// tiles and 2 r <= P, splitting those r tiles into 2 r halves lets the last round take
+// half as long (e.g. a 4095-row shard at N = 5120: 320 tiles on 74 pairs, 4.5 rounds
+// instead of 5).  A test hook can force a split count (ctu_debug_set_gemm_split).
+std::atomic<int> g_gemm_split{-1};
+
+int64_t split_tail_tiles(int64_t tiles, int64_t pairs, bool allowed) {
+    if (!allowed || pairs <= 0) return 0;
+    const int forced = g_gemm_split.load(std::memory_order_relaxed);
+    if (forced >= 0) return std::min<int64_t>(forced, tiles);
+    const int64_t rem = tiles % pairs;
+    return (rem != 0 && 2 * rem <= pairs) ? rem : 0;
+}
+
 template <int kMode, bool kPair>
 int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &args, int device, int num_sms,
                   cudaStream_t stream) {
@@ -327,7 +342,7 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
     constexpr uint32_t w_box_rows = kPair ? ctu::gemm::kHalfBN : kBN;
     // Packed int4 tiles are read by the converter warps with plain loads (no swizzle);
     // int8 tiles feed the MMA directly (128-byte swizzle).
-    CUtensorMap map_a, map_b;
+    CUtensorMap map_a, map_b, map_b_narrow;
     if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, a_packed ? args.k / 2 : args.k, args.m,
                            a_packed ? kBK / 2 : kBK, kBM,
                            a_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
@@ -336,6 +351,14 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
                            w_packed ? kBK / 2 : kBK, w_box_rows,
                            w_packed ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B))
         return rc;
+    if constexpr (kPair && !w_packed) {
+        // Half tiles (256 x 128) stage kHalfBN / 2 weight rows per CTA.
+        if (int rc = encode_2d(&map_b_narrow, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, kBK,
+                               ctu::gemm::kHalfBN / 2, CU_TENSOR_MAP_SWIZZLE_128B))
+            return rc;
+    } else {
+        map_b_narrow = map_b;
+    }
     using PL = ctu::gemm::PairLayout<kMode>;
     constexpr int smem = kPair                                ? PL::kSmemBytes
                          : kMode == ctu::gemm::kModeW8A8     ? ctu::gemm::kSmemBytes
@@ -343,7 +366,8 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
                                                              : ctu::gemm::kSmemBytesW4A4;
     constexpr int threads = kPair ? PL::kThreadCount
                                   : (kMode == ctu::gemm::kModeW8A8 ? ctu::gemm::kThreads : ctu::gemm::kThreadsW4);
-    constexpr auto kernel = kPair ? ctu::gemm::int8_gemm_pair_kernel<kMode> : ctu::gemm::int8_gemm_kernel<kMode>;
+    constexpr auto single_kernel = ctu::gemm::int8_gemm_kernel<kMode>;
+    constexpr auto pair_kernel = ctu::gemm::int8_gemm_pair_kernel<kMode>;
     // Function attributes belong to a device's context: set once per device.
     static bool attr_set[kMaxDevices] = {};
     bool need_attr = false;
@@ -352,17 +376,23 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
         need_attr = !attr_set[device];
     }
     if (need_attr) {
-        CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        if constexpr (kPair) {
+            CTU_CUDA(cudaFuncSetAttribute(pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        } else {
+            CTU_CUDA(cudaFuncSetAttribute(single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        }
         std::lock_guard<std::mutex> lock(g_mutex);
         attr_set[device] = true;
     }
     if constexpr (!kPair) {
+        constexpr auto kernel = single_kernel;
         const int64_t tiles = ((args.m + kBM - 1) / kBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
         const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms));
         kernel<<<grid, threads, smem, stream>>>(map_a, map_b, args);
         CTU_CUDA(cudaGetLastError());
         return CTU_OK;
     } else {
+        constexpr auto kernel = pair_kernel;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = 2;
@@ -388,8 +418,11 @@ int launch_gemm_t(const int8_t *a, const int8_t *w, const ctu::gemm::GemmArgs &a
         }
         const int64_t tiles =
             ((args.m + ctu::gemm::kPairBM - 1) / ctu::gemm::kPairBM) * static_cast<int64_t>((args.n + kBN - 1) / kBN);
-        cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, clusters)), 1, 1);
-        CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, args));
+        ctu::gemm::GemmArgs run = args;
+        run.split_tiles = static_cast<int>(split_tail_tiles(tiles, clusters, !w_packed));
+        const int64_t work = tiles + run.split_tiles;
+        cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(work, clusters)), 1, 1);
+        CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, map_b_narrow, run));
         return CTU_OK;
     }
 }
@@ -855,6 +888,11 @@ int ctu_debug_quant_plan(int64_t k, int act, int bits, int smem_optin, int *kind
     *warps = plan.warps;
     *rows_per_batch = plan.rows_per_batch;
     return CTU_OK;
+}
+
+int ctu_debug_set_gemm_split(int tiles) {
+    if (tiles < -1) return fail(CTU_ERR_INVALID_ARGUMENT, "split count must be -1 (automatic) or >= 0");
+    return g_gemm_split.exchange(tiles);
 }
 
 int ctu_debug_set_gemm_kernel(int which) {

@@ -46,6 +46,10 @@ struct GemmArgs {
     int out_mode;
     int inject_timeout;           // test hook (0 in production)
     unsigned long long inject_timeout_ns;
+    // CTA-pair W8A8 kernel: the last `split_tiles` 256 x 256 tiles run as two 256 x 128
+    // halves each, so a last wave that would leave most pairs idle is spread over twice
+    // as many work items (0: every tile whole).
+    int split_tiles;
 };
 
 // kModeW8A8: a int8 [m, k], w int8 [n, k]; kModeW4A8: w packed signed int4 [n, k/2];
@@ -90,9 +94,12 @@ struct PairLayout {
     static_assert(kSmemBytes <= 232448, "CTA-pair GEMM exceeds the shared memory of one SM");
 };
 
+// `tmap_b_narrow` is the weight map with a kHalfBN / 2-row box: the per-CTA weight rows of
+// a 128-column half tile (W8A8 only; the int4 modes never split tiles).
 template <int kMode>
 __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                      const __grid_constant__ CUtensorMap tmap_b, const GemmArgs args);
+                                      const __grid_constant__ CUtensorMap tmap_b,
+                                      const __grid_constant__ CUtensorMap tmap_b_narrow, const GemmArgs args);
 
 }  // namespace gemm
 }  // namespace ctu

@@ -97,7 +97,7 @@ __device__ __forceinline__ void settle_inflight_copies() {
 template <int kMode>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::kThreadCount, 1)
     int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                          const GemmArgs args) {
+                          const __grid_constant__ CUtensorMap tmap_b_narrow, const GemmArgs args) {
     using L = PairLayout<kMode>;
     constexpr bool kConvert = L::kConvert;
     constexpr int kStagesP = L::kStages;
@@ -121,6 +121,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
     const int num_m = (args.m + kPairBM - 1) / kPairBM;
     const int num_tiles = num_m * num_n;
     const int nk = (args.k + kBK - 1) / kBK;
+    // Work items: tiles [0, num_full) whole, then each of the last split_tiles tiles as
+    // two 128-column halves (W8A8 only).
+    const int split = kConvert ? 0 : args.split_tiles;
+    const int num_full = num_tiles - split;
+    const int num_work = num_tiles + split;
+    // Output tile row index, first column and width of work item w.
+    auto work_item = [&](int w, int &m_tile, int &n0, int &ncols) {
+        int t = w;
+        int half = 0;
+        if (w >= num_full) {
+            t = num_full + ((w - num_full) >> 1);
+            half = (w - num_full) & 1;
+        }
+        m_tile = t / num_n;
+        ncols = w >= num_full ? kHalfBN : kBN;
+        n0 = (t - m_tile * num_n) * kBN + half * kHalfBN;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStagesP; ++s) {
@@ -161,9 +178,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
             uint32_t ph = 0;
             uint32_t fills = 0;
             bool ok = true;
-            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
-                const int m0 = (t / num_n) * kPairBM + static_cast<int>(rank) * kBM;
-                const int w0 = (t % num_n) * kBN + static_cast<int>(rank) * kHalfBN;
+            for (int t = pair; t < num_work && ok; t += num_pairs) {
+                int m_tile, n0, ncols;
+                work_item(t, m_tile, n0, ncols);
+                const int m0 = m_tile * kPairBM + static_cast<int>(rank) * kBM;
+                const bool narrow = ncols != kBN;  // each CTA stages ncols / 2 weight rows
+                const int w0 = n0 + static_cast<int>(rank) * (ncols / 2);
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!ab_state.wait(&S.empty[s], ph ^ 1u, kErrTimeoutEmpty)) {
                         ok = false;
@@ -177,9 +197,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                         tma_load_2d(dst_b, &tmap_b, kb * (kBK / 2), w0, &S.full[s]);
                     } else {
                         const uint32_t leader_full = mapa_shared(smem_u32(&S.full[s]), 0u);
-                        if (leader) mbar_arrive_expect_tx(&S.full[s], 2 * (L::kAStageBytes + L::kBStageBytes));
+                        const uint32_t b_bytes = narrow ? L::kBStageBytes / 2 : L::kBStageBytes;
+                        if (leader) mbar_arrive_expect_tx(&S.full[s], 2 * (L::kAStageBytes + b_bytes));
                         tma_load_2d_pair(dst_a, &tmap_a, kb * kBK, m0, leader_full);
-                        tma_load_2d_pair(dst_b, &tmap_b, kb * kBK, w0, leader_full);
+                        tma_load_2d_pair(dst_b, narrow ? &tmap_b_narrow : &tmap_b, kb * kBK, w0, leader_full);
                     }
                     ++fills;
                     if (++s == kStagesP) {
@@ -204,7 +225,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
     } else if (warp == 1) {
         // ------------------------------------------------------------------ MMA issuer (leader)
         if (leader && lane == 0) {
-            constexpr uint32_t idesc = idesc_i8(kPairBM, kBN);
+            constexpr uint32_t idesc_full = idesc_i8(kPairBM, kBN);
+            constexpr uint32_t idesc_half = idesc_i8(kPairBM, kHalfBN);
             int s = 0;
             uint32_t ph = 0;
             int local = 0;
@@ -215,9 +237,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                     ab_state.raise();
                 ok = false;
             }
-            for (int t = pair; t < num_tiles && ok; t += num_pairs, ++local) {
+            for (int t = pair; t < num_work && ok; t += num_pairs, ++local) {
                 const int ab = local & 1;
                 const uint32_t aph = (local >> 1) & 1;
+                const uint32_t idesc = t >= num_full ? idesc_half : idesc_full;
                 if (!ab_state.wait_cluster(&S.acc_empty[ab], aph ^ 1u, kErrTimeoutAccumFree)) {
                     ok = false;
                     break;
@@ -268,14 +291,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
         const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&S.acc_empty[0]), 0u);
         bool alive = true;
         int local = 0;
-        for (int t = pair; t < num_tiles; t += num_pairs, ++local) {
+        for (int t = pair; t < num_work; t += num_pairs, ++local) {
             const int ab = local & 1;
             const uint32_t aph = (local >> 1) & 1;
-            const int m0 = (t / num_n) * kPairBM + static_cast<int>(rank) * kBM;
-            const int n0 = (t % num_n) * kBN;
+            int m_tile, n0, ncols;
+            work_item(t, m_tile, n0, ncols);
+            const int m0 = m_tile * kPairBM + static_cast<int>(rank) * kBM;
             named_barrier(1, kEpilogueThreads);
             if (args.out_mode == kOutBf16) {
-                for (int c = ethread; c < kBN; c += kEpilogueThreads) {
+                for (int c = ethread; c < ncols; c += kEpilogueThreads) {
                     const int n = n0 + c;
                     const bool in = n < args.n;
                     S.col_scale[c] = in ? args.w_scale[args.w_scale_count == 1 ? 0 : n] : 0.0f;
@@ -295,7 +319,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
             const bool row_ok = m < args.m;
             const float a_s = (row_ok && args.out_mode == kOutBf16) ? args.a_scale[m] : 0.0f;
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = 0; c < ncols / 32; ++c) {
                 uint32_t acc[32];
                 tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(ab * kBN + c * 32) +
                                        (static_cast<uint32_t>(quad * 32) << 16),
@@ -360,10 +384,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
 }
 
 template __global__ void int8_gemm_pair_kernel<kModeW8A8>(const __grid_constant__ CUtensorMap,
+                                                          const __grid_constant__ CUtensorMap,
                                                           const __grid_constant__ CUtensorMap, const GemmArgs);
 template __global__ void int8_gemm_pair_kernel<kModeW4A8>(const __grid_constant__ CUtensorMap,
+                                                          const __grid_constant__ CUtensorMap,
                                                           const __grid_constant__ CUtensorMap, const GemmArgs);
 template __global__ void int8_gemm_pair_kernel<kModeW4A4>(const __grid_constant__ CUtensorMap,
+                                                          const __grid_constant__ CUtensorMap,
                                                           const __grid_constant__ CUtensorMap, const GemmArgs);
 
 }  // namespace gemm

@@ -257,6 +257,13 @@ CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, in
  * selector, or a negative error code. */
 CTU_API int ctu_debug_set_gemm_kernel(int which);
 
+/* Test hook (no counterpart in the reference): how many of the last 256 x 256 output tiles
+ * the CTA-pair W8A8 GEMM runs as two 256 x 128 halves, for every later call in this
+ * process.  -1 = per problem (default: the last round's tiles when that halves the last
+ * round), 0 = never, n > 0 = the last n tiles.  Returns the previous setting, or a
+ * negative error code. */
+CTU_API int ctu_debug_set_gemm_split(int tiles);
+
 /* Test hook (no counterpart in the reference): choose the ConvRot quantizer for every
  * later call in this process.  0 = per width (default: the eight-lane kernel for
  * 4096 < K <= 6144, the four-lane kernel for other K <= 8192, the register-resident

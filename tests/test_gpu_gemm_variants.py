@@ -182,3 +182,56 @@ def test_fused_w4_kernels_at_long_sequences(C, kernel, mode):
     else:
         ref = oracle.w4a4_linear(act, wp, a_s.numpy(), w_s.numpy(), bias.numpy())
     assert np.array_equal(bf16_bits(out), ref)
+
+
+# ----------------------------------------------------------------------------- half-width tail tiles
+@pytest.mark.parametrize("m,n,k", [(257, 520, 1040), (600, 136, 1536), (1000, 1032, 5120), (4095, 5120, 512)])
+@pytest.mark.parametrize("split", [1, 3, 10**6])
+def test_pair_gemm_split_tiles_match_oracle(C, m, n, k, split):
+    """The CTA-pair W8A8 kernel with its last `split` tiles run as two 256 x 128 halves
+    (10**6: every tile) gives the oracle's bytes -- N tails that end inside the first
+    or second half, M tails inside a tile -- and so does its int32 output."""
+    from comfyui_turing_utils_kernel import _lib
+
+    g = torch.Generator().manual_seed(13 * m + 7 * n + k + split % 97)
+    a = torch.randint(-127, 128, (m, k), generator=g, dtype=torch.int8)
+    w = torch.randint(-127, 128, (n, k), generator=g, dtype=torch.int8)
+    a_s = torch.rand((m,), generator=g) * 0.02 + 1e-3
+    w_s = torch.rand((n,), generator=g) * 0.009 + 1e-3
+    bias = torch.randn((n,), generator=g) * 0.02
+    lib = _lib.load()
+    prev_kernel = lib.ctu_debug_set_gemm_kernel(2)
+    prev_split = lib.ctu_debug_set_gemm_split(split)
+    try:
+        out = C.turing_int8_linear(a.cuda(), w.cuda(), a_s.cuda(), w_s.cuda(), bias.cuda())
+        acc = C.int8_gemm_s32(a.cuda(), w.cuda())
+        torch.cuda.synchronize()
+    finally:
+        lib.ctu_debug_set_gemm_split(prev_split)
+        lib.ctu_debug_set_gemm_kernel(prev_kernel)
+    ref = oracle.int8_linear(a.numpy(), w.numpy(), a_s.numpy(), w_s.numpy(), bias.numpy())
+    assert np.array_equal(bf16_bits(out), ref)
+    assert np.array_equal(acc.cpu().numpy(), oracle.int8_gemm_s32(a.numpy(), w.numpy()))
+
+
+def test_pair_gemm_shard_shapes_split_automatically(C):
+    """Row shards of the configs[1] linears at 2 and 8 GPUs (16380 and 4095 rows): the
+    automatic tail split gives the same output as running every tile whole."""
+    from comfyui_turing_utils_kernel import _lib
+
+    lib = _lib.load()
+    for m, n, k in ((4095, 5120, 5120), (16380, 5120, 5120), (4095, 5120, 13824)):
+        g = torch.Generator(device="cuda").manual_seed(m + n + k)
+        a = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
+        w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+        a_s = torch.rand((m,), generator=g, device="cuda") * 0.02 + 1e-3
+        w_s = torch.rand((n,), generator=g, device="cuda") * 0.009 + 1e-3
+        bias = torch.randn((n,), generator=g, device="cuda") * 0.02
+        auto = C.turing_int8_linear(a, w, a_s, w_s, bias)
+        prev = lib.ctu_debug_set_gemm_split(0)
+        try:
+            whole = C.turing_int8_linear(a, w, a_s, w_s, bias)
+        finally:
+            lib.ctu_debug_set_gemm_split(prev)
+        torch.cuda.synchronize()
+        assert torch.equal(auto.view(torch.int16), whole.view(torch.int16)), (m, n, k)
