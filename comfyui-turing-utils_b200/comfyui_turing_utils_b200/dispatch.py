@@ -196,6 +196,10 @@ def codebook_w4a8_linear(
 w4a8_int8_linear = codebook_w4a8_linear
 
 
+# dispatch.py:873: the name comfy-kitchen's registry calls for the grouped-codebook format.
+w4a8_int8_linear = codebook_w4a8_linear
+
+
 def convrot_w4a4_linear(
     x: torch.Tensor,
     qweight: torch.Tensor,
