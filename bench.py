@@ -363,6 +363,44 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                                         (", int8 activations" if bits == 8 else ", int4 ConvRot activations") +
                                         "; int4 operands widened to int8 ahead of the W8A8 GEMM (M >= 512)"}
 
+        # the per-group-128 formats.  Asymmetric uint4 W4A8 (values
+        # U[0, 15], fp16 scale and uint4 zero point per 128 columns) on per-token int8
+        # ConvRot activations; W4A4 (symmetric int4 weights with fp16 per-group scales) on
+        # per-token-per-group int4 ConvRot activations.  Each step quantizes and runs all
+        # six linears, so the per-call weight widening is inside the timed work.
+        gg = torch.Generator(device=dev).manual_seed(91)
+        grouped = []
+        for k, n, w, _, b in layers:
+            u4 = torch.randint(0, 256, (n, k // 2), generator=gg, dtype=torch.int32, device=dev).to(torch.uint8)
+            zp = torch.randint(0, 16, (n, k // 128), generator=gg, dtype=torch.int32, device=dev).to(torch.uint8)
+            gsc = (torch.rand((n, k // 128), generator=gg, device=dev) * 0.009 + 1e-3).to(torch.float16)
+            s4 = (w[:, 0::2].to(torch.int32) % 15 - 7) & 0xF | (((w[:, 1::2].to(torch.int32) % 15 - 7) & 0xF) << 4)
+            grouped.append((u4, zp, gsc, s4.to(torch.int8), b))
+
+        def asym_w4a8_step():
+            for x, (u4, zp, gsc, _, b) in zip(xs, grouped):
+                q, s = kops.turing_bf16_int8_convrot_quantize(x, 256)
+                kops.turing_asym_w4a8_g128_linear(q, u4, s, gsc, zp, b)
+
+        def w4a4_g128_step():
+            for x, (_, _, gsc, s4, b) in zip(xs, grouped):
+                q, s = kops.turing_bf16_int4_g128_convrot_quantize(x, 256)
+                kops.turing_w4a4_g128_linear(q, s4, s, gsc, b)
+
+        for name, fn, fmt in (
+                ("asym_w4a8_g128", asym_w4a8_step,
+                 "configs[2]: asymmetric uint4 weights, fp16 scale + uint4 zero point per 128 columns, per-token "
+                 "int8 ConvRot activations; weights widened to (nibble - zero) int8, then the per-group CTA-pair "
+                 "GEMM (parity unpinned: kitchen's format)"),
+                ("w4a4_g128", w4a4_g128_step,
+                 "configs[3]: symmetric int4 weights with fp16 per-group-128 scales, int4 ConvRot activations with "
+                 "per-token-per-group-128 scales; both operands sign-extended, then the per-group CTA-pair GEMM "
+                 "(parity unpinned: kitchen's format)")):
+            ms = timed(fn, max(5, min(args.steps, 20)))
+            variants[name] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,
+                              "ms_per_step": ms, "format": fmt}
+        del grouped
+
         # Grouped-codebook W4A8 (group 16, e4m3 scales, 16-entry codebook): decode to int8,
         # then the W8A8 pair GEMM, per linear.
         gc = torch.Generator(device=dev).manual_seed(77)
@@ -388,8 +426,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         c0m, c0k, c0n = CFG0
         x0 = synth_activation(c0m, c0k, torch_generator(7)).to(dev)
         w0, ws0, b0 = (t.to(dev) for t in synth_weight(c0n, c0k, 2000))
-        ms = timed(lambda: kops.turing_int8_linear(*kops.turing_bf16_int8_convrot_quantize(x0, 256), w0, ws0, b0),
-                   50)
+        def cfg0_linear():
+            q0, s0 = kops.turing_bf16_int8_convrot_quantize(x0, 256)
+            return kops.turing_int8_linear(q0, w0, s0, ws0, b0)
+
+        ms = timed(cfg0_linear, 50)
         variants["cfg0"] = {"value": 2.0 * c0m * c0n * c0k / (ms * 1e-3) / 1e12, "unit": UNIT, "us": ms * 1e3,
                             "shape_mkn": list(CFG0),
                             "note": "configs[0] (Wan-1.3B FFN up) on one GPU: rotate+quantize + W8A8 GEMM; "

@@ -22,7 +22,7 @@ OUT_DIR = HERE / "comfyui_turing_utils_kernel"
 LIB = OUT_DIR / "libctu_b200.so"
 OBJ_DIR = HERE / "_build"
 
-SOURCES = ["capi.cu", "convrot_quant.cu", "convrot_quant_reg.cu", "convrot_quant_t4.cu", "convrot_quant_k8.cu", "gemm_i8.cu", "gemm_pair.cu", "dequant.cu", "noalloc.cu", "codebook.cu", "unpack_s4.cu", "norm_adaln.cu"]
+SOURCES = ["capi.cu", "convrot_quant.cu", "convrot_quant_reg.cu", "convrot_quant_t4.cu", "convrot_quant_k8.cu", "gemm_i8.cu", "gemm_pair.cu", "gemm_grouped.cu", "dequant.cu", "noalloc.cu", "codebook.cu", "unpack_s4.cu", "norm_adaln.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",

@@ -560,6 +560,117 @@ def int4_linear(qactivation, qweight, activation_scale, wscales, bias=None, out_
     return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 
 
+# Per-group (128 along K) formats.  The reference gets these from comfy-kitchen
+# (dispatch.py:876-936 and the AsymW4A8Int8Layout checkpoints, quantization/convrot.py:51-104),
+# whose source is not available; the arithmetic is this library's (see ctu_b200.h).
+QUANT_GROUP = 128
+
+
+def bf16_int4_g128_convrot_quantize(input, group_size=256):
+    """ConvRot rotation, then int4 codes with one scale per token and 128 columns:
+    ``(codes int8 [M, K/2] packed, scales fp32 [M, K/128])``."""
+    x = input.contiguous()
+    _check_cuda_2d(x, "input")
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("per-group INT4 ConvRot input must be bfloat16")
+    if group_size != 256:
+        raise RuntimeError("per-group INT4 ConvRot only supports group_size=256")
+    rows, k = x.shape
+    if rows <= 0 or k <= 0 or k % group_size != 0:
+        raise RuntimeError("per-group INT4 ConvRot width must be positive and divisible by 256")
+    x = _aligned(x)
+    codes = torch.empty((rows, k // 2), dtype=torch.int8, device=x.device)
+    scales = torch.empty((rows, k // QUANT_GROUP), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().ctu_convrot_quantize_int4_g128(_ptr(x), rows, k, _ptr(codes), _ptr(scales),
+                                                              _stream(x.device)))
+    return codes, scales
+
+
+def _group_major_scales(w_scale: torch.Tensor, n: int, groups: int) -> torch.Tensor:
+    """Checkpoint weight scales [N, K/128] (fp16) -> fp32 [K/128, N], group-major."""
+    if w_scale.shape != (n, groups):
+        raise RuntimeError(f"weight_scale must have shape [{n}, {groups}]")
+    return w_scale.to(torch.float16).to(torch.float32).t().contiguous()
+
+
+def _grouped_common(m, n, k, bias, dev):
+    if k % QUANT_GROUP != 0 or n % 8 != 0:
+        raise RuntimeError(f"per-group linears require K%128=0 and N%8=0 (got K={k}, N={n})")
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.float32).contiguous()
+        if bias.numel() != n:
+            raise RuntimeError("bias must contain one value per output channel")
+    return bias, torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+
+
+def asym_w4a8_g128_linear(activation, weight, activation_scale, weight_scale, weight_zero, bias=None):
+    """Asymmetric uint4 W4A8: int8 activations [M, K] with per-token scales; uint4
+    weights packed [N, K/2] (uint8 storage, even column in the low nibble) with an fp16
+    scale and a uint4 zero point per 128 columns ([N, K/128] each) -> bf16 [M, N]."""
+    activation = activation.contiguous()
+    weight = weight.contiguous()
+    _check_cuda_2d(activation, "activation")
+    _check_cuda_2d(weight, "weight")
+    if activation.dtype != torch.int8:
+        raise RuntimeError("asymmetric W4A8 activation must be int8")
+    if weight.dtype not in (torch.uint8, torch.int8):
+        raise RuntimeError("asymmetric W4A8 weight must use packed uint8 storage")
+    dev = activation.device
+    m, k = activation.shape
+    n = weight.shape[0]
+    if weight.shape[1] * 2 != k:
+        raise RuntimeError("asymmetric W4A8 packed weight must have K/2 columns")
+    bias, out = _grouped_common(m, n, k, bias, dev)
+    groups = k // QUANT_GROUP
+    w_scale = _group_major_scales(weight_scale, n, groups)
+    if weight_zero.shape != (n, groups):
+        raise RuntimeError(f"weight_zero must have shape [{n}, {groups}]")
+    w_zero = weight_zero.to(torch.uint8).contiguous()
+    a_scale = activation_scale.reshape(-1).to(torch.float32).contiguous()
+    if a_scale.numel() != m:
+        raise RuntimeError("activation_scale must contain one value per row")
+    if m > 0 and n > 0:
+        workspace = torch.empty((n, k), dtype=torch.int8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().ctu_asym_w4a8_g128_linear(
+                _ptr(_aligned(activation)), _ptr(_aligned(weight)), _ptr(a_scale), _ptr(w_scale), _ptr(w_zero),
+                _ptr(bias), _ptr(out), _ptr(workspace), m, n, k, _stream(dev)))
+    return out
+
+
+def w4a4_g128_linear(qactivation, qweight, activation_scale, weight_scale, bias=None):
+    """W4A4 with per-token-per-group activation scales: packed signed int4 activations
+    [M, K/2] with fp32 scales [M, K/128] (bf16_int4_g128_convrot_quantize), packed signed
+    int4 weights [N, K/2] with fp16 scales [N, K/128] -> bf16 [M, N]."""
+    qactivation = qactivation.contiguous()
+    qweight = qweight.contiguous()
+    _check_cuda_2d(qactivation, "activation")
+    _check_cuda_2d(qweight, "weight")
+    if qactivation.dtype != torch.int8 or qweight.dtype != torch.int8:
+        raise RuntimeError("W4A4 activation and weight must use packed int8 storage")
+    dev = qactivation.device
+    m, kp = qactivation.shape
+    n = qweight.shape[0]
+    k = 2 * kp
+    if qweight.shape[1] != kp:
+        raise RuntimeError("W4A4 packed K dimensions must match")
+    bias, out = _grouped_common(m, n, k, bias, dev)
+    groups = k // QUANT_GROUP
+    w_scale = _group_major_scales(weight_scale, n, groups)
+    a_scale = activation_scale.to(torch.float32).contiguous()
+    if a_scale.shape != (m, groups):
+        raise RuntimeError(f"activation_scale must have shape [{m}, {groups}]")
+    if m > 0 and n > 0:
+        a_ws = torch.empty((m, k), dtype=torch.int8, device=dev)
+        w_ws = torch.empty((n, k), dtype=torch.int8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().ctu_w4a4_g128_linear(
+                _ptr(_aligned(qactivation)), _ptr(_aligned(qweight)), _ptr(a_scale), _ptr(w_scale), _ptr(bias),
+                _ptr(out), _ptr(a_ws), _ptr(w_ws), m, n, k, _stream(dev)))
+    return out
+
+
 def int8_gemm_s32(activation, weight, out=None):
     """Exact int32 accumulators ``activation @ weight.T`` (no epilogue)."""
     _check_cuda_2d(activation, "activation")

@@ -7,9 +7,11 @@ them.  Attention (``turing_sage``) is outside this build's scope.
 """
 
 from .ops import (
+    turing_asym_w4a8_g128_linear,
     turing_bf16_gelu_int4_convrot_quantize,
     turing_bf16_gelu_int8_convrot_quantize,
     turing_bf16_int4_convrot_quantize,
+    turing_bf16_int4_g128_convrot_quantize,
     turing_bf16_int8_convrot_quantize,
     turing_codebook_w4a8_linear,
     turing_dequantize_int8_bf16,
@@ -21,6 +23,7 @@ from .ops import (
     turing_swiglu_int4_convrot_quantize,
     turing_swiglu_int8_convrot_quantize,
     turing_swiglu_int8_convrot_quantize_scaled,
+    turing_w4a4_g128_linear,
     turing_w4a8_linear,
 )
 
@@ -29,9 +32,11 @@ __version__ = "0.31.0"
 __b200_build__ = "0.1.0"
 
 __all__ = [
+    "turing_asym_w4a8_g128_linear",
     "turing_bf16_gelu_int4_convrot_quantize",
     "turing_bf16_gelu_int8_convrot_quantize",
     "turing_bf16_int4_convrot_quantize",
+    "turing_bf16_int4_g128_convrot_quantize",
     "turing_bf16_int8_convrot_quantize",
     "turing_codebook_w4a8_linear",
     "turing_dequantize_int8_bf16",
@@ -43,5 +48,6 @@ __all__ = [
     "turing_swiglu_int4_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize",
     "turing_swiglu_int8_convrot_quantize_scaled",
+    "turing_w4a4_g128_linear",
     "turing_w4a8_linear",
 ]

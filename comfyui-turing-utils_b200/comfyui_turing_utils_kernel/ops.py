@@ -376,3 +376,59 @@ def turing_layer_norm_adaln(
 @turing_layer_norm_adaln.register_fake
 def _turing_layer_norm_adaln_fake(x, scale, shift, epsilon=1.0e-5):
     return torch.empty_like(x)
+
+
+# Per-group (128 along K) formats.  No reference op carries them (the reference calls
+# comfy-kitchen for W4A4 and the asymmetric W4A8 layout, dispatch.py:876-936); the names
+# follow the turing_utils:: convention and the arithmetic is documented in ctu_b200.h.
+@torch.library.custom_op("turing_utils::bf16_int4_g128_convrot_quantize", mutates_args=())
+def turing_bf16_int4_g128_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
+    """ConvRot rotation + int4 codes with one scale per token per 128 columns."""
+    _require_cuda(x, "per-group INT4 ConvRot")
+    _check_bf16_2d(x, "per-group INT4 ConvRot")
+    return _C.bf16_int4_g128_convrot_quantize(x.contiguous(), group_size)
+
+
+@turing_bf16_int4_g128_convrot_quantize.register_fake
+def _turing_bf16_int4_g128_convrot_quantize_fake(x, group_size=256):
+    return (
+        torch.empty((x.size(0), x.size(1) // 2), dtype=torch.int8, device=x.device),
+        torch.empty((x.size(0), x.size(1) // 128), dtype=torch.float32, device=x.device),
+    )
+
+
+@torch.library.custom_op("turing_utils::asym_w4a8_g128_linear", mutates_args=())
+def turing_asym_w4a8_g128_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    weight_zero: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Asymmetric uint4 W4A8: fp16 scale and uint4 zero point per 128 columns of K."""
+    _require_cuda(activation, "asymmetric W4A8")
+    return _C.asym_w4a8_g128_linear(activation, weight, activation_scale, weight_scale, weight_zero, bias)
+
+
+@turing_asym_w4a8_g128_linear.register_fake
+def _turing_asym_w4a8_g128_linear_fake(activation, weight, activation_scale, weight_scale, weight_zero, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
+
+
+@torch.library.custom_op("turing_utils::w4a4_g128_linear", mutates_args=())
+def turing_w4a4_g128_linear(
+    activation: torch.Tensor,
+    weight: torch.Tensor,
+    activation_scale: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """W4A4 with per-token-per-group-128 activation scales and fp16 per-group weight scales."""
+    _require_cuda(activation, "per-group W4A4")
+    return _C.w4a4_g128_linear(activation, weight, activation_scale, weight_scale, bias)
+
+
+@turing_w4a4_g128_linear.register_fake
+def _turing_w4a4_g128_linear_fake(activation, weight, activation_scale, weight_scale, bias=None):
+    return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)

@@ -600,6 +600,84 @@ int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
     return launch_gemm(a, w, args, q.device, q.num_sms, stream);
 }
 
+// ---------------------------------------------------------------------------- per-group linears
+// Clusters of two CTAs of the grouped GEMM resident at once, per device and mode.
+int g_grouped_clusters[kMaxDevices][2] = {};
+
+template <int kGroupMode>
+int launch_grouped_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GroupedArgs &args, int device,
+                        cudaStream_t stream) {
+    using ctu::gemm::kGroupedBN;
+    using ctu::gemm::kGroupK;
+    CUtensorMap map_a, map_b;
+    if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, args.k, args.m, kGroupK, ctu::gemm::kBM))
+        return rc;
+    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, kGroupK, kGroupedBN / 2))
+        return rc;
+    constexpr auto kernel = ctu::gemm::int8_gemm_pair_grouped_kernel<kGroupMode>;
+    constexpr int smem = ctu::gemm::kGroupedSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(ctu::gemm::kGroupedThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        clusters = g_grouped_clusters[device][kGroupMode];
+    }
+    if (clusters == 0) {
+        int num_sms = 0;
+        CTU_CUDA(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
+        CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+        CTU_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
+        if (clusters <= 0) return fail(CTU_ERR_UNSUPPORTED, "no CTA pair of the grouped GEMM fits on device %d", device);
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_grouped_clusters[device][kGroupMode] = clusters;
+    }
+    const int64_t tiles = ((args.m + ctu::gemm::kPairBM - 1) / ctu::gemm::kPairBM) *
+                          static_cast<int64_t>((args.n + kGroupedBN - 1) / kGroupedBN);
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, clusters)), 1, 1);
+    CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, args));
+    return CTU_OK;
+}
+
+// Shapes of the per-group linears: K a multiple of the 128-column group, N of 8 (16-byte
+// rows of the bf16 output and of the fp32 scale rows' 32-byte copies).
+int check_grouped_shapes(const char *name, int64_t m, int64_t n, int64_t k) {
+    if (m < 0 || n < 0 || k < 0) return fail(CTU_ERR_INVALID_ARGUMENT, "%s dimensions must be non-negative", name);
+    if (m > INT32_MAX || n > INT32_MAX || k > INT32_MAX)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "%s dimensions exceed the kernel range", name);
+    if (k % 128 != 0 || n % 8 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "%s requires K%%128=0 and N%%8=0 (got K=%lld, N=%lld)", name,
+                    static_cast<long long>(k), static_cast<long long>(n));
+    if (m > 0 && n > 0 && k == 0) return fail(CTU_ERR_UNSUPPORTED, "K = 0 is not supported");
+    return CTU_OK;
+}
+
+int launch_widen(bool zero_points, const void *packed, const uint8_t *zeros, int8_t *out, int64_t rows, int64_t k,
+                 int num_sms, cudaStream_t stream) {
+    const int64_t items = rows * (k / 32);
+    if (items == 0) return CTU_OK;
+    const int threads = 256;
+    const int grid = static_cast<int>(std::min<int64_t>((items + threads - 1) / threads, static_cast<int64_t>(num_sms) * 8));
+    if (zero_points) {
+        ctu::w4::widen_u4_zero_kernel<<<grid, threads, 0, stream>>>(static_cast<const uint8_t *>(packed), zeros, out,
+                                                                      items);
+    } else {
+        ctu::w4::unpack_s4_kernel<<<grid, threads, 0, stream>>>(static_cast<const int8_t *>(packed), out, items);
+    }
+    CTU_CUDA(cudaGetLastError());
+    return CTU_OK;
+}
+
 }  // namespace host
 }  // namespace ctu
 
@@ -812,6 +890,75 @@ int ctu_codebook_w4a8_linear(const int8_t *a, const int8_t *w_packed, const floa
         if (int rc = launch_gemm(a, workspace, args, dev.device, dev.num_sms, s)) return rc;
     }
     return CTU_OK;
+}
+
+// ---------------------------------------------------------------- per-group W4A8 / W4A4
+int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *group_scales,
+                                   void *stream) {
+    if (int rc = check_quantize_args(x, rows, k, CTU_ACT_NONE, 4, codes, group_scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    QuantPlan plan;
+    const int g8_groups = k / 256 <= 24 ? 1 : 2;
+    if (!plan_quant_rows(k, CTU_ACT_NONE, dev.smem_optin, kQuantG8, &plan, g8_groups))
+        return fail(CTU_ERR_UNSUPPORTED, "no per-group int4 quantizer plan for width %lld", static_cast<long long>(k));
+    CUtensorMap map;
+    if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k / 64, 64,
+                           static_cast<uint32_t>(plan.box_rows)))
+        return rc;
+    ctu::rot::QuantArgs args{};
+    args.codes = codes;
+    args.group_scales = group_scales;
+    args.err = dev.err;
+    args.m = static_cast<int>(rows);
+    args.k = static_cast<int>(k);
+    args.rows_per_batch = plan.rows_per_batch;
+    args.box_rows = plan.box_rows;
+    args.copies = plan.copies;
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    using ctu::rot::kActNone;
+    const QuantKernel kernel = g8_groups == 2 ? ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 2, true>
+                                              : ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 1, true>;
+    return launch_quant_kernel(kernel, map, args, plan, q, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_asym_w4a8_g128_linear(const int8_t *a, const uint8_t *w_packed, const float *a_scale,
+                              const float *w_scale_gn, const uint8_t *w_zero, const float *bias, void *out,
+                              int8_t *w_workspace, int64_t m, int64_t n, int64_t k, void *stream) {
+    if (int rc = check_grouped_shapes("asymmetric W4A8", m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!a || !w_packed || !a_scale || !w_scale_gn || !w_zero || !out || !w_workspace)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(a) || !aligned16(w_packed) || !aligned16(out) || !aligned16(w_workspace) || !aligned16(w_scale_gn))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "activation, weight, scales, output and workspace must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (int rc = launch_widen(true, w_packed, w_zero, w_workspace, n, k, dev.num_sms, s)) return rc;
+    ctu::gemm::GroupedArgs args{a_scale, w_scale_gn, bias, out, dev.err, static_cast<int>(m), static_cast<int>(n),
+                                static_cast<int>(k)};
+    return launch_grouped_gemm<ctu::gemm::kGroupAsymW4A8>(a, w_workspace, args, dev.device, s);
+}
+
+int ctu_w4a4_g128_linear(const int8_t *a_packed, const int8_t *w_packed, const float *a_scale_mg,
+                         const float *w_scale_gn, const float *bias, void *out, int8_t *a_workspace,
+                         int8_t *w_workspace, int64_t m, int64_t n, int64_t k, void *stream) {
+    if (int rc = check_grouped_shapes("W4A4", m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!a_packed || !w_packed || !a_scale_mg || !w_scale_gn || !out || !a_workspace || !w_workspace)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "null tensor pointer");
+    if (!aligned16(a_packed) || !aligned16(w_packed) || !aligned16(out) || !aligned16(a_workspace) ||
+        !aligned16(w_workspace) || !aligned16(w_scale_gn))
+        return fail(CTU_ERR_INVALID_ARGUMENT, "activation, weight, scales, output and workspaces must be 16-byte aligned");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (int rc = launch_widen(false, a_packed, nullptr, a_workspace, m, k, dev.num_sms, s)) return rc;
+    if (int rc = launch_widen(false, w_packed, nullptr, w_workspace, n, k, dev.num_sms, s)) return rc;
+    ctu::gemm::GroupedArgs args{a_scale_mg, w_scale_gn, bias, out, dev.err, static_cast<int>(m), static_cast<int>(n),
+                                static_cast<int>(k)};
+    return launch_grouped_gemm<ctu::gemm::kGroupW4A4>(a_workspace, w_workspace, args, dev.device, s);
 }
 
 int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream) {

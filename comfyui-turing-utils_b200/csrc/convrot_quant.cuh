@@ -32,6 +32,9 @@ struct QuantArgs {
     const uint16_t *gelu_lut;    // [65536] bf16 bits, bf16-indexed
     const float *silu16_lut;     // [65536] fp32, fp16-indexed
     const uint16_t *gelu16_lut;  // [65536] fp16 bits, fp16-indexed
+    // Per-token-per-128-column int4 scales [m, k/128] (output of the group-scale
+    // quantizer; the per-row `scales` is then unused).
+    float *group_scales;
 };
 
 // Fills the activation tables: launch 256 blocks of 256 threads.
@@ -132,7 +135,9 @@ inline size_t quant_g8_smem_bytes(int rows, int k, int act, int warps) {
     return 1024 + 2 * in_bytes + static_cast<size_t>(kK8WarpBytes) * warps + 24 * static_cast<size_t>(rows) + 24;
 }
 
-template <int Act, int Bits, int G>
+// kGroupScales (plain rows, int4 only): every 128 columns of a rotated row get their own
+// scale (args.group_scales) and codes; no row statistics are exchanged.
+template <int Act, int Bits, int G, bool kGroupScales = false>
 __global__ void convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
 }  // namespace rot

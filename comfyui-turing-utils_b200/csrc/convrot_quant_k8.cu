@@ -431,10 +431,13 @@ __device__ __forceinline__ void g8_load_swiglu(uint32_t base, uint32_t slice, ui
 
 // Rotation of the team's group.  kHalve: the reference's order with the per-stage
 // halvings (W = bf16(y), NaN-ignoring absmax, NaN probe); otherwise unscaled (W = bf16(z),
-// z = 16 y, NaN-propagating absmax of z).  All 32 lanes of the warp take part.
-template <bool kHalve>
+// z = 16 y, NaN-propagating absmax of z).  Word W[u] of lane q holds columns 16u + 2q and
+// 16u + 2q + 1 of the group.  kHalves: `absmax` covers columns 0..127 (u < 8) and
+// `absmax_hi` columns 128..255; otherwise `absmax` covers the whole group.  All 32 lanes
+// of the warp take part.
+template <bool kHalve, bool kHalves = false>
 __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32_t rbase, uint32_t (&W)[16],
-                                          float &absmax, float &nan_probe) {
+                                          float &absmax, float &nan_probe, float &absmax_hi) {
     const f32x2 half = pk2(0.5f, 0.5f);
 #pragma unroll
     for (int a = 0; a < 4; ++a) {
@@ -479,17 +482,18 @@ __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32
         if constexpr (kHalve) butterfly2(R[w], R[w + 4], R[w + 8], R[w + 12], half);
         else butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
     }
-    float m = 0.0f;
+    float m = 0.0f, mh = 0.0f;
     f32x2 probe = pk2(0.0f, 0.0f);
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
         float lo, hi;
         unpk2(R[u], lo, hi);
+        float &acc = kHalves && u >= 8 ? mh : m;
         if constexpr (kHalve) {
             probe = fadd2(probe, R[u]);
-            m = max_abs3(m, lo, hi);
+            acc = max_abs3(acc, lo, hi);
         } else {
-            m = max_abs3_nan(m, lo, hi);
+            acc = max_abs3_nan(acc, lo, hi);
         }
         W[u] = pack_bf16x2(lo, hi);
     }
@@ -503,12 +507,15 @@ __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32
     for (int d = 1; d < 8; d <<= 1) {
         if constexpr (kHalve) {
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));  // NaN-ignoring, as the reference's fmaxf
+            if constexpr (kHalves) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, d));
             pr = __fadd_rn(pr, __shfl_xor_sync(0xffffffffu, pr, d));
         } else {
             m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, d));
+            if constexpr (kHalves) mh = max_nan(mh, __shfl_xor_sync(0xffffffffu, mh, d));
         }
     }
     absmax = m;
+    absmax_hi = mh;
     nan_probe = pr;
 }
 
@@ -545,9 +552,33 @@ static __device__ __noinline__ uint32_t quant8_int4_prescaled(uint4 w, float inv
 
 }  // namespace
 
-template <int Act, int Bits, int G>
+// int4 codes of the 8 words W[u0 .. u0 + 8) with scale `scale` of the unscaled (folded)
+// or halved rotation, the reference's int4 chain (see the row kernel below).
+__device__ __forceinline__ void g8_int4_half(const uint32_t *W, float scale, bool folded, int8_t *out) {
+    const float inv = __fdiv_rn(1.0f, scale);
+    if (folded && !(inv >= 0x1p-100f)) {
+#pragma unroll
+        for (int u = 0; u < 8; u += 4) {
+            const uint32_t c = quant8_int4_prescaled(make_uint4(W[u], W[u + 1], W[u + 2], W[u + 3]), inv);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) out[8 * (u + i)] = static_cast<int8_t>((c >> (8 * i)) & 0xFFu);
+        }
+    } else {
+        const float iv = folded ? inv * 0.0625f : inv;
+        const f32x2 i2 = pk2(iv, iv);
+#pragma unroll
+        for (int u = 0; u < 8; u += 4) {
+            const uint32_t c = quant8_int4(make_uint4(W[u], W[u + 1], W[u + 2], W[u + 3]), i2);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) out[8 * (u + i)] = static_cast<int8_t>((c >> (8 * i)) & 0xFFu);
+        }
+    }
+}
+
+template <int Act, int Bits, int G, bool kGroupScales>
 __global__ void __launch_bounds__(kG8MaxThreads)
     convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
+    static_assert(!kGroupScales || (Act == kActNone && Bits == 4), "group scales: plain rows, int4 codes");
     constexpr bool kFold = Act != kActSwiGLU;
     extern __shared__ uint8_t smem_raw[];
     // Shared-space addresses (32-bit), 1024-byte aligned as the 128-byte swizzle needs.
@@ -651,24 +682,42 @@ __global__ void __launch_bounds__(kG8MaxThreads)
             group_nan[s] = false;
             if (!alive || warp * 4 + s * teams >= tasks) continue;  // warp-uniform
             const bool active = team + s * teams < tasks;
-            float amax = 0.0f, probe = 0.0f;
+            float amax = 0.0f, probe = 0.0f, amax_hi = 0.0f;
             bool exact = true;
             if constexpr (kFold) {
                 f32x2 P[16];
                 g8_load<Act>(in, ld[s], P, lut);
-                g8_rotate<false>(P, wbase, rbase, W[s], amax, probe);
-                exact = __any_sync(0xffffffffu, !(amax <= 3.40282347e38f));
+                g8_rotate<false, kGroupScales>(P, wbase, rbase, W[s], amax, probe, amax_hi);
+                exact = __any_sync(0xffffffffu, !(amax <= 3.40282347e38f) || !(amax_hi <= 3.40282347e38f));
                 if (!exact) {
                     folded[s] = true;
                     amax *= 0.0625f;
+                    amax_hi *= 0.0625f;
                 }
             }
             if (exact) {  // warp-uniform: the reference's order, halvings included
                 f32x2 P[16];
                 if constexpr (Act == kActSwiGLU) g8_load_swiglu(in, slice_of[s], q, static_cast<uint32_t>(K / 64), P, lut);
                 else g8_load<Act>(in, ld[s], P, lut);
-                g8_rotate<true>(P, wbase, rbase, W[s], amax, probe);
+                g8_rotate<true, kGroupScales>(P, wbase, rbase, W[s], amax, probe, amax_hi);
                 group_nan[s] = isnan(probe);
+            }
+            if constexpr (kGroupScales) {
+                // Each 128-column half of the group is quantized on its own, right here.
+                if (active) {
+                    const int64_t row = row0 + r_of[s];
+                    int8_t *out = args.codes + row * (K / 2) + grp_of[s] * 128 + q;
+                    float *gs = args.group_scales + row * (K / 128) + 2 * grp_of[s];
+                    const float scale_lo = row_scale<4>(amax, false);
+                    const float scale_hi = row_scale<4>(amax_hi, false);
+                    if (q == 0) {
+                        gs[0] = scale_lo;
+                        gs[1] = scale_hi;
+                    }
+                    g8_int4_half(&W[s][0], scale_lo, folded[s], out);
+                    g8_int4_half(&W[s][8], scale_hi, folded[s], out + 64);
+                }
+                continue;
             }
             if (active && q == 0 && !given) {
                 atom_max_shared(amax_slot + 4u * r_of[s], __float_as_uint(amax));
@@ -692,6 +741,7 @@ __global__ void __launch_bounds__(kG8MaxThreads)
             }
         }
 
+        if constexpr (kGroupScales) continue;
 #pragma unroll
         for (int s = 0; s < G; ++s) {
             if (!alive || team + s * teams >= tasks) continue;
@@ -774,6 +824,10 @@ template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 1>(const __grid_co
 template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
 
 }  // namespace rot
 }  // namespace ctu

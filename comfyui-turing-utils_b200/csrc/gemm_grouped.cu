@@ -1,0 +1,411 @@
+// Per-group (128 along K) integer GEMMs for the asymmetric W4A8 and the W4A4 linears:
+//
+//   W4A8: t = sum_g fma(w_scale[g][n], float(acc_g[m, n]), t);  out = bf16(fma(t, a_scale[m], bias[n]))
+//   W4A4: t = sum_g fma(float(acc_g[m, n]) * a_scale[m][g], w_scale[g][n], t);  out = bf16(t + bias[n])
+//
+// with acc_g the exact int32 product of group g's 128 columns.  A cluster of two CTAs
+// owns a 256 x 128 output tile (tcgen05.mma.cta_group::2, M = 256, N = 128): CTA r stages
+// activation rows [128 r, 128 r + 128) and weight rows [64 r, 64 r + 64) of each group.
+// One ring stage is one group (four K = 32 MMAs).  Each group's partial lands in its own
+// 128-column TMEM buffer, and there are four, so the MMA runs up to three groups ahead of
+// the epilogue that converts and scales them.
+//
+// Conversion without I2F.  The group's first MMA overwrites the buffer, so it holds the
+// exact int32 partial acc, |acc| <= 128 * 128 * 15 < 2^22.  For such acc the bit pattern
+// (acc & 0x7FFFFF) ^ 0x4B400000 is the float 1.5 * 2^23 + acc (floats in [2^23, 2^24) are
+// the integers; bits 0..21 are acc's, bit 22 is the complement of its sign-extension
+// bit, the exponent is the constant's), so float(acc) is one bitwise operation and one
+// exact packed subtract of 1.5 * 2^23.  TMEM is only read: writing a pattern back costs
+// more TMEM bandwidth than the MMAs leave.
+//
+// Throughput.  Per group and CTA the epilogue does one ALU and 2 (W4A8) or 3 (W4A4) fp32
+// operations on each of 128 x 128 partials: 256 cycles of the ALU pipe and 256 or 384 of
+// the 128-lane FMA pipe, against about 262 cycles for the group's MMAs (M = 256, N = 128,
+// K = 128 on two SMs).  So the
+// per-group control work is kept to a few instructions per warp, each warp reads its 64
+// partials of a group with one TMEM load (one load latency per group) straight into
+// register pairs, and the scales arrive as pairs next to their use.
+//
+// Roles per CTA (persistent over tiles, n-fastest):
+//   warp 0      producer: the stage's A and B tiles (completing on the leader's `full`
+//               barrier), and the group's 128 fp32 weight scales into this CTA's scale
+//               ring (completing on its own `sc_full`).
+//   warp 1      pair TMEM allocation.  Leader: the MMA issuer; non-leader: forwards its
+//               epilogue's buffer releases to the leader's `acc_empty` (one remote
+//               arrival per release instead of one per epilogue warp).
+//   warps 2..9  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and
+//               columns 64 ((w - 2) / 4) .. +63; 64 fp32 running sums per thread.
+// Every wait is bounded; a role that gives up raises the abort flag in both CTAs, and
+// both CTAs stay resident until the final cluster barrier.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gemm_i8.cuh"
+#include "gemm_tile.cuh"
+#include "ptx.cuh"
+
+namespace ctu {
+namespace gemm {
+
+namespace {
+
+constexpr uint32_t kMagicBits = 0x4B400000u;  // 1.5 * 2^23
+constexpr uint32_t kAccMask = 0x007FFFFFu;
+constexpr float kMagic = 12582912.0f;
+constexpr int kGroupedTmemCols = kGroupedBuffers * kGroupedBN;  // 512
+constexpr int kLoadCols = 32;  // TMEM columns per epilogue load
+static_assert(kGroupedTmemCols == 512, "four 128-column buffers fill TMEM");
+static_assert(kGroupedBuffers < kGroupedStages, "the epilogue identifies a group's MMA completion by stage parity");
+
+struct GroupedSmem {
+    uint64_t full[kGroupedStages];
+    uint64_t empty[kGroupedStages];
+    uint64_t acc_empty[kGroupedBuffers];  // leader: 8 local epilogue warps + 1 forwarded peer release
+    uint64_t acc_local[kGroupedBuffers];  // non-leader: its 8 epilogue warps
+    uint64_t sc_full[kGroupedScaleSlots];
+    uint64_t sc_empty[kGroupedScaleSlots];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort_flag;
+    alignas(16) float scale_ring[kGroupedScaleSlots][kGroupedBN];
+    alignas(16) float col_bias[kGroupedBN];
+};
+static_assert(sizeof(GroupedSmem) <= kGroupedBookkeepingBytes, "grouped GEMM bookkeeping exceeds its reservation");
+
+__device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+struct GroupedAbort {
+    volatile int *flag;
+    uint32_t peer_flag;
+    uint32_t *err;
+
+    __device__ __forceinline__ void raise() const {
+        *flag = 1;
+        st_cluster_u32(peer_flag, 1u);
+    }
+    __device__ __forceinline__ bool wait(uint64_t *bar, uint32_t parity, uint32_t code) const {
+        if (mbar_wait(bar, parity, flag, err, code)) return true;
+        raise();
+        return false;
+    }
+    __device__ __forceinline__ bool wait_cluster(uint64_t *bar, uint32_t parity, uint32_t code) const {
+        if (mbar_wait_cluster(bar, parity, flag, err, code)) return true;
+        raise();
+        return false;
+    }
+};
+
+// Four fp32 of shared memory, as a volatile load: it stays where it is written (after the
+// TMEM read it pairs with) instead of being hoisted to the loop head, which would hold
+// every scale of the group in registers at once.
+// Returned as two packed pairs, so they feed the packed arithmetic without moves.
+__device__ __forceinline__ void lds_f32x2x2(uint32_t addr, f32x2 &a, f32x2 &b) {
+    asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
+}
+
+// Two int32 partials -> the bit patterns of 1.5 * 2^23 + acc (see the file comment).
+__device__ __forceinline__ f32x2 to_magic_pair(u32x2 v) {
+    const uint32_t lo = (static_cast<uint32_t>(v) & kAccMask) ^ kMagicBits;
+    const uint32_t hi = (static_cast<uint32_t>(v >> 32) & kAccMask) ^ kMagicBits;
+    return (static_cast<f32x2>(hi) << 32) | lo;
+}
+
+__device__ __forceinline__ void settle_inflight_copies_grouped() {
+    const uint64_t start = globaltimer();
+    while (globaltimer() - start < 1000000ull) __nanosleep(1000);
+}
+
+}  // namespace
+
+template <int kGroupMode>
+__global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
+    int8_gemm_pair_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                  const __grid_constant__ CUtensorMap tmap_b, const GroupedArgs args) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t *sA = smem;
+    uint8_t *sB = smem + kGroupedStages * kGroupedAStage;
+    GroupedSmem &S = *reinterpret_cast<GroupedSmem *>(smem + kGroupedStages * (kGroupedAStage + kGroupedBStage));
+
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int pair = blockIdx.x >> 1;
+    const int num_pairs = gridDim.x >> 1;
+    const int num_n = (args.n + kGroupedBN - 1) / kGroupedBN;
+    const int num_m = (args.m + kPairBM - 1) / kPairBM;
+    const int num_tiles = num_m * num_n;
+    const int nk = args.k / kGroupK;
+    const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / num_pairs + 1 : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kGroupedStages; ++s) {
+            mbar_init(&S.full[s], 1);
+            mbar_init(&S.empty[s], 1);
+        }
+        for (int b = 0; b < kGroupedBuffers; ++b) {
+            mbar_init(&S.acc_empty[b], kGroupedEpilogueWarps + 1);
+            mbar_init(&S.acc_local[b], kGroupedEpilogueWarps);
+        }
+        for (int r = 0; r < kGroupedScaleSlots; ++r) {
+            mbar_init(&S.sc_full[r], 1);
+            mbar_init(&S.sc_empty[r], kGroupedEpilogueWarps);
+        }
+        mbar_init(&S.drain, 1);
+        S.abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(&S.tmem_base, kGroupedTmemCols);
+        tmem_relinquish_pair();
+    }
+    if (warp == 0 && lane == 0) {
+        prefetch_tmap(&tmap_a);
+        prefetch_tmap(&tmap_b);
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = S.tmem_base;
+    const GroupedAbort ab{&S.abort_flag, mapa_shared(smem_u32(&S.abort_flag), rank ^ 1u), args.err};
+    volatile int *abort_flag = &S.abort_flag;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ producer
+        if (lane == 0) {
+            const uint32_t leader_full0 = mapa_shared(smem_u32(&S.full[0]), 0u);
+            uint32_t j = 0;  // group steps of this pair, over all its tiles
+            bool ok = true;
+            for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                const int m_tile = t / num_n;
+                const int n0 = (t - m_tile * num_n) * kGroupedBN;
+                const int m0 = m_tile * kPairBM + static_cast<int>(rank) * kBM;
+                const int w0 = n0 + static_cast<int>(rank) * (kGroupedBN / 2);
+                const uint32_t sc_bytes = static_cast<uint32_t>(min(kGroupedBN, args.n - n0)) * 4u;
+                for (int kb = 0; kb < nk; ++kb, ++j) {
+                    const uint32_t s = j % kGroupedStages;
+                    const uint32_t ph = (j / kGroupedStages) & 1u;
+                    const uint32_t r = j % kGroupedScaleSlots;
+                    const uint32_t rph = (j / kGroupedScaleSlots) & 1u;
+                    if (!ab.wait(&S.sc_empty[r], rph ^ 1u, kErrTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&S.sc_full[r], sc_bytes);
+                    bulk_load(&S.scale_ring[r][0], args.w_scale_gn + static_cast<int64_t>(kb) * args.n + n0, sc_bytes,
+                              &S.sc_full[r]);
+                    if (!ab.wait(&S.empty[s], ph ^ 1u, kErrTimeoutEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    if (leader) mbar_arrive_expect_tx(&S.full[s], 2 * (kGroupedAStage + kGroupedBStage));
+                    const uint32_t leader_full = leader_full0 + s * static_cast<uint32_t>(sizeof(uint64_t));
+                    tma_load_2d_pair(sA + s * kGroupedAStage, &tmap_a, kb * kGroupK, m0, leader_full);
+                    tma_load_2d_pair(sB + s * kGroupedBStage, &tmap_b, kb * kGroupK, w0, leader_full);
+                }
+            }
+            if (!ok || *abort_flag) settle_inflight_copies_grouped();
+        }
+    } else if (warp == 1) {
+        if (leader) {
+            // -------------------------------------------------------------- MMA issuer
+            if (lane == 0) {
+                constexpr uint32_t idesc = idesc_i8(kPairBM, kGroupedBN);
+                uint32_t j = 0;
+                bool ok = true;
+                for (int t = pair; t < num_tiles && ok; t += num_pairs) {
+                    for (int kb = 0; kb < nk; ++kb, ++j) {
+                        const uint32_t pb = j % kGroupedBuffers;
+                        const uint32_t use = j / kGroupedBuffers;
+                        // Completion `use - 1` of acc_empty[pb]: the epilogue's release of the
+                        // buffer's previous group in both CTAs (a fresh barrier passes use 0).
+                        if (!ab.wait_cluster(&S.acc_empty[pb], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t s = j % kGroupedStages;
+                        if (!ab.wait(&S.full[s], (j / kGroupedStages) & 1u, kErrTimeoutFull)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t a_addr = smem_u32(sA + s * kGroupedAStage);
+                        const uint32_t b_addr = smem_u32(sB + s * kGroupedBStage);
+                        const uint32_t d_tmem = tmem_base + pb * kGroupedBN;
+#pragma unroll
+                        for (int k = 0; k < kGroupK / kUmmaK; ++k) {  // the first overwrites the buffer
+                            mma_i8_pair(d_tmem, smem_desc_sw128(a_addr + k * kUmmaK),
+                                        smem_desc_sw128(b_addr + k * kUmmaK), idesc, k != 0 ? 1u : 0u);
+                        }
+                        // One commit per group: its arrival on empty[s] (both CTAs) frees the
+                        // stage for the producer and tells the epilogue the partial is ready.
+                        mma_commit_pair_both(&S.empty[s]);
+                    }
+                }
+                mma_commit_pair_local(&S.drain);
+                mbar_wait(&S.drain, 0u, nullptr, args.err, kErrTimeoutDrain);
+            }
+        } else if (lane == 0) {
+            // -------------------------------------------------------------- release forwarder
+            const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&S.acc_empty[0]), 0u);
+            const uint32_t releases = static_cast<uint32_t>(my_tiles) * static_cast<uint32_t>(nk);
+            for (uint32_t i = 0; i < releases; ++i) {
+                const uint32_t pb = i % kGroupedBuffers;
+                if (!ab.wait(&S.acc_local[pb], (i / kGroupedBuffers) & 1u, kErrTimeoutAccumFree)) break;
+                mbar_arrive_remote(leader_acc_empty0 + pb * static_cast<uint32_t>(sizeof(uint64_t)));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------------ epilogue
+        const int quad = warp & 3;  // TMEM lanes this warp may access
+        const int col0 = ((warp - 2) >> 2) * kGroupedEpilogueCols;
+        const int row = quad * 32 + lane;
+        const uint32_t col_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(col0);
+        uint64_t *release0 = leader ? &S.acc_empty[0] : &S.acc_local[0];
+        const f32x2 magic2 = pk2(kMagic, kMagic);
+
+        bool alive = true;
+        uint32_t j = 0;
+        uint32_t r = 0, rph = 0;  // scale ring slot of step j and its phase parity
+        for (int t = pair; t < num_tiles; t += num_pairs) {
+            const int m_tile = t / num_n;
+            const int n0 = (t - m_tile * num_n) * kGroupedBN;
+            const int m = m_tile * kPairBM + static_cast<int>(rank) * kBM + row;
+            const bool row_ok = m < args.m;
+            named_barrier(1, 32 * kGroupedEpilogueWarps);  // the previous tile's bias reads are done
+            for (int c = threadIdx.x - 64; c < kGroupedBN; c += 32 * kGroupedEpilogueWarps) {
+                const int n = n0 + c;
+                S.col_bias[c] = (n < args.n && args.bias != nullptr) ? args.bias[n] : 0.0f;
+            }
+            named_barrier(1, 32 * kGroupedEpilogueWarps);
+            if (!alive) {
+                j += static_cast<uint32_t>(nk);
+                continue;
+            }
+
+            f32x2 acc[kGroupedEpilogueCols / 2];
+#pragma unroll
+            for (int i = 0; i < kGroupedEpilogueCols / 2; ++i) acc[i] = pk2(0.0f, 0.0f);
+            // W4A4: this row's activation scales, fetched two groups ahead.
+            const float *a_row = args.a_scale + static_cast<int64_t>(row_ok ? m : 0) * nk;
+            float gs0 = 0.0f, gs1 = 0.0f;
+            if constexpr (kGroupMode == kGroupW4A4) {
+                gs0 = row_ok ? a_row[0] : 0.0f;
+                gs1 = (row_ok && nk > 1) ? a_row[1] : 0.0f;
+            }
+            for (int kb = 0; kb < nk; ++kb, ++j) {
+                const uint32_t pb = j % kGroupedBuffers;
+                float gs2 = 0.0f;
+                if constexpr (kGroupMode == kGroupW4A4) gs2 = (row_ok && kb + 2 < nk) ? a_row[kb + 2] : 0.0f;
+                // The group's MMAs are complete when stage j % kGroupedStages completes its
+                // phase j / kGroupedStages.  The MMA runs at most kGroupedBuffers - 1 groups
+                // ahead of this loop, fewer than the ring depth, so that phase is the
+                // current or the previous one of the barrier and its parity identifies it.
+                const bool ok = mbar_wait(&S.empty[j % kGroupedStages], (j / kGroupedStages) & 1u, abort_flag,
+                                          args.err, kErrTimeoutAccum) &&
+                                mbar_wait(&S.sc_full[r], rph, abort_flag, args.err, kErrTimeoutFull);
+                alive = __all_sync(0xffffffffu, ok);
+                if (!alive) {
+                    ab.raise();
+                    break;
+                }
+                tc_fence_after();
+                // Read this warp's 64 columns (kLoadCols per TMEM load) and release the
+                // buffer once all are read, accumulating as they arrive.
+                static_assert(kGroupedEpilogueCols == 64, "64 columns per warp and group");
+                const uint32_t sc = smem_u32(&S.scale_ring[r][col0]);
+                const f32x2 g2 = pk2(gs0, gs0);  // W4A4: this row's activation scale of the group
+#pragma unroll
+                for (int h = 0; h < 64 / kLoadCols; ++h) {
+                    u32x2 v[kLoadCols / 2];
+                    tmem_ld_32x32b_x32_pairs(col_base + pb * kGroupedBN + kLoadCols * h, v);
+                    if (h == 64 / kLoadCols - 1) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(release0 + pb);
+                    }
+#pragma unroll
+                    for (int i = 0; i < kLoadCols / 4; ++i) {
+                        f32x2 s01, s23;
+                        lds_f32x2x2(sc + 16u * (i + h * kLoadCols / 4), s01, s23);
+                        const f32x2 d0 = fsub2(to_magic_pair(v[2 * i]), magic2);
+                        const f32x2 d1 = fsub2(to_magic_pair(v[2 * i + 1]), magic2);
+                        f32x2 &t0 = acc[2 * i + h * kLoadCols / 2];
+                        f32x2 &t1 = acc[2 * i + 1 + h * kLoadCols / 2];
+                        if constexpr (kGroupMode == kGroupW4A4) {
+                            t0 = ffma2(fmul2(d0, g2), s01, t0);
+                            t1 = ffma2(fmul2(d1, g2), s23, t1);
+                        } else {
+                            t0 = ffma2(s01, d0, t0);
+                            t1 = ffma2(s23, d1, t1);
+                        }
+                    }
+                }
+                if constexpr (kGroupMode == kGroupW4A4) {
+                    gs0 = gs1;
+                    gs1 = gs2;
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.sc_empty[r]);
+                if (++r == kGroupedScaleSlots) {
+                    r = 0;
+                    rph ^= 1u;
+                }
+            }
+            if (!alive) continue;
+
+            // Tile done: bias (and the per-token scale) and the bf16 store of this warp's columns.
+            if (row_ok) {
+                const float a_s = kGroupMode == kGroupAsymW4A8 ? args.a_scale[m] : 0.0f;
+                __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(args.out) + static_cast<int64_t>(m) * args.n + n0 + col0;
+#pragma unroll
+                for (int c = 0; c < kGroupedEpilogueCols / 8; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        float lo, hi;
+                        unpk2(acc[4 * c + i], lo, hi);
+                        const float b0 = S.col_bias[col0 + 8 * c + 2 * i];
+                        const float b1 = S.col_bias[col0 + 8 * c + 2 * i + 1];
+                        if constexpr (kGroupMode == kGroupAsymW4A8) {
+                            lo = __fmaf_rn(lo, a_s, b0);
+                            hi = __fmaf_rn(hi, a_s, b1);
+                        } else {
+                            lo = __fadd_rn(lo, b0);
+                            hi = __fadd_rn(hi, b1);
+                        }
+                        w[i] = pack_bf16x2(lo, hi);
+                    }
+                    if (n0 + col0 + 8 * c < args.n) {
+                        *reinterpret_cast<uint4 *>(dst + 8 * c) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kGroupedTmemCols);
+    }
+}
+
+template __global__ void int8_gemm_pair_grouped_kernel<kGroupAsymW4A8>(const __grid_constant__ CUtensorMap,
+                                                                       const __grid_constant__ CUtensorMap,
+                                                                       const GroupedArgs);
+template __global__ void int8_gemm_pair_grouped_kernel<kGroupW4A4>(const __grid_constant__ CUtensorMap,
+                                                                   const __grid_constant__ CUtensorMap,
+                                                                   const GroupedArgs);
+
+}  // namespace gemm
+}  // namespace ctu

@@ -101,5 +101,51 @@ __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a
                                       const __grid_constant__ CUtensorMap tmap_b,
                                       const __grid_constant__ CUtensorMap tmap_b_narrow, const GemmArgs args);
 
+// ---------------------------------------------------------------------------
+// Per-group (128 along K) linears: every 128-column group of K has its own weight scale
+// (and, for W4A4, its own activation scale per token), so each group's int32 partial is
+// converted and scaled on its own.  A CTA pair computes a 256 x 128 output tile; one
+// ring stage is one group; four 128-column TMEM buffers hold the partials of four
+// consecutive groups, so the MMA runs up to three groups ahead of the epilogue.
+//
+//   kGroupAsymW4A8: t += w_scale[g][n] * float(acc_g);  out = bf16(fma(t, a_scale[m], bias[n]))
+//   kGroupW4A4:     t += (float(acc_g) * a_scale[m][g]) * w_scale[g][n];  out = bf16(t + bias[n])
+//
+// (each += one fused multiply-add, groups in order).  The operands are int8: the
+// asymmetric uint4 weights arrive widened to (nibble - zero), the int4 activations
+// sign-extended.
+enum GroupMode : int { kGroupAsymW4A8 = 0, kGroupW4A4 = 1 };
+
+constexpr int kGroupK = kBK;           // K columns per group = one ring stage
+constexpr int kGroupedBN = 128;        // output columns per pair tile
+constexpr int kGroupedStages = 8;      // ring depth (groups)
+constexpr int kGroupedBuffers = 4;     // TMEM partial buffers of kGroupedBN columns
+constexpr int kGroupedScaleSlots = 12; // weight-scale ring (one group's kGroupedBN scales per slot)
+constexpr int kGroupedEpilogueWarps = 8;  // 2 per TMEM lane quadrant, 64 columns each
+constexpr int kGroupedEpilogueCols = kGroupedBN / (kGroupedEpilogueWarps / 4);
+constexpr int kGroupedThreads = 64 + 32 * kGroupedEpilogueWarps;
+// 10 warps: two schedulers hold 3, so a thread may use 16384 / (3 * 32) registers.
+constexpr int kGroupedMaxRegisters = 168;
+constexpr int kGroupedAStage = kBM * kGroupK;                  // 16 KB
+constexpr int kGroupedBStage = (kGroupedBN / 2) * kGroupK;     // 8 KB: each CTA stages half the weight rows
+constexpr int kGroupedBookkeepingBytes = 12288;
+constexpr int kGroupedSmemBytes = 1024 + kGroupedStages * (kGroupedAStage + kGroupedBStage) + kGroupedBookkeepingBytes;
+static_assert(kGroupedSmemBytes <= 232448, "grouped GEMM exceeds the shared memory of one SM");
+
+struct GroupedArgs {
+    const float *a_scale;     // kGroupAsymW4A8: [m]; kGroupW4A4: [m, k / 128]
+    const float *w_scale_gn;  // [k / 128, n] fp32, group-major
+    const float *bias;        // [n] or null
+    void *out;                // bf16 [m, n]
+    uint32_t *err;            // device error word
+    int m, n, k;
+};
+
+// a int8 [m, k], w int8 [n, k] (tensor maps with a 128 x 128 and a 64 x 128 box, 128-byte
+// swizzle); launched as clusters of two CTAs of kGroupedThreads threads.
+template <int kGroupMode>
+__global__ void int8_gemm_pair_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                              const __grid_constant__ CUtensorMap tmap_b, const GroupedArgs args);
+
 }  // namespace gemm
 }  // namespace ctu

@@ -186,7 +186,39 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
         : "r"(taddr));
 }
 
+// Packed pair of 32-bit TMEM columns (2i in the low half, 2i + 1 in the high half).
+typedef unsigned long long u32x2;
+
+// 32 lanes x 32 consecutive 32-bit columns, waited for and returned as 16 packed pairs.
+__device__ __forceinline__ void tmem_ld_32x32b_x32_pairs(uint32_t taddr, u32x2 (&r)[16]) {
+    asm volatile(
+        "{\n\t.reg .b32 t0,t1,t2,t3,t4,t5,t6,t7,t8,t9,t10,t11,t12,t13,t14,t15,t16,t17,t18,t19,t20,t21,t22,t23,t24,t25,t26,t27,t28,t29,t30,t31;\n\t"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {t0,t1,t2,t3,t4,t5,t6,t7,t8,t9,t10,t11,t12,t13,t14,t15,t16,t17,t18,t19,t20,t21,t22,t23,t24,t25,t26,t27,t28,t29,t30,t31}, [%16];\n\t"
+        "tcgen05.wait::ld.sync.aligned;\n\t"
+        "mov.b64 %0, {t0, t1};\n\t"
+        "mov.b64 %1, {t2, t3};\n\t"
+        "mov.b64 %2, {t4, t5};\n\t"
+        "mov.b64 %3, {t6, t7};\n\t"
+        "mov.b64 %4, {t8, t9};\n\t"
+        "mov.b64 %5, {t10, t11};\n\t"
+        "mov.b64 %6, {t12, t13};\n\t"
+        "mov.b64 %7, {t14, t15};\n\t"
+        "mov.b64 %8, {t16, t17};\n\t"
+        "mov.b64 %9, {t18, t19};\n\t"
+        "mov.b64 %10, {t20, t21};\n\t"
+        "mov.b64 %11, {t22, t23};\n\t"
+        "mov.b64 %12, {t24, t25};\n\t"
+        "mov.b64 %13, {t26, t27};\n\t"
+        "mov.b64 %14, {t28, t29};\n\t"
+        "mov.b64 %15, {t30, t31};\n\t"
+        "}"
+        : "=l"(r[0]), "=l"(r[1]), "=l"(r[2]), "=l"(r[3]), "=l"(r[4]), "=l"(r[5]), "=l"(r[6]), "=l"(r[7]), "=l"(r[8]), "=l"(r[9]), "=l"(r[10]), "=l"(r[11]), "=l"(r[12]), "=l"(r[13]), "=l"(r[14]), "=l"(r[15])
+        : "r"(taddr)
+        : "memory");
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
 // 128-byte swizzle: rows of 128 bytes, 8-row core groups 1024 bytes apart.

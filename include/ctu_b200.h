@@ -188,6 +188,50 @@ CTU_API int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_
 CTU_API int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream);
 
 /*
+ * Per-group (128 columns of K) formats.  The reference reaches them only through
+ * comfy-kitchen (comfyui_turing_utils/quantization/dispatch.py:876-936: kitchen's int4
+ * quantizer and int4_linear for convrot_w4a4_linear; quantization/convrot.py:51-104 and
+ * fusions.py:14-38 for the asymmetric W4A8 checkpoint layout), whose source is not in
+ * the reference, so the arithmetic below is this library's definition (parity unpinned).
+ *
+ * ctu_convrot_quantize_int4_g128: the ConvRot rotation of ctu_convrot_quantize (bf16 x
+ * [rows, k], k % 256 == 0), then every 128 columns of each rotated row quantized on
+ * their own with the int4 chain: group_scales[r, g] = max(min(absmax, bf16 max) / 7,
+ * 1e-10), codes [rows, k/2] packed (even column in the low nibble) =
+ * clamp(rint(bf16(y) * (1 / scale)), -7, 7).  group_scales is fp32 [rows, k/128].
+ */
+CTU_API int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes,
+                                           float *group_scales, void *stream);
+
+/*
+ * Asymmetric uint4 W4A8: a int8 [m, k] with per-token a_scale [m]; w_packed uint8
+ * [n, k/2] (nibbles 0..15, even column in the low nibble) with, per 128 columns, a zero
+ * point w_zero uint8 [n, k/128] (0..15) and a scale given group-major as fp32
+ * w_scale_gn [k/128, n] (the checkpoint's fp16 scales widened).  With acc_g the exact
+ * int32 sum over group g of a[m, c] * (nibble[n, c] - zero[n, g]):
+ *   t = 0; for g in order: t = fma(w_scale_gn[g, n], float(acc_g), t)
+ *   out[m, n] = bf16(fma(t, a_scale[m], bias[n]))          (null bias: +0)
+ * w_workspace: int8 [n, k], 16-byte aligned (the widened weights).  k % 128 == 0,
+ * n % 8 == 0.
+ */
+CTU_API int ctu_asym_w4a8_g128_linear(const int8_t *a, const uint8_t *w_packed, const float *a_scale,
+                                      const float *w_scale_gn, const uint8_t *w_zero, const float *bias, void *out,
+                                      int8_t *w_workspace, int64_t m, int64_t n, int64_t k, void *stream);
+
+/*
+ * W4A4 with per-token-per-group activation scales: a_packed / w_packed signed int4
+ * [m, k/2] / [n, k/2] (even column in the low nibble), a_scale_mg fp32 [m, k/128] (as
+ * written by ctu_convrot_quantize_int4_g128), w_scale_gn fp32 [k/128, n]:
+ *   t = 0; for g in order: t = fma(float(acc_g) * a_scale_mg[m, g], w_scale_gn[g, n], t)
+ *   out[m, n] = bf16(t + bias[n])                          (null bias: +0)
+ * a_workspace int8 [m, k] and w_workspace int8 [n, k] receive the sign-extended
+ * operands.  k % 128 == 0, n % 8 == 0.
+ */
+CTU_API int ctu_w4a4_g128_linear(const int8_t *a_packed, const int8_t *w_packed, const float *a_scale_mg,
+                                 const float *w_scale_gn, const float *bias, void *out, int8_t *a_workspace,
+                                 int8_t *w_workspace, int64_t m, int64_t n, int64_t k, void *stream);
+
+/*
  * Affine RMSNorm + segmented AdaLN (replaces turing_segmented_rms_adaln,
  * kernel/csrc/bindings.cpp:767-834 -> kernel/csrc/turing/segmented_rms_adaln.cu:133-232,
  * 288-340).  out[r, c] = ((x[r, c] * rsqrt(mean(x[r]^2) + epsilon)) * weight[c])

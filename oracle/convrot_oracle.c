@@ -36,6 +36,7 @@
 #include <math.h>
 #include <omp.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #define KGROUP 256
@@ -296,6 +297,74 @@ void ctu_oracle_epilogue(const int32_t *acc, long acc_stride, const float *a_sca
     }
 }
 
+
+/* ---------------------------------------------------------------------------------
+ * Per-group (128 along K) formats of the W4A8 / W4A4 linears.  The reference reaches
+ * these through comfy-kitchen (dispatch.py:876-936 calls kitchen's int4 quantizer and
+ * int4_linear; the asymmetric W4A8 layout is kitchen's AsymW4A8Int8Layout), whose
+ * source is not available, so the definitions below are this build's and the parity of
+ * these two formats is UNPINNED: they follow the bundled kernels' arithmetic where it
+ * exists (rotation, int4 scale and code chain of convrot_quant.cu:475-500) and fix an
+ * fp32 accumulation order over the 128-column groups for the rest.
+ * --------------------------------------------------------------------------------- */
+#define QGROUP 128
+
+/* Rotate each row (256-column ConvRot groups), then quantize every 128-column group on
+ * its own: scale = max(min(absmax, FLT_MAX) / 7, 1e-10) over the group's rotated fp32
+ * values, codes = clamp(rint(bf16(y) * (1/scale)), -7, 7), even column in the low
+ * nibble.  packed: rows x k/2; scales: rows x k/128. */
+int ctu_oracle_convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, float *scales, long rows, int k) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
+    const int groups = k / QGROUP;
+#pragma omp parallel
+    {
+        uint16_t *ybits = (uint16_t *)malloc(sizeof(uint16_t) * (size_t)k);
+        float *yf = (float *)malloc(sizeof(float) * (size_t)k);
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            (void)rotate_row(x + r * (long)k, k, 0, ybits, yf);
+            for (int g = 0; g < groups; ++g) {
+                float absmax = 0.0f;
+                for (int i = 0; i < QGROUP; ++i) absmax = fmaxf(absmax, fabsf(yf[g * QGROUP + i]));
+                quantize_row_int4(ybits + g * QGROUP, QGROUP, absmax, packed + r * (long)(k / 2) + g * (QGROUP / 2),
+                                  scales + r * (long)groups + g, 0);
+            }
+        }
+        free(ybits);
+        free(yf);
+    }
+    return 0;
+}
+
+/* Epilogue over per-group int32 partials acc[g][i][j] (groups x m x n), fp32 weight
+ * scales w_scale_gn[g][j] (the fp16 checkpoint scales widened, group-major):
+ *   mode 0 (W4A8, per-token activation scale a_scale[i]):
+ *       t = 0; for g: t = fma(w_s[g][j], float(acc_g), t);   out = bf16(fma(t, a_s[i], bias[j]))
+ *   mode 1 (W4A4, per-token-per-group activation scale a_scale[i][g]):
+ *       t = 0; for g: t = fma(float(acc_g) * a_s[i][g], w_s[g][j], t);   out = bf16(t + bias[j])
+ * A null bias adds +0.0. */
+void ctu_oracle_grouped_epilogue(const int32_t *acc, int groups, const float *a_scale, const float *w_scale_gn,
+                                 const float *bias, uint16_t *out, long m, long n, int mode) {
+#pragma omp parallel for schedule(static)
+    for (long i = 0; i < m; ++i) {
+        for (long j = 0; j < n; ++j) {
+            float t = 0.0f;
+            for (int g = 0; g < groups; ++g) {
+                const float v = (float)acc[((long)g * m + i) * n + j];
+                const float s = w_scale_gn[(long)g * n + j];
+                if (mode == 0) {
+                    t = fmaf(s, v, t);
+                } else {
+                    const float u = v * a_scale[i * groups + g];
+                    t = fmaf(u, s, t);
+                }
+            }
+            const float b = bias ? bias[j] : 0.0f;
+            const float v = mode == 0 ? fmaf(t, a_scale[i], b) : t + b;
+            out[i * n + j] = ctu_oracle_f32_to_bf16(v);
+        }
+    }
+}
 
 /* ---------------------------------------------------------------------------------
  * Grouped-codebook W4A8 weight decode (kernel/csrc/turing/w4a8.cu:75-80, 903-976 and

@@ -84,6 +84,10 @@ def _load():
         lib.ctu_oracle_segmented_rms_adaln.restype = None
         lib.ctu_oracle_layer_norm_adaln.argtypes = [vp, vp, vp, vp, i64, i64, i32, i32, ctypes.c_float, i32]
         lib.ctu_oracle_layer_norm_adaln.restype = None
+        lib.ctu_oracle_convrot_quantize_int4_g128.argtypes = [vp, vp, vp, i64, i32]
+        lib.ctu_oracle_convrot_quantize_int4_g128.restype = i32
+        lib.ctu_oracle_grouped_epilogue.argtypes = [vp, i32, vp, vp, vp, vp, i64, i64, i32]
+        lib.ctu_oracle_grouped_epilogue.restype = None
         lib.ctu_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         lib.ctu_oracle_f32_to_bf16.restype = ctypes.c_uint16
         _lib = lib
@@ -302,6 +306,74 @@ def codebook_w4a8_linear(a, w_packed, a_scale, group_scale, channel_scale, codeb
     w = codebook_decode(w_packed, group_scale, codebook, group_size)
     return int8_linear(a, w, a_scale, channel_scale, bias)
 
+
+# ---------------------------------------------------------------------------------------
+# Per-group-128 formats (configs of the W4A8 / W4A4 linears).  The reference runs these
+# through comfy-kitchen (dispatch.py:876-936), whose source is not available: the
+# definitions here are this build's (parity unpinned), see convrot_oracle.c.
+QGROUP = 128
+
+
+def convrot_quantize_int4_g128(x_bits: np.ndarray):
+    """Rotate, then per-token-per-group-128 int4: ``(codes [M, K/2] packed, scales [M, K/128])``."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, k = x_bits.shape
+    codes = np.empty((rows, k // 2), dtype=np.int8)
+    scales = np.empty((rows, max(k // QGROUP, 1)), dtype=np.float32)
+    if _load().ctu_oracle_convrot_quantize_int4_g128(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k) != 0:
+        raise ValueError(f"unsupported ConvRot width {k}")
+    return codes, scales
+
+
+def widen_uint4_zero(w_packed: np.ndarray, zeros: np.ndarray) -> np.ndarray:
+    """Asymmetric uint4 weights [N, K/2] (even column in the low nibble) and uint4 zero
+    points [N, K/128] -> the int8 values ``nibble - zero`` [N, K] in [-15, 15]."""
+    p = np.asarray(w_packed).view(np.uint8).astype(np.int16)
+    n = p.shape[0]
+    vals = np.stack((p & 0x0F, (p >> 4) & 0x0F), axis=-1).reshape(n, -1)
+    z = np.repeat(np.asarray(zeros, dtype=np.uint8).astype(np.int16), QGROUP, axis=1)
+    return (vals - z).astype(np.int8)
+
+
+def grouped_partials(a: np.ndarray, w: np.ndarray) -> np.ndarray:
+    """Exact int32 partial products of every 128-column group: [K/128, M, N]."""
+    k = a.shape[1]
+    return np.stack([int8_gemm_s32(a[:, g:g + QGROUP], w[:, g:g + QGROUP]) for g in range(0, k, QGROUP)])
+
+
+def grouped_epilogue(partials: np.ndarray, a_scale: np.ndarray, w_scale_gn: np.ndarray, bias, mode: int) -> np.ndarray:
+    """bf16 bits of the per-group epilogue (mode 0: W4A8 per-token activation scale;
+    mode 1: W4A4 per-token-per-group activation scale), see convrot_oracle.c."""
+    partials = np.ascontiguousarray(partials, dtype=np.int32)
+    groups, m, n = partials.shape
+    a_scale = np.ascontiguousarray(a_scale, dtype=np.float32)
+    w_scale_gn = np.ascontiguousarray(w_scale_gn, dtype=np.float32)
+    bias_arr = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32).reshape(-1)
+    out = np.empty((m, n), dtype=np.uint16)
+    _load().ctu_oracle_grouped_epilogue(_ptr(partials), groups, _ptr(a_scale), _ptr(w_scale_gn),
+                                        None if bias_arr is None else _ptr(bias_arr), _ptr(out), m, n, mode)
+    return out
+
+
+def _group_major(w_scale) -> np.ndarray:
+    """fp16 checkpoint scales [N, K/128] -> fp32 [K/128, N]."""
+    return np.ascontiguousarray(np.asarray(w_scale, dtype=np.float16).astype(np.float32).T)
+
+
+def asym_w4a8_g128_linear(a, w_packed, a_scale, w_scale, w_zero, bias=None):
+    """Asymmetric uint4 W4A8 with fp16 scale and uint4 zero point per 128 columns:
+    a int8 [M, K], a_scale [M], w_packed uint8 [N, K/2], w_scale fp16 [N, K/128],
+    w_zero uint8 [N, K/128] -> bf16 bits [M, N]."""
+    w = widen_uint4_zero(w_packed, w_zero)
+    return grouped_epilogue(grouped_partials(a, w), np.asarray(a_scale).reshape(-1), _group_major(w_scale), bias, 0)
+
+
+def w4a4_g128_linear(a_packed, w_packed, a_scale, w_scale, bias=None):
+    """Symmetric int4 x int4 with per-token-per-group activation scales a_scale [M, K/128]
+    and fp16 weight scales w_scale [N, K/128] -> bf16 bits [M, N]."""
+    a = unpack_int4(a_packed)
+    w = unpack_int4(w_packed)
+    return grouped_epilogue(grouped_partials(a, w), a_scale, _group_major(w_scale), bias, 1)
 
 # Storage-type codes of the norm ops (bf16 and fp16 travel as uint16 bit patterns).
 NORM_BF16, NORM_FP16, NORM_FP32 = 0, 1, 2

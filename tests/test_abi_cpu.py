@@ -119,3 +119,74 @@ def test_quantizer_selection_per_width():
         lib.ctu_debug_set_quant_kernel(prev)
     assert lib.ctu_debug_quant_plan(300, 0, 8, 232448, ctypes.byref(ctypes.c_int()), ctypes.byref(ctypes.c_int()),
                                     ctypes.byref(ctypes.c_int())) == _lib.CTU_ERR_INVALID_ARGUMENT
+
+
+def test_grouped_entry_points_reject_bad_shapes_without_a_gpu():
+    import ctypes
+
+    from comfyui_turing_utils_kernel import _lib
+
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    rc = lib.ctu_asym_w4a8_g128_linear(null, null, null, null, null, null, null, null, 4, 8, 192, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "K%128=0" in lib.ctu_last_error().decode()
+    rc = lib.ctu_w4a4_g128_linear(null, null, null, null, null, null, null, null, 4, 12, 256, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "N%8=0" in lib.ctu_last_error().decode()
+    rc = lib.ctu_convrot_quantize_int4_g128(null, 4, 384, null, null, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "divisible by 256" in lib.ctu_last_error().decode()
+    assert lib.ctu_w4a4_g128_linear(null, null, null, null, null, null, null, null, 0, 16, 256, null) == _lib.CTU_OK
+    assert lib.ctu_convrot_quantize_int4_g128(null, 0, 512, null, null, null) == _lib.CTU_OK
+
+
+def test_grouped_custom_op_fake_shapes():
+    import comfyui_turing_utils_kernel as k
+
+    x = torch.empty((3, 512), dtype=torch.bfloat16, device="meta")
+    q, s = k.turing_bf16_int4_g128_convrot_quantize(x, 256)
+    assert q.shape == (3, 256) and q.dtype == torch.int8 and s.shape == (3, 4) and s.dtype == torch.float32
+    a = torch.empty((7, 256), dtype=torch.int8, device="meta")
+    w = torch.empty((16, 128), dtype=torch.uint8, device="meta")
+    out = k.turing_asym_w4a8_g128_linear(a, w, torch.empty(7, device="meta"), torch.empty((16, 2), device="meta"),
+                                         torch.empty((16, 2), dtype=torch.uint8, device="meta"))
+    assert out.shape == (7, 16) and out.dtype == torch.bfloat16
+    out = k.turing_w4a4_g128_linear(a[:, :128], w.view(torch.int8), torch.empty((7, 2), device="meta"),
+                                    torch.empty((16, 2), device="meta"))
+    assert out.shape == (7, 16)
+
+
+def test_oracle_grouped_formats_against_float64():
+    # The per-group oracle definitions reproduce the float64 dequantized product to the
+    # accuracy of their fp32 accumulation and bf16 output.
+    import numpy as np
+
+    import convrot_oracle as oracle
+
+    rng = np.random.default_rng(0)
+    m, k, n = 37, 512, 48
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x[:, rng.permutation(k)[:5]] *= 30
+    xb = oracle.f32_to_bf16_bits(x)
+    codes, scales = oracle.convrot_quantize_int4_g128(xb)
+    assert codes.shape == (m, k // 2) and scales.shape == (m, k // 128)
+    y = oracle.rotate(xb).astype(np.float64)
+    deq = oracle.unpack_int4(codes).astype(np.float64) * np.repeat(scales.astype(np.float64), 128, axis=1)
+    # int4 rounding: at most half a step of each group's scale (plus bf16 rounding of y).
+    assert np.all(np.abs(deq - y) <= np.repeat(scales, 128, axis=1) * 0.5 * (1 + 2 ** -7) + np.abs(y) * 2 ** -8)
+
+    wp = rng.integers(0, 256, (n, k // 2), dtype=np.uint8)
+    wz = rng.integers(0, 16, (n, k // 128), dtype=np.uint8)
+    ws = (rng.random((n, k // 128)) * 0.009 + 1e-3).astype(np.float16)
+    b = (rng.standard_normal(n) * 0.02).astype(np.float32)
+    a = rng.integers(-128, 128, (m, k), dtype=np.int8)
+    asc = (rng.random(m) * 0.01 + 1e-3).astype(np.float32)
+    out = oracle.bf16_bits_to_f32(oracle.asym_w4a8_g128_linear(a, wp, asc, ws, wz, b)).astype(np.float64)
+    w = oracle.widen_uint4_zero(wp, wz).astype(np.float64) * np.repeat(ws.astype(np.float64), 128, axis=1)
+    ref = (a.astype(np.float64) @ w.T) * asc[:, None] + b
+    assert np.max(np.abs(out - ref) / (np.abs(ref) + 1e-3)) < 2 ** -7
+
+    w4 = rng.integers(-7, 8, (n, k)).astype(np.int8)
+    out = oracle.bf16_bits_to_f32(oracle.w4a4_g128_linear(codes, oracle.pack_int4(w4), scales, ws, b))
+    a_deq = oracle.unpack_int4(codes).astype(np.float64) * np.repeat(scales.astype(np.float64), 128, axis=1)
+    w_deq = w4.astype(np.float64) * np.repeat(ws.astype(np.float64), 128, axis=1)
+    ref = a_deq @ w_deq.T + b
+    assert np.max(np.abs(out.astype(np.float64) - ref) / (np.abs(ref) + 1e-2)) < 2 ** -7
