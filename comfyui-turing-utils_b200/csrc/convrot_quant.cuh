@@ -15,6 +15,7 @@ constexpr int kMaxThreads = 256;   // 8 warps = 128 lane pairs = 128 groups in f
 constexpr int kMaxBoxRows = 64;    // 128-byte slices per TMA copy (8 KiB)
 
 struct QuantArgs {
+    const void *x;       // input rows (read by the warp-row kernel's bulk copies)
     int8_t *codes;       // [m, k] int8 or [m, k/2] packed int4
     float *scales;       // [m] (output; unused when given_scales is set)
     // Optional caller-supplied per-row scales (int8 only): the codes use them instead
@@ -134,6 +135,26 @@ inline size_t quant_g8_smem_bytes(int rows, int k, int act, int warps) {
     const size_t in_bytes = static_cast<size_t>(box) * copies * 128;
     return 1024 + 2 * in_bytes + static_cast<size_t>(kK8WarpBytes) * warps + 24 * static_cast<size_t>(rows) + 24;
 }
+
+// Warp-row variant (plain and GELU rows of at most 4 * kW8MaxGroupsPerTeam groups): each
+// warp owns whole rows -- one bulk copy of the row into its shared-memory buffer, its
+// four 8-lane teams rotating kGt groups each with the halvings folded, a warp-level row
+// absmax -- so no CTA barrier is ever taken; the next row's copy is issued as soon as
+// the row's input has been consumed, overlapping its quantization.
+constexpr int kW8MaxGroupsPerTeam = 6;
+constexpr int kW8Warps = 4;
+
+// Shared memory of one warp: its row buffer (1024-byte aligned) and 4 KB of transpose
+// area; the CTA adds alignment slack and one mbarrier per warp.
+inline size_t quant_w8_warp_bytes(int k) {
+    return ((static_cast<size_t>(k) * 2 + 1023) & ~size_t(1023)) + static_cast<size_t>(kK8WarpBytes);
+}
+inline size_t quant_w8_smem_bytes(int k, int warps) {
+    return 1024 + static_cast<size_t>(warps) * quant_w8_warp_bytes(k) + 8 * static_cast<size_t>(warps);
+}
+
+template <int Act, int Bits, int kGt>
+__global__ void convrot_quant_w8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
 // kGroupScales (plain rows, int4 only): every 128 columns of a rotated row get their own
 // scale (args.group_scales) and codes; no row statistics are exchanged.

@@ -805,6 +805,184 @@ __global__ void __launch_bounds__(kG8MaxThreads)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-row kernel (convrot_quant_w8_kernel).  Each warp owns whole rows, so the row
+// absmax is a warp reduction and no CTA barrier is ever taken: lane 0 copies the row
+// (contiguous bf16) into the warp's buffer with one bulk copy, the four 8-lane teams
+// rotate groups team, team + 4, ... (kGt each) exactly as the multi-group kernel does --
+// the halvings folded, the reference order recomputed from the still-resident input for
+// a slot where any group of the warp left the finite range -- keeping the bf16 words in
+// registers, and as soon as the last group is read lane 0 issues the next row's copy,
+// which lands while the row is quantized.
+//
+// Inputs are read as plain row-major bf16 (no swizzle): lane q of a team reads elements
+// 16q .. 16q + 15 and 128 + 16q .. 128 + 16q + 15 of its group, the layout the
+// transpose of g8_rotate expects.
+namespace {
+
+template <int Act>
+__device__ __forceinline__ void w8_load(uint32_t gaddr, uint32_t q, f32x2 (&P)[16], const ActLut &lut) {
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const uint4 a = ld_shared_v4u(gaddr + 32u * q + 16u * c);
+        const uint4 b = ld_shared_v4u(gaddr + 256u + 32u * q + 16u * c);
+        const uint32_t aw[4] = {a.x, a.y, a.z, a.w};
+        const uint32_t bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            P[8 * c + 2 * i] = pk2(activate<Act>(aw[i] << 16, 0, lut), activate<Act>(bw[i] << 16, 0, lut));
+            P[8 * c + 2 * i + 1] = pk2(activate<Act>(aw[i] & 0xFFFF0000u, 0, lut),
+                                       activate<Act>(bw[i] & 0xFFFF0000u, 0, lut));
+        }
+    }
+}
+
+}  // namespace
+
+template <int Act, int Bits, int kGt>
+__global__ void __launch_bounds__(32 * kW8Warps)
+    convrot_quant_w8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
+    static_assert(Act != kActSwiGLU, "the warp-row kernel takes bf16-valued rows");
+    static_assert(kGt >= 1 && kGt <= kW8MaxGroupsPerTeam, "groups per team");
+    (void)tmap_x;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t sbase = (raw + 1023u) & ~1023u;
+    uint8_t *smem = smem_raw + (sbase - raw);
+    const int K = args.k;
+    const int groups = K / 256;
+    const int Kout = Bits == 4 ? K / 2 : K;
+    const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
+    const uint32_t buf_bytes = (row_bytes + 1023u) & ~1023u;
+    const uint32_t warp_stride = buf_bytes + static_cast<uint32_t>(kK8WarpBytes);
+    const int nwarps = blockDim.x >> 5;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t g = static_cast<uint32_t>(lane >> 3);  // team
+    const uint32_t q = static_cast<uint32_t>(lane & 7);
+    const uint32_t buf = sbase + static_cast<uint32_t>(warp) * warp_stride;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(smem + static_cast<uint32_t>(nwarps) * warp_stride) + warp;
+    const uint32_t garea = buf + buf_bytes + g * kK8GroupBytes;
+    const uint32_t wbase = garea + 16u * ((4u * q) ^ (q >> 1) ^ (4u * (g & 1u)));
+    const uint32_t rbase = garea + 8u * (q & 1u) + 16u * ((q >> 1) ^ (4u * (g & 1u)));
+    const ActLut lut{args.silu_lut, args.gelu_lut};
+    const uint16_t *x = static_cast<const uint16_t *>(args.x);
+    const int row_step = gridDim.x * nwarps;
+    const int first = blockIdx.x * nwarps + warp;
+
+    if (lane == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+        if (first < args.m) {
+            mbar_arrive_expect_tx(bar, row_bytes);
+            bulk_load(smem + (buf - sbase), x + static_cast<int64_t>(first) * K, row_bytes, bar);
+        }
+    }
+    __syncwarp();
+
+    uint32_t it = 0;
+    bool pending = first < args.m;  // lane 0: a copy is in flight
+    for (int row = first; row < args.m; row += row_step, ++it) {
+        const bool ok = mbar_wait(bar, it & 1u, nullptr, args.err, kErrTimeoutFull);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        pending = false;
+
+        uint32_t W[kGt][16];
+        bool folded[kGt];
+        bool any_nan = false;
+        float amax = 0.0f;  // this team's groups (non-negative, never NaN)
+#pragma unroll
+        for (int i = 0; i < kGt; ++i) {
+            const int grp = static_cast<int>(g) + 4 * i;
+            const bool active = grp < groups;
+            const uint32_t gaddr = buf + 512u * static_cast<uint32_t>(active ? grp : groups - 1);
+            float ga = 0.0f, probe = 0.0f, unused = 0.0f;
+            f32x2 P[16];
+            w8_load<Act>(gaddr, q, P, lut);
+            g8_rotate<false>(P, wbase, rbase, W[i], ga, probe, unused);
+            folded[i] = !__any_sync(0xffffffffu, active && !(ga <= 3.40282347e38f));
+            if (folded[i]) {
+                ga *= 0.0625f;
+            } else {  // warp-uniform: the reference's order, halvings included
+                w8_load<Act>(gaddr, q, P, lut);
+                g8_rotate<true>(P, wbase, rbase, W[i], ga, probe, unused);
+                any_nan |= active && isnan(probe);
+            }
+            if (active) amax = fmaxf(amax, ga);
+        }
+        __syncwarp();  // every lane's reads of the buffer are done
+        const int next = row + row_step;
+        if (lane == 0 && next < args.m) {
+            mbar_arrive_expect_tx(bar, row_bytes);
+            bulk_load(smem + (buf - sbase), x + static_cast<int64_t>(next) * K, row_bytes, bar);
+            pending = true;
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
+        const bool row_nan = __any_sync(0xffffffffu, any_nan);
+        const float scale = row_scale<Bits>(amax, args.scale_mul != 0);
+        if (lane == 0) args.scales[row] = scale;
+
+        int8_t *out_row = args.codes + static_cast<int64_t>(row) * Kout;
+        if constexpr (Bits == 4) {
+            const float inv = __fdiv_rn(1.0f, scale);
+#pragma unroll
+            for (int i = 0; i < kGt; ++i) {
+                const int grp = static_cast<int>(g) + 4 * i;
+                if (grp >= groups) continue;
+                int8_t *out = out_row + grp * 128 + q;
+                if (folded[i] && !(inv >= 0x1p-100f)) {
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint32_t c = quant8_int4_prescaled(make_uint4(W[i][u], W[i][u + 1], W[i][u + 2], W[i][u + 3]), inv);
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) out[8 * (u + b)] = static_cast<int8_t>((c >> (8 * b)) & 0xFFu);
+                    }
+                } else {
+                    const float iv = folded[i] ? inv * 0.0625f : inv;
+                    const f32x2 i2 = pk2(iv, iv);
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint32_t c = quant8_int4(make_uint4(W[i][u], W[i][u + 1], W[i][u + 2], W[i][u + 3]), i2);
+#pragma unroll
+                        for (int b = 0; b < 4; ++b) out[8 * (u + b)] = static_cast<int8_t>((c >> (8 * b)) & 0xFFu);
+                    }
+                }
+            }
+        } else {
+            const float rs = __bfloat162float(__float2bfloat16_rn(scale));
+            const bool exact_chain = row_nan || isinf(amax);
+            const float rcp = __frcp_rn(rs);
+#pragma unroll
+            for (int i = 0; i < kGt; ++i) {
+                const int grp = static_cast<int>(g) + 4 * i;
+                if (grp >= groups) continue;
+                uint16_t *o16 = reinterpret_cast<uint16_t *>(out_row + grp * 256 + 2 * q);
+                if (exact_chain) {
+                    const float divisor = folded[i] ? rs * 16.0f : rs;
+#pragma unroll
+                    for (int u = 0; u < 16; u += 4) {
+                        const uint2 c = quant8_int8_exact(make_uint4(W[i][u], W[i][u + 1], W[i][u + 2], W[i][u + 3]), divisor);
+                        o16[8 * u] = static_cast<uint16_t>(c.x & 0xFFFFu);
+                        o16[8 * u + 8] = static_cast<uint16_t>(c.x >> 16);
+                        o16[8 * u + 16] = static_cast<uint16_t>(c.y & 0xFFFFu);
+                        o16[8 * u + 24] = static_cast<uint16_t>(c.y >> 16);
+                    }
+                } else {
+                    const float rc = rcp * (folded[i] ? 0.0625f : 1.0f);
+                    const f32x2 r2 = pk2(rc, rc);
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) o16[8 * u] = static_cast<uint16_t>(quant2_int8_fast(W[i][u], r2));
+                }
+            }
+        }
+    }
+    if (lane == 0 && pending) {
+        // A wait gave up with a copy still in flight: let it land before the CTA exits.
+        mbar_wait(bar, it & 1u, nullptr, args.err, kErrTimeoutDrain);
+    }
+}
+
 template __global__ void convrot_quant_k8_kernel<kActNone, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActNone, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_k8_kernel<kActSwiGLU, 8>(const __grid_constant__ CUtensorMap, const QuantArgs);
@@ -824,6 +1002,30 @@ template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 1>(const __grid_co
 template __global__ void convrot_quant_g8_kernel<kActGelu, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActGelu, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 5>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 5>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 4, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 5>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 8, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 1>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 2>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 3>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 4>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 5>(const __grid_constant__ CUtensorMap, const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1, true>(const __grid_constant__ CUtensorMap,
                                                                        const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2, true>(const __grid_constant__ CUtensorMap,

@@ -309,13 +309,13 @@ CTU_API int ctu_debug_set_gemm_kernel(int which);
 CTU_API int ctu_debug_set_gemm_split(int tiles);
 
 /* Test hook (no counterpart in the reference): choose the ConvRot quantizer for every
- * later call in this process.  0 = per width (default: the eight-lane kernel for
- * 4096 < K <= 6144, the four-lane kernel for other K <= 8192, the register-resident
- * kernel for other K <= 32768, the two-pass kernel beyond), 1 = two-pass kernel, 2 =
- * register-resident kernel, 3 = four-lane kernel, 4 = eight-lane kernel, 5 = multi-group
- * eight-lane kernel (groups per team chosen per width), 6 / 7 = multi-group eight-lane
- * kernel with 1 / 2 groups per team, all but the first wherever the width allows them.
- * Returns the previous selector, or a negative error code. */
+ * later call in this process.  0 = per width (the library's measured choice; see
+ * ctu_debug_quant_plan), 1 = two-pass kernel, 2 = register-resident kernel, 3 = four-lane
+ * kernel, 4 = eight-lane kernel, 5 = multi-group eight-lane kernel (groups per team
+ * chosen per width), 6 / 7 = multi-group eight-lane kernel with 1 / 2 groups per team,
+ * 8 = warp-row kernel (plain and GELU rows of at most 24 groups), all but the first
+ * wherever the width allows them.  Returns the previous selector, or a negative error
+ * code. */
 CTU_API int ctu_debug_set_quant_kernel(int which);
 
 /* Test hook (host only, no GPU needed): the quantizer plan a call of width k would use on a

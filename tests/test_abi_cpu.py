@@ -86,16 +86,16 @@ def test_ops_refuse_cpu_tensors():
 
 def test_quantizer_selection_per_width():
     # The per-width choice the measurements in the kernel sources justify, evaluated on the
-    # host for B200's 227 KB of opt-in shared memory: the multi-group eight-lane kernel for
-    # plain and GELU rows wider than 4096 (one group per team at K = 5120, two at K = 13824),
-    # eight lanes for SwiGLU at K = 5120, four lanes at K <= 4096, and the two-pass kernel
-    # beyond K = 32768.
+    # host for B200's 227 KB of opt-in shared memory: the warp-row kernel for plain and GELU
+    # rows of 4096 < K <= 6144 (four warps, one row each), the multi-group eight-lane kernel
+    # for wider plain and GELU rows (two groups per team at K = 13824), eight lanes for
+    # SwiGLU at K = 5120, four lanes at K <= 4096, and the two-pass kernel beyond K = 32768.
     import ctypes
 
     from comfyui_turing_utils_kernel import _lib
 
     lib = _lib.load()
-    two_pass, reg, t4, k8, g8 = 0, 1, 2, 3, 4
+    two_pass, reg, t4, k8, g8, w8 = 0, 1, 2, 3, 4, 5
 
     def plan(k, act=0, bits=8):
         kind, warps, rows = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
@@ -103,8 +103,9 @@ def test_quantizer_selection_per_width():
         assert rc == 0, lib.ctu_last_error().decode()
         return kind.value, warps.value, rows.value
 
-    assert plan(5120) == (g8, 5, 1)
-    assert plan(5120, act=2)[0] == g8 and plan(5120, bits=4)[0] == g8
+    assert plan(5120) == (w8, 4, 4)
+    assert plan(5120, act=2)[0] == w8 and plan(5120, bits=4)[0] == w8
+    assert plan(6400)[0] == g8
     assert plan(5120, act=1)[0] == k8
     for k in (256, 1536, 3072, 4096):
         assert plan(k)[0] == t4, k
@@ -115,6 +116,10 @@ def test_quantizer_selection_per_width():
     prev = lib.ctu_debug_set_quant_kernel(2)
     try:
         assert plan(5120)[0] == reg
+        lib.ctu_debug_set_quant_kernel(7)
+        assert plan(5120) == (g8, 5, 2)
+        lib.ctu_debug_set_quant_kernel(8)
+        assert plan(3072)[0] == w8 and plan(13824)[0] != w8  # wider than the warp-row kernel takes
     finally:
         lib.ctu_debug_set_quant_kernel(prev)
     assert lib.ctu_debug_quant_plan(300, 0, 8, 232448, ctypes.byref(ctypes.c_int()), ctypes.byref(ctypes.c_int()),

@@ -20,7 +20,7 @@ import torch
 pytestmark = pytest.mark.gpu
 
 REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libctu_ref.so"
-KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6}
+KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6, "w8": 8}
 ACT_SWIGLU, ACT_GELU = 1, 2
 
 

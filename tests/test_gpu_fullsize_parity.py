@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 REF_LIB = Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "libctu_ref.so"
 M = 32760
-QUANT_KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6}
+QUANT_KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6, "w8": 8}
 GEMM_KERNELS = {"single_cta": 1, "cta_pair": 2}
 
 needs_ref = pytest.mark.skipif(not REF_LIB.exists(), reason="reference kernels not built (make -C oracle ref)")

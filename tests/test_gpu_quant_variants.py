@@ -20,7 +20,7 @@ from pathlib import Path
 GOLDEN = Path(__file__).resolve().parent / "golden"
 QUANT = np.load(GOLDEN / "convrot_quant.npz")
 QUANT_NAMES = sorted({k.split("__")[0] for k in QUANT.files})
-KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6}
+KERNELS = {"two_pass": 1, "register": 2, "t4": 3, "k8": 4, "g8": 7, "g8_1": 6, "w8": 8}
 
 
 @pytest.fixture(scope="module")
