@@ -108,11 +108,18 @@ __device__ __forceinline__ void lds_f32x2x2(uint32_t addr, f32x2 &a, f32x2 &b) {
     asm volatile("ld.shared.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "r"(addr));
 }
 
-// Two int32 partials -> the bit patterns of 1.5 * 2^23 + acc (see the file comment).
+// Two int32 partials -> the bit patterns of 1.5 * 2^23 + acc (see the file comment): one
+// three-input logic operation, (acc & mask) ^ pattern, per partial.
 __device__ __forceinline__ f32x2 to_magic_pair(u32x2 v) {
-    const uint32_t lo = (static_cast<uint32_t>(v) & kAccMask) ^ kMagicBits;
-    const uint32_t hi = (static_cast<uint32_t>(v >> 32) & kAccMask) ^ kMagicBits;
-    return (static_cast<f32x2>(hi) << 32) | lo;
+    f32x2 r;
+    asm("{\n\t.reg .b32 lo, hi;\n\t"
+        "mov.b64 {lo, hi}, %1;\n\t"
+        "lop3.b32 lo, lo, %2, %3, 0x6A;\n\t"
+        "lop3.b32 hi, hi, %2, %3, 0x6A;\n\t"
+        "mov.b64 %0, {lo, hi};\n\t}"
+        : "=l"(r)
+        : "l"(v), "r"(kAccMask), "r"(kMagicBits));
+    return r;
 }
 
 __device__ __forceinline__ void settle_inflight_copies_grouped() {
