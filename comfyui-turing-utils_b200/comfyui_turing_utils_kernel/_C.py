@@ -560,9 +560,10 @@ def int4_linear(qactivation, qweight, activation_scale, wscales, bias=None, out_
     return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 
 
-# Per-group (128 along K) formats.  The reference gets these from comfy-kitchen
-# (dispatch.py:876-936 and the AsymW4A8Int8Layout checkpoints, quantization/convrot.py:51-104),
-# whose source is not available; the arithmetic is this library's (see ctu_b200.h).
+# Per-group (128 along K) formats.  The reference has no kernel or checkpoint layout for
+# them (its W4A4 path, dispatch.py:876-936, hands int4 activations to comfy-kitchen's
+# int4_linear with 64-column weight groups; its asym_w4a8_int8 format is the grouped
+# codebook); the arithmetic is this library's (see ctu_b200.h).
 QUANT_GROUP = 128
 
 

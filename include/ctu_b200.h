@@ -188,11 +188,12 @@ CTU_API int ctu_codebook_decode_s8(const int8_t *w_packed, const uint8_t *group_
 CTU_API int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, int64_t k, void *stream);
 
 /*
- * Per-group (128 columns of K) formats.  The reference reaches them only through
- * comfy-kitchen (comfyui_turing_utils/quantization/dispatch.py:876-936: kitchen's int4
- * quantizer and int4_linear for convrot_w4a4_linear; quantization/convrot.py:51-104 and
- * fusions.py:14-38 for the asymmetric W4A8 checkpoint layout), whose source is not in
- * the reference, so the arithmetic below is this library's definition (parity unpinned).
+ * Per-group (128 columns of K) formats.  The reference has no kernel or checkpoint layout
+ * for them: its W4A4 path (comfyui_turing_utils/quantization/dispatch.py:876-936) hands
+ * int4 activations to comfy-kitchen's int4_linear (not in the reference) with 64-column
+ * weight groups, and its asymmetric W4A8 format (asym_w4a8_int8, AsymW4A8Int8Layout,
+ * fusions.py:14-16) is the grouped codebook of ctu_codebook_w4a8_linear.  The arithmetic
+ * below is this library's definition (parity unpinned).
  *
  * ctu_convrot_quantize_int4_g128: the ConvRot rotation of ctu_convrot_quantize (bf16 x
  * [rows, k], k % 256 == 0), then every 128 columns of each rotated row quantized on

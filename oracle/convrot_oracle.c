@@ -299,11 +299,12 @@ void ctu_oracle_epilogue(const int32_t *acc, long acc_stride, const float *a_sca
 
 
 /* ---------------------------------------------------------------------------------
- * Per-group (128 along K) formats of the W4A8 / W4A4 linears.  The reference reaches
- * these through comfy-kitchen (dispatch.py:876-936 calls kitchen's int4 quantizer and
- * int4_linear; the asymmetric W4A8 layout is kitchen's AsymW4A8Int8Layout), whose
- * source is not available, so the definitions below are this build's and the parity of
- * these two formats is UNPINNED: they follow the bundled kernels' arithmetic where it
+ * Per-group (128 along K) formats of the W4A8 / W4A4 linears.  The reference has no
+ * kernel or checkpoint layout for them: its W4A4 path (dispatch.py:876-936) hands int4
+ * activations to comfy-kitchen's int4_linear (source not available) with 64-column
+ * weight groups, and its asymmetric W4A8 checkpoint format (asym_w4a8_int8,
+ * AsymW4A8Int8Layout, fusions.py:14-16) is the grouped codebook.  The definitions below
+ * are this build's, and the parity of these two formats is UNPINNED: they follow the bundled kernels' arithmetic where it
  * exists (rotation, int4 scale and code chain of convrot_quant.cu:475-500) and fix an
  * fp32 accumulation order over the 128-column groups for the rest.
  * --------------------------------------------------------------------------------- */
