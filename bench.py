@@ -366,6 +366,19 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         packed = [(k, n, (w[:, 0::2].to(torch.int32) & 7 | ((w[:, 1::2].to(torch.int32) & 7) << 4)).to(torch.int8),
                    w_s, b) for k, n, w, w_s, b in layers]
 
+        # The same W8A8 sweep through the one-call linear (ctu_convrot_int8_linear): where it
+        # measured faster (N <= 8192, M >= 8192: the four Q/K/V/O linears of a full-M step)
+        # one kernel quantizes rows while its tensor cores work on finished ones.
+        def one_call_step():
+            for x, (k, n, w, w_s, b) in zip(xs, layers):
+                kops.turing_convrot_int8_linear(x, w, w_s, b)
+
+        ms = timed(one_call_step, max(5, min(args.steps, 30)))
+        variants["convrot_int8_linear"] = {
+            "value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "format": "configs[1] W8A8 through turing_utils::convrot_int8_linear: the fused quantizer + CTA-pair "
+                      "GEMM kernel for N <= 8192 at M >= 8192, quantizer then GEMM otherwise"}
+
         def w4_step(act_bits):
             for x, (k, n, wp, w_s, b) in zip(xs, packed):
                 q, s = (kops.turing_bf16_int8_convrot_quantize if act_bits == 8
@@ -411,11 +424,11 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                 ("asym_w4a8_g128", asym_w4a8_step,
                  "configs[2]: asymmetric uint4 weights, fp16 scale + uint4 zero point per 128 columns, per-token "
                  "int8 ConvRot activations; weights widened to (nibble - zero) int8, then the per-group CTA-pair "
-                 "GEMM (parity unpinned: kitchen's format)"),
+                 "GEMM (parity unpinned: no reference kernel)"),
                 ("w4a4_g128", w4a4_g128_step,
                  "configs[3]: symmetric int4 weights with fp16 per-group-128 scales, int4 ConvRot activations with "
                  "per-token-per-group-128 scales; both operands sign-extended, then the per-group CTA-pair GEMM "
-                 "(parity unpinned: kitchen's format)")):
+                 "(parity unpinned: no reference kernel)")):
             ms = timed(fn, max(5, min(args.steps, 20)))
             variants[name] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,
                               "ms_per_step": ms, "format": fmt}

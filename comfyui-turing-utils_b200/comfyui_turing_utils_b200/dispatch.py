@@ -156,9 +156,23 @@ def int8_linear(
     _require(input_act in _FUSED_ACTS, f"input activation {input_act!r}")
     original_shape = x.shape
     x2d = x.reshape(-1, original_shape[-1]).contiguous()
-    qactivation, activation_scale = _quantize_int8(x2d, convrot_groupsize, input_act)
-    output = _int8_gemm(qactivation, weight.contiguous(), activation_scale, weight_scale, bias,
-                        out_dtype or x.dtype)
+    if input_act is None and weight.ndim == 2 and weight.shape[1] == x2d.shape[1]:
+        # Plain rows: one library call (the fused quantizer + GEMM kernel where it pays).
+        n = weight.shape[0]
+        weight_scale = weight_scale.to(device=x2d.device, dtype=torch.float32).reshape(-1).contiguous()
+        if weight_scale.numel() not in (1, n):
+            raise ValueError(f"W8A8 weight scale must be scalar or have {n} values, got {weight_scale.numel()}")
+        if weight_scale.numel() == 1:
+            weight_scale = weight_scale.expand(n).contiguous()
+        if bias is not None:
+            bias = bias.to(device=x2d.device, dtype=torch.float32)
+        output = ops.turing_convrot_int8_linear(x2d, weight.contiguous(), weight_scale, bias, convrot_groupsize)
+        dtype = out_dtype or x.dtype
+        output = output if dtype == torch.bfloat16 else output.to(dtype)
+    else:
+        qactivation, activation_scale = _quantize_int8(x2d, convrot_groupsize, input_act)
+        output = _int8_gemm(qactivation, weight.contiguous(), activation_scale, weight_scale, bias,
+                            out_dtype or x.dtype)
     return output.reshape(*original_shape[:-1], weight.shape[0])
 
 

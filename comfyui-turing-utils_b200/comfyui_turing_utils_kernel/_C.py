@@ -197,6 +197,54 @@ def turing_int8_linear(activation, weight, activation_scale, weight_scale, bias=
     return out
 
 
+def convrot_int8_linear(input, weight, weight_scale, bias=None, group_size=256, return_quantized=False):
+    """ConvRot W8A8 linear from bf16 rows: the plugin's dispatch.int8_linear for plain rows
+    (dispatch.py:748-800: turing_bf16_int8_convrot_quantize, then turing_int8_linear) as one
+    library call.  Codes, scales and outputs equal those of the two ops bit for bit; for
+    K <= 5120 one kernel quantizes rows while its tensor cores work on finished ones.
+    ``return_quantized`` also returns the int8 codes [M, K] and scales [M, 1]."""
+    x = input.contiguous()
+    _check_cuda_2d(x, "input")
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("ConvRot INT8 linear input must be bfloat16")
+    if group_size != 256:
+        raise RuntimeError("ConvRot INT8 linear only supports group_size=256")
+    weight = weight.contiguous()
+    _check_cuda_2d(weight, "weight")
+    if weight.dtype != torch.int8:
+        raise RuntimeError("Turing INT8 linear activation and weight must be int8")
+    weight_scale = weight_scale.reshape(-1).to(torch.float32).contiguous()
+    if bias is not None:
+        bias = bias.reshape(-1).to(torch.float32).contiguous()
+    dev = x.device
+    if weight.device != dev or weight_scale.device != dev:
+        raise RuntimeError("Turing INT8 linear tensors must use the same CUDA device")
+    m, k = x.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k:
+        raise RuntimeError("INT8 linear K dimensions must match")
+    if m <= 0 or k <= 0 or k % group_size != 0:
+        raise RuntimeError("BF16 row-buffer ConvRot width must be positive and divisible by 256")
+    if n % 8 != 0:
+        raise RuntimeError("Turing INT8 linear requires K%16=0 and N%8=0")
+    if weight_scale.numel() != n:
+        raise RuntimeError("weight_scale must contain one value per output channel")
+    if bias is not None and (not bias.is_cuda or bias.device != dev or bias.numel() != n):
+        raise RuntimeError("bias must contain one value per output channel on the same CUDA device")
+    lib = _lib.load()
+    x, weight = _aligned(x), _aligned(weight)
+    codes = torch.empty((m, k), dtype=torch.int8, device=dev)
+    scales = torch.empty((m, 1), dtype=torch.float32, device=dev)
+    sync = torch.empty((lib.ctu_convrot_int8_linear_sync_words(m),), dtype=torch.int32, device=dev)
+    out = torch.empty((m, n), dtype=torch.bfloat16, device=dev)
+    if n > 0:
+        with torch.cuda.device(dev):
+            _lib.check(lib.ctu_convrot_int8_linear(
+                _ptr(x), _ptr(weight), _ptr(weight_scale), n, _ptr(bias), _ptr(out), _ptr(codes), _ptr(scales),
+                _ptr(sync), m, n, k, _stream(dev)))
+    return (out, codes, scales) if return_quantized else out
+
+
 # From this many activation rows on, the W4 linears widen their packed int4 operands to
 # int8 once (a streaming pass) and run the W8A8 tensor-core GEMM, instead of widening every
 # weight tile inside the GEMM for each row block: the pass costs about as much as the GEMM

@@ -40,6 +40,8 @@ SIGNATURES = {
     "ctu_asym_w4a8_g128_linear": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_w4a4_g128_linear": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int8_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ctu_convrot_int8_linear": (_i32, [_vp, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "ctu_convrot_int8_linear_sync_words": (_i64, [_i64]),
     "ctu_w4a8_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_w4a4_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int8_gemm_s32": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp]),
@@ -49,6 +51,7 @@ SIGNATURES = {
     "ctu_layer_norm_adaln": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _f32, _i32, _vp]),
     "ctu_debug_gemm_injected_timeout": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _u64, _vp]),
     "ctu_debug_set_gemm_kernel": (_i32, [_i32]),
+    "ctu_debug_set_fused_linear": (_i32, [_i32]),
     "ctu_debug_set_gemm_split": (_i32, [_i32]),
     "ctu_debug_set_quant_kernel": (_i32, [_i32]),
     "ctu_debug_quant_plan": (_i32, [_i64, _i32, _i32, _i32, _vp, _vp, _vp]),

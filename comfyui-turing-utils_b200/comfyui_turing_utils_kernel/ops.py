@@ -105,6 +105,25 @@ def _turing_int8_linear_fake(activation, weight, activation_scale, weight_scale,
     return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
 
 
+@torch.library.custom_op("turing_utils::convrot_int8_linear", mutates_args=())
+def turing_convrot_int8_linear(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    weight_scale: torch.Tensor,
+    bias: torch.Tensor | None = None,
+    group_size: int = 256,
+) -> torch.Tensor:
+    """ConvRot W8A8 linear from bf16 rows (quantize + int8_linear in one call; no
+    reference op: the plugin composes the two in dispatch.int8_linear, dispatch.py:748-800)."""
+    _require_cuda(x, "ConvRot INT8 linear")
+    return _C.convrot_int8_linear(x, weight, weight_scale, bias, group_size)
+
+
+@turing_convrot_int8_linear.register_fake
+def _turing_convrot_int8_linear_fake(x, weight, weight_scale, bias=None, group_size=256):
+    return torch.empty((x.size(0), weight.size(0)), dtype=torch.bfloat16, device=x.device)
+
+
 # ops.py:129-160
 @torch.library.custom_op("turing_utils::dequantize_int8_bf16", mutates_args=())
 def turing_dequantize_int8_bf16(
@@ -378,9 +397,10 @@ def _turing_layer_norm_adaln_fake(x, scale, shift, epsilon=1.0e-5):
     return torch.empty_like(x)
 
 
-# Per-group (128 along K) formats.  No reference op carries them (the reference calls
-# comfy-kitchen for W4A4 and the asymmetric W4A8 layout, dispatch.py:876-936); the names
-# follow the turing_utils:: convention and the arithmetic is documented in ctu_b200.h.
+# Per-group (128 along K) formats.  No reference op carries them (the reference's W4A4
+# path calls comfy-kitchen's int4_linear with 64-column weight groups, dispatch.py:876-936,
+# and it has no per-group asymmetric W4A8 format); the names follow the turing_utils::
+# convention and the arithmetic is documented in ctu_b200.h.
 @torch.library.custom_op("turing_utils::bf16_int4_g128_convrot_quantize", mutates_args=())
 def turing_bf16_int4_g128_convrot_quantize(x: torch.Tensor, group_size: int = 256) -> tuple[torch.Tensor, torch.Tensor]:
     """ConvRot rotation + int4 codes with one scale per token per 128 columns."""

@@ -646,6 +646,101 @@ int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
     return launch_gemm(a, w, args, q.device, q.num_sms, stream);
 }
 
+// ---------------------------------------------------------------------------- fused ConvRot linear
+// Whether ctu_convrot_int8_linear runs the fused kernel: 0 chooses per problem, 1 forces
+// the separate quantizer and GEMM, 2 the fused kernel wherever it applies (test hook
+// ctu_debug_set_fused_linear).
+std::atomic<int> g_fused_linear{0};
+
+// Clusters of the fused kernel resident at once, per device and groups per team.
+int g_fused_clusters[kMaxDevices][ctu::gemm::kFusedMaxGt + 1] = {};
+
+// The fused kernel is the CTA-pair W8A8 GEMM with quantizer warps whose row buffers fit
+// beside the ring: rows of at most 4 * kFusedMaxGt groups, more than one row tile (the
+// single-CTA GEMM keeps the separate quantizer).  Per problem it runs where it measured
+// faster than the quantizer and GEMM back to back on power-capped B200s: N <= 8192 and
+// M >= 8192 (5120 x 5120 at 16384 rows: 5-9 % faster; at 32760 rows: about 2 %).  With
+// fewer rows the first row blocks' quantization delays the tensor cores (4095 rows: 10 %
+// slower), and at N = 13824 the quantizer's extra power lowers the clock of a GEMM that is
+// already at the power cap (3-7 % slower).
+bool use_fused_linear(int64_t m, int64_t n, int64_t k) {
+    const int sel = g_fused_linear.load(std::memory_order_relaxed);
+    if (sel == 1) return false;
+    if (k > 1024 * ctu::gemm::kFusedMaxGt) return false;
+    const int forced = g_gemm_kernel.load(std::memory_order_relaxed);
+    if (forced == 1) return false;
+    if (sel == 2) return forced == 2 || m > ctu::gemm::kBM;
+    return m >= 8192 && n <= 8192;
+}
+
+template <int kGt>
+int launch_fused_linear(const int8_t *w, const ctu::gemm::GemmArgs &base, int device, cudaStream_t stream) {
+    using ctu::gemm::kBK;
+    using ctu::gemm::kBM;
+    using ctu::gemm::kBN;
+    using ctu::gemm::kHalfBN;
+    CUtensorMap map_a, map_b, map_b_narrow;
+    if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base.qcodes, base.k, base.m, kBK, kBM,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, base.k, base.n, kBK, kHalfBN,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    if (int rc = encode_2d(&map_b_narrow, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, base.k, base.n, kBK, kHalfBN / 2,
+                           CU_TENSOR_MAP_SWIZZLE_128B))
+        return rc;
+    constexpr auto kernel = ctu::gemm::int8_gemm_pair_kernel<ctu::gemm::kModeW8A8, kGt>;
+    // The attribute covers the widest rows of this kGt, so one setting serves every k.
+    constexpr int max_smem = 1024 + ctu::gemm::kFusedQuantOffset +
+                             ctu::gemm::kFusedQuantWarps * (2 * 1024 * kGt + ctu::gemm::kFusedQuantTransposeBytes);
+    static bool attr_set[kMaxDevices] = {};
+    bool need_attr = false;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        need_attr = !attr_set[device];
+    }
+    if (need_attr) {
+        CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem));
+        std::lock_guard<std::mutex> lock(g_mutex);
+        attr_set[device] = true;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.blockDim = dim3(ctu::gemm::kFusedThreadCount, 1, 1);
+    cfg.dynamicSmemBytes = max_smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        clusters = g_fused_clusters[device][kGt];
+    }
+    if (clusters == 0) {
+        DeviceInfo dev;
+        if (int rc = device_info(&dev)) return rc;
+        cfg.gridDim = dim3(2 * (dev.num_sms / 2), 1, 1);
+        CTU_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
+        if (clusters <= 0) return fail(CTU_ERR_UNSUPPORTED, "no CTA pair of the fused linear fits on device %d", device);
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_fused_clusters[device][kGt] = clusters;
+    }
+    cfg.dynamicSmemBytes = static_cast<size_t>(ctu::gemm::fused_smem_bytes(base.k));
+    const int64_t tiles = ((base.m + ctu::gemm::kPairBM - 1) / ctu::gemm::kPairBM) *
+                          static_cast<int64_t>((base.n + kBN - 1) / kBN);
+    ctu::gemm::GemmArgs run = base;
+    run.split_tiles = static_cast<int>(split_tail_tiles(tiles, clusters, true));
+    const int64_t work = tiles + run.split_tiles;
+    cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(work, clusters)), 1, 1);
+    CTU_CUDA(cudaMemsetAsync(base.qsync, 0, sizeof(uint32_t) * ctu_convrot_int8_linear_sync_words(base.m), stream));
+    CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, map_b_narrow, run));
+    return CTU_OK;
+}
+
 // ---------------------------------------------------------------------------- per-group linears
 // Clusters of two CTAs of the grouped GEMM resident at once, per device and mode.
 int g_grouped_clusters[kMaxDevices][2] = {};
@@ -809,6 +904,58 @@ int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, cons
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_int8_linear(a, w, a_scale, w_scale, w_scale_count, bias, out, m, n, k, dev.err, q,
                            static_cast<cudaStream_t>(stream));
+}
+
+int64_t ctu_convrot_int8_linear_sync_words(int64_t m) { return m <= 0 ? 1 : 1 + (m + 127) / 128; }
+
+int ctu_convrot_int8_linear(const void *x, const int8_t *w, const float *w_scale, int64_t w_scale_count,
+                            const float *bias, void *out, int8_t *codes, float *scales, uint32_t *sync, int64_t m,
+                            int64_t n, int64_t k, void *stream) {
+    if (int rc = check_quantize_args(x, m, k, CTU_ACT_NONE, 8, codes, scales)) return rc;
+    if (int rc = check_gemm_shapes(codes, w, out, m, n, k)) return rc;
+    if (m == 0 || n == 0) return CTU_OK;
+    if (!w_scale) return fail(CTU_ERR_INVALID_ARGUMENT, "null scale pointer");
+    if (w_scale_count != 1 && w_scale_count != n)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "weight_scale must be scalar or contain one value per output channel");
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (!use_fused_linear(m, n, k)) {
+        if (int rc = run_quantize(x, m, k, CTU_ACT_NONE, 8, codes, scales, dev.err, q, s, nullptr, false, false))
+            return rc;
+        return run_int8_linear(codes, w, scales, w_scale, w_scale_count, bias, out, m, n, k, dev.err, q, s);
+    }
+    if (!sync || reinterpret_cast<uintptr_t>(sync) % 4 != 0)
+        return fail(CTU_ERR_INVALID_ARGUMENT, "sync must be a 4-byte aligned array of ctu_convrot_int8_linear_sync_words(m) words");
+    ctu::gemm::GemmArgs args{};
+    args.a_scale = scales;
+    args.w_scale = w_scale;
+    args.bias = bias;
+    args.out = out;
+    args.err = dev.err;
+    args.m = static_cast<int>(m);
+    args.n = static_cast<int>(n);
+    args.k = static_cast<int>(k);
+    args.ldc = static_cast<int>(n);
+    args.w_scale_count = static_cast<int>(w_scale_count);
+    args.out_mode = ctu::gemm::kOutBf16;
+    args.qx = x;
+    args.qcodes = codes;
+    args.qscales = scales;
+    args.qsync = sync;
+    switch ((k / 256 + 3) / 4) {
+    case 1: return launch_fused_linear<1>(w, args, dev.device, s);
+    case 2: return launch_fused_linear<2>(w, args, dev.device, s);
+    case 3: return launch_fused_linear<3>(w, args, dev.device, s);
+    case 4: return launch_fused_linear<4>(w, args, dev.device, s);
+    default: return launch_fused_linear<5>(w, args, dev.device, s);
+    }
+}
+
+int ctu_debug_set_fused_linear(int which) {
+    if (which < 0 || which > 2) return fail(CTU_ERR_INVALID_ARGUMENT, "fused linear selector must be 0, 1 or 2");
+    return g_fused_linear.exchange(which);
 }
 
 static int int4_linear(int mode, const int8_t *a, const int8_t *w_packed, const float *a_scale, const float *w_scale,

@@ -50,6 +50,15 @@ struct GemmArgs {
     // halves each, so a last wave that would leave most pairs idle is spread over twice
     // as many work items (0: every tile whole).
     int split_tiles;
+    // Fused ConvRot linear (int8_gemm_pair_kernel<kModeW8A8, kGt> with kGt > 0): the bf16
+    // input rows [m, k], the int8 codes [m, k] and per-row scales [m] its quantizer warps
+    // write (the A operand and `a_scale` of the GEMM), and the progress counters --
+    // qsync[0] the next unclaimed row, qsync[1 + b] the finished rows of 128-row block b --
+    // which must be zero at launch.
+    const void *qx;
+    int8_t *qcodes;
+    float *qscales;
+    uint32_t *qsync;
 };
 
 // kModeW8A8: a int8 [m, k], w int8 [n, k]; kModeW4A8: w packed signed int4 [n, k/2];
@@ -94,9 +103,39 @@ struct PairLayout {
     static_assert(kSmemBytes <= 232448, "CTA-pair GEMM exceeds the shared memory of one SM");
 };
 
+// Fused ConvRot linear: the W8A8 pair kernel with kFusedQuantWarps more warps per CTA
+// that rotate and quantize the bf16 input rows (the warp-row pipeline of the stand-alone
+// quantizer; rows claimed in order from a global counter) while the tensor cores work on
+// the rows already finished.  A CTA's producer loads an activation tile only once its
+// 128-row block is complete.  Each quantizer warp stages one row in its own buffer of
+// shared memory after the ring and the bookkeeping area: kGt = groups per team =
+// ceil(k / 1024), so k <= 256 * 4 * kFusedMaxGt.
+#ifndef CTU_FUSED_QUANT_WARPS
+#define CTU_FUSED_QUANT_WARPS 4
+#endif
+#ifndef CTU_FUSED_STAGES
+#define CTU_FUSED_STAGES 5
+#endif
+constexpr int kFusedQuantWarps = CTU_FUSED_QUANT_WARPS;
+constexpr int kFusedStages = CTU_FUSED_STAGES;  // ring depth: the quantizer buffers take the rest
+constexpr int kFusedMaxGt = 5;
+constexpr int kFusedStructOffset =
+    kFusedStages * (PairLayout<kModeW8A8>::kAStageBytes + PairLayout<kModeW8A8>::kBStageBytes);
+constexpr int kFusedQuantOffset = kFusedStructOffset + 4096;
+constexpr int kFusedQuantTransposeBytes = 4096;  // 1 KB per team
+constexpr int kFusedThreadCount = PairLayout<kModeW8A8>::kThreadCount + 32 * kFusedQuantWarps;
+__host__ __device__ inline int fused_quant_buffer_bytes(int k) { return ((2 * k + 1023) / 1024) * 1024; }
+inline int fused_smem_bytes(int k) {
+    return 1024 + kFusedQuantOffset + kFusedQuantWarps * (fused_quant_buffer_bytes(k) + kFusedQuantTransposeBytes);
+}
+static_assert(1024 + kFusedQuantOffset + kFusedQuantWarps * (2 * 256 * 4 * kFusedMaxGt + kFusedQuantTransposeBytes) <=
+                  232448,
+              "fused ConvRot linear exceeds the shared memory of one SM");
+
 // `tmap_b_narrow` is the weight map with a kHalfBN / 2-row box: the per-CTA weight rows of
-// a 128-column half tile (W8A8 only; the int4 modes never split tiles).
-template <int kMode>
+// a 128-column half tile (W8A8 only; the int4 modes never split tiles).  kGt > 0 (W8A8
+// only): the fused ConvRot linear above.
+template <int kMode, int kGt = 0>
 __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                       const __grid_constant__ CUtensorMap tmap_b,
                                       const __grid_constant__ CUtensorMap tmap_b_narrow, const GemmArgs args);

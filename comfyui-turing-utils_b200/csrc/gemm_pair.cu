@@ -24,6 +24,11 @@
 //               this CTA's packed tiles of the stage into the stage's 128-byte-swizzled
 //               int8 copies, then arrive on the leader's `bu_full[stage]` (one arrival
 //               per converter warp of each CTA).
+//               (fused ConvRot linear, kGt > 0) quantizer warps: claim bf16 input rows
+//               in order, rotate and quantize each with the warp-row pipeline, write its
+//               codes and scale, and count it in its 128-row block; the producer loads an
+//               activation tile once its block is complete, so quantization of later
+//               rows overlaps the MMAs of earlier ones.
 // Every wait is bounded; a role that gives up raises the abort flag in both CTAs so
 // the pair stops together, and both CTAs stay resident until the final cluster
 // barrier, so no remote arrival or copy can target a CTA that has exited.
@@ -33,6 +38,7 @@
 
 #include <cstdint>
 
+#include "convrot_rowwarp.cuh"
 #include "gemm_i8.cuh"
 #include "gemm_tile.cuh"
 #include "ptx.cuh"
@@ -49,6 +55,7 @@ struct PairSmem {
     uint64_t acc_empty[2];  // used in the leader only
     uint64_t bu_full[8];    // int4 modes, leader only: stage s converted in both CTAs
     uint64_t drain;
+    uint64_t qbar[kFusedQuantWarps];  // fused linear: row copy of each quantizer warp
     uint32_t tmem_base;
     int abort_flag;
     float col_scale[kBN];
@@ -92,24 +99,56 @@ __device__ __forceinline__ void settle_inflight_copies() {
     while (globaltimer() - start < 1000000ull) __nanosleep(1000);
 }
 
+// int8 codes of a row by the reciprocal chain (rows without NaN or an infinite absmax),
+// written as 4-byte words: lanes q and q ^ 1 of a team hold columns 2q, 2q + 1 of every
+// 16-column segment u, so one shuffle per two segments gives the even lane segment u's
+// four bytes 2(q & ~1) .. 2(q & ~1) + 3 and the odd lane those of segment u + 1.
+template <int kGt>
+__device__ __forceinline__ void store_codes_paired(const uint32_t (&W)[kGt][16], const bool (&folded)[kGt],
+                                                   float scale, int groups, uint32_t g, uint32_t q, int8_t *out_row) {
+    const float rs = __bfloat162float(__float2bfloat16_rn(scale));
+    const float rcp = __frcp_rn(rs);
+    const bool odd = (q & 1u) != 0u;
+#pragma unroll
+    for (int i = 0; i < kGt; ++i) {
+        const int grp = static_cast<int>(g) + 4 * i;
+        const bool active = grp < groups;  // every lane shuffles; inactive slots store nothing
+        const float rc = rcp * (folded[i] ? 0.0625f : 1.0f);
+        const f32x2 r2 = pk2(rc, rc);
+        int8_t *base = out_row + (active ? grp : 0) * 256 + 2 * (q & ~1u) + (odd ? 16 : 0);
+#pragma unroll
+        for (int u = 0; u < 16; u += 2) {
+            const uint32_t c0 = ctu::rot::quant2_int8_fast(W[i][u], r2);
+            const uint32_t c1 = ctu::rot::quant2_int8_fast(W[i][u + 1], r2);
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, odd ? c0 : c1, 1);
+            const uint32_t word = odd ? (recv | (c1 << 16)) : (c0 | (recv << 16));
+            if (active) *reinterpret_cast<uint32_t *>(base + 16 * u) = word;
+        }
+    }
+}
+
 }  // namespace
 
-template <int kMode>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::kThreadCount, 1)
+template <int kMode, int kGt>
+__global__ void __cluster_dims__(2, 1, 1)
+    __launch_bounds__(kGt > 0 ? kFusedThreadCount : PairLayout<kMode>::kThreadCount, 1)
     int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                           const __grid_constant__ CUtensorMap tmap_b_narrow, const GemmArgs args) {
     using L = PairLayout<kMode>;
     constexpr bool kConvert = L::kConvert;
-    constexpr int kStagesP = L::kStages;
+    constexpr bool kFused = kGt > 0;
+    // The fused linear runs a shallower ring so the quantizer warps' row buffers fit.
+    constexpr int kStagesP = kFused ? kFusedStages : L::kStages;
     static_assert(kStagesP <= 8, "barrier arrays hold 8 stages");
+    static_assert(!kFused || (kMode == kModeW8A8 && kGt <= kFusedMaxGt), "fused linear: W8A8, k <= 5120");
     extern __shared__ uint8_t smem_raw[];
     // Same offset in both CTAs: the MMA addresses the peer's operands at this CTA's offsets.
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem + L::kAOffset;
-    uint8_t *sB = smem + L::kBOffset;
+    uint8_t *sB = smem + (kFused ? kFusedStages * L::kAStageBytes : L::kBOffset);
     uint8_t *sAu = smem + L::kAuOffset;
     uint8_t *sBu = smem + L::kBuOffset;
-    PairSmem &S = *reinterpret_cast<PairSmem *>(smem + L::kStructOffset);
+    PairSmem &S = *reinterpret_cast<PairSmem *>(smem + (kFused ? kFusedStructOffset : L::kStructOffset));
 
     const uint32_t rank = cluster_ctarank();
     const bool leader = rank == 0;
@@ -152,6 +191,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
             mbar_init(&S.acc_empty[b], 2 * kEpilogueWarps);
         }
         mbar_init(&S.drain, 1);
+        for (int i = 0; i < kFusedQuantWarps; ++i) mbar_init(&S.qbar[i], 1);
         S.abort_flag = 0;
         fence_mbar_init();
     }
@@ -184,6 +224,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                 const int m0 = m_tile * kPairBM + static_cast<int>(rank) * kBM;
                 const bool narrow = ncols != kBN;  // each CTA stages ncols / 2 weight rows
                 const int w0 = n0 + static_cast<int>(rank) * (ncols / 2);
+                if constexpr (kFused) {
+                    // This CTA's activation rows must all be quantized before the tile's
+                    // first copy; the proxy fence makes the tensor-map loads read them.
+                    const int need = min(kBM, args.m - m0);
+                    if (need > 0 && !counter_wait(args.qsync + 1 + (m0 >> 7), static_cast<uint32_t>(need), abort_flag,
+                                                  args.err, kErrTimeoutRows)) {
+                        ab_state.raise();
+                        ok = false;
+                        break;
+                    }
+                    fence_proxy_async_global();
+                }
                 for (int kb = 0; kb < nk; ++kb) {
                     if (!ab_state.wait(&S.empty[s], ph ^ 1u, kErrTimeoutEmpty)) {
                         ok = false;
@@ -317,7 +369,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
             const int row = quad * 32 + lane;
             const int m = m0 + row;
             const bool row_ok = m < args.m;
-            const float a_s = (row_ok && args.out_mode == kOutBf16) ? args.a_scale[m] : 0.0f;
+            float a_s = 0.0f;
+            if constexpr (kFused) {
+                // The producer saw this block complete before loading it; this acquire
+                // orders the scale loads after the quantizer warps' release as well.
+                const int need = min(kBM, args.m - m0);
+                if (need > 0) counter_wait(args.qsync + 1 + (m0 >> 7), static_cast<uint32_t>(need), abort_flag, args.err,
+                                           kErrTimeoutRows);
+                if (row_ok) a_s = __ldcg(args.a_scale + m);
+            } else {
+                a_s = (row_ok && args.out_mode == kOutBf16) ? args.a_scale[m] : 0.0f;
+            }
 #pragma unroll 1
             for (int c = 0; c < ncols / 32; ++c) {
                 uint32_t acc[32];
@@ -372,6 +434,94 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairLayout<kMode>::k
                 mbar_arrive(&S.empty[s]);
             }
         }
+    } else if constexpr (kFused) {
+        // ------------------------------------------------------------------ ConvRot quantizer warps
+        // Warp-row pipeline (convrot_rowwarp.cuh): a row is copied into this warp's
+        // buffer by one bulk copy, rotated with the halvings folded, and quantized to
+        // int8 with the per-row scale absmax / 127; the next claimed row's copy is in
+        // flight while the codes are written.
+        const int qw = warp - (2 + kEpilogueWarps);
+        const int K = args.k;
+        const int groups = K / 256;
+        const uint32_t row_bytes = static_cast<uint32_t>(K) * 2u;
+        const uint32_t buf_bytes = static_cast<uint32_t>(fused_quant_buffer_bytes(K));
+        uint8_t *qbuf = smem + kFusedQuantOffset + qw * (buf_bytes + kFusedQuantTransposeBytes);
+        const uint32_t buf = smem_u32(qbuf);
+        uint64_t *bar = &S.qbar[qw];
+        const uint32_t g = static_cast<uint32_t>(lane >> 3);
+        const uint32_t q = static_cast<uint32_t>(lane & 7);
+        const uint32_t garea = buf + buf_bytes + g * 1024u;
+        const uint32_t wbase = garea + 16u * ((4u * q) ^ (q >> 1) ^ (4u * (g & 1u)));
+        const uint32_t rbase = garea + 8u * (q & 1u) + 16u * ((q >> 1) ^ (4u * (g & 1u)));
+        const ctu::rot::ActLut lut{nullptr, nullptr};
+        const uint16_t *x = static_cast<const uint16_t *>(args.qx);
+        uint32_t *claim = args.qsync;
+        uint32_t *done = args.qsync + 1;
+
+        int row = 0;
+        if (lane == 0) {
+            row = static_cast<int>(atomicAdd(claim, 1u));
+            if (row < args.m) {
+                mbar_arrive_expect_tx(bar, row_bytes);
+                bulk_load(qbuf, x + static_cast<int64_t>(row) * K, row_bytes, bar);
+            }
+        }
+        row = __shfl_sync(0xffffffffu, row, 0);
+        bool pending = row < args.m;  // lane 0: a copy is in flight
+        uint32_t it = 0;
+        // A row is counted in its block one row later, once its code stores are long
+        // complete, so the fence in front of the count does not stall on them.
+        int unpublished = -1;
+        auto publish = [&](int r) {
+            // Codes are read by other SMs' tensor-map loads (async proxy), the scale by
+            // their epilogues.  __syncwarp orders every lane's stores before lane 0's
+            // release, which is cumulative over them.
+            fence_proxy_async_global();
+            __syncwarp();
+            if (lane == 0) red_release_gpu_add(done + (r >> 7), 1u);
+        };
+        while (row < args.m) {
+            int next = 0;
+            if (lane == 0) next = static_cast<int>(atomicAdd(claim, 1u));  // used after the rotation
+            int ok = 1;
+            if (lane == 0) ok = mbar_wait(bar, it & 1u, abort_flag, args.err, kErrTimeoutFull) ? 1 : 0;
+            if (__shfl_sync(0xffffffffu, ok, 0) == 0) {
+                ab_state.raise();
+                break;
+            }
+            pending = false;
+            uint32_t W[kGt > 0 ? kGt : 1][16];
+            bool folded[kGt > 0 ? kGt : 1];
+            float amax = 0.0f;
+            bool any_nan = false;
+            ctu::rot::w8_rotate_row<ctu::rot::kActNone, kGt>(buf, groups, g, q, wbase, rbase, lut, W, folded, amax,
+                                                             any_nan);
+            next = __shfl_sync(0xffffffffu, next, 0);
+            if (lane == 0 && next < args.m) {
+                mbar_arrive_expect_tx(bar, row_bytes);
+                bulk_load(qbuf, x + static_cast<int64_t>(next) * K, row_bytes, bar);
+                pending = true;
+            }
+            amax = ctu::rot::w8_row_absmax(amax);
+            const bool row_nan = __any_sync(0xffffffffu, any_nan);
+            const float scale = ctu::rot::row_scale<8>(amax, false);
+            if (unpublished >= 0) publish(unpublished);
+            if (lane == 0) args.qscales[row] = scale;
+            int8_t *out_row = args.qcodes + static_cast<int64_t>(row) * K;
+            if (row_nan || isinf(amax)) {  // warp-uniform: the reference's exact chain
+                ctu::rot::w8_store_codes<8, kGt>(W, folded, amax, scale, row_nan, groups, g, q, out_row);
+            } else {
+                store_codes_paired<kGt>(W, folded, scale, groups, g, q, out_row);
+            }
+            unpublished = row;
+            row = next;
+            ++it;
+        }
+        if (unpublished >= 0 && row >= args.m) publish(unpublished);  // not after an abort
+        if (lane == 0 && pending) {
+            // A wait gave up with a copy still in flight: let it land before the CTA exits.
+            mbar_wait(bar, it & 1u, nullptr, args.err, kErrTimeoutDrain);
+        }
     }
 
     tc_fence_before();
@@ -392,6 +542,16 @@ template __global__ void int8_gemm_pair_kernel<kModeW4A8>(const __grid_constant_
 template __global__ void int8_gemm_pair_kernel<kModeW4A4>(const __grid_constant__ CUtensorMap,
                                                           const __grid_constant__ CUtensorMap,
                                                           const __grid_constant__ CUtensorMap, const GemmArgs);
+#define CTU_FUSED_LINEAR(GT)                                                                                    \
+    template __global__ void int8_gemm_pair_kernel<kModeW8A8, GT>(                                              \
+        const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, const __grid_constant__ CUtensorMap, \
+        const GemmArgs);
+CTU_FUSED_LINEAR(1)
+CTU_FUSED_LINEAR(2)
+CTU_FUSED_LINEAR(3)
+CTU_FUSED_LINEAR(4)
+CTU_FUSED_LINEAR(5)
+#undef CTU_FUSED_LINEAR
 
 }  // namespace gemm
 }  // namespace ctu

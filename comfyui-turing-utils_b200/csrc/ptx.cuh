@@ -22,6 +22,7 @@ enum DeviceError : uint32_t {
     kErrTimeoutDrain = 1u << 4,     // teardown waited too long for copies in flight
     kErrTmemAlloc = 1u << 5,        // TMEM allocation returned an unusable address
     kErrInjected = 1u << 6,         // test hook: a wait on a barrier nobody arrives on
+    kErrTimeoutRows = 1u << 7,      // fused linear: GEMM waited too long for quantized rows
 };
 
 // Wait limit in nanoseconds of %globaltimer.  Far above any legitimate wait in
@@ -116,6 +117,45 @@ __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wa
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Orders this thread's generic-proxy view of global memory with its async-proxy
+// (TMA) accesses: after acquiring data that other SMs wrote with ordinary stores, a
+// tensor-map load issued behind this fence reads those values.
+__device__ __forceinline__ void fence_proxy_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Cross-CTA progress counters in global memory (gpu scope)
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(uint32_t *p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait until *counter >= target, with acquire semantics on success.  Sleeps
+// briefly between polls so the waiting warp leaves the issue slots to the others.
+__device__ __forceinline__ bool counter_wait(const uint32_t *counter, uint32_t target, volatile int *abort_flag,
+                                             uint32_t *err, uint32_t code, uint64_t limit_ns = kWaitLimitNs) {
+    if (ld_acquire_gpu(counter) >= target) return true;
+    const uint64_t start = globaltimer();
+    for (uint32_t i = 1;; ++i) {
+        __nanosleep(100);
+        if (ld_acquire_gpu(counter) >= target) return true;
+        if ((i & 15u) == 0u) {
+            if (abort_flag != nullptr && *abort_flag) return false;
+            if (globaltimer() - start > limit_ns) {
+                if (abort_flag != nullptr) *abort_flag = 1;
+                atomicOr(err, code);
+                return false;
+            }
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------

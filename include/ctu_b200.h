@@ -116,6 +116,30 @@ CTU_API int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_sca
                     void *stream);
 
 /*
+ * ConvRot W8A8 linear from bf16 rows in one call: ctu_convrot_quantize(x, m, k, NONE, 8,
+ * codes, scales) followed by ctu_int8_linear(codes, w, scales, w_scale, ..., out), with
+ * the same codes, scales and outputs bit for bit.  Replaces the plugin's
+ * dispatch.int8_linear for plain ConvRot W8A8 rows (comfyui_turing_utils/quantization/
+ * dispatch.py:748-800: _quantize_turing_int8_activation, then turing_int8_linear).
+ *   x bf16 [m, k] (k % 256 == 0), w int8 [n, k], w_scale fp32 [n] or scalar, bias fp32 [n]
+ *   or NULL, out bf16 [m, n]; codes int8 [m, k] and scales fp32 [m] receive the quantized
+ *   activation; sync is a workspace of ctu_convrot_int8_linear_sync_words(m) uint32 words
+ *   (4-byte aligned; cleared on the stream by the call).
+ * For k <= 5120, n <= 8192 and m >= 8192 one kernel does both: quantizer warps inside the
+ * CTA-pair GEMM publish each finished 128-row block and the GEMM loads a block once it is
+ * complete, so the rotation of later rows overlaps the tensor-core work on earlier ones.
+ * Otherwise (where that measured slower) the quantizer and the GEMM run back to back.
+ * Requires n % 8 == 0 and 16-byte aligned x, w, codes and out.
+ */
+CTU_API int ctu_convrot_int8_linear(const void *x, const int8_t *w, const float *w_scale, int64_t w_scale_count,
+                                    const float *bias, void *out, int8_t *codes, float *scales, uint32_t *sync,
+                                    int64_t m, int64_t n, int64_t k, void *stream);
+
+/* Words of the sync workspace ctu_convrot_int8_linear needs for m rows:
+ * 1 + ceil(m / 128). */
+CTU_API int64_t ctu_convrot_int8_linear_sync_words(int64_t m);
+
+/*
  * W4A8 linear: as ctu_int8_linear, with signed 4-bit weights packed two per byte,
  *   w_packed int8 [n, k/2], byte j of a row = k 2j (low nibble) and 2j+1 (high nibble),
  *   each nibble two's-complement in [-8, 7].  The packed tile is sign-extended to int8
@@ -301,6 +325,12 @@ CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, in
  * when M > 128), 1 = single-CTA kernel, 2 = CTA-pair kernel.  Returns the previous
  * selector, or a negative error code. */
 CTU_API int ctu_debug_set_gemm_kernel(int which);
+
+/* Test hook (no counterpart in the reference): how ctu_convrot_int8_linear runs.  0 = per
+ * problem (default; see ctu_convrot_int8_linear), 1 = always the separate quantizer and
+ * GEMM, 2 = the fused kernel wherever it applies (k <= 5120, more than 128 rows).  Returns
+ * the previous setting, or a negative error code. */
+CTU_API int ctu_debug_set_fused_linear(int which);
 
 /* Test hook (no counterpart in the reference): how many of the last 256 x 256 output tiles
  * the CTA-pair W8A8 GEMM runs as two 256 x 128 halves, for every later call in this

@@ -43,6 +43,25 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert rc == _lib.CTU_OK  # empty batch is a no-op
 
 
+def test_fused_linear_contract_without_a_gpu():
+    import ctypes
+
+    from comfyui_turing_utils_kernel import _lib
+
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    # One claim counter plus one finished-row counter per 128-row block.
+    assert [lib.ctu_convrot_int8_linear_sync_words(m) for m in (0, 1, 128, 129, 32760)] == [1, 2, 2, 3, 257]
+    rc = lib.ctu_convrot_int8_linear(null, null, null, 8, null, null, null, null, null, 4, 8, 300, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "divisible by 256" in lib.ctu_last_error().decode()
+    fake = ctypes.c_void_p(0x10000)  # aligned, never dereferenced: the shape check fails first
+    rc = lib.ctu_convrot_int8_linear(fake, fake, fake, 12, null, fake, fake, fake, fake, 4, 12, 512, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "N%8=0" in lib.ctu_last_error().decode()
+    rc = lib.ctu_convrot_int8_linear(null, null, null, 8, null, null, null, null, null, 0, 8, 512, null)
+    assert rc == _lib.CTU_OK  # no rows: nothing to do
+    assert lib.ctu_debug_set_fused_linear(3) == _lib.CTU_ERR_INVALID_ARGUMENT
+
+
 def test_reference_c_module_attribute_names():
     # Names probed by the plugin through kernel_extension_has_symbol (kernel_api.py:26-37).
     from comfyui_turing_utils_kernel import _C
