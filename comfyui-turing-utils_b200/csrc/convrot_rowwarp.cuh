@@ -80,9 +80,10 @@ __device__ __forceinline__ uint4 ld_shared_v4u(uint32_t addr) {
 // halvings (W = bf16(y), NaN-ignoring absmax, NaN probe); otherwise unscaled (W = bf16(z),
 // z = 16 y, NaN-propagating absmax of z).  Word W[u] of lane q holds columns 16u + 2q and
 // 16u + 2q + 1 of the group.  kHalves: `absmax` covers columns 0..127 (u < 8) and
-// `absmax_hi` columns 128..255; otherwise `absmax` covers the whole group.  All 32 lanes
-// of the warp take part.
-template <bool kHalve, bool kHalves = false>
+// `absmax_hi` columns 128..255; otherwise `absmax` covers the whole group.  kTeamReduce:
+// the statistics are reduced over the team's 8 lanes; otherwise each lane returns its own
+// (the warp-row pipeline reduces once per row).  All 32 lanes of the warp take part.
+template <bool kHalve, bool kHalves = false, bool kTeamReduce = true>
 __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32_t rbase, uint32_t (&W)[16],
                                           float &absmax, float &nan_probe, float &absmax_hi) {
     const f32x2 half = pk2(0.5f, 0.5f);
@@ -151,7 +152,7 @@ __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32
         pr = __fadd_rn(p0, p1);
     }
 #pragma unroll
-    for (int d = 1; d < 8; d <<= 1) {
+    for (int d = 1; d < (kTeamReduce ? 8 : 1); d <<= 1) {
         if constexpr (kHalve) {
             m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));  // NaN-ignoring, as the reference's fmaxf
             if constexpr (kHalves) mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, d));
@@ -223,14 +224,18 @@ __device__ __forceinline__ void w8_load(uint32_t gaddr, uint32_t q, f32x2 (&P)[1
 // rotates groups g, g + 4, ..., g + 4 (kGt - 1) (slots past the last group rotate the
 // last group again and are ignored) and keeps their bf16 words in registers.
 
-// Rotates the row: W[i] / folded[i] for slot i, the team's absmax over its groups (of
-// the halved rotation: folded slots are rescaled by 1/16) and whether a non-folded
-// group produced a NaN.  All 32 lanes take part; the buffer is no longer read when
-// this returns and every lane has passed a __syncwarp.
+// Rotates the row: W[i] / folded[i] for slot i, this lane's absmax over its values of
+// the row (of the halved rotation: folded slots are rescaled by 1/16) and whether one of
+// its values of a non-folded group is NaN.  The statistics stay per lane -- max and "any"
+// do not depend on the order of reduction, and the fold test is a warp-wide vote -- so
+// the warp reduces them once per row instead of once per group.  (A row with +inf and
+// -inf but no NaN, which a summed probe would flag, has an infinite absmax and takes the
+// same exact chain.)  All 32 lanes take part; the buffer is no longer read when this
+// returns and every lane has passed a __syncwarp.
 template <int Act, int kGt>
 __device__ __forceinline__ void w8_rotate_row(uint32_t buf, int groups, uint32_t g, uint32_t q, uint32_t wbase,
                                               uint32_t rbase, const ActLut &lut, uint32_t (&W)[kGt][16],
-                                              bool (&folded)[kGt], float &team_amax, bool &any_nan) {
+                                              bool (&folded)[kGt], float &lane_amax, bool &any_nan) {
     float amax = 0.0f;  // non-negative, never NaN
     bool nan_seen = false;
 #pragma unroll
@@ -241,26 +246,28 @@ __device__ __forceinline__ void w8_rotate_row(uint32_t buf, int groups, uint32_t
         float ga = 0.0f, probe = 0.0f, unused = 0.0f;
         f32x2 P[16];
         w8_load<Act>(gaddr, q, P, lut);
-        g8_rotate<false>(P, wbase, rbase, W[i], ga, probe, unused);
+        g8_rotate<false, false, false>(P, wbase, rbase, W[i], ga, probe, unused);
         folded[i] = !__any_sync(0xffffffffu, active && !(ga <= 3.40282347e38f));
         if (folded[i]) {
             ga *= 0.0625f;
         } else {  // warp-uniform: the reference's order, halvings included
             w8_load<Act>(gaddr, q, P, lut);
-            g8_rotate<true>(P, wbase, rbase, W[i], ga, probe, unused);
+            g8_rotate<true, false, false>(P, wbase, rbase, W[i], ga, probe, unused);
             nan_seen |= active && isnan(probe);
         }
         if (active) amax = fmaxf(amax, ga);
     }
     __syncwarp();  // every lane's reads of the buffer are done
-    team_amax = amax;
+    lane_amax = amax;
     any_nan = nan_seen;
 }
 
-// Row absmax from the four teams' maxima (every lane receives it).
-__device__ __forceinline__ float w8_row_absmax(float team_amax) {
-    float m = fmaxf(team_amax, __shfl_xor_sync(0xffffffffu, team_amax, 8));
-    return fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 16));
+// Row absmax from the lanes' maxima (every lane receives it).
+__device__ __forceinline__ float w8_row_absmax(float lane_amax) {
+    float m = lane_amax;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, d));
+    return m;
 }
 
 // Codes of the row (int8: [K] bytes; int4: [K / 2] packed) from the rotated words,
