@@ -367,7 +367,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                    w_s, b) for k, n, w, w_s, b in layers]
 
         # The same W8A8 sweep through the one-call linear (ctu_convrot_int8_linear): where it
-        # measured faster (N <= 8192, M >= 8192: the four Q/K/V/O linears of a full-M step)
+        # measured faster (N <= 8192, M >= 16384: the four Q/K/V/O linears of a full-M step)
         # one kernel quantizes rows while its tensor cores work on finished ones.
         def one_call_step():
             for x, (k, n, w, w_s, b) in zip(xs, layers):
@@ -377,7 +377,7 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         variants["convrot_int8_linear"] = {
             "value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
             "format": "configs[1] W8A8 through turing_utils::convrot_int8_linear: the fused quantizer + CTA-pair "
-                      "GEMM kernel for N <= 8192 at M >= 8192, quantizer then GEMM otherwise"}
+                      "GEMM kernel for N <= 8192 at M >= 16384, quantizer then GEMM otherwise"}
 
         def w4_step(act_bits):
             for x, (k, n, wp, w_s, b) in zip(xs, packed):

@@ -659,10 +659,10 @@ int g_fused_clusters[kMaxDevices][ctu::gemm::kFusedMaxGt + 1] = {};
 // beside the ring: rows of at most 4 * kFusedMaxGt groups, more than one row tile (the
 // single-CTA GEMM keeps the separate quantizer).  Per problem it runs where it measured
 // faster than the quantizer and GEMM back to back on power-capped B200s: N <= 8192 and
-// M >= 8192 (5120 x 5120 at 16384 rows: 5-9 % faster; at 32760 rows: about 2 %).  With
-// fewer rows the first row blocks' quantization delays the tensor cores (4095 rows: 10 %
-// slower), and at N = 13824 the quantizer's extra power lowers the clock of a GEMM that is
-// already at the power cap (3-7 % slower).
+// M >= 16384 (5120 x 5120 at 16384 and 32760 rows: 2-7 % faster).  With fewer rows the
+// first row blocks' quantization delays the tensor cores (8192 rows: 3 % slower, 4095:
+// 6-10 %), and at N = 13824 the quantizer's extra power lowers the clock of a GEMM that is
+// already at the power cap (0-3 % slower).
 bool use_fused_linear(int64_t m, int64_t n, int64_t k) {
     const int sel = g_fused_linear.load(std::memory_order_relaxed);
     if (sel == 1) return false;
@@ -670,7 +670,7 @@ bool use_fused_linear(int64_t m, int64_t n, int64_t k) {
     const int forced = g_gemm_kernel.load(std::memory_order_relaxed);
     if (forced == 1) return false;
     if (sel == 2) return forced == 2 || m > ctu::gemm::kBM;
-    return m >= 8192 && n <= 8192;
+    return m >= 16384 && n <= 8192;
 }
 
 template <int kGt>

@@ -125,7 +125,7 @@ CTU_API int ctu_int8_linear(const int8_t *a, const int8_t *w, const float *a_sca
  *   or NULL, out bf16 [m, n]; codes int8 [m, k] and scales fp32 [m] receive the quantized
  *   activation; sync is a workspace of ctu_convrot_int8_linear_sync_words(m) uint32 words
  *   (4-byte aligned; cleared on the stream by the call).
- * For k <= 5120, n <= 8192 and m >= 8192 one kernel does both: quantizer warps inside the
+ * For k <= 5120, n <= 8192 and m >= 16384 one kernel does both: quantizer warps inside the
  * CTA-pair GEMM publish each finished 128-row block and the GEMM loads a block once it is
  * complete, so the rotation of later rows overlaps the tensor-core work on earlier ones.
  * Otherwise (where that measured slower) the quantizer and the GEMM run back to back.
