@@ -22,9 +22,10 @@
 // operations on each of 128 x 128 partials: 256 cycles of the ALU pipe and 256 or 384 of
 // the 128-lane FMA pipe, against about 262 cycles for the group's MMAs (M = 256, N = 128,
 // K = 128 on two SMs).  So the
-// per-group control work is kept to a few instructions per warp, each warp reads its 64
+// per-group control work is kept to a few instructions per warp, each warp reads its
 // partials of a group with one TMEM load (one load latency per group) straight into
-// register pairs, and the scales arrive as pairs next to their use.
+// register pairs, the scales arrive as pairs next to their use, and 16 epilogue warps (4
+// per scheduler) keep enough of these latency-bound chains in flight.
 //
 // Roles per CTA (persistent over tiles, n-fastest):
 //   warp 0      producer: the stage's A and B tiles (completing on the leader's `full`
@@ -33,8 +34,9 @@
 //   warp 1      pair TMEM allocation.  Leader: the MMA issuer; non-leader: forwards its
 //               epilogue's buffer releases to the leader's `acc_empty` (one remote
 //               arrival per release instead of one per epilogue warp).
-//   warps 2..9  epilogue: warp w reads TMEM lanes 32 (w % 4) .. +31 (its rows) and
-//               columns 64 ((w - 2) / 4) .. +63; 64 fp32 running sums per thread.
+//   warps 2..   epilogue (kGroupedEpilogueWarps): warp w reads TMEM lanes 32 (w % 4) ..
+//               +31 (its rows) and kGroupedEpilogueCols columns from
+//               kGroupedEpilogueCols ((w - 2) / 4); one fp32 running sum per column.
 // Every wait is bounded; a role that gives up raises the abort flag in both CTAs, and
 // both CTAs stay resident until the final cluster barrier.
 #include <cuda.h>
@@ -63,8 +65,8 @@ static_assert(kGroupedBuffers < kGroupedStages, "the epilogue identifies a group
 struct GroupedSmem {
     uint64_t full[kGroupedStages];
     uint64_t empty[kGroupedStages];
-    uint64_t acc_empty[kGroupedBuffers];  // leader: 8 local epilogue warps + 1 forwarded peer release
-    uint64_t acc_local[kGroupedBuffers];  // non-leader: its 8 epilogue warps
+    uint64_t acc_empty[kGroupedBuffers];  // leader: its epilogue warps + 1 forwarded peer release
+    uint64_t acc_local[kGroupedBuffers];  // non-leader: its epilogue warps
     uint64_t sc_full[kGroupedScaleSlots];
     uint64_t sc_empty[kGroupedScaleSlots];
     uint64_t drain;
@@ -324,16 +326,16 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                     break;
                 }
                 tc_fence_after();
-                // Read this warp's 64 columns (kLoadCols per TMEM load) and release the
-                // buffer once all are read, accumulating as they arrive.
-                static_assert(kGroupedEpilogueCols == 64, "64 columns per warp and group");
+                // Read this warp's columns (kLoadCols per TMEM load) and release the buffer
+                // once all are read, accumulating as they arrive.
+                static_assert(kGroupedEpilogueCols % kLoadCols == 0, "whole TMEM loads per warp and group");
                 const uint32_t sc = smem_u32(&S.scale_ring[r][col0]);
                 const f32x2 g2 = pk2(gs0, gs0);  // W4A4: this row's activation scale of the group
 #pragma unroll
-                for (int h = 0; h < 64 / kLoadCols; ++h) {
+                for (int h = 0; h < kGroupedEpilogueCols / kLoadCols; ++h) {
                     u32x2 v[kLoadCols / 2];
                     tmem_ld_32x32b_x32_pairs(col_base + pb * kGroupedBN + kLoadCols * h, v);
-                    if (h == 64 / kLoadCols - 1) {
+                    if (h == kGroupedEpilogueCols / kLoadCols - 1) {
                         tc_fence_before();
                         __syncwarp();
                         if (lane == 0) mbar_arrive(release0 + pb);

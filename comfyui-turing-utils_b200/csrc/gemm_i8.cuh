@@ -160,11 +160,17 @@ constexpr int kGroupedBN = 128;        // output columns per pair tile
 constexpr int kGroupedStages = 8;      // ring depth (groups)
 constexpr int kGroupedBuffers = 4;     // TMEM partial buffers of kGroupedBN columns
 constexpr int kGroupedScaleSlots = 12; // weight-scale ring (one group's kGroupedBN scales per slot)
-constexpr int kGroupedEpilogueWarps = 8;  // 2 per TMEM lane quadrant, 64 columns each
+#ifndef CTU_GROUPED_EPILOGUE_WARPS
+#define CTU_GROUPED_EPILOGUE_WARPS 16
+#endif
+// Epilogue warps per CTA: 4 per TMEM lane quadrant, 32 columns each, so every scheduler
+// has four of them to hide the latency of the per-group convert-and-accumulate chains.
+constexpr int kGroupedEpilogueWarps = CTU_GROUPED_EPILOGUE_WARPS;
 constexpr int kGroupedEpilogueCols = kGroupedBN / (kGroupedEpilogueWarps / 4);
 constexpr int kGroupedThreads = 64 + 32 * kGroupedEpilogueWarps;
-// 10 warps: two schedulers hold 3, so a thread may use 16384 / (3 * 32) registers.
-constexpr int kGroupedMaxRegisters = 168;
+// A warp's registers come from its scheduler's quarter of the register file (16384), and
+// the busiest scheduler holds ceil(warps / 4) warps (18 warps: 5, so 96 registers a thread).
+constexpr int kGroupedMaxRegisters = (16384 / (((kGroupedThreads / 32 + 3) / 4) * 32)) / 8 * 8;
 constexpr int kGroupedAStage = kBM * kGroupK;                  // 16 KB
 constexpr int kGroupedBStage = (kGroupedBN / 2) * kGroupK;     // 8 KB: each CTA stages half the weight rows
 constexpr int kGroupedBookkeepingBytes = 12288;
