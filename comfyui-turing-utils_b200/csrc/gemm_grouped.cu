@@ -7,8 +7,8 @@
 // owns a 256 x 128 output tile (tcgen05.mma.cta_group::2, M = 256, N = 128): CTA r stages
 // activation rows [128 r, 128 r + 128) and weight rows [64 r, 64 r + 64) of each group.
 // One ring stage is one group (four K = 32 MMAs).  Each group's partial lands in its own
-// 128-column TMEM buffer, and there are four, so the MMA runs up to three groups ahead of
-// the epilogue that converts and scales them.
+// 128-column TMEM buffer, and there are four (freed in pairs), so the MMA runs up to four
+// groups ahead of the epilogue that converts and scales them.
 //
 // Conversion without I2F.  The group's first MMA overwrites the buffer, so it holds the
 // exact int32 partial acc, |acc| <= 128 * 128 * 15 < 2^22.  For such acc the bit pattern
@@ -33,7 +33,12 @@
 //               ring (completing on its own `sc_full`).
 //   warp 1      pair TMEM allocation.  Leader: the MMA issuer; non-leader: forwards its
 //               epilogue's buffer releases to the leader's `acc_empty` (one remote
-//               arrival per release instead of one per epilogue warp).
+//               arrival per release instead of one per epilogue warp).  The four buffers
+//               are released in pairs (groups 2i and 2i + 1 together): a remote arrival
+//               with cluster-scope release keeps the forwarding thread about a microsecond
+//               (a globaltimer trace; a relaxed or CTA-scope arrival is faster but let the
+//               MMA overwrite partials the peer had not finished reading), so one per two
+//               groups halves the time the forwarder paces the pair at.
 //   warps 2..   epilogue (kGroupedEpilogueWarps): warp w reads TMEM lanes 32 (w % 4) ..
 //               +31 (its rows) and kGroupedEpilogueCols columns from
 //               kGroupedEpilogueCols ((w - 2) / 4); one fp32 running sum per column.
@@ -65,8 +70,9 @@ static_assert(kGroupedBuffers < kGroupedStages, "the epilogue identifies a group
 struct GroupedSmem {
     uint64_t full[kGroupedStages];
     uint64_t empty[kGroupedStages];
-    uint64_t acc_empty[kGroupedBuffers];  // leader: its epilogue warps + 1 forwarded peer release
-    uint64_t acc_local[kGroupedBuffers];  // non-leader: its epilogue warps
+    // Buffer pairs {0, 1} and {2, 3}, each released once both of its groups are read.
+    uint64_t acc_empty[kGroupedBuffers / 2];  // leader: its epilogue warps (x2) + 1 forwarded peer release
+    uint64_t acc_local[kGroupedBuffers / 2];  // non-leader: its epilogue warps (x2)
     uint64_t sc_full[kGroupedScaleSlots];
     uint64_t sc_empty[kGroupedScaleSlots];
     uint64_t drain;
@@ -158,9 +164,9 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
-        for (int b = 0; b < kGroupedBuffers; ++b) {
-            mbar_init(&S.acc_empty[b], kGroupedEpilogueWarps + 1);
-            mbar_init(&S.acc_local[b], kGroupedEpilogueWarps);
+        for (int b = 0; b < kGroupedBuffers / 2; ++b) {
+            mbar_init(&S.acc_empty[b], 2 * kGroupedEpilogueWarps + 1);
+            mbar_init(&S.acc_local[b], 2 * kGroupedEpilogueWarps);
         }
         for (int r = 0; r < kGroupedScaleSlots; ++r) {
             mbar_init(&S.sc_full[r], 1);
@@ -235,7 +241,9 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                         const uint32_t use = j / kGroupedBuffers;
                         // Completion `use - 1` of acc_empty[pb]: the epilogue's release of the
                         // buffer's previous group in both CTAs (a fresh barrier passes use 0).
-                        if (!ab.wait_cluster(&S.acc_empty[pb], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
+                        // (Buffers are released in pairs: the first of a pair waits for both.)
+                        if ((pb & 1u) == 0u &&
+                            !ab.wait_cluster(&S.acc_empty[pb >> 1], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
                             ok = false;
                             break;
                         }
@@ -265,10 +273,12 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
             // -------------------------------------------------------------- release forwarder
             const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&S.acc_empty[0]), 0u);
             const uint32_t releases = static_cast<uint32_t>(my_tiles) * static_cast<uint32_t>(nk);
-            for (uint32_t i = 0; i < releases; ++i) {
-                const uint32_t pb = i % kGroupedBuffers;
-                if (!ab.wait(&S.acc_local[pb], (i / kGroupedBuffers) & 1u, kErrTimeoutAccumFree)) break;
-                mbar_arrive_remote(leader_acc_empty0 + pb * static_cast<uint32_t>(sizeof(uint64_t)));
+            // Groups i and i + 1 (i even) share a buffer pair; an unpaired last group is
+            // never waited for by the MMA, so it is not forwarded.
+            for (uint32_t i = 0; i + 1 < releases; i += 2) {
+                const uint32_t pp = (i % kGroupedBuffers) >> 1;
+                if (!ab.wait(&S.acc_local[pp], (i / kGroupedBuffers) & 1u, kErrTimeoutAccumFree)) break;
+                mbar_arrive_remote(leader_acc_empty0 + pp * static_cast<uint32_t>(sizeof(uint64_t)));
             }
         }
     } else {
@@ -314,9 +324,10 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                 float gs2 = 0.0f;
                 if constexpr (kGroupMode == kGroupW4A4) gs2 = (row_ok && kb + 2 < nk) ? a_row[kb + 2] : 0.0f;
                 // The group's MMAs are complete when stage j % kGroupedStages completes its
-                // phase j / kGroupedStages.  The MMA runs at most kGroupedBuffers - 1 groups
-                // ahead of this loop, fewer than the ring depth, so that phase is the
-                // current or the previous one of the barrier and its parity identifies it.
+                // phase j / kGroupedStages.  The MMA runs at most kGroupedBuffers groups
+                // ahead of this loop (buffers are freed in pairs), fewer than the ring depth,
+                // so that phase is the current or the previous one of the barrier and its
+                // parity identifies it.
                 const bool ok = mbar_wait(&S.empty[j % kGroupedStages], (j / kGroupedStages) & 1u, abort_flag,
                                           args.err, kErrTimeoutAccum) &&
                                 mbar_wait(&S.sc_full[r], rph, abort_flag, args.err, kErrTimeoutFull);
@@ -338,7 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                     if (h == kGroupedEpilogueCols / kLoadCols - 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(release0 + pb);
+                        if (lane == 0) mbar_arrive(release0 + (pb >> 1));
                     }
 #pragma unroll
                     for (int i = 0; i < kLoadCols / 4; ++i) {

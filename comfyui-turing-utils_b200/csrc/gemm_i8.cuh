@@ -145,7 +145,7 @@ __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a
 // (and, for W4A4, its own activation scale per token), so each group's int32 partial is
 // converted and scaled on its own.  A CTA pair computes a 256 x 128 output tile; one
 // ring stage is one group; four 128-column TMEM buffers hold the partials of four
-// consecutive groups, so the MMA runs up to three groups ahead of the epilogue.
+// consecutive groups (freed in pairs), so the MMA runs up to four groups ahead of the epilogue.
 //
 //   kGroupAsymW4A8: t += w_scale[g][n] * float(acc_g);  out = bf16(fma(t, a_scale[m], bias[n]))
 //   kGroupW4A4:     t += (float(acc_g) * a_scale[m][g]) * w_scale[g][n];  out = bf16(t + bias[n])
