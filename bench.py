@@ -379,6 +379,20 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
             "format": "configs[1] W8A8 through turing_utils::convrot_int8_linear: the fused quantizer + CTA-pair "
                       "GEMM kernel for N <= 8192 at M >= 16384, quantizer then GEMM otherwise"}
 
+        # configs[0]-[3] name rotation block 128: the same sweep with the block-128 quantizer
+        # (this build's definition of that rotation; parity unpinned) and the W8A8 GEMM.
+        def block128_step():
+            for x, (k, n, w, w_s, b) in zip(xs, layers):
+                q, s = kops.turing_bf16_int8_convrot_quantize_b128(x)
+                kops.turing_int8_linear(q, w, s, w_s, b)
+
+        ms = timed(block128_step, max(5, min(args.steps, 30)))
+        variants["rotation_block_128"] = {
+            "value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT, "ms_per_step": ms,
+            "format": "configs[1] W8A8 with rotation block 128: (1/sqrt 2) H2 x M x M x M per 128 columns (the "
+                      "reference's radix-4 stages at strides 1, 4, 16, then radix-2 at stride 64); parity "
+                      "unpinned: the reference's ops take block 256 only"}
+
         def w4_step(act_bits):
             for x, (k, n, wp, w_s, b) in zip(xs, packed):
                 q, s = (kops.turing_bf16_int8_convrot_quantize if act_bits == 8

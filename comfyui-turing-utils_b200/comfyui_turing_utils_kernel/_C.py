@@ -88,6 +88,26 @@ def turing_bf16_int8_convrot_quantize(input, group_size=256, swiglu=False, force
     return _convrot_quantize(input, group_size, act, 8, "BF16 row-buffer ConvRot")
 
 
+def bf16_int8_convrot_quantize_b128(input):
+    """ConvRot int8 quantize with rotation block 128 (this library's definition, parity
+    unpinned: the reference's ops take 256 only; see ctu_b200.h).  Returns the int8
+    codes [M, K] and the per-token scales [M, 1]."""
+    x = input.contiguous()
+    _check_cuda_2d(x, "input")
+    if x.dtype != torch.bfloat16:
+        raise RuntimeError("block-128 ConvRot input must be bfloat16")
+    rows, width = x.shape
+    if rows <= 0 or width <= 0 or width % 256 != 0:
+        raise RuntimeError("block-128 ConvRot width must be positive and divisible by 256")
+    x = _aligned(x)
+    codes = torch.empty((rows, width), dtype=torch.int8, device=x.device)
+    scales = torch.empty((rows, 1), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().ctu_convrot_quantize_b128(_ptr(x), rows, width, _ptr(codes), _ptr(scales),
+                                                         _stream(x.device)))
+    return codes, scales
+
+
 def turing_bf16_int4_convrot_quantize(input, group_size=256, swiglu=False):
     """bindings.cpp:681-717."""
     act = _lib.ACT_SWIGLU if swiglu else _lib.ACT_NONE

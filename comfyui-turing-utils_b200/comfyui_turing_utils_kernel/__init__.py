@@ -13,6 +13,7 @@ from .ops import (
     turing_bf16_int4_convrot_quantize,
     turing_bf16_int4_g128_convrot_quantize,
     turing_bf16_int8_convrot_quantize,
+    turing_bf16_int8_convrot_quantize_b128,
     turing_codebook_w4a8_linear,
     turing_convrot_int8_linear,
     turing_dequantize_int8_bf16,
@@ -39,6 +40,7 @@ __all__ = [
     "turing_bf16_int4_convrot_quantize",
     "turing_bf16_int4_g128_convrot_quantize",
     "turing_bf16_int8_convrot_quantize",
+    "turing_bf16_int8_convrot_quantize_b128",
     "turing_codebook_w4a8_linear",
     "turing_convrot_int8_linear",
     "turing_dequantize_int8_bf16",

@@ -31,6 +31,7 @@ SIGNATURES = {
     "ctu_last_error": (ctypes.c_char_p, []),
     "ctu_get_device_error": (_i32, [_i32, ctypes.POINTER(ctypes.c_uint32), _i32]),
     "ctu_convrot_quantize": (_i32, [_vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp]),
+    "ctu_convrot_quantize_b128": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "ctu_convrot_quantize_staged": (_i32, [_vp, _i64, _i64, _i32, _i32, _i32, _vp, _vp, _vp]),
     "ctu_swiglu_int8_convrot_quantize_scaled": (_i32, [_vp, _i64, _i64, _i32, _vp, _vp, _vp]),
     "ctu_codebook_w4a8_linear": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),

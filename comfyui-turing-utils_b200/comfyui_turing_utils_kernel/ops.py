@@ -105,6 +105,20 @@ def _turing_int8_linear_fake(activation, weight, activation_scale, weight_scale,
     return torch.empty((activation.size(0), weight.size(0)), dtype=torch.bfloat16, device=activation.device)
 
 
+@torch.library.custom_op("turing_utils::bf16_int8_convrot_quantize_b128", mutates_args=())
+def turing_bf16_int8_convrot_quantize_b128(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """ConvRot int8 quantize with rotation block 128 (no reference op: the reference's
+    quantizers take block 256 only; the block-128 rotation is defined in ctu_b200.h)."""
+    _require_cuda(x, "block-128 ConvRot")
+    return _C.bf16_int8_convrot_quantize_b128(x.contiguous())
+
+
+@turing_bf16_int8_convrot_quantize_b128.register_fake
+def _turing_bf16_int8_convrot_quantize_b128_fake(x):
+    return (torch.empty_like(x, dtype=torch.int8),
+            torch.empty((x.size(0), 1), dtype=torch.float32, device=x.device))
+
+
 @torch.library.custom_op("turing_utils::convrot_int8_linear", mutates_args=())
 def turing_convrot_int8_linear(
     x: torch.Tensor,

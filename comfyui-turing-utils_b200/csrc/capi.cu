@@ -622,6 +622,49 @@ int run_quantize(const void *x, int64_t rows, int64_t k, int act, int bits, int8
                      : launch_quant<kActGelu, 4>(map, args, plan, q, stream);
 }
 
+// Rotation block 128 (plain int8 rows): the warp-row kernel up to 4 * kW8MaxGroupsPerTeam
+// groups a row, the multi-group kernel beyond, both in their block-128 form.
+int run_quantize_b128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *scales, uint32_t *err,
+                      const DeviceQuery &q, cudaStream_t stream) {
+    if (int rc = check_quantize_args(x, rows, k, CTU_ACT_NONE, 8, codes, scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    using ctu::rot::kActNone;
+    QuantPlan plan;
+    QuantKernel kernel = nullptr;
+    const int groups = static_cast<int>(k / 256);
+    if (groups <= 4 * ctu::rot::kW8MaxGroupsPerTeam && plan_quant_w8(k, CTU_ACT_NONE, q.smem_optin, &plan)) {
+        switch (plan.groups_per_team) {
+        case 1: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 1, true>; break;
+        case 2: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 2, true>; break;
+        case 3: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 3, true>; break;
+        case 4: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 4, true>; break;
+        case 5: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 5, true>; break;
+        default: kernel = ctu::rot::convrot_quant_w8_kernel<kActNone, 8, 6, true>; break;
+        }
+    } else if (plan_quant_rows(k, CTU_ACT_NONE, q.smem_optin, kQuantG8, &plan, groups <= 24 ? 1 : 2)) {
+        kernel = plan.groups_per_team == 2 ? ctu::rot::convrot_quant_g8_kernel<kActNone, 8, 2, false, true>
+                                           : ctu::rot::convrot_quant_g8_kernel<kActNone, 8, 1, false, true>;
+    } else {
+        return fail(CTU_ERR_UNSUPPORTED, "the block-128 ConvRot quantizer takes rows of at most %d columns",
+                    256 * 4 * 2 * (ctu::rot::kG8MaxThreads / 32));
+    }
+    CUtensorMap map;
+    if (int rc = encode_2d(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, x, 64, static_cast<uint64_t>(rows) * k / 64, 64,
+                           static_cast<uint32_t>(plan.box_rows)))
+        return rc;
+    ctu::rot::QuantArgs args{};
+    args.x = x;
+    args.codes = codes;
+    args.scales = scales;
+    args.err = err;
+    args.m = static_cast<int>(rows);
+    args.k = static_cast<int>(k);
+    args.rows_per_batch = plan.rows_per_batch;
+    args.box_rows = plan.box_rows;
+    args.copies = plan.copies;
+    return launch_quant_kernel(kernel, map, args, plan, q, stream);
+}
+
 int run_int8_linear(const int8_t *a, const int8_t *w, const float *a_scale, const float *w_scale,
                     int64_t w_scale_count, const float *bias, void *out, int64_t m, int64_t n, int64_t k,
                     uint32_t *err, const DeviceQuery &q, cudaStream_t stream) {
@@ -865,6 +908,15 @@ int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act, int bi
     if (int rc = device_info(&dev)) return rc;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     return run_quantize(x, rows, k, act, bits, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_convrot_quantize_b128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *scales, void *stream) {
+    if (int rc = check_quantize_args(x, rows, k, CTU_ACT_NONE, 8, codes, scales)) return rc;
+    if (rows == 0) return CTU_OK;
+    DeviceInfo dev;
+    if (int rc = device_info(&dev)) return rc;
+    DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
+    return run_quantize_b128(x, rows, k, codes, scales, dev.err, q, static_cast<cudaStream_t>(stream));
 }
 
 int ctu_convrot_quantize_staged(const void *x, int64_t rows, int64_t k, int act, int bits, int dtype, int8_t *codes,

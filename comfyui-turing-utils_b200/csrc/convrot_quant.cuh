@@ -153,12 +153,14 @@ inline size_t quant_w8_smem_bytes(int k, int warps) {
     return 1024 + static_cast<size_t>(warps) * quant_w8_warp_bytes(k) + 8 * static_cast<size_t>(warps);
 }
 
-template <int Act, int Bits, int kGt>
+// kBlock128 (plain rows, int8 only): the block-128 rotation (radix-2 last stage) in the
+// halved order; see ctu_convrot_quantize_b128.
+template <int Act, int Bits, int kGt, bool kBlock128 = false>
 __global__ void convrot_quant_w8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
 // kGroupScales (plain rows, int4 only): every 128 columns of a rotated row get their own
-// scale (args.group_scales) and codes; no row statistics are exchanged.
-template <int Act, int Bits, int G, bool kGroupScales = false>
+// scale (args.group_scales) and codes; no row statistics are exchanged.  kBlock128 as above.
+template <int Act, int Bits, int G, bool kGroupScales = false, bool kBlock128 = false>
 __global__ void convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args);
 
 }  // namespace rot

@@ -411,11 +411,12 @@ __device__ __forceinline__ void g8_int4_half(const uint32_t *W, float scale, boo
     }
 }
 
-template <int Act, int Bits, int G, bool kGroupScales>
+template <int Act, int Bits, int G, bool kGroupScales, bool kBlock128>
 __global__ void __launch_bounds__(kG8MaxThreads)
     convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
     static_assert(!kGroupScales || (Act == kActNone && Bits == 4), "group scales: plain rows, int4 codes");
-    constexpr bool kFold = Act != kActSwiGLU;
+    static_assert(!kBlock128 || (Act == kActNone && Bits == 8 && !kGroupScales), "block 128: plain int8 rows");
+    constexpr bool kFold = Act != kActSwiGLU && !kBlock128;
     extern __shared__ uint8_t smem_raw[];
     // Shared-space addresses (32-bit), 1024-byte aligned as the 128-byte swizzle needs.
     const uint32_t raw = smem_u32(smem_raw);
@@ -535,7 +536,7 @@ __global__ void __launch_bounds__(kG8MaxThreads)
                 f32x2 P[16];
                 if constexpr (Act == kActSwiGLU) g8_load_swiglu(in, slice_of[s], q, static_cast<uint32_t>(K / 64), P, lut);
                 else g8_load<Act>(in, ld[s], P, lut);
-                g8_rotate<true, kGroupScales>(P, wbase, rbase, W[s], amax, probe, amax_hi);
+                g8_rotate<true, kGroupScales, true, kBlock128>(P, wbase, rbase, W[s], amax, probe, amax_hi);
                 group_nan[s] = isnan(probe);
             }
             if constexpr (kGroupScales) {
@@ -656,10 +657,11 @@ __global__ void __launch_bounds__(kG8MaxThreads)
 // transpose of g8_rotate expects.  The rotation and code chains are the warp-row
 // pipeline of convrot_rowwarp.cuh.
 
-template <int Act, int Bits, int kGt>
+template <int Act, int Bits, int kGt, bool kBlock128>
 __global__ void __launch_bounds__(32 * kW8Warps)
     convrot_quant_w8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
     static_assert(Act != kActSwiGLU, "the warp-row kernel takes bf16-valued rows");
+    static_assert(!kBlock128 || (Act == kActNone && Bits == 8), "block 128: plain int8 rows");
     static_assert(kGt >= 1 && kGt <= kW8MaxGroupsPerTeam, "groups per team");
     (void)tmap_x;
     extern __shared__ uint8_t smem_raw[];
@@ -708,7 +710,7 @@ __global__ void __launch_bounds__(32 * kW8Warps)
         bool folded[kGt];
         bool any_nan = false;
         float amax = 0.0f;
-        w8_rotate_row<Act, kGt>(buf, groups, g, q, wbase, rbase, lut, W, folded, amax, any_nan);
+        w8_rotate_row<Act, kGt, kBlock128>(buf, groups, g, q, wbase, rbase, lut, W, folded, amax, any_nan);
         const int next = row + row_step;
         if (lane == 0 && next < args.m) {
             mbar_arrive_expect_tx(bar, row_bytes);
@@ -772,6 +774,23 @@ template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 4>(const __grid_co
 template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 5>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+// Rotation block 128 (plain int8 rows).
+template __global__ void convrot_quant_g8_kernel<kActNone, 8, 1, false, true>(const __grid_constant__ CUtensorMap,
+                                                                              const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 8, 2, false, true>(const __grid_constant__ CUtensorMap,
+                                                                              const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 1, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 2, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 3, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 4, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 5, true>(const __grid_constant__ CUtensorMap,
+                                                                       const QuantArgs);
+template __global__ void convrot_quant_w8_kernel<kActNone, 8, 6, true>(const __grid_constant__ CUtensorMap,
                                                                        const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2, true>(const __grid_constant__ CUtensorMap,
                                                                        const QuantArgs);

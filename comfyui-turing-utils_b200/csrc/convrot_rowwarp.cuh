@@ -82,8 +82,11 @@ __device__ __forceinline__ uint4 ld_shared_v4u(uint32_t addr) {
 // 16u + 2q + 1 of the group.  kHalves: `absmax` covers columns 0..127 (u < 8) and
 // `absmax_hi` columns 128..255; otherwise `absmax` covers the whole group.  kTeamReduce:
 // the statistics are reduced over the team's 8 lanes; otherwise each lane returns its own
-// (the warp-row pipeline reduces once per row).  All 32 lanes of the warp take part.
-template <bool kHalve, bool kHalves = false, bool kTeamReduce = true>
+// (the warp-row pipeline reduces once per row).  kBlock128 (with kHalve): rotation
+// block 128 -- the last stage is radix-2 at stride 64 scaled by RN(1/sqrt 2), each
+// 128-column half of the group on its own (this build's definition; see
+// convrot_oracle.c).  All 32 lanes of the warp take part.
+template <bool kHalve, bool kHalves = false, bool kTeamReduce = true, bool kBlock128 = false>
 __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32_t rbase, uint32_t (&W)[16],
                                           float &absmax, float &nan_probe, float &absmax_hi) {
     const f32x2 half = pk2(0.5f, 0.5f);
@@ -127,8 +130,22 @@ __device__ __forceinline__ void g8_rotate(f32x2 (&P)[16], uint32_t wbase, uint32
     }
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-        if constexpr (kHalve) butterfly2(R[w], R[w + 4], R[w + 8], R[w + 12], half);
-        else butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
+        if constexpr (kBlock128) {
+            static_assert(kHalve, "the block-128 rotation keeps the halvings");
+            // u bit 2 is column bit 6; u bit 3 (column bit 7) selects the 128-block.
+            const f32x2 c2 = pk2(0x1.6a09e6p-1f, 0x1.6a09e6p-1f);
+#pragma unroll
+            for (int blk = 0; blk < 16; blk += 8) {
+                const f32x2 t = fadd2(R[w + blk], R[w + blk + 4]);
+                const f32x2 d = fsub2(R[w + blk], R[w + blk + 4]);
+                R[w + blk] = fmul2(t, c2);
+                R[w + blk + 4] = fmul2(d, c2);
+            }
+        } else if constexpr (kHalve) {
+            butterfly2(R[w], R[w + 4], R[w + 8], R[w + 12], half);
+        } else {
+            butterfly2_unscaled(R[w], R[w + 4], R[w + 8], R[w + 12]);
+        }
     }
     float m = 0.0f, mh = 0.0f;
     f32x2 probe = pk2(0.0f, 0.0f);
@@ -232,7 +249,8 @@ __device__ __forceinline__ void w8_load(uint32_t gaddr, uint32_t q, f32x2 (&P)[1
 // -inf but no NaN, which a summed probe would flag, has an infinite absmax and takes the
 // same exact chain.)  All 32 lanes take part; the buffer is no longer read when this
 // returns and every lane has passed a __syncwarp.
-template <int Act, int kGt>
+// kBlock128: the block-128 rotation, always in the halved order (no fold).
+template <int Act, int kGt, bool kBlock128 = false>
 __device__ __forceinline__ void w8_rotate_row(uint32_t buf, int groups, uint32_t g, uint32_t q, uint32_t wbase,
                                               uint32_t rbase, const ActLut &lut, uint32_t (&W)[kGt][16],
                                               bool (&folded)[kGt], float &lane_amax, bool &any_nan) {
@@ -245,6 +263,14 @@ __device__ __forceinline__ void w8_rotate_row(uint32_t buf, int groups, uint32_t
         const uint32_t gaddr = buf + 512u * static_cast<uint32_t>(active ? grp : groups - 1);
         float ga = 0.0f, probe = 0.0f, unused = 0.0f;
         f32x2 P[16];
+        if constexpr (kBlock128) {
+            w8_load<Act>(gaddr, q, P, lut);
+            g8_rotate<true, false, false, true>(P, wbase, rbase, W[i], ga, probe, unused);
+            folded[i] = false;
+            nan_seen |= active && isnan(probe);
+            if (active) amax = fmaxf(amax, ga);
+            continue;
+        }
         w8_load<Act>(gaddr, q, P, lut);
         g8_rotate<false, false, false>(P, wbase, rbase, W[i], ga, probe, unused);
         folded[i] = !__any_sync(0xffffffffu, active && !(ga <= 3.40282347e38f));

@@ -71,6 +71,19 @@ CTU_API int ctu_convrot_quantize(const void *x, int64_t rows, int64_t k, int act
                          void *stream);
 
 /*
+ * ConvRot int8 quantize with rotation block 128 (the block size the benchmark's configs
+ * name; the reference's ops accept 256 only -- dispatch.py:765, convrot_quant.cu:24 -- so
+ * this rotation is this library's definition, parity unpinned): each 128-column block is
+ * rotated by (1/sqrt 2) H2 (x) M (x) M (x) M, evaluated as the reference's radix-4 stages at
+ * strides 1, 4, 16 followed by a radix-2 stage at stride 64,
+ *   y0 = (x0 + x1) * c,  y1 = (x0 - x1) * c,  c = RN_fp32(1/sqrt 2),
+ * then quantized with the int8 chain of ctu_convrot_quantize (per-row scale absmax / 127).
+ *   x bf16 [rows, k] (k % 256 == 0, k <= 32768), codes int8 [rows, k], scales fp32 [rows].
+ */
+CTU_API int ctu_convrot_quantize_b128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *scales,
+                                      void *stream);
+
+/*
  * The staged quantizers (replace turing_swiglu_int{8,4}_convrot_quantize and
  * turing_gelu_int{8,4}_convrot_quantize, kernel/csrc/bindings.cpp:474-633 ->
  * kernel/csrc/turing/convrot_quant.cu:184-358, 577-663): ctu_convrot_quantize with the

@@ -299,6 +299,58 @@ void ctu_oracle_epilogue(const int32_t *acc, long acc_stride, const float *a_sca
 
 
 /* ---------------------------------------------------------------------------------
+ * Rotation block 128 (the benchmark's configs[0]-[3] name it; the reference's ops accept
+ * 256 only, dispatch.py:765, convrot_quant.cu:24, so this is this build's definition and
+ * its parity is UNPINNED).  The 128-point rotation is (1/sqrt 2) H2 (x) M (x) M (x) M with
+ * M the reference's radix-4 stage (fht_stage): the three radix-4 stages at strides 1, 4
+ * and 16 exactly as the reference evaluates them, then one radix-2 stage at stride 64,
+ *   y0 = (x0 + x1) * c,  y1 = (x0 - x1) * c,  c = RN_fp32(1/sqrt 2) = 0x1.6a09e6p-1,
+ * each operation rounded to fp32.  The radix-2 stage comes last so that it stays inside
+ * one lane of the GPU kernels' layout.  A 256-column group holds two independent
+ * 128-blocks.  Codes and scales follow the int8 chain of the 256 rotation.
+ * --------------------------------------------------------------------------------- */
+#define RSQRT2_F32 0x1.6a09e6p-1f
+
+void ctu_oracle_rotate_group_b128(const float *in, float *out) {
+    float a[KGROUP], b[KGROUP];
+    fht_stage(in, a, 1);
+    fht_stage(a, b, 4);
+    fht_stage(b, a, 16);
+    for (int blk = 0; blk < KGROUP; blk += 128) {
+        for (int i = 0; i < 64; ++i) {
+            const float x0 = a[blk + i], x1 = a[blk + 64 + i];
+            out[blk + i] = (x0 + x1) * RSQRT2_F32;
+            out[blk + 64 + i] = (x0 - x1) * RSQRT2_F32;
+        }
+    }
+}
+
+int ctu_oracle_convrot_quantize_b128(const uint16_t *x, int8_t *codes, float *scales, long rows, int k) {
+    if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
+#pragma omp parallel
+    {
+        uint16_t ybits[65536];
+        float in[KGROUP], out[KGROUP];
+#pragma omp for schedule(static)
+        for (long r = 0; r < rows; ++r) {
+            const uint16_t *row = x + r * (long)k;
+            float absmax = 0.0f;
+            for (int g = 0; g < k / KGROUP; ++g) {
+                for (int i = 0; i < KGROUP; ++i) in[i] = bf16_to_f32(row[g * KGROUP + i]);
+                ctu_oracle_rotate_group_b128(in, out);
+                for (int i = 0; i < KGROUP; ++i) {
+                    ybits[g * KGROUP + i] = ctu_oracle_f32_to_bf16(out[i]);
+                    absmax = fmaxf(absmax, fabsf(out[i]));
+                }
+            }
+            quantize_row_int8(ybits, k, absmax, codes + r * (long)k, scales + r, 0);
+        }
+    }
+    return 0;
+}
+
+
+/* ---------------------------------------------------------------------------------
  * Per-group (128 along K) formats of the W4A8 / W4A4 linears.  The reference has no
  * kernel or checkpoint layout for them: its W4A4 path (dispatch.py:876-936) hands int4
  * activations to comfy-kitchen's int4_linear (source not available) with 64-column

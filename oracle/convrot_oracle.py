@@ -88,6 +88,10 @@ def _load():
         lib.ctu_oracle_convrot_quantize_int4_g128.restype = i32
         lib.ctu_oracle_grouped_epilogue.argtypes = [vp, i32, vp, vp, vp, vp, i64, i64, i32]
         lib.ctu_oracle_grouped_epilogue.restype = None
+        lib.ctu_oracle_convrot_quantize_b128.argtypes = [vp, vp, vp, i64, i32]
+        lib.ctu_oracle_convrot_quantize_b128.restype = i32
+        lib.ctu_oracle_rotate_group_b128.argtypes = [vp, vp]
+        lib.ctu_oracle_rotate_group_b128.restype = None
         lib.ctu_oracle_f32_to_bf16.argtypes = [ctypes.c_float]
         lib.ctu_oracle_f32_to_bf16.restype = ctypes.c_uint16
         _lib = lib
@@ -323,6 +327,31 @@ def convrot_quantize_int4_g128(x_bits: np.ndarray):
     if _load().ctu_oracle_convrot_quantize_int4_g128(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k) != 0:
         raise ValueError(f"unsupported ConvRot width {k}")
     return codes, scales
+
+
+RSQRT2_F32 = np.float32(0.70710676908493042)  # RN_fp32(1 / sqrt 2) = 0x1.6a09e6p-1
+
+
+def convrot_quantize_b128(x_bits: np.ndarray):
+    """Rotation block 128 (this build's definition, parity unpinned: the reference's ops
+    take 256 only): the reference's radix-4 stages at strides 1, 4, 16, then a radix-2
+    stage at stride 64, ``y0 = (x0 + x1) * c, y1 = (x0 - x1) * c`` with c = RN(1/sqrt 2),
+    then the int8 chain of the 256 rotation.  Returns ``(codes [M, K] int8, scales [M])``."""
+    x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    rows, k = x_bits.shape
+    codes = np.empty((rows, k), dtype=np.int8)
+    scales = np.empty((rows,), dtype=np.float32)
+    if _load().ctu_oracle_convrot_quantize_b128(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k) != 0:
+        raise ValueError(f"unsupported ConvRot width {k}")
+    return codes, scales
+
+
+def rotate_group_b128(values: np.ndarray) -> np.ndarray:
+    """The fp32 block-128 rotation of one 256-column group (two independent 128-blocks)."""
+    v = np.ascontiguousarray(values, dtype=np.float32).reshape(256)
+    out = np.empty(256, dtype=np.float32)
+    _load().ctu_oracle_rotate_group_b128(_ptr(v), _ptr(out))
+    return out
 
 
 def widen_uint4_zero(w_packed: np.ndarray, zeros: np.ndarray) -> np.ndarray:

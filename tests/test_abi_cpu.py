@@ -214,3 +214,34 @@ def test_oracle_grouped_formats_against_float64():
     w_deq = w4.astype(np.float64) * np.repeat(ws.astype(np.float64), 128, axis=1)
     ref = a_deq @ w_deq.T + b
     assert np.max(np.abs(out.astype(np.float64) - ref) / (np.abs(ref) + 1e-2)) < 2 ** -7
+
+
+def test_block128_oracle_is_the_kronecker_rotation():
+    # The block-128 rotation of the oracle is (1/sqrt 2) H2 (x) M (x) M (x) M on each 128-column
+    # block (M the reference's radix-4 stage): compare it with that matrix in float64.
+    import numpy as np
+
+    import convrot_oracle as oracle
+
+    m4 = 0.5 * np.array([[1, 1, 1, -1], [1, 1, -1, 1], [1, -1, 1, 1], [-1, 1, 1, 1]], dtype=np.float64)
+    h2 = np.array([[1, 1], [1, -1]], dtype=np.float64) / np.sqrt(2.0)
+    t = np.kron(h2, np.kron(m4, np.kron(m4, m4)))
+    assert np.allclose(t @ t.T, np.eye(128), atol=1e-12)  # orthogonal
+    rng = np.random.default_rng(5)
+    for _ in range(20):
+        x = (rng.standard_normal(256) * rng.choice([1e-3, 1.0, 30.0], 256)).astype(np.float32)
+        y = oracle.rotate_group_b128(x).astype(np.float64)
+        ref = np.concatenate([t @ x[:128].astype(np.float64), t @ x[128:].astype(np.float64)])
+        assert np.max(np.abs(y - ref)) <= 1e-5 * np.max(np.abs(ref))
+
+
+def test_block128_entry_rejects_bad_widths_without_a_gpu():
+    import ctypes
+
+    from comfyui_turing_utils_kernel import _lib
+
+    lib = _lib.load()
+    null = ctypes.c_void_p(0)
+    rc = lib.ctu_convrot_quantize_b128(null, 4, 384, null, null, null)
+    assert rc == _lib.CTU_ERR_INVALID_ARGUMENT and "divisible by 256" in lib.ctu_last_error().decode()
+    assert lib.ctu_convrot_quantize_b128(null, 0, 512, null, null, null) == _lib.CTU_OK
