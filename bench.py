@@ -410,11 +410,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
                                         (", int8 activations" if bits == 8 else ", int4 ConvRot activations") +
                                         "; int4 operands widened to int8 ahead of the W8A8 GEMM (M >= 512)"}
 
-        # the per-group-128 formats.  Asymmetric uint4 W4A8 (values
-        # U[0, 15], fp16 scale and uint4 zero point per 128 columns) on per-token int8
-        # ConvRot activations; W4A4 (symmetric int4 weights with fp16 per-group scales) on
-        # per-token-per-group int4 ConvRot activations.  Each step quantizes and runs all
-        # six linears, so the per-call weight widening is inside the timed work.
+        # the per-group-128 formats, with the rotation block those
+        # configs name (128).  Asymmetric uint4 W4A8 (values U[0, 15], fp16 scale and uint4
+        # zero point per 128 columns) on per-token int8 ConvRot activations; W4A4 (symmetric
+        # int4 weights with fp16 per-group scales) on per-token-per-group int4 ConvRot
+        # activations.  Each step quantizes and runs all six linears, so the per-call weight
+        # widening is inside the timed work.
         gg = torch.Generator(device=dev).manual_seed(91)
         grouped = []
         for k, n, w, _, b in layers:
@@ -426,22 +427,22 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
 
         def asym_w4a8_step():
             for x, (u4, zp, gsc, _, b) in zip(xs, grouped):
-                q, s = kops.turing_bf16_int8_convrot_quantize(x, 256)
+                q, s = kops.turing_bf16_int8_convrot_quantize_b128(x)
                 kops.turing_asym_w4a8_g128_linear(q, u4, s, gsc, zp, b)
 
         def w4a4_g128_step():
             for x, (_, _, gsc, s4, b) in zip(xs, grouped):
-                q, s = kops.turing_bf16_int4_g128_convrot_quantize(x, 256)
+                q, s = kops.turing_bf16_int4_g128_convrot_quantize(x, 128)
                 kops.turing_w4a4_g128_linear(q, s4, s, gsc, b)
 
         for name, fn, fmt in (
                 ("asym_w4a8_g128", asym_w4a8_step,
                  "configs[2]: asymmetric uint4 weights, fp16 scale + uint4 zero point per 128 columns, per-token "
-                 "int8 ConvRot activations; weights widened to (nibble - zero) int8, then the per-group CTA-pair "
+                 "int8 ConvRot activations (rotation block 128); weights widened to (nibble - zero) int8, then the per-group CTA-pair "
                  "GEMM (parity unpinned: no reference kernel)"),
                 ("w4a4_g128", w4a4_g128_step,
                  "configs[3]: symmetric int4 weights with fp16 per-group-128 scales, int4 ConvRot activations with "
-                 "per-token-per-group-128 scales; both operands sign-extended, then the per-group CTA-pair GEMM "
+                 "per-token-per-group-128 scales (rotation block 128); both operands sign-extended, then the per-group CTA-pair GEMM "
                  "(parity unpinned: no reference kernel)")):
             ms = timed(fn, max(5, min(args.steps, 20)))
             variants[name] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,

@@ -637,22 +637,25 @@ QUANT_GROUP = 128
 
 def bf16_int4_g128_convrot_quantize(input, group_size=256):
     """ConvRot rotation, then int4 codes with one scale per token and 128 columns:
-    ``(codes int8 [M, K/2] packed, scales fp32 [M, K/128])``."""
+    ``(codes int8 [M, K/2] packed, scales fp32 [M, K/128])``.  ``group_size`` is the
+    rotation block: 256 (the reference's rotation) or 128 (this library's block-128
+    rotation, see ctu_b200.h)."""
     x = input.contiguous()
     _check_cuda_2d(x, "input")
     if x.dtype != torch.bfloat16:
         raise RuntimeError("per-group INT4 ConvRot input must be bfloat16")
-    if group_size != 256:
-        raise RuntimeError("per-group INT4 ConvRot only supports group_size=256")
+    if group_size not in (128, 256):
+        raise RuntimeError("per-group INT4 ConvRot supports group_size=256 or 128")
     rows, k = x.shape
-    if rows <= 0 or k <= 0 or k % group_size != 0:
+    if rows <= 0 or k <= 0 or k % 256 != 0:
         raise RuntimeError("per-group INT4 ConvRot width must be positive and divisible by 256")
     x = _aligned(x)
     codes = torch.empty((rows, k // 2), dtype=torch.int8, device=x.device)
     scales = torch.empty((rows, k // QUANT_GROUP), dtype=torch.float32, device=x.device)
     with torch.cuda.device(x.device):
-        _lib.check(_lib.load().ctu_convrot_quantize_int4_g128(_ptr(x), rows, k, _ptr(codes), _ptr(scales),
-                                                              _stream(x.device)))
+        fn = (_lib.load().ctu_convrot_quantize_int4_g128_b128 if group_size == 128
+              else _lib.load().ctu_convrot_quantize_int4_g128)
+        _lib.check(fn(_ptr(x), rows, k, _ptr(codes), _ptr(scales), _stream(x.device)))
     return codes, scales
 
 

@@ -38,6 +38,7 @@ SIGNATURES = {
     "ctu_codebook_decode_s8": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int4_unpack_s8": (_i32, [_vp, _vp, _i64, _i64, _vp]),
     "ctu_convrot_quantize_int4_g128": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp]),
+    "ctu_convrot_quantize_int4_g128_b128": (_i32, [_vp, _i64, _i64, _vp, _vp, _vp]),
     "ctu_asym_w4a8_g128_linear": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_w4a4_g128_linear": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "ctu_int8_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp]),

@@ -1138,8 +1138,8 @@ int ctu_codebook_w4a8_linear(const int8_t *a, const int8_t *w_packed, const floa
 }
 
 // ---------------------------------------------------------------- per-group W4A8 / W4A4
-int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *group_scales,
-                                   void *stream) {
+static int quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *group_scales,
+                              void *stream, bool block128) {
     if (int rc = check_quantize_args(x, rows, k, CTU_ACT_NONE, 4, codes, group_scales)) return rc;
     if (rows == 0) return CTU_OK;
     DeviceInfo dev;
@@ -1163,9 +1163,22 @@ int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_
     args.copies = plan.copies;
     DeviceQuery q{dev.device, dev.num_sms, dev.smem_optin};
     using ctu::rot::kActNone;
-    const QuantKernel kernel = g8_groups == 2 ? ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 2, true>
-                                              : ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 1, true>;
+    const QuantKernel kernel =
+        block128 ? (g8_groups == 2 ? ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 2, true, true>
+                                   : ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 1, true, true>)
+                 : (g8_groups == 2 ? ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 2, true>
+                                   : ctu::rot::convrot_quant_g8_kernel<kActNone, 4, 1, true>);
     return launch_quant_kernel(kernel, map, args, plan, q, static_cast<cudaStream_t>(stream));
+}
+
+int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *group_scales,
+                                   void *stream) {
+    return quantize_int4_g128(x, rows, k, codes, group_scales, stream, false);
+}
+
+int ctu_convrot_quantize_int4_g128_b128(const void *x, int64_t rows, int64_t k, int8_t *codes, float *group_scales,
+                                        void *stream) {
+    return quantize_int4_g128(x, rows, k, codes, group_scales, stream, true);
 }
 
 int ctu_asym_w4a8_g128_linear(const int8_t *a, const uint8_t *w_packed, const float *a_scale,

@@ -415,7 +415,8 @@ template <int Act, int Bits, int G, bool kGroupScales, bool kBlock128>
 __global__ void __launch_bounds__(kG8MaxThreads)
     convrot_quant_g8_kernel(const __grid_constant__ CUtensorMap tmap_x, const QuantArgs args) {
     static_assert(!kGroupScales || (Act == kActNone && Bits == 4), "group scales: plain rows, int4 codes");
-    static_assert(!kBlock128 || (Act == kActNone && Bits == 8 && !kGroupScales), "block 128: plain int8 rows");
+    static_assert(!kBlock128 || (Act == kActNone && (Bits == 8) != kGroupScales),
+                  "block 128: plain rows, int8 codes or per-group int4 codes");
     constexpr bool kFold = Act != kActSwiGLU && !kBlock128;
     extern __shared__ uint8_t smem_raw[];
     // Shared-space addresses (32-bit), 1024-byte aligned as the 128-byte swizzle needs.
@@ -775,7 +776,11 @@ template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 5>(const __grid_co
 template __global__ void convrot_quant_w8_kernel<kActGelu, 4, 6>(const __grid_constant__ CUtensorMap, const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1, true>(const __grid_constant__ CUtensorMap,
                                                                        const QuantArgs);
-// Rotation block 128 (plain int8 rows).
+// Rotation block 128 (plain rows: int8, and per-group int4).
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 1, true, true>(const __grid_constant__ CUtensorMap,
+                                                                             const QuantArgs);
+template __global__ void convrot_quant_g8_kernel<kActNone, 4, 2, true, true>(const __grid_constant__ CUtensorMap,
+                                                                             const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 8, 1, false, true>(const __grid_constant__ CUtensorMap,
                                                                               const QuantArgs);
 template __global__ void convrot_quant_g8_kernel<kActNone, 8, 2, false, true>(const __grid_constant__ CUtensorMap,

@@ -241,6 +241,11 @@ CTU_API int ctu_int4_unpack_s8(const int8_t *packed, int8_t *out, int64_t rows, 
 CTU_API int ctu_convrot_quantize_int4_g128(const void *x, int64_t rows, int64_t k, int8_t *codes,
                                            float *group_scales, void *stream);
 
+/* ctu_convrot_quantize_int4_g128 with the block-128 rotation of ctu_convrot_quantize_b128
+ * (each 128-column block rotated on its own, then scaled and quantized on its own). */
+CTU_API int ctu_convrot_quantize_int4_g128_b128(const void *x, int64_t rows, int64_t k, int8_t *codes,
+                                                float *group_scales, void *stream);
+
 /*
  * Asymmetric uint4 W4A8: a int8 [m, k] with per-token a_scale [m]; w_packed uint8
  * [n, k/2] (nibbles 0..15, even column in the low nibble) with, per 128 columns, a zero

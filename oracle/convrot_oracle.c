@@ -366,7 +366,8 @@ int ctu_oracle_convrot_quantize_b128(const uint16_t *x, int8_t *codes, float *sc
  * its own: scale = max(min(absmax, FLT_MAX) / 7, 1e-10) over the group's rotated fp32
  * values, codes = clamp(rint(bf16(y) * (1/scale)), -7, 7), even column in the low
  * nibble.  packed: rows x k/2; scales: rows x k/128. */
-int ctu_oracle_convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, float *scales, long rows, int k) {
+/* block = 256: the reference's rotation; block = 128: ctu_oracle_rotate_group_b128. */
+static int convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, float *scales, long rows, int k, int block) {
     if (k <= 0 || k % KGROUP != 0 || k > 65536) return -1;
     const int groups = k / QGROUP;
 #pragma omp parallel
@@ -375,7 +376,19 @@ int ctu_oracle_convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, flo
         float *yf = (float *)malloc(sizeof(float) * (size_t)k);
 #pragma omp for schedule(static)
         for (long r = 0; r < rows; ++r) {
-            (void)rotate_row(x + r * (long)k, k, 0, ybits, yf);
+            if (block == 128) {
+                float in[KGROUP], out[KGROUP];
+                for (int g = 0; g < k / KGROUP; ++g) {
+                    for (int i = 0; i < KGROUP; ++i) in[i] = bf16_to_f32(x[r * (long)k + g * KGROUP + i]);
+                    ctu_oracle_rotate_group_b128(in, out);
+                    for (int i = 0; i < KGROUP; ++i) {
+                        ybits[g * KGROUP + i] = ctu_oracle_f32_to_bf16(out[i]);
+                        yf[g * KGROUP + i] = out[i];
+                    }
+                }
+            } else {
+                (void)rotate_row(x + r * (long)k, k, 0, ybits, yf);
+            }
             for (int g = 0; g < groups; ++g) {
                 float absmax = 0.0f;
                 for (int i = 0; i < QGROUP; ++i) absmax = fmaxf(absmax, fabsf(yf[g * QGROUP + i]));
@@ -387,6 +400,15 @@ int ctu_oracle_convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, flo
         free(yf);
     }
     return 0;
+}
+
+int ctu_oracle_convrot_quantize_int4_g128(const uint16_t *x, int8_t *packed, float *scales, long rows, int k) {
+    return convrot_quantize_int4_g128(x, packed, scales, rows, k, 256);
+}
+
+/* The same with the block-128 rotation (this build's definition, parity unpinned). */
+int ctu_oracle_convrot_quantize_int4_g128_b128(const uint16_t *x, int8_t *packed, float *scales, long rows, int k) {
+    return convrot_quantize_int4_g128(x, packed, scales, rows, k, 128);
 }
 
 /* Epilogue over per-group int32 partials acc[g][i][j] (groups x m x n), fp32 weight

@@ -88,6 +88,8 @@ def _load():
         lib.ctu_oracle_convrot_quantize_int4_g128.restype = i32
         lib.ctu_oracle_grouped_epilogue.argtypes = [vp, i32, vp, vp, vp, vp, i64, i64, i32]
         lib.ctu_oracle_grouped_epilogue.restype = None
+        lib.ctu_oracle_convrot_quantize_int4_g128_b128.argtypes = [vp, vp, vp, i64, i32]
+        lib.ctu_oracle_convrot_quantize_int4_g128_b128.restype = i32
         lib.ctu_oracle_convrot_quantize_b128.argtypes = [vp, vp, vp, i64, i32]
         lib.ctu_oracle_convrot_quantize_b128.restype = i32
         lib.ctu_oracle_rotate_group_b128.argtypes = [vp, vp]
@@ -318,13 +320,16 @@ def codebook_w4a8_linear(a, w_packed, a_scale, group_scale, channel_scale, codeb
 QGROUP = 128
 
 
-def convrot_quantize_int4_g128(x_bits: np.ndarray):
-    """Rotate, then per-token-per-group-128 int4: ``(codes [M, K/2] packed, scales [M, K/128])``."""
+def convrot_quantize_int4_g128(x_bits: np.ndarray, block: int = 256):
+    """Rotate (block 256: the reference's rotation; 128: this build's block-128 rotation),
+    then per-token-per-group-128 int4: ``(codes [M, K/2] packed, scales [M, K/128])``."""
     x_bits = np.ascontiguousarray(x_bits, dtype=np.uint16)
     rows, k = x_bits.shape
     codes = np.empty((rows, k // 2), dtype=np.int8)
     scales = np.empty((rows, max(k // QGROUP, 1)), dtype=np.float32)
-    if _load().ctu_oracle_convrot_quantize_int4_g128(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k) != 0:
+    fn = (_load().ctu_oracle_convrot_quantize_int4_g128_b128 if block == 128
+          else _load().ctu_oracle_convrot_quantize_int4_g128)
+    if fn(_ptr(x_bits), _ptr(codes), _ptr(scales), rows, k) != 0:
         raise ValueError(f"unsupported ConvRot width {k}")
     return codes, scales
 

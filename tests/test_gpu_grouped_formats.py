@@ -30,39 +30,46 @@ def K():
     assert _lib.device_error(0, clear=True) == 0, "a kernel recorded a bounded-wait timeout"
 
 
-def quantize(K, xb):
-    codes, scales = K.turing_bf16_int4_g128_convrot_quantize(to_bf16_tensor(xb).cuda(), 256)
+def quantize(K, xb, block=256):
+    codes, scales = K.turing_bf16_int4_g128_convrot_quantize(to_bf16_tensor(xb).cuda(), block)
     torch.cuda.synchronize()
     return codes.cpu().numpy(), scales.cpu().numpy()
 
 
-def check_quant(K, xb):
-    codes, scales = quantize(K, xb)
-    ref_codes, ref_scales = oracle.convrot_quantize_int4_g128(xb)
+def check_quant(K, xb, block=256):
+    codes, scales = quantize(K, xb, block)
+    ref_codes, ref_scales = oracle.convrot_quantize_int4_g128(xb, block)
     assert np.array_equal(codes, ref_codes)
     assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
 
 
+# block: the rotation block -- 256 (the reference's rotation) or 128 (this build's block-128
+# rotation, the block the benchmark's configs name).
+@pytest.mark.parametrize("block", [256, 128])
 @pytest.mark.parametrize("rows,k", [(1, 256), (7, 512), (33, 1280), (129, 5120), (64, 13824), (5, 16384),
                                     (3, 32768), (130, 768)])
-def test_group_quantizer_matches_oracle(K, rows, k):
-    check_quant(K, bf16_bits(activations(rows, k, seed=rows * 17 + k)))
+def test_group_quantizer_matches_oracle(K, rows, k, block):
+    check_quant(K, bf16_bits(activations(rows, k, seed=rows * 17 + k)), block)
 
 
+@pytest.mark.parametrize("block", [256, 128])
 @pytest.mark.parametrize("rows,k", [(12, 512), (18, 5120), (7, 13824)])
-def test_group_quantizer_special_values(K, rows, k):
-    check_quant(K, special_rows(rows, k, seed=rows + k + 5))
+def test_group_quantizer_special_values(K, rows, k, block):
+    check_quant(K, special_rows(rows, k, seed=rows + k + 5), block)
 
 
+@pytest.mark.parametrize("block", [256, 128])
 @pytest.mark.parametrize("rows,k", [(14, 512), (14, 5120), (7, 13824)])
-def test_group_quantizer_large_magnitudes(K, rows, k):
-    check_quant(K, large_rows(rows, k, seed=rows * 5 + k))
+def test_group_quantizer_large_magnitudes(K, rows, k, block):
+    check_quant(K, large_rows(rows, k, seed=rows * 5 + k), block)
 
 
 def test_group_quantizer_rejects_bad_widths(K):
     for width in (128, 300):
         with pytest.raises(RuntimeError):
             K.turing_bf16_int4_g128_convrot_quantize(torch.zeros((4, width), dtype=torch.bfloat16, device="cuda"))
+    with pytest.raises(RuntimeError):  # rotation blocks other than 256 and 128
+        K.turing_bf16_int4_g128_convrot_quantize(torch.zeros((4, 512), dtype=torch.bfloat16, device="cuda"), 64)
     with pytest.raises(TypeError):  # the op layer's dtype check, as for the other bf16 quantizers
         K.turing_bf16_int4_g128_convrot_quantize(torch.zeros((4, 256), dtype=torch.float16, device="cuda"))
 
