@@ -241,8 +241,8 @@ int plan_quant(int64_t k, int act, int bits, int smem_optin, QuantPlan *plan, bo
     const bool prefer_g8 = act != CTU_ACT_SWIGLU && k > 4096;
     // The warp-row kernel for plain and GELU rows of 4096 < K <= 6144: no CTA barrier and
     // 21 % fewer instructions than the multi-group kernel, at 12 instead of 20 warps per
-    // SM.  Measured at M = 32760, K = 5120: 142.5 us against 145.4 us back to back, 157.1
-    // against 161.7 us right after a W8A8 GEMM.
+    // SM.  Measured at M = 32760, K = 5120: 137.2 us (statistics per lane, one warp
+    // reduction per row) against 145.4 us back to back.
     const bool prefer_w8 = act != CTU_ACT_SWIGLU && k > 4096 && k <= 6144;
     if ((forced == 8 || (forced == 0 && prefer_w8)) && plan_quant_w8(k, act, smem_optin, plan)) return CTU_OK;
     if ((forced >= 5 && forced <= 7) || (forced == 0 && prefer_g8)) {
