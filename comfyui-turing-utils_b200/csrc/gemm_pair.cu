@@ -99,34 +99,6 @@ __device__ __forceinline__ void settle_inflight_copies() {
     while (globaltimer() - start < 1000000ull) __nanosleep(1000);
 }
 
-// int8 codes of a row by the reciprocal chain (rows without NaN or an infinite absmax),
-// written as 4-byte words: lanes q and q ^ 1 of a team hold columns 2q, 2q + 1 of every
-// 16-column segment u, so one shuffle per two segments gives the even lane segment u's
-// four bytes 2(q & ~1) .. 2(q & ~1) + 3 and the odd lane those of segment u + 1.
-template <int kGt>
-__device__ __forceinline__ void store_codes_paired(const uint32_t (&W)[kGt][16], const bool (&folded)[kGt],
-                                                   float scale, int groups, uint32_t g, uint32_t q, int8_t *out_row) {
-    const float rs = __bfloat162float(__float2bfloat16_rn(scale));
-    const float rcp = __frcp_rn(rs);
-    const bool odd = (q & 1u) != 0u;
-#pragma unroll
-    for (int i = 0; i < kGt; ++i) {
-        const int grp = static_cast<int>(g) + 4 * i;
-        const bool active = grp < groups;  // every lane shuffles; inactive slots store nothing
-        const float rc = rcp * (folded[i] ? 0.0625f : 1.0f);
-        const f32x2 r2 = pk2(rc, rc);
-        int8_t *base = out_row + (active ? grp : 0) * 256 + 2 * (q & ~1u) + (odd ? 16 : 0);
-#pragma unroll
-        for (int u = 0; u < 16; u += 2) {
-            const uint32_t c0 = ctu::rot::quant2_int8_fast(W[i][u], r2);
-            const uint32_t c1 = ctu::rot::quant2_int8_fast(W[i][u + 1], r2);
-            const uint32_t recv = __shfl_xor_sync(0xffffffffu, odd ? c0 : c1, 1);
-            const uint32_t word = odd ? (recv | (c1 << 16)) : (c0 | (recv << 16));
-            if (active) *reinterpret_cast<uint32_t *>(base + 16 * u) = word;
-        }
-    }
-}
-
 }  // namespace
 
 template <int kMode, int kGt>
@@ -507,12 +479,8 @@ __global__ void __cluster_dims__(2, 1, 1)
             const float scale = ctu::rot::row_scale<8>(amax, false);
             if (unpublished >= 0) publish(unpublished);
             if (lane == 0) args.qscales[row] = scale;
-            int8_t *out_row = args.qcodes + static_cast<int64_t>(row) * K;
-            if (row_nan || isinf(amax)) {  // warp-uniform: the reference's exact chain
-                ctu::rot::w8_store_codes<8, kGt>(W, folded, amax, scale, row_nan, groups, g, q, out_row);
-            } else {
-                store_codes_paired<kGt>(W, folded, scale, groups, g, q, out_row);
-            }
+            ctu::rot::w8_store_codes<8, kGt>(W, folded, amax, scale, row_nan, groups, g, q,
+                                             args.qcodes + static_cast<int64_t>(row) * K);
             unpublished = row;
             row = next;
             ++it;
