@@ -438,12 +438,12 @@ def run_b200(args, rank: int, world: int, local_rank: int) -> None:
         for name, fn, fmt in (
                 ("asym_w4a8_g128", asym_w4a8_step,
                  "configs[2]: asymmetric uint4 weights, fp16 scale + uint4 zero point per 128 columns, per-token "
-                 "int8 ConvRot activations (rotation block 128); weights widened to (nibble - zero) int8, then the per-group CTA-pair "
-                 "GEMM (parity unpinned: no reference kernel)"),
+                 "int8 ConvRot activations (rotation block 128); weights widened to (nibble - zero) int8, then the per-group GEMM "
+                 "(single-CTA 128 x 128 tiles; parity unpinned: no reference kernel)"),
                 ("w4a4_g128", w4a4_g128_step,
                  "configs[3]: symmetric int4 weights with fp16 per-group-128 scales, int4 ConvRot activations with "
-                 "per-token-per-group-128 scales (rotation block 128); both operands sign-extended, then the per-group CTA-pair GEMM "
-                 "(parity unpinned: no reference kernel)")):
+                 "per-token-per-group-128 scales (rotation block 128); both operands sign-extended, then the per-group GEMM "
+                 "(single-CTA 128 x 128 tiles; parity unpinned: no reference kernel)")):
             ms = timed(fn, max(5, min(args.steps, 20)))
             variants[name] = {"value": world * ops_per_step(m) / (ms * 1e-3) / 1e12, "unit": UNIT,
                               "ms_per_step": ms, "format": fmt}

@@ -785,21 +785,24 @@ int launch_fused_linear(const int8_t *w, const ctu::gemm::GemmArgs &base, int de
 }
 
 // ---------------------------------------------------------------------------- per-group linears
-// Clusters of two CTAs of the grouped GEMM resident at once, per device and mode.
-int g_grouped_clusters[kMaxDevices][2] = {};
+// Tiles of the per-group GEMM resident at once (CTA pairs, or single CTAs), per device,
+// mode and tiling.
+int g_grouped_units[kMaxDevices][2][2] = {};
 
-template <int kGroupMode>
-int launch_grouped_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GroupedArgs &args, int device,
-                        cudaStream_t stream) {
+template <int kGroupMode, bool kPair>
+int launch_grouped_tiling(const int8_t *a, const int8_t *w, const ctu::gemm::GroupedArgs &args, int device,
+                          cudaStream_t stream) {
+    using L = ctu::gemm::GroupedLayout<kPair>;
     using ctu::gemm::kGroupedBN;
     using ctu::gemm::kGroupK;
     CUtensorMap map_a, map_b;
     if (int rc = encode_2d(&map_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a, args.k, args.m, kGroupK, ctu::gemm::kBM))
         return rc;
-    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, kGroupK, kGroupedBN / 2))
+    if (int rc = encode_2d(&map_b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, w, args.k, args.n, kGroupK,
+                           kPair ? kGroupedBN / 2 : kGroupedBN))
         return rc;
-    constexpr auto kernel = ctu::gemm::int8_gemm_pair_grouped_kernel<kGroupMode>;
-    constexpr int smem = ctu::gemm::kGroupedSmemBytes;
+    constexpr auto kernel = ctu::gemm::int8_gemm_grouped_kernel<kGroupMode, kPair>;
+    constexpr int smem = L::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
@@ -810,27 +813,49 @@ int launch_grouped_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::Group
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    int clusters = 0;
+    cfg.numAttrs = kPair ? 1 : 0;
+    int units = 0;
     {
         std::lock_guard<std::mutex> lock(g_mutex);
-        clusters = g_grouped_clusters[device][kGroupMode];
+        units = g_grouped_units[device][kGroupMode][kPair ? 1 : 0];
     }
-    if (clusters == 0) {
+    if (units == 0) {
         int num_sms = 0;
         CTU_CUDA(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
         CTU_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
-        CTU_CUDA(cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg));
-        if (clusters <= 0) return fail(CTU_ERR_UNSUPPORTED, "no CTA pair of the grouped GEMM fits on device %d", device);
+        if (kPair) {
+            cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+            CTU_CUDA(cudaOccupancyMaxActiveClusters(&units, kernel, &cfg));
+        } else {
+            int per_sm = 0;
+            CTU_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, ctu::gemm::kGroupedThreads, smem));
+            units = per_sm * num_sms;
+        }
+        if (units <= 0) return fail(CTU_ERR_UNSUPPORTED, "no CTA of the grouped GEMM fits on device %d", device);
         std::lock_guard<std::mutex> lock(g_mutex);
-        g_grouped_clusters[device][kGroupMode] = clusters;
+        g_grouped_units[device][kGroupMode][kPair ? 1 : 0] = units;
     }
-    const int64_t tiles = ((args.m + ctu::gemm::kPairBM - 1) / ctu::gemm::kPairBM) *
+    const int64_t tiles = ((args.m + L::kTileM - 1) / L::kTileM) *
                           static_cast<int64_t>((args.n + kGroupedBN - 1) / kGroupedBN);
-    cfg.gridDim = dim3(2 * static_cast<unsigned>(std::min<int64_t>(tiles, clusters)), 1, 1);
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(tiles, units));
+    cfg.gridDim = dim3(kPair ? 2 * grid : grid, 1, 1);
     CTU_CUDA(cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, args));
     return CTU_OK;
+}
+
+// The per-group GEMM's tiling: single CTAs (128 x 128 tiles whose TMEM buffers return to
+// the MMA through a CTA-local barrier; the default) or CTA pairs (256 x 128 tiles whose
+// weight rows are staged once for both CTAs).  Bit-identical outputs; the single tiling
+// measured 8-15 % faster for the asymmetric W4A8 linear and 0-10 % for W4A4 at
+// M = 4096..32760, K, N in {5120, 13824}.  ctu_debug_set_gemm_kernel forces one: 1 single,
+// 2 pair.
+template <int kGroupMode>
+int launch_grouped_gemm(const int8_t *a, const int8_t *w, const ctu::gemm::GroupedArgs &args, int device,
+                        cudaStream_t stream) {
+    const int forced = g_gemm_kernel.load(std::memory_order_relaxed);
+    const bool pair = forced == 2;
+    return pair ? launch_grouped_tiling<kGroupMode, true>(a, w, args, device, stream)
+                : launch_grouped_tiling<kGroupMode, false>(a, w, args, device, stream);
 }
 
 // Shapes of the per-group linears: K a multiple of the 128-column group, N of 8 (16-byte

@@ -3,12 +3,18 @@
 //   W4A8: t = sum_g fma(w_scale[g][n], float(acc_g[m, n]), t);  out = bf16(fma(t, a_scale[m], bias[n]))
 //   W4A4: t = sum_g fma(float(acc_g[m, n]) * a_scale[m][g], w_scale[g][n], t);  out = bf16(t + bias[n])
 //
-// with acc_g the exact int32 product of group g's 128 columns.  A cluster of two CTAs
-// owns a 256 x 128 output tile (tcgen05.mma.cta_group::2, M = 256, N = 128): CTA r stages
-// activation rows [128 r, 128 r + 128) and weight rows [64 r, 64 r + 64) of each group.
+// with acc_g the exact int32 product of group g's 128 columns.  Two tilings share the code:
+//   single (kPair = false)  one CTA owns a 128 x 128 output tile (tcgen05.mma.cta_group::1,
+//                           M = 128, N = 128) and stages 128 activation and 128 weight rows
+//                           of each group;
+//   pair   (kPair = true)   a cluster of two CTAs owns a 256 x 128 tile (cta_group::2,
+//                           M = 256): CTA r stages activation rows [128 r, 128 r + 128)
+//                           and weight rows [64 r, 64 r + 64) of each group.
 // One ring stage is one group (four K = 32 MMAs).  Each group's partial lands in its own
-// 128-column TMEM buffer, and there are four (freed in pairs), so the MMA runs up to four
-// groups ahead of the epilogue that converts and scales them.
+// 128-column TMEM buffer, and there are four, so the MMA runs up to four groups ahead of
+// the epilogue that converts and scales them.  The single tiling stages twice the weight
+// bytes per MMA, but each buffer goes back to the MMA through a CTA-local barrier; the
+// pair's non-leader must relay its releases to the leader (see the roles below).
 //
 // Conversion without I2F.  The group's first MMA overwrites the buffer, so it holds the
 // exact int32 partial acc, |acc| <= 128 * 128 * 15 < 2^22.  For such acc the bit pattern
@@ -21,7 +27,7 @@
 // Throughput.  Per group and CTA the epilogue does one ALU and 2 (W4A8) or 3 (W4A4) fp32
 // operations on each of 128 x 128 partials: 256 cycles of the ALU pipe and 256 or 384 of
 // the 128-lane FMA pipe, against about 262 cycles for the group's MMAs (M = 256, N = 128,
-// K = 128 on two SMs).  So the
+// K = 128 on two SMs, or M = 128 on one).  So the
 // per-group control work is kept to a few instructions per warp, each warp reads its
 // partials of a group with one TMEM load (one load latency per group) straight into
 // register pairs, the scales arrive as pairs next to their use, and 16 epilogue warps (4
@@ -31,7 +37,8 @@
 //   warp 0      producer: the stage's A and B tiles (completing on the leader's `full`
 //               barrier), and the group's 128 fp32 weight scales into this CTA's scale
 //               ring (completing on its own `sc_full`).
-//   warp 1      pair TMEM allocation.  Leader: the MMA issuer; non-leader: forwards its
+//   warp 1      TMEM allocation.  Single CTA: the MMA issuer, which waits for each buffer's
+//               release on `acc_free`.  Pair leader: the MMA issuer; non-leader: forwards its
 //               epilogue's buffer releases to the leader's `acc_empty` (one remote
 //               arrival per release instead of one per epilogue warp).  The four buffers
 //               are released in pairs (groups 2i and 2i + 1 together): a remote arrival
@@ -65,14 +72,18 @@ constexpr float kMagic = 12582912.0f;
 constexpr int kGroupedTmemCols = kGroupedBuffers * kGroupedBN;  // 512
 constexpr int kLoadCols = 32;  // TMEM columns per epilogue load
 static_assert(kGroupedTmemCols == 512, "four 128-column buffers fill TMEM");
-static_assert(kGroupedBuffers < kGroupedStages, "the epilogue identifies a group's MMA completion by stage parity");
+static_assert(kGroupedBuffers < GroupedLayout<true>::kStages && kGroupedBuffers < GroupedLayout<false>::kStages,
+              "the epilogue identifies a group's MMA completion by stage parity");
+static_assert(GroupedLayout<true>::kStages <= kGroupedMaxStages && GroupedLayout<false>::kStages <= kGroupedMaxStages,
+              "ring barriers");
 
 struct GroupedSmem {
-    uint64_t full[kGroupedStages];
-    uint64_t empty[kGroupedStages];
-    // Buffer pairs {0, 1} and {2, 3}, each released once both of its groups are read.
+    uint64_t full[kGroupedMaxStages];
+    uint64_t empty[kGroupedMaxStages];
+    // Pair: buffer pairs {0, 1} and {2, 3}, each released once both of its groups are read.
     uint64_t acc_empty[kGroupedBuffers / 2];  // leader: its epilogue warps (x2) + 1 forwarded peer release
     uint64_t acc_local[kGroupedBuffers / 2];  // non-leader: its epilogue warps (x2)
+    uint64_t acc_free[kGroupedBuffers];       // single CTA: its epilogue warps, per buffer
     uint64_t sc_full[kGroupedScaleSlots];
     uint64_t sc_empty[kGroupedScaleSlots];
     uint64_t drain;
@@ -89,12 +100,12 @@ __device__ __forceinline__ void st_cluster_u32(uint32_t cluster_addr, uint32_t v
 
 struct GroupedAbort {
     volatile int *flag;
-    uint32_t peer_flag;
+    uint32_t peer_flag;  // the pair's other CTA's flag; 0 for a single CTA
     uint32_t *err;
 
     __device__ __forceinline__ void raise() const {
         *flag = 1;
-        st_cluster_u32(peer_flag, 1u);
+        if (peer_flag != 0u) st_cluster_u32(peer_flag, 1u);
     }
     __device__ __forceinline__ bool wait(uint64_t *bar, uint32_t parity, uint32_t code) const {
         if (mbar_wait(bar, parity, flag, err, code)) return true;
@@ -137,36 +148,42 @@ __device__ __forceinline__ void settle_inflight_copies_grouped() {
 
 }  // namespace
 
-template <int kGroupMode>
-__global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
-    int8_gemm_pair_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                  const __grid_constant__ CUtensorMap tmap_b, const GroupedArgs args) {
+template <int kGroupMode, bool kPair>
+__global__ void __maxnreg__(kGroupedMaxRegisters)
+    int8_gemm_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+                             const GroupedArgs args) {
+    using L = GroupedLayout<kPair>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *sA = smem;
-    uint8_t *sB = smem + kGroupedStages * kGroupedAStage;
-    GroupedSmem &S = *reinterpret_cast<GroupedSmem *>(smem + kGroupedStages * (kGroupedAStage + kGroupedBStage));
+    uint8_t *sB = smem + L::kStages * kGroupedAStage;
+    GroupedSmem &S = *reinterpret_cast<GroupedSmem *>(smem + L::kStages * (kGroupedAStage + L::kBStage));
 
-    const uint32_t rank = cluster_ctarank();
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
     const bool leader = rank == 0;
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int pair = blockIdx.x >> 1;
-    const int num_pairs = gridDim.x >> 1;
+    // "pair": this tile's owner -- a CTA pair, or a single CTA.
+    const int pair = kPair ? blockIdx.x >> 1 : blockIdx.x;
+    const int num_pairs = kPair ? gridDim.x >> 1 : gridDim.x;
     const int num_n = (args.n + kGroupedBN - 1) / kGroupedBN;
-    const int num_m = (args.m + kPairBM - 1) / kPairBM;
+    const int num_m = (args.m + L::kTileM - 1) / L::kTileM;
     const int num_tiles = num_m * num_n;
     const int nk = args.k / kGroupK;
     const int my_tiles = pair < num_tiles ? (num_tiles - 1 - pair) / num_pairs + 1 : 0;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kGroupedStages; ++s) {
+        for (int s = 0; s < L::kStages; ++s) {
             mbar_init(&S.full[s], 1);
             mbar_init(&S.empty[s], 1);
         }
-        for (int b = 0; b < kGroupedBuffers / 2; ++b) {
-            mbar_init(&S.acc_empty[b], 2 * kGroupedEpilogueWarps + 1);
-            mbar_init(&S.acc_local[b], 2 * kGroupedEpilogueWarps);
+        if constexpr (kPair) {
+            for (int b = 0; b < kGroupedBuffers / 2; ++b) {
+                mbar_init(&S.acc_empty[b], 2 * kGroupedEpilogueWarps + 1);
+                mbar_init(&S.acc_local[b], 2 * kGroupedEpilogueWarps);
+            }
+        } else {
+            for (int b = 0; b < kGroupedBuffers; ++b) mbar_init(&S.acc_free[b], kGroupedEpilogueWarps);
         }
         for (int r = 0; r < kGroupedScaleSlots; ++r) {
             mbar_init(&S.sc_full[r], 1);
@@ -177,8 +194,13 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
         fence_mbar_init();
     }
     if (warp == 1) {
-        tmem_alloc_pair(&S.tmem_base, kGroupedTmemCols);
-        tmem_relinquish_pair();
+        if constexpr (kPair) {
+            tmem_alloc_pair(&S.tmem_base, kGroupedTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(&S.tmem_base, kGroupedTmemCols);
+            tmem_relinquish();
+        }
     }
     if (warp == 0 && lane == 0) {
         prefetch_tmap(&tmap_a);
@@ -186,27 +208,27 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
     }
     tc_fence_before();
     __syncthreads();
-    cluster_sync();
+    if constexpr (kPair) cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = S.tmem_base;
-    const GroupedAbort ab{&S.abort_flag, mapa_shared(smem_u32(&S.abort_flag), rank ^ 1u), args.err};
+    const GroupedAbort ab{&S.abort_flag, kPair ? mapa_shared(smem_u32(&S.abort_flag), rank ^ 1u) : 0u, args.err};
     volatile int *abort_flag = &S.abort_flag;
 
     if (warp == 0) {
         // ------------------------------------------------------------------ producer
         if (lane == 0) {
-            const uint32_t leader_full0 = mapa_shared(smem_u32(&S.full[0]), 0u);
+            const uint32_t leader_full0 = kPair ? mapa_shared(smem_u32(&S.full[0]), 0u) : 0u;
             uint32_t j = 0;  // group steps of this pair, over all its tiles
             bool ok = true;
             for (int t = pair; t < num_tiles && ok; t += num_pairs) {
                 const int m_tile = t / num_n;
                 const int n0 = (t - m_tile * num_n) * kGroupedBN;
-                const int m0 = m_tile * kPairBM + static_cast<int>(rank) * kBM;
-                const int w0 = n0 + static_cast<int>(rank) * (kGroupedBN / 2);
+                const int m0 = m_tile * L::kTileM + static_cast<int>(rank) * kBM;
+                const int w0 = n0 + static_cast<int>(rank) * (kGroupedBN / 2);  // rank 0 for a single CTA
                 const uint32_t sc_bytes = static_cast<uint32_t>(min(kGroupedBN, args.n - n0)) * 4u;
                 for (int kb = 0; kb < nk; ++kb, ++j) {
-                    const uint32_t s = j % kGroupedStages;
-                    const uint32_t ph = (j / kGroupedStages) & 1u;
+                    const uint32_t s = j % L::kStages;
+                    const uint32_t ph = (j / L::kStages) & 1u;
                     const uint32_t r = j % kGroupedScaleSlots;
                     const uint32_t rph = (j / kGroupedScaleSlots) & 1u;
                     if (!ab.wait(&S.sc_empty[r], rph ^ 1u, kErrTimeoutEmpty)) {
@@ -220,10 +242,16 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                         ok = false;
                         break;
                     }
-                    if (leader) mbar_arrive_expect_tx(&S.full[s], 2 * (kGroupedAStage + kGroupedBStage));
-                    const uint32_t leader_full = leader_full0 + s * static_cast<uint32_t>(sizeof(uint64_t));
-                    tma_load_2d_pair(sA + s * kGroupedAStage, &tmap_a, kb * kGroupK, m0, leader_full);
-                    tma_load_2d_pair(sB + s * kGroupedBStage, &tmap_b, kb * kGroupK, w0, leader_full);
+                    if constexpr (kPair) {
+                        if (leader) mbar_arrive_expect_tx(&S.full[s], 2 * (kGroupedAStage + L::kBStage));
+                        const uint32_t leader_full = leader_full0 + s * static_cast<uint32_t>(sizeof(uint64_t));
+                        tma_load_2d_pair(sA + s * kGroupedAStage, &tmap_a, kb * kGroupK, m0, leader_full);
+                        tma_load_2d_pair(sB + s * L::kBStage, &tmap_b, kb * kGroupK, w0, leader_full);
+                    } else {
+                        mbar_arrive_expect_tx(&S.full[s], kGroupedAStage + L::kBStage);
+                        tma_load_2d(sA + s * kGroupedAStage, &tmap_a, kb * kGroupK, m0, &S.full[s]);
+                        tma_load_2d(sB + s * L::kBStage, &tmap_b, kb * kGroupK, w0, &S.full[s]);
+                    }
                 }
             }
             if (!ok || *abort_flag) settle_inflight_copies_grouped();
@@ -232,44 +260,64 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
         if (leader) {
             // -------------------------------------------------------------- MMA issuer
             if (lane == 0) {
-                constexpr uint32_t idesc = idesc_i8(kPairBM, kGroupedBN);
+                constexpr uint32_t idesc = idesc_i8(L::kTileM, kGroupedBN);
                 uint32_t j = 0;
                 bool ok = true;
                 for (int t = pair; t < num_tiles && ok; t += num_pairs) {
                     for (int kb = 0; kb < nk; ++kb, ++j) {
                         const uint32_t pb = j % kGroupedBuffers;
                         const uint32_t use = j / kGroupedBuffers;
-                        // Completion `use - 1` of acc_empty[pb]: the epilogue's release of the
-                        // buffer's previous group in both CTAs (a fresh barrier passes use 0).
-                        // (Buffers are released in pairs: the first of a pair waits for both.)
-                        if ((pb & 1u) == 0u &&
-                            !ab.wait_cluster(&S.acc_empty[pb >> 1], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
+                        // Completion `use - 1` of the buffer's release barrier: the epilogue's
+                        // release of the buffer's previous group (in both CTAs of a pair; a fresh
+                        // barrier passes use 0).  A pair releases buffers in pairs: the first of
+                        // a pair waits for both.
+                        if constexpr (kPair) {
+                            if ((pb & 1u) == 0u &&
+                                !ab.wait_cluster(&S.acc_empty[pb >> 1], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
+                                ok = false;
+                                break;
+                            }
+                        } else if (!ab.wait(&S.acc_free[pb], (use & 1u) ^ 1u, kErrTimeoutAccumFree)) {
                             ok = false;
                             break;
                         }
-                        const uint32_t s = j % kGroupedStages;
-                        if (!ab.wait(&S.full[s], (j / kGroupedStages) & 1u, kErrTimeoutFull)) {
+                        const uint32_t s = j % L::kStages;
+                        if (!ab.wait(&S.full[s], (j / L::kStages) & 1u, kErrTimeoutFull)) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint32_t a_addr = smem_u32(sA + s * kGroupedAStage);
-                        const uint32_t b_addr = smem_u32(sB + s * kGroupedBStage);
+                        const uint32_t b_addr = smem_u32(sB + s * L::kBStage);
                         const uint32_t d_tmem = tmem_base + pb * kGroupedBN;
 #pragma unroll
                         for (int k = 0; k < kGroupK / kUmmaK; ++k) {  // the first overwrites the buffer
-                            mma_i8_pair(d_tmem, smem_desc_sw128(a_addr + k * kUmmaK),
-                                        smem_desc_sw128(b_addr + k * kUmmaK), idesc, k != 0 ? 1u : 0u);
+                            const uint64_t a_desc = smem_desc_sw128(a_addr + k * kUmmaK);
+                            const uint64_t b_desc = smem_desc_sw128(b_addr + k * kUmmaK);
+                            if constexpr (kPair) {
+                                mma_i8_pair(d_tmem, a_desc, b_desc, idesc, k != 0 ? 1u : 0u);
+                            } else {
+                                mma_i8(d_tmem, a_desc, b_desc, idesc, k != 0 ? 1u : 0u);
+                            }
                         }
-                        // One commit per group: its arrival on empty[s] (both CTAs) frees the
-                        // stage for the producer and tells the epilogue the partial is ready.
-                        mma_commit_pair_both(&S.empty[s]);
+                        // One commit per group: its arrival on empty[s] (both CTAs of a pair)
+                        // frees the stage for the producer and tells the epilogue the partial
+                        // is ready.
+                        if constexpr (kPair) {
+                            mma_commit_pair_both(&S.empty[s]);
+                        } else {
+                            mma_commit(&S.empty[s]);
+                        }
                     }
                 }
-                mma_commit_pair_local(&S.drain);
+                if constexpr (kPair) {
+                    mma_commit_pair_local(&S.drain);
+                } else {
+                    mma_commit(&S.drain);
+                }
                 mbar_wait(&S.drain, 0u, nullptr, args.err, kErrTimeoutDrain);
             }
-        } else if (lane == 0) {
+        } else if (kPair && lane == 0) {
             // -------------------------------------------------------------- release forwarder
             const uint32_t leader_acc_empty0 = mapa_shared(smem_u32(&S.acc_empty[0]), 0u);
             const uint32_t releases = static_cast<uint32_t>(my_tiles) * static_cast<uint32_t>(nk);
@@ -287,7 +335,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
         const int col0 = ((warp - 2) >> 2) * kGroupedEpilogueCols;
         const int row = quad * 32 + lane;
         const uint32_t col_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(col0);
-        uint64_t *release0 = leader ? &S.acc_empty[0] : &S.acc_local[0];
+        uint64_t *release0 = !kPair ? &S.acc_free[0] : leader ? &S.acc_empty[0] : &S.acc_local[0];
         const f32x2 magic2 = pk2(kMagic, kMagic);
 
         bool alive = true;
@@ -296,7 +344,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
         for (int t = pair; t < num_tiles; t += num_pairs) {
             const int m_tile = t / num_n;
             const int n0 = (t - m_tile * num_n) * kGroupedBN;
-            const int m = m_tile * kPairBM + static_cast<int>(rank) * kBM + row;
+            const int m = m_tile * L::kTileM + static_cast<int>(rank) * kBM + row;
             const bool row_ok = m < args.m;
             named_barrier(1, 32 * kGroupedEpilogueWarps);  // the previous tile's bias reads are done
             for (int c = threadIdx.x - 64; c < kGroupedBN; c += 32 * kGroupedEpilogueWarps) {
@@ -323,13 +371,12 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                 const uint32_t pb = j % kGroupedBuffers;
                 float gs2 = 0.0f;
                 if constexpr (kGroupMode == kGroupW4A4) gs2 = (row_ok && kb + 2 < nk) ? a_row[kb + 2] : 0.0f;
-                // The group's MMAs are complete when stage j % kGroupedStages completes its
-                // phase j / kGroupedStages.  The MMA runs at most kGroupedBuffers groups
-                // ahead of this loop (buffers are freed in pairs), fewer than the ring depth,
-                // so that phase is the current or the previous one of the barrier and its
-                // parity identifies it.
-                const bool ok = mbar_wait(&S.empty[j % kGroupedStages], (j / kGroupedStages) & 1u, abort_flag,
-                                          args.err, kErrTimeoutAccum) &&
+                // The group's MMAs are complete when stage j % kStages completes its phase
+                // j / kStages.  The MMA runs at most kGroupedBuffers groups ahead of this
+                // loop, fewer than the ring depth, so that phase is the current or the
+                // previous one of the barrier and its parity identifies it.
+                const bool ok = mbar_wait(&S.empty[j % L::kStages], (j / L::kStages) & 1u, abort_flag, args.err,
+                                          kErrTimeoutAccum) &&
                                 mbar_wait(&S.sc_full[r], rph, abort_flag, args.err, kErrTimeoutFull);
                 alive = __all_sync(0xffffffffu, ok);
                 if (!alive) {
@@ -349,7 +396,7 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
                     if (h == kGroupedEpilogueCols / kLoadCols - 1) {
                         tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(release0 + (pb >> 1));
+                        if (lane == 0) mbar_arrive(release0 + (kPair ? pb >> 1 : pb));
                     }
 #pragma unroll
                     for (int i = 0; i < kLoadCols / 4; ++i) {
@@ -413,19 +460,26 @@ __global__ void __cluster_dims__(2, 1, 1) __maxnreg__(kGroupedMaxRegisters)
 
     tc_fence_before();
     __syncthreads();
-    cluster_sync();
+    if constexpr (kPair) cluster_sync();
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc_pair(tmem_base, kGroupedTmemCols);
+        if constexpr (kPair) {
+            tmem_dealloc_pair(tmem_base, kGroupedTmemCols);
+        } else {
+            tmem_dealloc(tmem_base, kGroupedTmemCols);
+        }
     }
 }
 
-template __global__ void int8_gemm_pair_grouped_kernel<kGroupAsymW4A8>(const __grid_constant__ CUtensorMap,
-                                                                       const __grid_constant__ CUtensorMap,
-                                                                       const GroupedArgs);
-template __global__ void int8_gemm_pair_grouped_kernel<kGroupW4A4>(const __grid_constant__ CUtensorMap,
-                                                                   const __grid_constant__ CUtensorMap,
-                                                                   const GroupedArgs);
+#define CTU_GROUPED_GEMM(mode, pair)                                                                      \
+    template __global__ void int8_gemm_grouped_kernel<mode, pair>(const __grid_constant__ CUtensorMap,  \
+                                                                  const __grid_constant__ CUtensorMap,  \
+                                                                  const GroupedArgs);
+CTU_GROUPED_GEMM(kGroupAsymW4A8, false)
+CTU_GROUPED_GEMM(kGroupAsymW4A8, true)
+CTU_GROUPED_GEMM(kGroupW4A4, false)
+CTU_GROUPED_GEMM(kGroupW4A4, true)
+#undef CTU_GROUPED_GEMM
 
 }  // namespace gemm
 }  // namespace ctu

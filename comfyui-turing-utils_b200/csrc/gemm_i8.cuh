@@ -143,9 +143,11 @@ __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a
 // ---------------------------------------------------------------------------
 // Per-group (128 along K) linears: every 128-column group of K has its own weight scale
 // (and, for W4A4, its own activation scale per token), so each group's int32 partial is
-// converted and scaled on its own.  A CTA pair computes a 256 x 128 output tile; one
-// ring stage is one group; four 128-column TMEM buffers hold the partials of four
-// consecutive groups (freed in pairs), so the MMA runs up to four groups ahead of the epilogue.
+// converted and scaled on its own.  One ring stage is one group; four 128-column TMEM
+// buffers hold the partials of four consecutive groups, so the MMA runs up to four groups
+// ahead of the epilogue.  Two tilings: a single CTA per 128 x 128 output tile
+// (cta_group::1, each buffer released by its own epilogue warps), or a CTA pair per
+// 256 x 128 tile (cta_group::2, buffers freed in pairs through the peer's relay).
 //
 //   kGroupAsymW4A8: t += w_scale[g][n] * float(acc_g);  out = bf16(fma(t, a_scale[m], bias[n]))
 //   kGroupW4A4:     t += (float(acc_g) * a_scale[m][g]) * w_scale[g][n];  out = bf16(t + bias[n])
@@ -156,8 +158,7 @@ __global__ void int8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a
 enum GroupMode : int { kGroupAsymW4A8 = 0, kGroupW4A4 = 1 };
 
 constexpr int kGroupK = kBK;           // K columns per group = one ring stage
-constexpr int kGroupedBN = 128;        // output columns per pair tile
-constexpr int kGroupedStages = 8;      // ring depth (groups)
+constexpr int kGroupedBN = 128;        // output columns per tile
 constexpr int kGroupedBuffers = 4;     // TMEM partial buffers of kGroupedBN columns
 constexpr int kGroupedScaleSlots = 12; // weight-scale ring (one group's kGroupedBN scales per slot)
 #ifndef CTU_GROUPED_EPILOGUE_WARPS
@@ -171,11 +172,19 @@ constexpr int kGroupedThreads = 64 + 32 * kGroupedEpilogueWarps;
 // A warp's registers come from its scheduler's quarter of the register file (16384), and
 // the busiest scheduler holds ceil(warps / 4) warps (18 warps: 5, so 96 registers a thread).
 constexpr int kGroupedMaxRegisters = (16384 / (((kGroupedThreads / 32 + 3) / 4) * 32)) / 8 * 8;
-constexpr int kGroupedAStage = kBM * kGroupK;                  // 16 KB
-constexpr int kGroupedBStage = (kGroupedBN / 2) * kGroupK;     // 8 KB: each CTA stages half the weight rows
+constexpr int kGroupedAStage = kBM * kGroupK;  // 16 KB: 128 activation rows of one group
 constexpr int kGroupedBookkeepingBytes = 12288;
-constexpr int kGroupedSmemBytes = 1024 + kGroupedStages * (kGroupedAStage + kGroupedBStage) + kGroupedBookkeepingBytes;
-static_assert(kGroupedSmemBytes <= 232448, "grouped GEMM exceeds the shared memory of one SM");
+
+// Per-tiling layout: output rows per tile, ring depth and weight rows staged per CTA.
+template <bool kPair>
+struct GroupedLayout {
+    static constexpr int kTileM = kPair ? kPairBM : kBM;
+    static constexpr int kBStage = (kPair ? kGroupedBN / 2 : kGroupedBN) * kGroupK;  // 8 KB (half each) or 16 KB
+    static constexpr int kStages = kPair ? 8 : 6;
+    static constexpr int kSmemBytes = 1024 + kStages * (kGroupedAStage + kBStage) + kGroupedBookkeepingBytes;
+    static_assert(kSmemBytes <= 232448, "grouped GEMM exceeds the shared memory of one SM");
+};
+constexpr int kGroupedMaxStages = 8;
 
 struct GroupedArgs {
     const float *a_scale;     // kGroupAsymW4A8: [m]; kGroupW4A4: [m, k / 128]
@@ -186,11 +195,12 @@ struct GroupedArgs {
     int m, n, k;
 };
 
-// a int8 [m, k], w int8 [n, k] (tensor maps with a 128 x 128 and a 64 x 128 box, 128-byte
-// swizzle); launched as clusters of two CTAs of kGroupedThreads threads.
-template <int kGroupMode>
-__global__ void int8_gemm_pair_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                                              const __grid_constant__ CUtensorMap tmap_b, const GroupedArgs args);
+// a int8 [m, k], w int8 [n, k] (tensor maps with a 128 x 128 box for A and a
+// (kGroupedBN or kGroupedBN / 2) x 128 box for B, 128-byte swizzle).  kPair: launched as
+// clusters of two CTAs; otherwise one CTA per SM.  kGroupedThreads threads per CTA.
+template <int kGroupMode, bool kPair>
+__global__ void int8_gemm_grouped_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                                         const __grid_constant__ CUtensorMap tmap_b, const GroupedArgs args);
 
 }  // namespace gemm
 }  // namespace ctu

@@ -340,8 +340,9 @@ CTU_API int ctu_debug_gemm_injected_timeout(const int8_t *a, const int8_t *w, in
 
 /* Test hook (no counterpart in the reference): choose the integer GEMM kernel for
  * every later call in this process.  0 = per problem (default: the CTA-pair kernel
- * when M > 128), 1 = single-CTA kernel, 2 = CTA-pair kernel.  Returns the previous
- * selector, or a negative error code. */
+ * when M > 128; the single-CTA tiling for the per-group-128 linears), 1 = single-CTA
+ * kernel, 2 = CTA-pair kernel (both also for the per-group-128 linears).  Returns the
+ * previous selector, or a negative error code. */
 CTU_API int ctu_debug_set_gemm_kernel(int which);
 
 /* Test hook (no counterpart in the reference): how ctu_convrot_int8_linear runs.  0 = per

@@ -30,6 +30,17 @@ def K():
     assert _lib.device_error(0, clear=True) == 0, "a kernel recorded a bounded-wait timeout"
 
 
+@pytest.fixture(params=["single", "pair"])
+def tiling(request):
+    """The per-group GEMM's tiling, forced through the GEMM-kernel test hook: 128 x 128
+    tiles on single CTAs (1) or 256 x 128 tiles on CTA pairs (2)."""
+    from comfyui_turing_utils_kernel import _lib
+
+    prev = _lib.load().ctu_debug_set_gemm_kernel(1 if request.param == "single" else 2)
+    yield request.param
+    _lib.load().ctu_debug_set_gemm_kernel(prev)
+
+
 def quantize(K, xb, block=256):
     codes, scales = K.turing_bf16_int4_g128_convrot_quantize(to_bf16_tensor(xb).cuda(), block)
     torch.cuda.synchronize()
@@ -92,7 +103,7 @@ def int8_activations(m, k, seed):
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
 @pytest.mark.parametrize("with_bias", [True, False])
-def test_asym_w4a8_matches_oracle(K, m, n, k, with_bias):
+def test_asym_w4a8_matches_oracle(K, tiling, m, n, k, with_bias):
     a, a_scale = int8_activations(m, k, seed=m + n + k)
     packed, zeros, scales, bias = weights(n, k, seed=3 * n + k)
     bias = bias if with_bias else None
@@ -106,7 +117,7 @@ def test_asym_w4a8_matches_oracle(K, m, n, k, with_bias):
 
 @pytest.mark.parametrize("m,n,k", SHAPES)
 @pytest.mark.parametrize("with_bias", [True, False])
-def test_w4a4_matches_oracle(K, m, n, k, with_bias):
+def test_w4a4_matches_oracle(K, tiling, m, n, k, with_bias):
     g = torch.Generator().manual_seed(m * 7 + k)
     a_packed = torch.randint(-128, 128, (m, k // 2), generator=g, dtype=torch.int32).to(torch.int8)
     w_packed = torch.randint(-128, 128, (n, k // 2), generator=g, dtype=torch.int32).to(torch.int8)
@@ -121,7 +132,7 @@ def test_w4a4_matches_oracle(K, m, n, k, with_bias):
     assert np.array_equal(bf16_bits(out), ref)
 
 
-def test_w4a4_end_to_end_from_bf16_rows(K):
+def test_w4a4_end_to_end_from_bf16_rows(K, tiling):
     m, n, k = 300, 264, 5120
     xb = bf16_bits(activations(m, k, seed=11))
     codes, scales = K.turing_bf16_int4_g128_convrot_quantize(to_bf16_tensor(xb).cuda())
@@ -149,9 +160,9 @@ def test_grouped_linears_reject_bad_shapes(K):
 
 
 @pytest.mark.parametrize("k,n", [(5120, 5120), (13824, 5120)], ids=["k5120", "k13824"])
-def test_full_size_grouped_linears_on_sampled_rows(K, k, n):
+def test_full_size_grouped_linears_on_sampled_rows(K, tiling, k, n):
     # Wan-14B shapes (M = 32760); rows are independent, so the oracle checks a sample of
-    # rows spread over every pair tile position, bit for bit.
+    # rows spread over every tile position, bit for bit.
     m = 32760
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(k)
