@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import convrot_oracle as oracle
-from test_gpu_quant_variants import activations, bf16_bits, large_rows, special_rows, to_bf16_tensor
+from test_gpu_quant_variants import activations, bf16_bits, large_rows, special_rows, tiny_rows, to_bf16_tensor
 
 pytestmark = pytest.mark.gpu
 
@@ -50,6 +50,11 @@ def test_special_values(K, rows, k):
 @pytest.mark.parametrize("rows,k", [(14, 512), (14, 5120), (7, 13824)])
 def test_large_magnitudes(K, rows, k):
     check(K, large_rows(rows, k, seed=rows * 3 + k + 1))
+
+
+@pytest.mark.parametrize("rows,k", [(16, 512), (16, 5120), (8, 13824)])
+def test_scale_floor_rows(K, rows, k):
+    check(K, tiny_rows(rows, k, seed=rows * 5 + k + 1))
 
 
 def test_differs_from_block_256(K):

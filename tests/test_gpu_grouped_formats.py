@@ -12,7 +12,7 @@ import pytest
 import torch
 
 import convrot_oracle as oracle
-from test_gpu_quant_variants import activations, bf16_bits, large_rows, special_rows, to_bf16_tensor
+from test_gpu_quant_variants import activations, bf16_bits, large_rows, special_rows, tiny_rows, to_bf16_tensor
 
 pytestmark = pytest.mark.gpu
 
@@ -73,6 +73,13 @@ def test_group_quantizer_special_values(K, rows, k, block):
 @pytest.mark.parametrize("rows,k", [(14, 512), (14, 5120), (7, 13824)])
 def test_group_quantizer_large_magnitudes(K, rows, k, block):
     check_quant(K, large_rows(rows, k, seed=rows * 5 + k), block)
+
+
+@pytest.mark.parametrize("block", [256, 128])
+@pytest.mark.parametrize("rows,k", [(16, 512), (16, 5120), (8, 13824)])
+def test_group_quantizer_scale_floor_rows(K, rows, k, block):
+    # Per-group scales meet their 1e-10 floor in the tiny rows' groups.
+    check_quant(K, tiny_rows(rows, k, seed=rows * 7 + k), block)
 
 
 def test_group_quantizer_rejects_bad_widths(K):

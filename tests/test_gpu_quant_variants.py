@@ -133,6 +133,32 @@ def large_rows(rows, k, seed):
     return bf16_bits(x.to(torch.bfloat16))
 
 
+def tiny_rows(rows, k, seed):
+    """Rows small enough that the scale's floor decides it (int8: 1e-30, so a row absmax
+    below 127e-30; int4: 1e-10, below 7e-10) while their codes are still non-zero, and
+    rows mixing one such group with ordinary ones.  All values stay normal bf16."""
+    x = activations(rows, k, seed).float()
+    mags = [1e-28, 1e-29, 5e-29, 3e-31, 5e-10, 1e-36, 3e-10, 3e-11]
+    for r in range(rows):
+        m = mags[r % len(mags)]
+        if r % 2 == 0:
+            x[r] = x[r] / x[r].abs().max() * m
+        else:  # only the first group of the row is tiny
+            x[r, :256] = x[r, :256] / x[r, :256].abs().max() * m
+    return bf16_bits(x.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("rows,k", [(16, 512), (16, 5120), (8, 13824)])
+def test_scale_floor_rows(C, kernel, rows, k, bits):
+    xb = tiny_rows(rows, k, seed=rows * 5 + k)
+    codes, scales = run_quant(C, xb, bits)
+    ref_codes, ref_scales = oracle.convrot_quantize(xb, bits)
+    assert np.count_nonzero(ref_codes[0::2]) > 0  # floored rows with non-zero codes
+    assert np.array_equal(codes, ref_codes)
+    assert np.array_equal(scales.view(np.uint32), ref_scales.view(np.uint32))
+
+
 @pytest.mark.parametrize("bits", [8, 4])
 @pytest.mark.parametrize("rows,k", [(14, 512), (14, 5120), (7, 13824)])
 def test_large_magnitudes(C, kernel, rows, k, bits):
