@@ -10,6 +10,8 @@ kernels on the same inputs as the reference's row-buffer quantizer
 not a sample.  The fused tanh-GELU quantizer of the FFN-down input is checked the same
 way at full size, against both the reference's row-buffer kernel
 (convrot_quant.cu:715-745) and its staged two-kernel path (convrot_quant.cu:184-358).
+The W8A8 epilogue is also compared with the reference's at non-finite, overflowing,
+subnormal and signed-zero scales and biases.
 """
 
 import sys
@@ -163,3 +165,38 @@ def test_gelu_quantizer_full_size_against_reference_kernels(K, ref):
     codes, scales = K.turing_gelu_int8_convrot_quantize(x, 256)
     assert torch.equal(codes, st_codes), "staged GELU int8 codes differ"
     assert _same_scales(scales, st_scales), "staged GELU scales differ"
+
+
+@needs_ref
+def test_linear_epilogue_extremes_against_reference_kernel(K, ref):
+    """Scales and biases at the edges of fp32 -- inf, NaN, 3e38, subnormal, +-0 -- and
+    all-zero activation rows (0 x inf): outputs that overflow to inf, become NaN, land
+    in the bf16 subnormal range or keep a zero's sign, through both GEMM kernels and the
+    reference's W8A8 GEMM (w4a8.cu:1185-1219), bit for bit."""
+    mg, lib = ref
+    p = mg.p
+    m, n, k = 300, 264, 512
+    g = torch.Generator(device="cuda").manual_seed(77)
+    a = torch.randint(-127, 128, (m, k), generator=g, device="cuda", dtype=torch.int8)
+    a[20:22] = 0
+    w = torch.randint(-127, 128, (n, k), generator=g, device="cuda", dtype=torch.int8)
+    a_scale = torch.rand((m,), generator=g, device="cuda") * 0.02 + 1e-3
+    a_scale[5:10] = torch.tensor([1e30, 1e-30, 3e38, 0.0, 1e-40])
+    w_scale = torch.rand((n,), generator=g, device="cuda") * 0.009 + 1e-3
+    w_scale[:9] = torch.tensor([float("inf"), float("-inf"), float("nan"), 3e38, 1e-38, 1e-41, 0.0, -0.0, 1e20])
+    bias = torch.randn((n,), generator=g, device="cuda") * 0.02
+    bias[4:6] = 0.0  # outputs of the tiny weight scales stay tiny: bf16 subnormals
+    bias[10:16] = torch.tensor([float("nan"), float("inf"), float("-inf"), -0.0, 3e38, -3e38])
+
+    ref_out = torch.empty((m, n), dtype=torch.bfloat16, device="cuda")
+    mg.check(lib, lib.ref_int8_linear(p(a), p(w), p(a_scale), p(w_scale), p(bias), p(ref_out), m, n, k, 0,
+                                      mg.stream()))
+    torch.cuda.synchronize()
+    r = ref_out.float()
+    assert torch.isinf(r).any() and torch.isnan(r).any()
+    assert ((r != 0) & (r.abs() < 2.0 ** -126)).any()  # bf16 subnormal outputs
+    for name, sel in GEMM_KERNELS.items():
+        with _Forced(gemm=sel):
+            out = K.turing_int8_linear(a, w, a_scale, w_scale, bias)
+        torch.cuda.synchronize()
+        assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16)), f"{name}: bf16 output differs"
