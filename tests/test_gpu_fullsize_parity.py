@@ -11,12 +11,14 @@ not a sample.  The fused tanh-GELU quantizer of the FFN-down input is checked th
 way at full size, against both the reference's row-buffer kernel
 (convrot_quant.cu:715-745) and its staged two-kernel path (convrot_quant.cu:184-358).
 The W8A8 epilogue is also compared with the reference's at non-finite, overflowing,
-subnormal and signed-zero scales and biases.
+subnormal and signed-zero scales and biases, and every quantizer kernel with the
+reference's on NaN / inf / subnormal, huge and scale-floor rows.
 """
 
 import sys
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -200,3 +202,31 @@ def test_linear_epilogue_extremes_against_reference_kernel(K, ref):
             out = K.turing_int8_linear(a, w, a_scale, w_scale, bias)
         torch.cuda.synchronize()
         assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16)), f"{name}: bf16 output differs"
+
+
+@needs_ref
+@pytest.mark.parametrize("bits", [8, 4])
+@pytest.mark.parametrize("k", [5120, 13824])
+def test_quantizer_edge_rows_against_reference_kernel(K, ref, k, bits):
+    """NaN / inf / subnormal / largest-finite rows, rows at 1e30-3e37 and 2^120-2^124, and
+    rows whose scale sits at its floor (int8 1e-30, int4 1e-10), through every B200
+    quantizer kernel and the reference's row-buffer kernel (convrot_quant.cu:665-713):
+    codes and scales bit for bit."""
+    from test_gpu_quant_variants import large_rows, special_rows, tiny_rows, to_bf16_tensor
+
+    mg, lib = ref
+    p = mg.p
+    xb = np.concatenate([special_rows(18, k, seed=k + 1), large_rows(14, k, seed=k + 2), tiny_rows(16, k, seed=k + 3)])
+    x = to_bf16_tensor(xb).cuda()
+    rows = x.shape[0]
+    ref_codes = torch.empty((rows, k if bits == 8 else k // 2), dtype=torch.int8, device="cuda")
+    ref_scales = torch.empty((rows, 1), dtype=torch.float32, device="cuda")
+    mg.check(lib, lib.ref_bf16_convrot_quantize(p(x), p(ref_codes), p(ref_scales), rows, k, bits, 0, 1024,
+                                                mg.stream()))
+    quantize = K.turing_bf16_int8_convrot_quantize if bits == 8 else K.turing_bf16_int4_convrot_quantize
+    for name, sel in QUANT_KERNELS.items():
+        with _Forced(quant=sel):
+            codes, scales = quantize(x, 256)
+        torch.cuda.synchronize()
+        assert torch.equal(codes, ref_codes), f"{name}: codes differ"
+        assert _same_scales(scales, ref_scales), f"{name}: scales differ"
