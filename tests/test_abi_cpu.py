@@ -26,6 +26,27 @@ def test_library_exports_every_declared_symbol():
     assert lib.ctu_version() >= (0 << 16) | (1 << 8)
 
 
+def test_c99_binding_links_and_reports_errors(tmp_path):
+    """include/ctu_b200.h compiles as strict C99 and the built library links into a C
+    program (as a cgo / N-API / JNI binding would use it); tests/native/abi_c99.c checks
+    the argument contracts, sizes and host-side plans there, without a GPU."""
+    import shutil
+    import subprocess
+
+    from comfyui_turing_utils_kernel import _lib
+
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lib_path = _lib.library_path()
+    exe = tmp_path / "abi_c99"
+    subprocess.run(["gcc", "-std=c99", "-pedantic", "-Wall", "-Wextra", "-Werror", "-I", str(ROOT / "include"),
+                    "-o", str(exe), str(ROOT / "tests" / "native" / "abi_c99.c"), str(lib_path),
+                    f"-Wl,-rpath,{lib_path.parent}"], check=True)
+    run = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert run.returncode == 0, run.stderr
+    assert "C99 ABI checks passed" in run.stdout
+
+
 def test_argument_errors_are_reported_without_a_gpu():
     import ctypes
 
